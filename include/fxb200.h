@@ -1,0 +1,231 @@
+/*
+ * fxb200.h - C ABI of libfxb200.so, the sm_100a (B200) kernels behind the
+ * fxlm / fxgpu operator surface.
+ *
+ * The reference launches runtime-compiled HIP kernels through ctypes
+ * (ml/fxgpu/hip_kernel.py:50-145: compile_kernel / compile_module / launch).
+ * This library is built ahead of time and exposes one plain C function per
+ * operation instead. Conventions:
+ *   - every pointer is a device pointer owned by the caller; the library
+ *     never allocates or frees device memory (workspaces are passed in, their
+ *     sizes come from the *_workspace functions);
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); no function
+ *     synchronises the host except fxb_device_error;
+ *   - functions return FXB_OK (0) or a negative FXB_E* code; the message of
+ *     the last failure on the calling thread is returned by fxb_last_error().
+ *     Nothing exits, aborts or traps.
+ *   - dtype codes: FXB_DTYPE_F32 / F16 / BF16.
+ */
+#ifndef FXB200_H
+#define FXB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FXB_OK 0
+#define FXB_EINVAL (-1)      /* bad shape / stride / alignment / pointer */
+#define FXB_EUNSUPPORTED (-2) /* valid request this build does not implement */
+#define FXB_ECUDA (-3)       /* CUDA runtime / driver error (see fxb_last_error) */
+
+#define FXB_DTYPE_F32 0
+#define FXB_DTYPE_F16 1
+#define FXB_DTYPE_BF16 2
+
+/* ------------------------------------------------------------------ misc */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fxb_version(void);
+
+/* Message of the last failed call on this thread ("" if none).
+ * Replaces the RuntimeError text of _chk, ml/fxgpu/hip_kernel.py:45-47. */
+const char* fxb_last_error(void);
+
+/* Reads (and with clear != 0 resets) the device error word that kernels set
+ * when a bounded wait expires (bit 1 GEMM, 2 attention, 4 gather). Synchronises
+ * the current device. No reference counterpart (the reference has no bounded
+ * waits). */
+int fxb_device_error(int32_t* code, int32_t clear);
+
+/* Number of streaming multiprocessors of the current device (grid sizing). */
+int fxb_num_sms(int32_t* out);
+
+/* ABI self-check for bindings: sizeof(fxb_gemm_args) for which == 0,
+ * sizeof(fxb_attn_args) for which == 1, 0 otherwise. */
+size_t fxb_abi_struct_size(int32_t which);
+
+/* ------------------------------------------------------------------ RMSNorm */
+
+/* y = x * rsqrt(mean(x^2) + eps) * w, rstd saved (fp32, one per row).
+ * x, y: (rows, D) contiguous; w: (D,). D % 8 == 0, D <= 8192.
+ * Replaces rms_norm_fwd (ml/fxlm/kernels/norm.hip:33) as launched by
+ * _RMSNorm.forward (ml/fxlm/norm.py:45-60). */
+int fxb_rmsnorm_fwd(int32_t dtype, const void* x, const void* w, void* y, float* rstd,
+                    int64_t rows, int32_t D, float eps, void* stream);
+
+/* Bytes of fp32 workspace fxb_rmsnorm_bwd needs for the dw partial sums. */
+size_t fxb_rmsnorm_bwd_workspace(int64_t rows, int32_t D);
+
+/* dx = rstd*w*dy - x*rstd^3*sum(x*w*dy)/D ; dw = sum_rows x*rstd*dy.
+ * dw (dtype dw_dtype, e.g. an fp32 flat-gradient slot) is written
+ * (dw_accumulate == 0) or added to (dw_accumulate != 0). D <= 2048 for 16-bit
+ * dtypes (1024 for fp32). Deterministic: per-block partials, then a
+ * fixed-order sum.
+ * Replaces rms_norm_bwd_dx + rms_norm_bwd_dw + part.sum(0)
+ * (ml/fxlm/kernels/norm.hip:64,102; ml/fxlm/norm.py:62-84). */
+int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rstd,
+                    const void* dy, void* dx, void* dw, int32_t dw_dtype,
+                    int32_t dw_accumulate, float* workspace, int64_t rows, int32_t D,
+                    void* stream);
+
+/* ------------------------------------------------------------------ cross entropy */
+
+/* Row-wise softmax cross entropy with the gradient written in the same pass.
+ *   loss_sum += sum over valid rows of (logsumexp(row) - row[target])
+ *   grad[r,:] = (softmax(row) - onehot(target)) * (*mul)   (0 for ignored rows)
+ * A row is valid when target != ignore_index and 0 <= target < V.
+ * grad may be NULL (loss only) or equal to logits (in place).
+ * logits/grad: (rows, V) with row stride ld (elements); target int64 (rows,);
+ * loss_sum and mul are fp32 device scalars (no host sync).
+ * Replaces ce_fwd_grad (ml/fxlm/kernels/ce.hip:32) as launched by _ce_rows
+ * (ml/fxlm/cross_entropy.py:47-59). */
+int fxb_ce_fwd_grad(int32_t dtype, const void* logits, int64_t ld, const int64_t* target,
+                    void* grad, float* loss_sum, const float* mul, int64_t rows, int32_t V,
+                    int64_t ignore_index, void* stream);
+
+/* ------------------------------------------------------------------ FlatAdamW */
+
+/* scratch[0] += sum(g^2); flags |= 1 if any g is non-finite. g: flat (n,).
+ * Replaces adamw_sumsq (ml/fxlm/kernels/optim.hip:26) over the per-tensor
+ * TensorList of FlatAdamW._chunks (ml/fxlm/optim.py:107-144). */
+int fxb_adamw_sumsq(int32_t gdtype, const void* grad, int64_t n, float* scratch,
+                    int32_t* flags, void* stream);
+
+/* One thread: found_inf = flags || !isfinite(scratch[0]);
+ * norm = sqrt(scratch[0]) / scale; scratch[1] = clip coefficient
+ * min(1, max_norm/(norm+1e-6)) (0 when found_inf); step += !found_inf;
+ * flags and scratch[0] reset for the next step.
+ * Replaces adamw_final (ml/fxlm/kernels/optim.hip:77-93). */
+int fxb_adamw_final(float* scratch, int32_t* flags, int32_t* step, float* found_inf,
+                    float* norm_out, const float* scale, float max_norm, void* stream);
+
+/* Flat decoupled-weight-decay AdamW over n elements (skipped when *found_inf):
+ *   g = grad * scratch[1] / scale; w -= lr*wd*w (segments with seg_wd != 0);
+ *   m = b1*m + (1-b1) g; v = b2*v + (1-b2) g^2;
+ *   w -= lr * (m / (1-b1^step)) / (sqrt(v / (1-b2^step)) + eps);
+ *   master = w; param = (pdtype) w; grad = 0 (the gradient is consumed, also
+ *   when the step is skipped, so the buffer is ready for the next backward).
+ * Segments: seg_end[i] (exclusive, device int64, ascending, multiples of 8) and
+ * seg_wd[i] (device int32), nseg <= 1024.
+ * Replaces adamw_update (ml/fxlm/kernels/optim.hip:96-162). */
+int fxb_adamw_update(int32_t gdtype, int32_t pdtype, const void* grad, float* master,
+                     float* m, float* v, void* param, int64_t n, const int64_t* seg_end,
+                     const int32_t* seg_wd, int32_t nseg, const float* scratch,
+                     const float* found_inf, const float* scale, const int32_t* step,
+                     float lr, float beta1, float beta2, float eps, float weight_decay,
+                     void* stream);
+
+/* ------------------------------------------------------------------ GEMM */
+
+/* Epilogues applied to acc = sum_k A[m,k] * B[n,k] (fp32 in tensor memory). */
+#define FXB_EPI_STORE 0     /* C = alpha*acc */
+#define FXB_EPI_RESIDUAL 1  /* C = alpha*acc + R  (R may alias C: accumulate) */
+#define FXB_EPI_GELU 2      /* Z = acc ; C = gelu_tanh(acc) */
+#define FXB_EPI_DGELU 3     /* C = acc * gelu_tanh'(R)   (R = pre-activation) */
+#define FXB_EPI_BIAS 4      /* C = acc + bias[n] */
+#define FXB_EPI_BIAS_GELU 5 /* Z = acc + bias[n] ; C = gelu_tanh(Z) */
+#define FXB_EPI_BIAS_SILU 6 /* Z = acc + bias[n] ; C = silu(Z) */
+#define FXB_EPI_ACCUM_F32 7 /* C(fp32) += alpha*acc (red.add; enables split-K) */
+
+typedef struct fxb_gemm_args {
+  int32_t dtype;     /* A/B dtype: FXB_DTYPE_BF16 or FXB_DTYPE_F16 */
+  int32_t M, N, K;
+  const void* A;     /* a_trans == 0: (M,K) row stride lda; 1: (K,M) row stride lda */
+  int64_t lda;
+  int32_t a_trans;
+  const void* B;     /* b_trans == 0: (N,K) row stride ldb; 1: (K,N) row stride ldb */
+  int64_t ldb;
+  int32_t b_trans;
+  void* C;           /* (M,N) row stride ldc, dtype c_dtype */
+  int64_t ldc;
+  int32_t c_dtype;
+  int32_t epilogue;  /* FXB_EPI_* */
+  float alpha;
+  const void* R;     /* residual / pre-activation input, dtype c_dtype, row stride ldr */
+  int64_t ldr;
+  void* Z;           /* second output (pre-activation), dtype c_dtype, row stride ldz */
+  int64_t ldz;
+  const void* bias;  /* (N,), dtype c_dtype */
+} fxb_gemm_args;
+
+/* tcgen05 / TMEM GEMM with TMA-fed operands. Requires K % 8 == 0 for K-major
+ * operands and M (resp. N) % 8 == 0 for transposed ones (16-byte TMA rows),
+ * 16-byte aligned bases, N % 8 == 0 for C.
+ * Replaces the rocBLAS matmuls on the hot path: nn.Linear qkv/proj/fc/fc2
+ * (ml/fxlm/model.py:48-51,61,69-71), the linear-CE chunk mm's
+ * (ml/fxlm/cross_entropy.py:131-135,180) and the fxgpu dW mm
+ * (ml/fxgpu/fused_linear.py:94). */
+int fxb_gemm(const fxb_gemm_args* args, void* stream);
+
+/* ------------------------------------------------------------------ attention */
+
+typedef struct fxb_attn_args {
+  int32_t dtype;          /* FXB_DTYPE_BF16 or FXB_DTYPE_F16 */
+  int32_t B, T, H, D;     /* D = head dim (64 or 128) */
+  float scale;
+  int32_t causal;
+  /* (B,T,H,D) views with unit stride on D; strides in elements (b, t, h) */
+  const void* q; int64_t q_sb, q_st, q_sh;
+  const void* k; int64_t k_sb, k_st, k_sh;
+  const void* v; int64_t v_sb, v_st, v_sh;
+  void* o;       int64_t o_sb, o_st, o_sh;   /* forward output; backward input */
+  float* lse;                                /* (B,H,T) natural-log LSE of scaled scores */
+  const void* dout; int64_t do_sb, do_st, do_sh;
+  void* dq;      int64_t dq_sb, dq_st, dq_sh;
+  void* dk;      int64_t dk_sb, dk_st, dk_sh;
+  void* dv;      int64_t dv_sb, dv_st, dv_sh;
+  float* workspace;                          /* backward: fxb_attn_bwd_workspace bytes */
+} fxb_attn_args;
+
+/* Causal / non-causal flash-attention forward: o = softmax(q k^T * scale) v,
+ * lse = logsumexp of the scaled scores (natural log).
+ * Replaces attn_fwd (ml/fxlm/kernels/attention.hip:104) as launched by _fwd
+ * (ml/fxlm/attention.py:87-104). */
+int fxb_attn_fwd(const fxb_attn_args* args, void* stream);
+
+/* Workspace bytes for fxb_attn_bwd (delta = rowsum(dO*O), fp32 dQ staging). */
+size_t fxb_attn_bwd_workspace(int32_t B, int32_t T, int32_t H, int32_t D);
+
+/* Flash-attention backward: dq, dk, dv from q, k, v, o, lse, dout.
+ * Replaces attn_bwd_prep + attn_bwd_dkv + attn_bwd_dq
+ * (ml/fxlm/kernels/attention.hip:229,256,411) as launched by _bwd
+ * (ml/fxlm/attention.py:107-134). */
+int fxb_attn_bwd(const fxb_attn_args* args, void* stream);
+
+/* ------------------------------------------------------------------ embedding / glue */
+
+/* out[b,t,:] = tok[idx[b,t],:] + pos[t,:]. idx int64 (B*T). Rows of out are D
+ * contiguous. Replaces tok_emb(idx) + pos_emb[:T] (ml/fxlm/model.py:118). */
+int fxb_embedding_fwd(int32_t dtype, const int64_t* idx, const void* tok, const void* pos,
+                      void* out, int64_t B, int64_t T, int32_t D, int64_t V, void* stream);
+
+/* dtok_ws[idx[b,t],:] += dout[b,t,:], dpos_ws[t,:] += dout[b,t,:] (fp32
+ * workspaces, zeroed by the caller). Backward of ml/fxlm/model.py:118. */
+int fxb_embedding_bwd(int32_t dtype, const int64_t* idx, const void* dout, float* dtok_ws,
+                      float* dpos_ws, int64_t B, int64_t T, int32_t D, int64_t V,
+                      void* stream);
+
+/* dst[i] = (accumulate ? dst[i] : 0) + src[i] * (scale ? *scale : 1) for i < n.
+ * dst dtype ddtype, src dtype sdtype, scale an fp32 device scalar or NULL.
+ * Carries the linear-CE backward rescale (ml/fxlm/cross_entropy.py:140-149). */
+int fxb_axpy(int32_t ddtype, void* dst, int32_t sdtype, const void* src, const float* scale,
+             int32_t accumulate, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FXB200_H */

@@ -1,0 +1,258 @@
+// FlatAdamW kernels for sm_100a (HBM-bound).
+//
+// Semantics follow ml/fxlm/kernels/optim.hip: adamw_sumsq (:26-75, sum of
+// squared grads + non-finite flag), adamw_final (:77-93, found_inf / norm /
+// clip / step), adamw_update (:96-162, decoupled weight decay on ndim>=2
+// params, m/v update, bias correction with powf, fp32 master + low-precision
+// copy). The reference walks a list of per-parameter gradient tensors; here
+// gradients live in one flat buffer with the same offsets as the master, so
+// each kernel is a single grid-stride pass of 16-byte vectors, and the
+// per-parameter weight-decay flag becomes a sorted segment table.
+#include "common.cuh"
+#include "internal.h"
+
+namespace {
+
+template <typename G> FXB_DEV void load8(const G* p, float* f) {
+  if constexpr (sizeof(G) == 4) {
+    float4 a = *reinterpret_cast<const float4*>(p);
+    float4 b = *reinterpret_cast<const float4*>(p + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    unpack8<G>(*reinterpret_cast<const uint4*>(p), f);
+  }
+}
+template <typename P> FXB_DEV void store8(P* p, const float* f) {
+  if constexpr (sizeof(P) == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(f[4], f[5], f[6], f[7]);
+  } else {
+    *reinterpret_cast<uint4*>(p) = pack8<P>(f);
+  }
+}
+
+template <typename G>
+__global__ void __launch_bounds__(256)
+adamw_sumsq_kernel(const G* __restrict__ g, int64_t n, float* __restrict__ scratch,
+                   int* __restrict__ flags) {
+  float ss = 0.f;
+  int bad = 0;
+  const int64_t ngroups = n >> 3;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += stride) {
+    float f[8];
+    load8<G>(g + i * 8, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      ss += f[j] * f[j];
+      bad |= !isfinite(f[j]);
+    }
+  }
+  // tail (n not a multiple of 8)
+  if (blockIdx.x == 0) {
+    for (int64_t i = ngroups * 8 + threadIdx.x; i < n; i += blockDim.x) {
+      float f = to_f<G>(g[i]);
+      ss += f * f;
+      bad |= !isfinite(f);
+    }
+  }
+  __shared__ float sred[8];
+  __shared__ int bred[8];
+  ss = warp_sum(ss);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) { sred[wid] = ss; bred[wid] = bad; }
+  __syncthreads();
+  if (wid == 0) {
+    ss = lane < 8 ? sred[lane] : 0.f;
+    bad = lane < 8 ? bred[lane] : 0;
+    ss = warp_sum(ss);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    if (lane == 0) {
+      if (ss != 0.f) atomicAdd(&scratch[0], ss);
+      if (bad) atomicOr(flags, 1);
+    }
+  }
+}
+
+__global__ void adamw_final_kernel(float* scratch, int* flags, int* step, float* found_inf,
+                                   float* norm_out, const float* scale, float max_norm) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int bad = (*flags != 0) || !isfinite(scratch[0]);
+  *found_inf = bad ? 1.f : 0.f;
+  const float norm = sqrtf(scratch[0]) / (*scale);
+  *norm_out = norm;
+  scratch[1] = bad ? 0.f : fminf(1.f, max_norm / (norm + 1e-6f));
+  if (!bad) *step += 1;
+  *flags = 0;
+  scratch[0] = 0.f;
+}
+
+constexpr int kMaxSeg = 1024;
+
+template <typename G, typename P>
+__global__ void __launch_bounds__(256)
+adamw_update_kernel(const G* g, float* __restrict__ master, float* __restrict__ m,
+                    float* __restrict__ v, P* __restrict__ p, int64_t n,
+                    const int64_t* __restrict__ seg_end, const int* __restrict__ seg_wd, int nseg,
+                    const float* __restrict__ scratch, const float* __restrict__ found_inf,
+                    const float* __restrict__ scale_p, const int* __restrict__ step_p, float lr,
+                    float b1, float b2, float eps, float wd) {
+  const int64_t ngroups = n >> 3;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (*found_inf != 0.f) {
+    // step skipped: master / m / v untouched, the gradient is still consumed
+    for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < ngroups; gi += stride) {
+      const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      store8<G>(const_cast<G*>(g) + gi * 8, z);
+    }
+    return;
+  }
+  __shared__ int64_t s_end[kMaxSeg];
+  __shared__ int s_wd[kMaxSeg];
+  for (int i = threadIdx.x; i < nseg; i += blockDim.x) {
+    s_end[i] = seg_end[i];
+    s_wd[i] = seg_wd[i];
+  }
+  __syncthreads();
+  const float inv = scratch[1] / (*scale_p);  // clip coefficient / loss scale
+  const int step = *step_p;
+  const float bc1 = 1.f - powf(b1, (float)step);
+  const float bc2 = 1.f - powf(b2, (float)step);
+  const float b1c = 1.f - b1, b2c = 1.f - b2;
+  const float lrwd = lr * wd;
+  const float zero8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < ngroups; gi += stride) {
+    const int64_t e0 = gi * 8;
+    // segment containing e0: first index with s_end > e0
+    int lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+      int mid = (lo + hi) >> 1;
+      if (s_end[mid] > e0) hi = mid; else lo = mid + 1;
+    }
+    const bool wd_on = s_wd[lo] != 0;
+    float gv[8], mw[8], mv[8], vv[8];
+    load8<G>(g + e0, gv);
+    store8<G>(const_cast<G*>(g) + e0, zero8);  // gradient consumed
+    load8<float>(master + e0, mw);
+    load8<float>(m + e0, mv);
+    load8<float>(v + e0, vv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float gg = gv[j] * inv;
+      float w = mw[j];
+      if (wd_on) w -= lrwd * w;
+      float a = mv[j] * b1 + b1c * gg;
+      float b = vv[j] * b2 + b2c * gg * gg;
+      mv[j] = a;
+      vv[j] = b;
+      w -= lr * (a / bc1) / (sqrtf(b / bc2) + eps);
+      mw[j] = w;
+    }
+    store8<float>(master + e0, mw);
+    store8<float>(m + e0, mv);
+    store8<float>(v + e0, vv);
+    store8<P>(p + e0, mw);
+  }
+}
+
+template <typename G, typename P>
+int launch_update(const void* g, float* master, float* m, float* v, void* p, int64_t n,
+                  const int64_t* se, const int* sw, int nseg, const float* scratch,
+                  const float* fi, const float* sc, const int* stp, float lr, float b1, float b2,
+                  float eps, float wd, cudaStream_t st) {
+  int64_t groups = n >> 3;
+  int64_t want = (groups + 255) / 256;
+  int64_t cap = (int64_t)fxb::num_sms() * 8;
+  int blocks = (int)(want < cap ? want : cap);
+  if (blocks < 1) blocks = 1;
+  adamw_update_kernel<G, P><<<blocks, 256, 0, st>>>(static_cast<const G*>(g), master, m, v,
+                                                    static_cast<P*>(p), n, se, sw, nseg, scratch,
+                                                    fi, sc, stp, lr, b1, b2, eps, wd);
+  return fxb::check_launch("adamw_update");
+}
+
+template <typename G>
+int dispatch_update_p(int32_t pdtype, const void* g, float* master, float* m, float* v, void* p,
+                      int64_t n, const int64_t* se, const int* sw, int nseg, const float* scratch,
+                      const float* fi, const float* sc, const int* stp, float lr, float b1,
+                      float b2, float eps, float wd, cudaStream_t st) {
+  switch (pdtype) {
+    case FXB_DTYPE_BF16:
+      return launch_update<G, __nv_bfloat16>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, b1, b2, eps, wd, st);
+    case FXB_DTYPE_F16:
+      return launch_update<G, __half>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, b1, b2, eps, wd, st);
+    default:
+      return launch_update<G, float>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, b1, b2, eps, wd, st);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int fxb_adamw_sumsq(int32_t gdtype, const void* grad, int64_t n, float* scratch, int32_t* flags,
+                    void* stream) {
+  if (fxb::dtype_size(gdtype) == 0) return fxb::set_error(FXB_EINVAL, "adamw_sumsq: bad dtype");
+  if (n < 0 || !scratch || !flags) return fxb::set_error(FXB_EINVAL, "adamw_sumsq: bad args");
+  if (n == 0) return FXB_OK;
+  if (!fxb::aligned16(grad)) return fxb::set_error(FXB_EINVAL, "adamw_sumsq: grad not 16-byte aligned");
+  cudaStream_t st = fxb::as_stream(stream);
+  int64_t want = ((n >> 3) + 255) / 256;
+  int64_t cap = (int64_t)fxb::num_sms() * 8;
+  int blocks = (int)(want < cap ? want : cap);
+  if (blocks < 1) blocks = 1;
+  switch (gdtype) {
+    case FXB_DTYPE_BF16:
+      adamw_sumsq_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(grad), n, scratch, flags);
+      break;
+    case FXB_DTYPE_F16:
+      adamw_sumsq_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(grad), n, scratch, flags);
+      break;
+    default:
+      adamw_sumsq_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(grad), n, scratch, flags);
+  }
+  return fxb::check_launch("adamw_sumsq");
+}
+
+int fxb_adamw_final(float* scratch, int32_t* flags, int32_t* step, float* found_inf,
+                    float* norm_out, const float* scale, float max_norm, void* stream) {
+  if (!scratch || !flags || !step || !found_inf || !norm_out || !scale)
+    return fxb::set_error(FXB_EINVAL, "adamw_final: NULL pointer");
+  adamw_final_kernel<<<1, 32, 0, fxb::as_stream(stream)>>>(scratch, flags, step, found_inf,
+                                                          norm_out, scale, max_norm);
+  return fxb::check_launch("adamw_final");
+}
+
+int fxb_adamw_update(int32_t gdtype, int32_t pdtype, const void* grad, float* master, float* m,
+                     float* v, void* param, int64_t n, const int64_t* seg_end,
+                     const int32_t* seg_wd, int32_t nseg, const float* scratch,
+                     const float* found_inf, const float* scale, const int32_t* step, float lr,
+                     float beta1, float beta2, float eps, float weight_decay, void* stream) {
+  if (fxb::dtype_size(gdtype) == 0 || fxb::dtype_size(pdtype) == 0)
+    return fxb::set_error(FXB_EINVAL, "adamw_update: bad dtype");
+  if (n < 0 || (n & 7) != 0)
+    return fxb::set_error(FXB_EINVAL, "adamw_update: n=%lld must be a multiple of 8", (long long)n);
+  if (nseg < 1 || nseg > kMaxSeg)
+    return fxb::set_error(FXB_EINVAL, "adamw_update: nseg=%d outside [1, %d]", nseg, kMaxSeg);
+  if (!fxb::aligned16(grad) || !fxb::aligned16(master) || !fxb::aligned16(m) ||
+      !fxb::aligned16(v) || !fxb::aligned16(param))
+    return fxb::set_error(FXB_EINVAL, "adamw_update: buffers must be 16-byte aligned");
+  if (!seg_end || !seg_wd || !scratch || !found_inf || !scale || !step)
+    return fxb::set_error(FXB_EINVAL, "adamw_update: NULL pointer");
+  if (n == 0) return FXB_OK;
+  cudaStream_t st = fxb::as_stream(stream);
+  switch (gdtype) {
+    case FXB_DTYPE_BF16:
+      return dispatch_update_p<__nv_bfloat16>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, beta1, beta2, eps, weight_decay, st);
+    case FXB_DTYPE_F16:
+      return dispatch_update_p<__half>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, beta1, beta2, eps, weight_decay, st);
+    default:
+      return dispatch_update_p<float>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, beta1, beta2, eps, weight_decay, st);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,779 @@
+// Flash attention forward / backward on tcgen05 tensor cores (sm_100a).
+//
+// Semantics follow the reference FA2 kernels (ml/fxlm/kernels/attention.hip):
+//   forward  :104-224  o = softmax(q k^T * scale [causal: key <= query]) v,
+//                      lse = max + log(sum) of the scaled scores, natural log
+//                      (:210-223), written (B,H,T) fp32;
+//   bwd prep :229-251  delta = rowsum(dO * O);
+//   bwd      :256-534  P = exp(s*scale - lse), dS = P * (dP - delta) * scale,
+//                      dV = P^T dO, dK = dS^T Q, dQ = dS K.
+// B200 design (new): 128x128 tiles; TMA (4-D maps over the strided (B,T,H,D)
+// views, no copies, no multicast) feeds shared memory; one thread issues
+// tcgen05.mma into tensor memory; softmax warps own one row each and read
+// scores with tcgen05.ld. Forward keeps O in registers and receives each P.V
+// product from TMEM (online-softmax rescale in registers). Backward works per
+// key tile: S^T and dP^T land in TMEM, dV and dK accumulate in TMEM across
+// query tiles, and each dQ partial is reduced into an fp32 workspace with
+// vector red.add. Every wait is bounded (FXB_DERR_ATTN_WAIT).
+#include "common.cuh"
+#include "internal.h"
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr int TILE = 128;
+constexpr int kThreads = 192;  // warps 0-3 softmax, 4 MMA, 5 TMA
+
+struct FwdParams {
+  int B, T, H, nqt, nkt, causal;
+  float scale_log2;
+  void* o;
+  int64_t o_sb, o_st, o_sh;
+  float* lse;
+  int* err;
+};
+
+struct BwdParams {
+  int B, T, H, nqt, nkt, causal;
+  float scale_log2;  // scale * log2(e)
+  float scale;
+  const float* lse;
+  const float* delta;
+  float* dq_acc;  // (B*H, T, D) fp32
+  void* dk;
+  int64_t dk_sb, dk_st, dk_sh;
+  void* dv;
+  int64_t dv_sb, dv_st, dv_sh;
+  int* err;
+};
+
+// byte offset of 16-byte chunk `chunk` (0..15 across two 64-column blocks) of
+// row `r` in a [128 rows][128 cols] 16-bit tile stored as two 128B-swizzled
+// column blocks of 16 KB
+FXB_DEV uint32_t sw128_offset(int r, int chunk) {
+  const int blk = chunk >> 3, c = chunk & 7;
+  return (uint32_t)(blk * 16384 + r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+template <typename T> FXB_DEV uint32_t pack2(float a, float b) {
+  T lo = from_f<T>(a), hi = from_f<T>(b);
+  return (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) |
+         ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+}
+
+// K-major operand tile [128 rows][D] stored as D/64 swizzled column blocks
+FXB_DEV uint64_t kmajor_desc(uint32_t base, int kk) {
+  return umma_desc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+// MN-major view of the same storage: MN along the columns, K along the rows
+FXB_DEV uint64_t mnmajor_desc(uint32_t base, int kk) {
+  return umma_desc_sw128(base + kk * 2048, 16384, 1024);
+}
+
+// ============================================================ forward
+template <int DH, int FMT>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
+  constexpr int QB = TILE * DH * 2;  // bytes of one [128][DH] tile
+  constexpr int NBOX = DH / 64;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base;
+  const uint32_t sK = sQ + QB;          // 2 stages
+  const uint32_t sV = sK + 2 * QB;      // 2 stages
+  const uint32_t sP = sV + 2 * QB;      // [128][128] 16-bit
+  const uint32_t bars = sP + 32768;
+  const uint32_t q_full = bars;
+  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto v_full = [&](int s) { return bars + 8u * (3 + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (5 + s); };
+  auto s_full = [&](int s) { return bars + 8u * (7 + s); };
+  auto s_empty = [&](int s) { return bars + 8u * (9 + s); };
+  const uint32_t p_full = bars + 8u * 11;
+  const uint32_t pv_full = bars + 8u * 12;
+  const uint32_t final_bar = bars + 8u * 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * 14);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = (p.causal ? (p.nqt - 1 - (int)blockIdx.x) : (int)blockIdx.x);
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int q0 = qt * TILE;
+  const int n_kv = p.causal ? min(qt + 1, p.nkt) : p.nkt;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+      mbar_init(s_full(s), 1);
+      mbar_init(s_empty(s), 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_full, 1);
+    mbar_init(final_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;         // S buffers at columns 0 and 128
+  const uint32_t tPV = tmem + 256;  // P.V product, DH columns
+
+  if (warp == 5) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_expect_tx(q_full, QB);
+#pragma unroll
+      for (int c = 0; c < NBOX; ++c) tma_load_4d(sQ + c * 16384, &tmQ, q_full, 64 * c, q0, h, b);
+      int armed = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_empty(st), ((j >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
+        mbar_expect_tx(k_full(st), QB);
+#pragma unroll
+        for (int c = 0; c < NBOX; ++c)
+          tma_load_4d(sK + st * QB + c * 16384, &tmK, k_full(st), 64 * c, j * TILE, h, b);
+        mbar_expect_tx(v_full(st), QB);
+#pragma unroll
+        for (int c = 0; c < NBOX; ++c)
+          tma_load_4d(sV + st * QB + c * 16384, &tmV, v_full(st), 64 * c, j * TILE, h, b);
+        armed = j + 1;
+      }
+      // drain what was issued
+      mbar_wait(q_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+      for (int j = (armed > 2 ? armed - 2 : 0); j < armed; ++j) {
+        mbar_wait(k_full(j & 1), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+        mbar_wait(v_full(j & 1), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 4) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
+      constexpr uint32_t IPV = umma_idesc_f16(FMT, 0, 1, TILE, DH);
+      bool ok = mbar_wait(q_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(k_full(st), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(s_empty(st), ((j >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk)
+          umma_f16(tS + st * TILE, kmajor_desc(sQ, kk), kmajor_desc(sK + st * QB, kk), IS, kk > 0);
+        umma_commit(s_full(st));
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
+        const int st = j & 1;
+        if (!mbar_wait(p_full, j & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        if (!mbar_wait(v_full(st), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TILE / 16; ++kk)
+          umma_f16(tPV, kmajor_desc(sP, kk), mnmajor_desc(sV + st * QB, kk), IPV, kk > 0);
+        umma_commit(pv_full);
+        umma_commit(kv_empty(st));
+      }
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, p.err, FXB_DERR_ATTN_WAIT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ softmax warps: row r
+    const int r = warp * 32 + lane;
+    const int q = q0 + r;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float o[DH];
+#pragma unroll
+    for (int d = 0; d < DH; ++d) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f, a_prev = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(s_full(st), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      tc_fence_after();
+      const int kv0 = j * TILE;
+      const uint32_t sAddr = tS + st * TILE + lane_off;
+      const bool need_mask = (kv0 + TILE > p.T) || (p.causal && kv0 + TILE > q0);
+      // pass 1: row max
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(sAddr + c * 32, rr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = kv0 + c * 32 + i;
+          float y = __uint_as_float(rr[i]) * p.scale_log2;
+          if (need_mask && (col >= p.T || (p.causal && col > q))) y = -INFINITY;
+          mx = fmaxf(mx, y);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = exp2f(m - m_new);
+      // P.V of the previous tile must be folded in before P is overwritten
+      if (j > 0) {
+        if (!mbar_wait(pv_full, (j - 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(tPV + lane_off + c * 32, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * a_prev + __uint_as_float(rr[i]);
+        }
+      }
+      // pass 2: probabilities -> P (16-bit, swizzled) and row sum
+      float rs = 0.f;
+      uint8_t* pbase = gbase + (sP - base);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(sAddr + c * 32, rr);
+        tmem_wait_ld();
+        float pv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = kv0 + c * 32 + i;
+          float y = __uint_as_float(rr[i]) * p.scale_log2;
+          if (need_mask && (col >= p.T || (p.causal && col > q))) y = -INFINITY;
+          pv[i] = exp2f(y - m_new);
+          rs += pv[i];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 w;
+          w.x = pack2<T16>(pv[8 * u + 0], pv[8 * u + 1]);
+          w.y = pack2<T16>(pv[8 * u + 2], pv[8 * u + 3]);
+          w.z = pack2<T16>(pv[8 * u + 4], pv[8 * u + 5]);
+          w.w = pack2<T16>(pv[8 * u + 6], pv[8 * u + 7]);
+          *reinterpret_cast<uint4*>(pbase + sw128_offset(r, c * 4 + u)) = w;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_empty(st));
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+      l = l * alpha + rs;
+      m = m_new;
+      a_prev = alpha;
+    }
+    if (ok && mbar_wait(pv_full, (n_kv - 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < DH / 32; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(tPV + lane_off + c * 32, rr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * a_prev + __uint_as_float(rr[i]);
+      }
+      if (q < p.T) {
+        const float inv = 1.f / l;
+        T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh;
+#pragma unroll
+        for (int d = 0; d < DH; d += 8) {
+          float f[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = o[d + i] * inv;
+          *reinterpret_cast<uint4*>(orow + d) = pack8<T16>(f);
+        }
+        p.lse[(int64_t)bh * p.T + q] = (m + log2f(l)) * kLn2;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================ backward
+// delta[bh, t] = sum_d dO*O ; zero the dQ accumulator
+template <typename T16, int DH>
+__global__ void attn_bwd_prep_kernel(const T16* __restrict__ o, int64_t o_sb, int64_t o_st,
+                                     int64_t o_sh, const T16* __restrict__ dout, int64_t do_sb,
+                                     int64_t do_st, int64_t do_sh, float* __restrict__ delta,
+                                     float* __restrict__ dq_acc, int B, int T, int H) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (b*H + h)*T + t
+  if (row >= (int64_t)B * H * T) return;
+  const int t = (int)(row % T);
+  const int bh = (int)(row / T);
+  const int b = bh / H, h = bh - b * H;
+  const T16* orow = o + b * o_sb + (int64_t)t * o_st + h * o_sh;
+  const T16* grow = dout + b * do_sb + (int64_t)t * do_st + h * do_sh;
+  float s = 0.f;
+#pragma unroll
+  for (int d = 0; d < DH; d += 8) {
+    float a[8], g[8];
+    unpack8<T16>(*reinterpret_cast<const uint4*>(orow + d), a);
+    unpack8<T16>(*reinterpret_cast<const uint4*>(grow + d), g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += a[i] * g[i];
+  }
+  delta[row] = s;
+  float4* z = reinterpret_cast<float4*>(dq_acc + row * DH);
+#pragma unroll
+  for (int d = 0; d < DH / 4; ++d) z[d] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// dq = dq_acc * scale in the caller's layout
+template <typename T16, int DH>
+__global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, T16* __restrict__ dq,
+                                     int64_t dq_sb, int64_t dq_st, int64_t dq_sh, float scale,
+                                     int B, int T, int H) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // row*DH/8 + chunk
+  const int64_t rows = (int64_t)B * H * T;
+  if (idx >= rows * (DH / 8)) return;
+  const int64_t row = idx / (DH / 8);
+  const int d = (int)(idx % (DH / 8)) * 8;
+  const int t = (int)(row % T);
+  const int bh = (int)(row / T);
+  const int b = bh / H, h = bh - b * H;
+  const float4* src = reinterpret_cast<const float4*>(dq_acc + row * DH + d);
+  float4 u = src[0], w = src[1];
+  float f[8] = {u.x * scale, u.y * scale, u.z * scale, u.w * scale,
+                w.x * scale, w.y * scale, w.z * scale, w.w * scale};
+  *reinterpret_cast<uint4*>(dq + b * dq_sb + (int64_t)t * dq_st + h * dq_sh + d) = pack8<T16>(f);
+}
+
+FXB_DEV void red_add_v4f(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                const BwdParams p) {
+  constexpr int DH = 64;
+  using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
+  constexpr int QB = TILE * DH * 2;  // 16 KB
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sK = base;
+  const uint32_t sV = sK + QB;
+  const uint32_t sQ = sV + QB;        // 2 stages
+  const uint32_t sDO = sQ + 2 * QB;   // 2 stages
+  const uint32_t sPT = sDO + 2 * QB;  // [128 kv][128 q] 16-bit
+  const uint32_t sDS = sPT + 32768;   // [128 kv][128 q] 16-bit
+  const uint32_t sStat = sDS + 32768; // lse2[2][128], delta[2][128] fp32
+  float* lse_s = reinterpret_cast<float*>(gbase + (sStat - base));
+  float* del_s = lse_s + 256;
+  const uint32_t bars = sStat + 2048;
+  const uint32_t kv_full = bars;
+  auto qdo_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto qdo_empty = [&](int s) { return bars + 8u * (3 + s); };
+  const uint32_t s_full = bars + 8u * 5;
+  const uint32_t s_empty = bars + 8u * 6;
+  const uint32_t ds_full = bars + 8u * 7;
+  const uint32_t dq_full = bars + 8u * 8;
+  const uint32_t dq_empty = bars + 8u * 9;
+  const uint32_t acc_full = bars + 8u * 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * 11);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int kv0 = kt * TILE;
+  const int i0 = p.causal ? kt : 0;
+  const int n_it = p.nqt - i0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(qdo_full(s), 1);
+      mbar_init(qdo_empty(s), 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 128);
+    mbar_init(ds_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 128);
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
+
+  if (warp == 5) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV); tma_prefetch_desc(&tmDO);
+      mbar_expect_tx(kv_full, 2 * QB);
+      tma_load_4d(sK, &tmK, kv_full, 0, kv0, h, b);
+      tma_load_4d(sV, &tmV, kv_full, 0, kv0, h, b);
+      int armed = 0;
+      for (int it = 0; it < n_it; ++it) {
+        const int st = it & 1;
+        const int qq0 = (i0 + it) * TILE;
+        if (!mbar_wait(qdo_empty(st), ((it >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
+        mbar_expect_tx(qdo_full(st), 2 * QB);
+        tma_load_4d(sQ + st * QB, &tmQ, qdo_full(st), 0, qq0, h, b);
+        tma_load_4d(sDO + st * QB, &tmDO, qdo_full(st), 0, qq0, h, b);
+        armed = it + 1;
+      }
+      mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+      for (int it = (armed > 2 ? armed - 2 : 0); it < armed; ++it)
+        mbar_wait(qdo_full(it & 1), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+    }
+    __syncwarp();
+  } else if (warp == 4) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t I_SS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);  // S^T, dP^T
+      constexpr uint32_t I_KV = umma_idesc_f16(FMT, 0, 1, TILE, DH);    // dV, dK
+      constexpr uint32_t I_Q = umma_idesc_f16(FMT, 1, 1, TILE, DH);     // dQ
+      bool ok = mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it & 1;
+        const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
+        if (!mbar_wait(qdo_full(st), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk)
+          umma_f16(tST, kmajor_desc(sK, kk), kmajor_desc(q_s, kk), I_SS, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk)
+          umma_f16(tDPT, kmajor_desc(sV, kk), kmajor_desc(do_s, kk), I_SS, kk > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(ds_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TILE / 16; ++kk)
+          umma_f16(tDV, kmajor_desc(sPT, kk), mnmajor_desc(do_s, kk), I_KV, (it > 0 || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < TILE / 16; ++kk)
+          umma_f16(tDK, kmajor_desc(sDS, kk), mnmajor_desc(q_s, kk), I_KV, (it > 0 || kk > 0));
+        if (!mbar_wait(dq_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TILE / 16; ++kk)
+          umma_f16(tDQ, mnmajor_desc(sDS, kk), mnmajor_desc(sK, kk), I_Q, kk > 0);
+        umma_commit(dq_full);
+        umma_commit(qdo_empty(st));
+      }
+      umma_commit(acc_full);
+      mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ softmax / dS warps
+    const int r = warp * 32 + lane;  // kv row for S^T/dP^T, q row for dQ
+    const int kv = kv0 + r;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    uint8_t* pt = gbase + (sPT - base);
+    uint8_t* ds = gbase + (sDS - base);
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = (i0 + it) * TILE;
+      const int sb = it & 1;
+      {
+        const int q = q0 + r;
+        const bool v = q < p.T;
+        lse_s[sb * 128 + r] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
+        del_s[sb * 128 + r] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
+      }
+      named_bar_sync(1, 128);
+      if (!mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = p.causal && (q0 < kv0 + TILE);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tST + lane_off + c * 32, sr);
+        tmem_ld32(tDPT + lane_off + c * 32, dr);
+        tmem_wait_ld();
+        float pv[32], dsv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int qc = c * 32 + i;
+          const int q = q0 + qc;
+          float pp = exp2f(__uint_as_float(sr[i]) * p.scale_log2 - lse_s[sb * 128 + qc]);
+          if (kv >= p.T || (diag && q < kv)) pp = 0.f;
+          pv[i] = pp;
+          dsv[i] = pp * (__uint_as_float(dr[i]) - del_s[sb * 128 + qc]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 w, x;
+          w.x = pack2<T16>(pv[8 * u + 0], pv[8 * u + 1]);
+          w.y = pack2<T16>(pv[8 * u + 2], pv[8 * u + 3]);
+          w.z = pack2<T16>(pv[8 * u + 4], pv[8 * u + 5]);
+          w.w = pack2<T16>(pv[8 * u + 6], pv[8 * u + 7]);
+          x.x = pack2<T16>(dsv[8 * u + 0], dsv[8 * u + 1]);
+          x.y = pack2<T16>(dsv[8 * u + 2], dsv[8 * u + 3]);
+          x.z = pack2<T16>(dsv[8 * u + 4], dsv[8 * u + 5]);
+          x.w = pack2<T16>(dsv[8 * u + 6], dsv[8 * u + 7]);
+          // P^T / dS^T smem is free: the previous iteration's dQ commit was waited below
+          *reinterpret_cast<uint4*>(pt + sw128_offset(r, c * 4 + u)) = w;
+          *reinterpret_cast<uint4*>(ds + sw128_offset(r, c * 4 + u)) = x;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_empty);
+      fence_proxy_async_smem();
+      mbar_arrive(ds_full);
+      // dQ partial of this query tile: row r is query q0 + r
+      if (!mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      tc_fence_after();
+      {
+        const int q = q0 + r;
+        float* dst = p.dq_acc + ((int64_t)bh * p.T + q) * DH;
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(tDQ + lane_off + c * 32, rr);
+          tmem_wait_ld();
+          if (q < p.T) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              red_add_v4f(dst + c * 32 + 4 * u, __uint_as_float(rr[4 * u]), __uint_as_float(rr[4 * u + 1]),
+                          __uint_as_float(rr[4 * u + 2]), __uint_as_float(rr[4 * u + 3]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_empty);
+    }
+    // final dK (scaled) and dV for key row kv
+    if (ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < DH / 32; ++c) {
+        uint32_t rk[32], rv[32];
+        tmem_ld32(tDK + lane_off + c * 32, rk);
+        tmem_ld32(tDV + lane_off + c * 32, rv);
+        tmem_wait_ld();
+        if (kv < p.T) {
+          T16* krow = static_cast<T16*>(p.dk) + b * p.dk_sb + (int64_t)kv * p.dk_st + h * p.dk_sh + c * 32;
+          T16* vrow = static_cast<T16*>(p.dv) + b * p.dv_sb + (int64_t)kv * p.dv_st + h * p.dv_sh + c * 32;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float fk[8], fv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              fk[i] = __uint_as_float(rk[8 * u + i]) * p.scale;
+              fv[i] = __uint_as_float(rv[8 * u + i]);
+            }
+            *reinterpret_cast<uint4*>(krow + 8 * u) = pack8<T16>(fk);
+            *reinterpret_cast<uint4*>(vrow + 8 * u) = pack8<T16>(fv);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================ host side
+// Each CTA allocates all 512 TMEM columns, so at most one CTA may be resident
+// per SM: the dynamic shared memory request is padded above half of the SM's
+// 228 KB so a second CTA of any TMEM-using kernel can never be co-scheduled.
+constexpr int kOneCtaPerSm = 120 * 1024;
+template <int DH> constexpr int fwd_smem() {
+  return (5 * TILE * DH * 2 + 32768 + 1024 + 256) > kOneCtaPerSm
+             ? (5 * TILE * DH * 2 + 32768 + 1024 + 256)
+             : kOneCtaPerSm;
+}
+constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 2 * 32768 + 2048 + 1024 + 256; }
+
+int make_map4(CUtensorMap* map, int dtype, const void* ptr, int D, int T, int H, int B,
+              int64_t sb, int64_t st, int64_t sh) {
+  uint64_t dims[4] = {(uint64_t)D, (uint64_t)T, (uint64_t)H, (uint64_t)B};
+  uint64_t strides[3] = {(uint64_t)st * 2, (uint64_t)sh * 2, (uint64_t)sb * 2};
+  uint32_t box[4] = {64, (uint32_t)TILE, 1, 1};
+  CUtensorMapDataType dt =
+      dtype == FXB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return fxb::encode_tiled(map, dt, 4, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+bool strides_ok(int64_t sb, int64_t st, int64_t sh) {
+  return sb % 8 == 0 && st % 8 == 0 && sh % 8 == 0 && sb > 0 && st > 0 && sh > 0;
+}
+
+int check_args(const fxb_attn_args* a, bool bwd) {
+  if (!a) return fxb::set_error(FXB_EINVAL, "attn: args is NULL");
+  if (a->dtype != FXB_DTYPE_BF16 && a->dtype != FXB_DTYPE_F16)
+    return fxb::set_error(FXB_EUNSUPPORTED, "attn: dtype %d (bf16 or f16)", a->dtype);
+  if (a->D != 64 && a->D != 128)
+    return fxb::set_error(FXB_EINVAL, "attn: head_dim %d not supported (64 or 128)", a->D);
+  if (a->B < 1 || a->T < 1 || a->H < 1)
+    return fxb::set_error(FXB_EINVAL, "attn: bad shape B=%d T=%d H=%d", a->B, a->T, a->H);
+  if ((int64_t)a->B * a->H > 65535)
+    return fxb::set_error(FXB_EINVAL, "attn: B*H=%lld > 65535", (long long)a->B * a->H);
+  const void* ptrs[4] = {a->q, a->k, a->v, a->o};
+  for (const void* q : ptrs)
+    if (!q || !fxb::aligned16(q)) return fxb::set_error(FXB_EINVAL, "attn: q/k/v/o must be 16-byte aligned");
+  if (!strides_ok(a->q_sb, a->q_st, a->q_sh) || !strides_ok(a->k_sb, a->k_st, a->k_sh) ||
+      !strides_ok(a->v_sb, a->v_st, a->v_sh) || !strides_ok(a->o_sb, a->o_st, a->o_sh))
+    return fxb::set_error(FXB_EINVAL, "attn: strides must be positive multiples of 8 elements");
+  if (!a->lse) return fxb::set_error(FXB_EINVAL, "attn: lse is NULL");
+  if (bwd) {
+    if (a->D != 64)
+      return fxb::set_error(FXB_EUNSUPPORTED, "attn bwd: head_dim %d (this build: 64)", a->D);
+    const void* g[4] = {a->dout, a->dq, a->dk, a->dv};
+    for (const void* q : g)
+      if (!q || !fxb::aligned16(q)) return fxb::set_error(FXB_EINVAL, "attn bwd: dout/dq/dk/dv alignment");
+    if (!strides_ok(a->do_sb, a->do_st, a->do_sh) || !strides_ok(a->dq_sb, a->dq_st, a->dq_sh) ||
+        !strides_ok(a->dk_sb, a->dk_st, a->dk_sh) || !strides_ok(a->dv_sb, a->dv_st, a->dv_sh))
+      return fxb::set_error(FXB_EINVAL, "attn bwd: strides must be positive multiples of 8");
+    if (!a->workspace || !fxb::aligned16(a->workspace))
+      return fxb::set_error(FXB_EINVAL, "attn bwd: workspace NULL or misaligned");
+  }
+  return FXB_OK;
+}
+
+template <typename K> int set_smem(K k, int bytes) {
+  return fxb::check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                         "attn smem attribute");
+}
+
+template <int DH, int FMT>
+int launch_fwd(const fxb_attn_args* a, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  int r;
+  if ((r = make_map4(&mq, a->dtype, a->q, DH, a->T, a->H, a->B, a->q_sb, a->q_st, a->q_sh))) return r;
+  if ((r = make_map4(&mk, a->dtype, a->k, DH, a->T, a->H, a->B, a->k_sb, a->k_st, a->k_sh))) return r;
+  if ((r = make_map4(&mv, a->dtype, a->v, DH, a->T, a->H, a->B, a->v_sb, a->v_st, a->v_sh))) return r;
+  FwdParams p;
+  p.B = a->B; p.T = a->T; p.H = a->H;
+  p.nqt = (a->T + TILE - 1) / TILE;
+  p.nkt = p.nqt;
+  p.causal = a->causal ? 1 : 0;
+  p.scale_log2 = a->scale * kLog2e;
+  p.o = a->o; p.o_sb = a->o_sb; p.o_st = a->o_st; p.o_sh = a->o_sh;
+  p.lse = a->lse;
+  p.err = fxb::dev_error_ptr();
+  if (!p.err) return FXB_ECUDA;
+  auto k = attn_fwd_kernel<DH, FMT>;
+  static bool once[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!once[dev & 63]) {
+    if ((r = set_smem(k, fwd_smem<DH>()))) return r;
+    once[dev & 63] = true;
+  }
+  dim3 grid(p.nqt, a->B * a->H);
+  k<<<grid, kThreads, fwd_smem<DH>(), st>>>(mq, mk, mv, p);
+  return fxb::check_launch("attn_fwd");
+}
+
+template <int FMT>
+int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
+  using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
+  constexpr int DH = 64;
+  const int64_t rows = (int64_t)a->B * a->H * a->T;
+  float* delta = a->workspace;
+  float* dq_acc = a->workspace + ((rows + 3) / 4) * 4;
+  attn_bwd_prep_kernel<T16, DH><<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(
+      static_cast<const T16*>(a->o), a->o_sb, a->o_st, a->o_sh, static_cast<const T16*>(a->dout),
+      a->do_sb, a->do_st, a->do_sh, delta, dq_acc, a->B, a->T, a->H);
+  int r = fxb::check_launch("attn_bwd_prep");
+  if (r) return r;
+  CUtensorMap mq, mk, mv, mdo;
+  if ((r = make_map4(&mq, a->dtype, a->q, DH, a->T, a->H, a->B, a->q_sb, a->q_st, a->q_sh))) return r;
+  if ((r = make_map4(&mk, a->dtype, a->k, DH, a->T, a->H, a->B, a->k_sb, a->k_st, a->k_sh))) return r;
+  if ((r = make_map4(&mv, a->dtype, a->v, DH, a->T, a->H, a->B, a->v_sb, a->v_st, a->v_sh))) return r;
+  if ((r = make_map4(&mdo, a->dtype, a->dout, DH, a->T, a->H, a->B, a->do_sb, a->do_st, a->do_sh))) return r;
+  BwdParams p;
+  p.B = a->B; p.T = a->T; p.H = a->H;
+  p.nqt = (a->T + TILE - 1) / TILE;
+  p.nkt = p.nqt;
+  p.causal = a->causal ? 1 : 0;
+  p.scale_log2 = a->scale * kLog2e;
+  p.scale = a->scale;
+  p.lse = a->lse;
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.dk = a->dk; p.dk_sb = a->dk_sb; p.dk_st = a->dk_st; p.dk_sh = a->dk_sh;
+  p.dv = a->dv; p.dv_sb = a->dv_sb; p.dv_st = a->dv_st; p.dv_sh = a->dv_sh;
+  p.err = fxb::dev_error_ptr();
+  if (!p.err) return FXB_ECUDA;
+  auto k = attn_bwd_kernel<FMT>;
+  static bool once[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!once[dev & 63]) {
+    if ((r = set_smem(k, bwd_smem()))) return r;
+    once[dev & 63] = true;
+  }
+  dim3 grid(p.nkt, a->B * a->H);
+  k<<<grid, kThreads, bwd_smem(), st>>>(mq, mk, mv, mdo, p);
+  if ((r = fxb::check_launch("attn_bwd"))) return r;
+  const int64_t n = rows * (DH / 8);
+  attn_bwd_post_kernel<T16, DH><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+      dq_acc, static_cast<T16*>(a->dq), a->dq_sb, a->dq_st, a->dq_sh, a->scale, a->B, a->T, a->H);
+  return fxb::check_launch("attn_bwd_post");
+}
+
+}  // namespace
+
+extern "C" {
+
+int fxb_attn_fwd(const fxb_attn_args* a, void* stream) {
+  int r = check_args(a, false);
+  if (r) return r;
+  cudaStream_t st = fxb::as_stream(stream);
+  if (a->dtype == FXB_DTYPE_BF16)
+    return a->D == 64 ? launch_fwd<64, 1>(a, st) : launch_fwd<128, 1>(a, st);
+  return a->D == 64 ? launch_fwd<64, 0>(a, st) : launch_fwd<128, 0>(a, st);
+}
+
+size_t fxb_attn_bwd_workspace(int32_t B, int32_t T, int32_t H, int32_t D) {
+  if (B < 1 || T < 1 || H < 1 || D < 1) return 0;
+  const int64_t rows = (int64_t)B * H * T;
+  return (size_t)(((rows + 3) / 4) * 4 + rows * D) * sizeof(float);
+}
+
+int fxb_attn_bwd(const fxb_attn_args* a, void* stream) {
+  int r = check_args(a, true);
+  if (r) return r;
+  cudaStream_t st = fxb::as_stream(stream);
+  return a->dtype == FXB_DTYPE_BF16 ? launch_bwd<1>(a, st) : launch_bwd<0>(a, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,229 @@
+// Fused softmax cross-entropy forward + gradient for sm_100a (HBM-bound).
+//
+// Semantics follow ce_fwd_grad (ml/fxlm/kernels/ce.hip:32-116): per row,
+// logsumexp in fp32, loss_sum += lse - x[target] for valid rows (atomic, like
+// ce.hip:89-92), grad = (softmax - onehot) * (*mul), zero for rows whose target
+// is ignore_index or out of [0, V) (ce.hip:43,97-115). The B200 layout keeps
+// the whole row in registers (16-byte vectors), so logits are read from HBM
+// once and the gradient written once; the gradient may overwrite the logits.
+#include "common.cuh"
+#include "internal.h"
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+template <typename T> struct CEVec { static constexpr int N = 16 / sizeof(T); };
+
+template <typename T> FXB_DEV void ld_vec(const T* p, float* f) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  if constexpr (sizeof(T) == 4) {
+    const float* q = reinterpret_cast<const float*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = q[i];
+  } else {
+    unpack8<T>(u, f);
+  }
+}
+template <typename T> FXB_DEV void st_vec(T* p, const float* f) {
+  uint4 u;
+  if constexpr (sizeof(T) == 4) {
+    float* q = reinterpret_cast<float*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = f[i];
+  } else {
+    u = pack8<T>(f);
+  }
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// Block-wide (or warp-wide when NT == 32) max and sum.
+template <int NT> FXB_DEV float block_max(float v, float* red) {
+  v = warp_max(v);
+  if constexpr (NT == 32) return v;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float r = (lane < NT / 32) ? red[lane] : -INFINITY;
+  return warp_max(r);
+}
+template <int NT> FXB_DEV float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  if constexpr (NT == 32) return v;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float r = (lane < NT / 32) ? red[lane] : 0.f;
+  return warp_sum(r);
+}
+
+// NT threads per row (32 = warp per row, else block per row); VPT vectors per
+// thread cache the row. Rows handled grid-stride.
+template <typename T, int NT, int VPT>
+__global__ void __launch_bounds__(NT == 32 ? 256 : NT)
+ce_cached_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
+                 T* grad, float* __restrict__ loss_sum, const float* __restrict__ mul,
+                 int64_t rows, int V, int64_t ignore_index) {
+  constexpr int E = CEVec<T>::N;
+  __shared__ float red[32];
+  const int nvec = V / E;
+  const int tid = (NT == 32) ? (threadIdx.x & 31) : threadIdx.x;
+  const int64_t group = (NT == 32) ? ((int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5))
+                                   : (int64_t)blockIdx.x;
+  const int64_t ngroups = (NT == 32) ? ((int64_t)gridDim.x * (blockDim.x / 32)) : (int64_t)gridDim.x;
+  const float gm = grad ? *mul : 0.f;
+  for (int64_t r = group; r < rows; r += ngroups) {
+    const T* row = logits + r * ld;
+    float xv[VPT][E];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      int v = i * NT + tid;
+      if (v < nvec) {
+        ld_vec<T>(row + (int64_t)v * E, xv[i]);
+#pragma unroll
+        for (int j = 0; j < E; ++j) mx = fmaxf(mx, xv[i][j]);
+      }
+    }
+    mx = block_max<NT>(mx, red);
+    const float mxl = mx * kLog2e;
+    const int64_t t = target[r];
+    const bool valid = (t != ignore_index) && (t >= 0) && (t < (int64_t)V);
+    float s = 0.f, xt = 0.f;
+    bool owner = false;  // this thread holds column t in its registers
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      int v = i * NT + tid;
+      if (v < nvec) {
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          if ((int64_t)(v * E + j) == t) { xt = xv[i][j]; owner = true; }
+          xv[i][j] = exp2f(fmaf(xv[i][j], kLog2e, -mxl));  // now holds exp(x - max)
+          s += xv[i][j];
+        }
+      }
+    }
+    s = block_sum<NT>(s, red);
+    // the logit of the target comes from registers: with grad == logits the
+    // row in memory is being overwritten by other threads below
+    if (valid && owner) atomicAdd(loss_sum, mx + log2f(s) * kLn2 - xt);
+    if (grad) {
+      const float scale = valid ? gm / s : 0.f;
+      const float sub = valid ? gm : 0.f;
+      T* grow = grad + r * ld;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        int v = i * NT + tid;
+        if (v < nvec) {
+          float o[E];
+#pragma unroll
+          for (int j = 0; j < E; ++j) {
+            o[j] = xv[i][j] * scale;
+            if ((int64_t)(v * E + j) == t) o[j] -= sub;
+          }
+          st_vec<T>(grow + (int64_t)v * E, o);
+        }
+      }
+    }
+    if constexpr (NT != 32) __syncthreads();  // red[] reuse across rows
+  }
+}
+
+// Generic path (any V, any alignment): block per row, three streaming passes.
+template <typename T>
+__global__ void __launch_bounds__(256)
+ce_generic_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
+                  T* grad, float* __restrict__ loss_sum, const float* __restrict__ mul,
+                  int64_t rows, int V, int64_t ignore_index) {
+  __shared__ float red[32];
+  const float gm = grad ? *mul : 0.f;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* row = logits + r * ld;
+    float mx = -INFINITY;
+    for (int d = threadIdx.x; d < V; d += 256) mx = fmaxf(mx, to_f<T>(row[d]));
+    const int64_t t = target[r];
+    const bool valid = (t != ignore_index) && (t >= 0) && (t < (int64_t)V);
+    // read before the barrier inside block_sum: later passes may overwrite the row
+    const float xt = (valid && threadIdx.x == 0) ? to_f<T>(row[t]) : 0.f;
+    mx = block_max<256>(mx, red);
+    const float mxl = mx * kLog2e;
+    float s = 0.f;
+    for (int d = threadIdx.x; d < V; d += 256) s += exp2f(fmaf(to_f<T>(row[d]), kLog2e, -mxl));
+    s = block_sum<256>(s, red);
+    if (valid && threadIdx.x == 0) atomicAdd(loss_sum, mx + log2f(s) * kLn2 - xt);
+    if (grad) {
+      const float scale = valid ? gm / s : 0.f;
+      T* grow = grad + r * ld;
+      for (int d = threadIdx.x; d < V; d += 256) {
+        float p = exp2f(fmaf(to_f<T>(row[d]), kLog2e, -mxl)) * scale;
+        if (valid && d == t) p -= gm;
+        grow[d] = from_f<T>(p);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+int launch_ce(const void* lg, int64_t ld, const int64_t* tg, void* gr, float* loss,
+              const float* mul, int64_t rows, int V, int64_t ign, cudaStream_t st) {
+  constexpr int E = CEVec<T>::N;
+  auto L = static_cast<const T*>(lg);
+  auto G = static_cast<T*>(gr);
+  const int sms = fxb::num_sms();
+  const bool vec_ok = (V % E == 0) && (ld % E == 0) && fxb::aligned16(lg) && (!gr || fxb::aligned16(gr));
+  const int nvec = V / E;
+  if (vec_ok && nvec <= 32 * 8) {
+    // warp per row, 8 rows per block
+    int vpt = (nvec + 31) / 32;
+    int64_t want = (rows + 7) / 8;
+    int blocks = (int)(want < (int64_t)sms * 32 ? want : (int64_t)sms * 32);
+#define FXB_CE_W(VP) case VP: ce_cached_kernel<T, 32, VP><<<blocks, 256, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign); break;
+    switch (vpt) { FXB_CE_W(1) FXB_CE_W(2) FXB_CE_W(3) FXB_CE_W(4) FXB_CE_W(5) FXB_CE_W(6) FXB_CE_W(7) FXB_CE_W(8) }
+#undef FXB_CE_W
+    return fxb::check_launch("ce_fwd_grad(warp)");
+  }
+  if (vec_ok && nvec <= 512 * 16) {
+    int vpt = (nvec + 511) / 512;
+    int blocks = (int)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
+#define FXB_CE_B(VP) case VP: ce_cached_kernel<T, 512, VP><<<blocks, 512, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign); break;
+    switch (vpt) {
+      FXB_CE_B(1) FXB_CE_B(2) FXB_CE_B(3) FXB_CE_B(4) FXB_CE_B(5) FXB_CE_B(6) FXB_CE_B(7) FXB_CE_B(8)
+      default:
+        if (vpt <= 12) { ce_cached_kernel<T, 512, 12><<<blocks, 512, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign); }
+        else { ce_cached_kernel<T, 512, 16><<<blocks, 512, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign); }
+    }
+#undef FXB_CE_B
+    return fxb::check_launch("ce_fwd_grad(block)");
+  }
+  int blocks = (int)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
+  ce_generic_kernel<T><<<blocks, 256, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign);
+  return fxb::check_launch("ce_fwd_grad(generic)");
+}
+
+}  // namespace
+
+extern "C" int fxb_ce_fwd_grad(int32_t dtype, const void* logits, int64_t ld,
+                               const int64_t* target, void* grad, float* loss_sum,
+                               const float* mul, int64_t rows, int32_t V, int64_t ignore_index,
+                               void* stream) {
+  if (fxb::dtype_size(dtype) == 0) return fxb::set_error(FXB_EINVAL, "ce: bad dtype %d", dtype);
+  if (V <= 0 || rows < 0 || ld < V)
+    return fxb::set_error(FXB_EINVAL, "ce: bad shape rows=%lld V=%d ld=%lld", (long long)rows, V,
+                          (long long)ld);
+  if (!logits || !target || !loss_sum || (grad && !mul))
+    return fxb::set_error(FXB_EINVAL, "ce: NULL pointer");
+  if (rows == 0) return FXB_OK;
+  cudaStream_t st = fxb::as_stream(stream);
+  switch (dtype) {
+    case FXB_DTYPE_BF16:
+      return launch_ce<__nv_bfloat16>(logits, ld, target, grad, loss_sum, mul, rows, V, ignore_index, st);
+    case FXB_DTYPE_F16:
+      return launch_ce<__half>(logits, ld, target, grad, loss_sum, mul, rows, V, ignore_index, st);
+    default:
+      return launch_ce<float>(logits, ld, target, grad, loss_sum, mul, rows, V, ignore_index, st);
+  }
+}

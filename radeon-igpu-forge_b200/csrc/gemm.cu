@@ -1,0 +1,510 @@
+// tcgen05 / TMEM GEMM for sm_100a with TMA-fed operands and fused epilogues.
+//
+//   C[m, n] = epilogue( sum_k A[m, k] * B[n, k] )
+//
+// Replaces the rocBLAS matmuls of the reference hot path (nn.Linear in
+// ml/fxlm/model.py:48-51, torch.mm in ml/fxlm/cross_entropy.py:131-135 and
+// ml/fxgpu/fused_linear.py:94). Design (B200-first, no reference analogue):
+//   - persistent CTAs (one per SM), static tile schedule grouped along M for
+//     L2 reuse; optional split-K for skinny outputs (dW), reduced with fp32
+//     red.add into the destination;
+//   - warp 0: TMA producer (128B-swizzled boxes, no multicast), warp 1: MMA
+//     issuer (one thread, tcgen05.mma cta_group::1 M=128 N=BN K=16) and TMEM
+//     owner, warps 2-5: epilogue (tcgen05.ld 32x32b -> fused op -> global);
+//   - STAGES-deep smem ring (full/empty mbarriers), two TMEM accumulators so
+//     the epilogue of tile i overlaps the mainloop of tile i+1;
+//   - operands K-major or MN-major (transposed) so forward, dX and dW GEMMs
+//     all read their operands in place.
+// Every mbarrier wait is bounded (common.cuh); on expiry the kernel records
+// FXB_DERR_GEMM_WAIT, drains what it issued and frees its tensor memory.
+#include "common.cuh"
+#include "internal.h"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 x 16-bit = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n, splits, kb_per_split, num_kb;
+  int epi;
+  int c_dtype;
+  float alpha;
+  void* C;
+  int64_t ldc;
+  const void* R;
+  int64_t ldr;
+  void* Z;
+  int64_t ldz;
+  const void* bias;
+  int* err;
+};
+
+template <int BN> struct Cfg {
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+FXB_DEV void tile_coords(int unit, const GemmParams& p, int& tm, int& tn, int& split) {
+  const int tiles = p.tiles_m * p.tiles_n;
+  split = unit / tiles;
+  int t = unit - split * tiles;
+  constexpr int G = 8;  // group of M tiles sharing B tiles in L2
+  const int per_group = G * p.tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * G;
+  int gs = p.tiles_m - first_m;
+  if (gs > G) gs = G;
+  const int r = t - g * per_group;
+  tm = first_m + r % gs;
+  tn = r / gs;
+}
+
+// ---------------------------------------------------------------- epilogue helpers
+FXB_DEV float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+template <typename T> FXB_DEV void load32(const T* p, float* f) {
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 u = reinterpret_cast<const float4*>(p)[q];
+      f[4 * q] = u.x; f[4 * q + 1] = u.y; f[4 * q + 2] = u.z; f[4 * q + 3] = u.w;
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) unpack8<T>(reinterpret_cast<const uint4*>(p)[q], f + 8 * q);
+  }
+}
+// store the first `n8` groups of 8 columns
+template <typename T> FXB_DEV void store32(T* p, const float* f, int n8) {
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q < 2 * n8)
+        reinterpret_cast<float4*>(p)[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (q < n8) reinterpret_cast<uint4*>(p)[q] = pack8<T>(f + 8 * q);
+  }
+}
+template <typename T> FXB_DEV void load32_part(const T* p, float* f, int n8) {
+  if (n8 >= 4) { load32<T>(p, f); return; }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) f[i] = 0.f;
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q < 2 * n8) {
+        float4 u = reinterpret_cast<const float4*>(p)[q];
+        f[4 * q] = u.x; f[4 * q + 1] = u.y; f[4 * q + 2] = u.z; f[4 * q + 3] = u.w;
+      }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (q < n8) unpack8<T>(reinterpret_cast<const uint4*>(p)[q], f + 8 * q);
+  }
+}
+
+FXB_DEV void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+template <typename CT>
+FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v) {
+  const int n8 = min(4, (p.N - n0) >> 3);  // groups of 8 valid columns (N % 8 == 0)
+  if (n8 <= 0) return;
+  CT* crow = static_cast<CT*>(p.C) + (int64_t)m * p.ldc + n0;
+  switch (p.epi) {
+    case FXB_EPI_STORE: {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
+      store32<CT>(crow, v, n8);
+      break;
+    }
+    case FXB_EPI_RESIDUAL: {
+      float r[32];
+      load32_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, r, n8);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = v[i] * p.alpha + r[i];
+      store32<CT>(crow, v, n8);
+      break;
+    }
+    case FXB_EPI_GELU:
+    case FXB_EPI_BIAS_GELU:
+    case FXB_EPI_BIAS_SILU:
+    case FXB_EPI_BIAS: {
+      if (p.epi != FXB_EPI_GELU) {
+        float b[32];
+        load32_part<CT>(static_cast<const CT*>(p.bias) + n0, b, n8);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += b[i];
+      }
+      if (p.epi == FXB_EPI_BIAS) {
+        store32<CT>(crow, v, n8);
+        break;
+      }
+      // round the pre-activation once; the activation is computed from the
+      // stored value so that backward (which reads Z) sees the same input
+      float zr[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) zr[i] = to_f<CT>(from_f<CT>(v[i]));
+      if (p.Z) store32<CT>(static_cast<CT*>(p.Z) + (int64_t)m * p.ldz + n0, zr, n8);
+      if (p.epi == FXB_EPI_BIAS_SILU) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = silu_f(zr[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(zr[i]);
+      }
+      store32<CT>(crow, v, n8);
+      break;
+    }
+    case FXB_EPI_DGELU: {
+      float z[32];
+      load32_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, z, n8);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= gelu_tanh_grad(z[i]);
+      store32<CT>(crow, v, n8);
+      break;
+    }
+    default: {  // FXB_EPI_ATOMIC_F32: red.add into fp32 C
+      float* c32 = static_cast<float*>(p.C) + (int64_t)m * p.ldc + n0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < 2 * n8)
+          red_add_v4(c32 + 4 * q, v[4 * q] * p.alpha, v[4 * q + 1] * p.alpha,
+                     v[4 * q + 2] * p.alpha, v[4 * q + 3] * p.alpha);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- kernel
+template <int BN, bool A_MN, bool B_MN, int AB_FMT>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const GemmParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // 1024B aligned for 128B swizzle
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + C::STAGES * C::STAGE_BYTES;
+  // barrier layout: full[S], empty[S], tfull[2], tempty[2], final, then tmem slot
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+  auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + b); };
+  auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + 2 + b); };
+  const uint32_t final_bar = bar0 + 8u * (2 * C::STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + 8 * (2 * C::STAGES + 5));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 128);
+    }
+    mbar_init(final_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_units = p.tiles_m * p.tiles_n * p.splits;
+  constexpr uint32_t IDESC = umma_idesc_f16(AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, BM, BN);
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;          // bit s: stage s armed at least once
+      uint32_t armed_parity = 0;   // bit s: parity of the last arming of stage s
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
+        int tm, tn, split;
+        tile_coords(unit, p, tm, tn, split);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
+          const uint32_t sa = base + stage * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+          mbar_expect_tx(full_bar(stage), C::STAGE_BYTES);
+          armed |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          const int k0 = kb * BK;
+          if (A_MN) {
+            tma_load_2d(sa, &tmA, full_bar(stage), tm * BM, k0);
+            tma_load_2d(sa + 8192, &tmA, full_bar(stage), tm * BM + 64, k0);
+          } else {
+            tma_load_2d(sa, &tmA, full_bar(stage), k0, tm * BM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * 8192, &tmB, full_bar(stage), tn * BN + 64 * j, k0);
+          } else {
+            tma_load_2d(sb, &tmB, full_bar(stage), k0, tn * BN);
+          }
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: every copy this thread issued has landed before smem goes away
+      for (int s = 0; s < C::STAGES; ++s)
+        if (armed & (1u << s)) mbar_wait(full_bar(s), (armed_parity >> s) & 1u, p.err, FXB_DERR_GEMM_WAIT);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int abuf = 0;
+      uint32_t aphase = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
+        int tm, tn, split;
+        tile_coords(unit, p, tm, tn, split);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        if (!mbar_wait(tempty_bar(abuf), aphase ^ 1, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t dcol = tmem_base + abuf * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = base + stage * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? umma_desc_sw128(sa + kk * 2048, 8192, 1024)
+                                     : umma_desc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? umma_desc_sw128(sb + kk * 2048, 8192, 1024)
+                                     : umma_desc_sw128(sb + kk * 32, 16, 1024);
+            umma_f16(dcol, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(abuf));
+        if (++abuf == 2) { abuf = 0; aphase ^= 1; }
+      }
+      // all MMAs issued by this thread complete before TMEM is released
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, p.err, FXB_DERR_GEMM_WAIT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int abuf = 0;
+    uint32_t aphase = 0;
+    for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x) {
+      int tm, tn, split;
+      tile_coords(unit, p, tm, tn, split);
+      if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
+      tc_fence_after();
+      const int m = tm * BM + row_in_tile;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        tmem_wait_ld();
+        const int n0 = tn * BN + c * 32;
+        if (m < p.M && n0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          switch (p.c_dtype) {
+            case FXB_DTYPE_BF16: epilogue_chunk<__nv_bfloat16>(p, m, n0, v); break;
+            case FXB_DTYPE_F16: epilogue_chunk<__half>(p, m, n0, v); break;
+            default: epilogue_chunk<float>(p, m, n0, v); break;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar(abuf));
+      if (++abuf == 2) { abuf = 0; aphase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+constexpr int FXB_EPI_ATOMIC_F32 = FXB_EPI_ACCUM_F32;
+
+template <int BN, bool A_MN, bool B_MN, int AB_FMT>
+int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+               cudaStream_t st) {
+  auto k = gemm_tc_kernel<BN, A_MN, B_MN, AB_FMT>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    int r = fxb::check_cuda(
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM),
+        "gemm smem attribute");
+    if (r) return r;
+    attr_set[dev] = true;
+  }
+  k<<<grid, kThreads, Cfg<BN>::SMEM, st>>>(ta, tb, p);
+  return fxb::check_launch("gemm_tc");
+}
+
+template <int BN, int AB_FMT>
+int launch_layout(bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb,
+                  const GemmParams& p, int grid, cudaStream_t st) {
+  if (!amn && !bmn) return launch_one<BN, false, false, AB_FMT>(ta, tb, p, grid, st);
+  if (!amn && bmn) return launch_one<BN, false, true, AB_FMT>(ta, tb, p, grid, st);
+  if (amn && bmn) return launch_one<BN, true, true, AB_FMT>(ta, tb, p, grid, st);
+  return launch_one<BN, true, false, AB_FMT>(ta, tb, p, grid, st);
+}
+
+// Pick BN (128 or 256) and split-K to minimise waves x per-tile work.
+void plan(int M, int N, int K, bool allow_split, int sms, int& BN, int& splits) {
+  const int tm = (M + BM - 1) / BM;
+  const int nkb = (K + BK - 1) / BK;
+  double best = 1e30;
+  BN = 128;
+  splits = 1;
+  for (int bn : {256, 128}) {
+    const int tn = (N + bn - 1) / bn;
+    for (int s = 1; s <= (allow_split ? 16 : 1); s *= 2) {
+      if (s > 1 && nkb / s < 4) break;  // keep >= 4 k-blocks per split
+      const int kbs = (nkb + s - 1) / s;
+      const long units = (long)tm * tn * s;
+      const long waves = (units + sms - 1) / sms;
+      // cost: waves x (k-blocks per unit x tile width + fixed epilogue/fill cost)
+      const double cost = (double)waves * ((double)kbs * bn + 6.0 * bn) + (s > 1 ? 0.02 * units : 0);
+      if (cost < best - 1e-9) { best = cost; BN = bn; splits = s; }
+    }
+  }
+}
+
+int make_map(CUtensorMap* map, int ab_dtype, const void* ptr, uint64_t inner, uint64_t outer,
+             int64_t ld, uint32_t box_inner, uint32_t box_outer) {
+  uint64_t dims[2] = {inner, outer};
+  uint64_t strides[1] = {(uint64_t)ld * 2};
+  uint32_t box[2] = {box_inner, box_outer};
+  CUtensorMapDataType dt = ab_dtype == FXB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return fxb::encode_tiled(map, dt, 2, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace
+
+namespace fxb {
+// Internal entry (also used by the fxgpu gather path): epi may be the internal
+// FXB_EPI_ATOMIC_F32 value 7; force_splits > 0 overrides the planner.
+int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t st) {
+  const int M = a->M, N = a->N, K = a->K;
+  if (a->dtype != FXB_DTYPE_BF16 && a->dtype != FXB_DTYPE_F16)
+    return set_error(FXB_EUNSUPPORTED, "gemm: A/B dtype %d (bf16 or f16 only)", a->dtype);
+  if (dtype_size(a->c_dtype) == 0) return set_error(FXB_EINVAL, "gemm: bad c_dtype");
+  if (M < 0 || N < 0 || K < 0) return set_error(FXB_EINVAL, "gemm: negative size");
+  if (N % 8) return set_error(FXB_EINVAL, "gemm: N=%d must be a multiple of 8", N);
+  if (!a->A || !a->B || !a->C) return set_error(FXB_EINVAL, "gemm: NULL operand");
+  if (!aligned16(a->A) || !aligned16(a->B) || !aligned16(a->C))
+    return set_error(FXB_EINVAL, "gemm: operands must be 16-byte aligned");
+  const int csz = dtype_size(a->c_dtype);
+  if ((a->ldc * csz) % 16) return set_error(FXB_EINVAL, "gemm: ldc*esize must be a multiple of 16");
+  if (a->a_trans ? (M % 8 || a->lda < M) : (K % 8 || a->lda < K))
+    return set_error(FXB_EINVAL, "gemm: A needs 16-byte rows (M or K %% 8) and lda >= row");
+  if (a->b_trans ? (a->ldb < N) : (K % 8 || a->ldb < K))
+    return set_error(FXB_EINVAL, "gemm: B needs 16-byte rows and ldb >= row");
+  if ((a->lda % 8) || (a->ldb % 8)) return set_error(FXB_EINVAL, "gemm: lda/ldb must be multiples of 8");
+  if (a->ldc < N) return set_error(FXB_EINVAL, "gemm: ldc < N");
+  const bool needs_r = (epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU);
+  if (needs_r && (!a->R || !aligned16(a->R) || (a->ldr * csz) % 16))
+    return set_error(FXB_EINVAL, "gemm: epilogue needs an aligned R");
+  const bool has_bias = (epi == FXB_EPI_BIAS || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU);
+  if (has_bias && (!a->bias || !aligned16(a->bias)))
+    return set_error(FXB_EINVAL, "gemm: epilogue needs an aligned bias");
+  if (a->Z && (!aligned16(a->Z) || (a->ldz * csz) % 16))
+    return set_error(FXB_EINVAL, "gemm: Z misaligned");
+  if (epi == FXB_EPI_ATOMIC_F32 && a->c_dtype != FXB_DTYPE_F32)
+    return set_error(FXB_EINVAL, "gemm: accumulate epilogue needs fp32 C");
+  if (epi < 0 || epi > FXB_EPI_ATOMIC_F32) return set_error(FXB_EINVAL, "gemm: bad epilogue %d", epi);
+  if (M == 0 || N == 0) return FXB_OK;
+  if (K == 0) return set_error(FXB_EUNSUPPORTED, "gemm: K == 0");
+
+  int* err = dev_error_ptr();
+  if (!err) return FXB_ECUDA;
+  const int sms = num_sms();
+  int BN, splits;
+  plan(M, N, K, epi == FXB_EPI_ATOMIC_F32, sms, BN, splits);
+  if (force_splits > 0 && epi == FXB_EPI_ATOMIC_F32) splits = force_splits;
+
+  CUtensorMap ta, tb;
+  int r;
+  if (a->a_trans) r = make_map(&ta, a->dtype, a->A, (uint64_t)M, (uint64_t)K, a->lda, 64, 64);
+  else r = make_map(&ta, a->dtype, a->A, (uint64_t)K, (uint64_t)M, a->lda, 64, 128);
+  if (r) return r;
+  if (a->b_trans) r = make_map(&tb, a->dtype, a->B, (uint64_t)N, (uint64_t)K, a->ldb, 64, 64);
+  else r = make_map(&tb, a->dtype, a->B, (uint64_t)K, (uint64_t)N, a->ldb, 64, (uint32_t)BN);
+  if (r) return r;
+
+  GemmParams p;
+  p.M = M; p.N = N; p.K = K;
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = (N + BN - 1) / BN;
+  p.num_kb = (K + BK - 1) / BK;
+  p.splits = splits;
+  p.kb_per_split = (p.num_kb + splits - 1) / splits;
+  p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;  // no empty splits
+  p.epi = epi;
+  p.c_dtype = a->c_dtype;
+  p.alpha = a->alpha;
+  p.C = a->C; p.ldc = a->ldc;
+  p.R = a->R; p.ldr = a->ldr;
+  p.Z = a->Z; p.ldz = a->ldz;
+  p.bias = a->bias;
+  p.err = err;
+  const long units = (long)p.tiles_m * p.tiles_n * p.splits;
+  const int grid = (int)(units < sms ? units : sms);
+  const bool amn = a->a_trans != 0, bmn = a->b_trans != 0;
+  if (a->dtype == FXB_DTYPE_BF16) {
+    return BN == 256 ? launch_layout<256, 1>(amn, bmn, ta, tb, p, grid, st)
+                     : launch_layout<128, 1>(amn, bmn, ta, tb, p, grid, st);
+  }
+  return BN == 256 ? launch_layout<256, 0>(amn, bmn, ta, tb, p, grid, st)
+                   : launch_layout<128, 0>(amn, bmn, ta, tb, p, grid, st);
+}
+}  // namespace fxb
+
+extern "C" int fxb_gemm(const fxb_gemm_args* args, void* stream) {
+  if (!args) return fxb::set_error(FXB_EINVAL, "gemm: args is NULL");
+  return fxb::gemm_launch(args, args->epilogue, 0, fxb::as_stream(stream));
+}

@@ -1,0 +1,48 @@
+// Host-side helpers shared by the C ABI translation units.
+#pragma once
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "../../include/fxb200.h"
+
+namespace fxb {
+
+// Records the message for fxb_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+// Wraps a CUDA runtime status; FXB_OK when success.
+int check_cuda(cudaError_t e, const char* what);
+
+// Launch-time check: picks up configuration errors of the launch just made.
+inline int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int dtype_size(int32_t dt) {
+  switch (dt) {
+    case FXB_DTYPE_F32: return 4;
+    case FXB_DTYPE_F16: return 2;
+    case FXB_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+// Device address of the error word of the current device (kernels OR bits
+// into it when a bounded wait expires); nullptr + error set on failure.
+int* dev_error_ptr();
+
+// Cached SM count of the current device.
+int num_sms();
+
+// cuTensorMapEncodeTiled obtained through the runtime's driver entry point
+// (the library does not link libcuda directly).
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, const void* base,
+                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                 CUtensorMapSwizzle swizzle);
+
+}  // namespace fxb

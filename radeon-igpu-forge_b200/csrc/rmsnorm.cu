@@ -1,0 +1,305 @@
+// RMSNorm forward / backward for sm_100a (HBM-bound).
+//
+// Math follows the reference kernels ml/fxlm/kernels/norm.hip:33-59 (fwd),
+// :64-95 (dx) and :102-127 (dw partials), which compute in fp32 over 16-bit
+// inputs. Layout differs: one warp owns a row, the row lives in registers as
+// 16-byte vectors (one HBM read of x, one write of y), and the dw reduction is
+// a per-block partial followed by a fixed-order column sum (deterministic).
+#include "common.cuh"
+#include "internal.h"
+
+namespace {
+
+constexpr int kWarps = 8;  // warps per block
+
+template <typename T> struct Vec {
+  static constexpr int N = 16 / sizeof(T);  // elements per 16-byte vector
+};
+
+template <typename T> FXB_DEV void load_vec(const T* p, float* f) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  if constexpr (sizeof(T) == 4) {
+    const float* q = reinterpret_cast<const float*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = q[i];
+  } else {
+    unpack8<T>(u, f);
+  }
+}
+template <typename T> FXB_DEV void store_vec(T* p, const float* f) {
+  uint4 u;
+  if constexpr (sizeof(T) == 4) {
+    float* q = reinterpret_cast<float*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = f[i];
+  } else {
+    u = pack8<T>(f);
+  }
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// VPL = 16-byte vectors per lane (row length D <= VPL * 32 * Vec<T>::N)
+template <typename T, int VPL>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                   float* __restrict__ rstd, int64_t rows, int D, float eps) {
+  constexpr int E = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int nvec = D / E;
+  float wv[VPL][E];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    int v = i * 32 + lane;
+    if (v < nvec) load_vec<T>(w + (int64_t)v * E, wv[i]);
+  }
+  const int64_t warp0 = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  for (int64_t r = warp0; r < rows; r += nwarps) {
+    const T* xr = x + r * D;
+    float xv[VPL][E];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int v = i * 32 + lane;
+      if (v < nvec) {
+        load_vec<T>(xr + (int64_t)v * E, xv[i]);
+#pragma unroll
+        for (int j = 0; j < E; ++j) ss += xv[i][j] * xv[i][j];
+      }
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / (float)D + eps);
+    if (lane == 0) rstd[r] = rs;
+    T* yr = y + r * D;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int v = i * 32 + lane;
+      if (v < nvec) {
+        float o[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) o[j] = xv[i][j] * rs * wv[i][j];
+        store_vec<T>(yr + (int64_t)v * E, o);
+      }
+    }
+  }
+}
+
+// dx per row + per-block dw partial (part[blockIdx.x, :]).
+template <typename T, int VPL>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                   const float* __restrict__ rstd, const T* __restrict__ dy, T* __restrict__ dx,
+                   float* __restrict__ part, int64_t rows, int D) {
+  constexpr int E = Vec<T>::N;
+  extern __shared__ float sdw[];  // kWarps x D
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  const int nvec = D / E;
+  float wv[VPL][E], acc[VPL][E];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    int v = i * 32 + lane;
+#pragma unroll
+    for (int j = 0; j < E; ++j) acc[i][j] = 0.f;
+    if (v < nvec) load_vec<T>(w + (int64_t)v * E, wv[i]);
+  }
+  const float invD = 1.f / (float)D;
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + wid; r < rows; r += (int64_t)gridDim.x * kWarps) {
+    const T* xr = x + r * D;
+    const T* gr = dy + r * D;
+    float xv[VPL][E], gv[VPL][E];
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int v = i * 32 + lane;
+      if (v < nvec) {
+        load_vec<T>(xr + (int64_t)v * E, xv[i]);
+        load_vec<T>(gr + (int64_t)v * E, gv[i]);
+#pragma unroll
+        for (int j = 0; j < E; ++j) t += xv[i][j] * wv[i][j] * gv[i][j];
+      }
+    }
+    t = warp_sum(t);
+    const float rs = rstd[r];
+    const float corr = rs * rs * rs * t * invD;
+    T* dr = dx + r * D;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int v = i * 32 + lane;
+      if (v < nvec) {
+        float o[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          o[j] = rs * wv[i][j] * gv[i][j] - xv[i][j] * corr;
+          acc[i][j] += xv[i][j] * rs * gv[i][j];
+        }
+        store_vec<T>(dr + (int64_t)v * E, o);
+      }
+    }
+  }
+  // fixed-order reduction of the warps' partials
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    int v = i * 32 + lane;
+    if (v < nvec) {
+#pragma unroll
+      for (int j = 0; j < E; ++j) sdw[wid * D + v * E + j] = acc[i][j];
+    }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) s += sdw[k * D + d];
+    part[(int64_t)blockIdx.x * D + d] = s;
+  }
+}
+
+// dw[d] = (acc ? dw[d] : 0) + sum_b part[b, d]   (fixed order over b)
+template <typename T>
+__global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ part, int nparts, int D,
+                                         T* __restrict__ dw, int accumulate) {
+  // (dw dtype is independent of the activation dtype)
+  int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  float s = 0.f;
+  for (int b = 0; b < nparts; ++b) s += part[(int64_t)b * D + d];
+  if (accumulate) s += to_f<T>(dw[d]);
+  dw[d] = from_f<T>(s);
+}
+
+template <typename T>
+int launch_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows, int D, float eps,
+               cudaStream_t st) {
+  constexpr int E = Vec<T>::N;
+  const int vpl = (D / E + 31) / 32;
+  int64_t blocks64 = (rows + kWarps - 1) / kWarps;
+  int cap = fxb::num_sms() * 16;
+  int blocks = (int)(blocks64 < cap ? blocks64 : cap);
+  if (blocks < 1) blocks = 1;
+  auto X = static_cast<const T*>(x);
+  auto W = static_cast<const T*>(w);
+  auto Y = static_cast<T*>(y);
+#define FXB_RMS_FWD(V)                                                            \
+  case V:                                                                         \
+    rmsnorm_fwd_kernel<T, V><<<blocks, kWarps * 32, 0, st>>>(X, W, Y, rstd, rows, D, eps); \
+    break;
+  switch (vpl) {
+    FXB_RMS_FWD(1) FXB_RMS_FWD(2) FXB_RMS_FWD(3) FXB_RMS_FWD(4) FXB_RMS_FWD(5) FXB_RMS_FWD(6)
+    FXB_RMS_FWD(7) FXB_RMS_FWD(8)
+    default:
+      if (vpl <= 16) { rmsnorm_fwd_kernel<T, 16><<<blocks, kWarps * 32, 0, st>>>(X, W, Y, rstd, rows, D, eps); }
+      else if (vpl <= 32) { rmsnorm_fwd_kernel<T, 32><<<blocks, kWarps * 32, 0, st>>>(X, W, Y, rstd, rows, D, eps); }
+      else return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm: D=%d too large", D);
+  }
+#undef FXB_RMS_FWD
+  return fxb::check_launch("rmsnorm_fwd");
+}
+
+int bwd_blocks(int64_t rows) {
+  int64_t want = (rows + kWarps * 4 - 1) / (kWarps * 4);  // >= ~4 rows per warp
+  int cap = fxb::num_sms() * 2;
+  int b = (int)(want < cap ? want : cap);
+  return b < 1 ? 1 : b;
+}
+
+template <typename T>
+int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, void* dx, void* dw,
+               int dw_dtype, int acc, float* ws, int64_t rows, int D, cudaStream_t st) {
+  constexpr int E = Vec<T>::N;
+  const int vpl = (D / E + 31) / 32;
+  const int blocks = bwd_blocks(rows);
+  const size_t smem = (size_t)kWarps * D * sizeof(float);
+  auto X = static_cast<const T*>(x);
+  auto W = static_cast<const T*>(w);
+  auto G = static_cast<const T*>(dy);
+  auto DX = static_cast<T*>(dx);
+#define FXB_RMS_BWD(V)                                                                   \
+  case V: {                                                                              \
+    auto k = rmsnorm_bwd_kernel<T, V>;                                                   \
+    if (smem > 48 * 1024)                                                                \
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
+    k<<<blocks, kWarps * 32, smem, st>>>(X, W, rstd, G, DX, ws, rows, D);                \
+    break;                                                                               \
+  }
+  switch (vpl) {
+    FXB_RMS_BWD(1) FXB_RMS_BWD(2) FXB_RMS_BWD(3) FXB_RMS_BWD(4) FXB_RMS_BWD(5) FXB_RMS_BWD(6)
+    FXB_RMS_BWD(7) FXB_RMS_BWD(8)
+    default:
+      return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm bwd: D=%d > %d not supported", D, 8 * 32 * E);
+  }
+#undef FXB_RMS_BWD
+  int r = fxb::check_launch("rmsnorm_bwd");
+  if (r) return r;
+  const int g = (D + 255) / 256;
+  switch (dw_dtype) {
+    case FXB_DTYPE_BF16:
+      rmsnorm_dw_reduce_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(ws, blocks, D, static_cast<__nv_bfloat16*>(dw), acc);
+      break;
+    case FXB_DTYPE_F16:
+      rmsnorm_dw_reduce_kernel<__half><<<g, 256, 0, st>>>(ws, blocks, D, static_cast<__half*>(dw), acc);
+      break;
+    default:
+      rmsnorm_dw_reduce_kernel<float><<<g, 256, 0, st>>>(ws, blocks, D, static_cast<float*>(dw), acc);
+  }
+  return fxb::check_launch("rmsnorm_dw_reduce");
+}
+
+int check_common(int32_t dtype, const void* x, const void* w, int64_t rows, int32_t D) {
+  if (fxb::dtype_size(dtype) == 0) return fxb::set_error(FXB_EINVAL, "rmsnorm: bad dtype %d", dtype);
+  if (D <= 0 || D % 8 != 0 || D > 8192)
+    return fxb::set_error(FXB_EINVAL, "rmsnorm: D=%d needs D %% 8 == 0 and D <= 8192", D);
+  if (rows < 0) return fxb::set_error(FXB_EINVAL, "rmsnorm: rows=%lld", (long long)rows);
+  if (!fxb::aligned16(x) || !fxb::aligned16(w))
+    return fxb::set_error(FXB_EINVAL, "rmsnorm: x and w must be 16-byte aligned");
+  return FXB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fxb_rmsnorm_fwd(int32_t dtype, const void* x, const void* w, void* y, float* rstd,
+                    int64_t rows, int32_t D, float eps, void* stream) {
+  int r = check_common(dtype, x, w, rows, D);
+  if (r) return r;
+  if (!fxb::aligned16(y)) return fxb::set_error(FXB_EINVAL, "rmsnorm: y must be 16-byte aligned");
+  if (rows == 0) return FXB_OK;
+  cudaStream_t st = fxb::as_stream(stream);
+  switch (dtype) {
+    case FXB_DTYPE_BF16: return launch_fwd<__nv_bfloat16>(x, w, y, rstd, rows, D, eps, st);
+    case FXB_DTYPE_F16: return launch_fwd<__half>(x, w, y, rstd, rows, D, eps, st);
+    default: return launch_fwd<float>(x, w, y, rstd, rows, D, eps, st);
+  }
+}
+
+size_t fxb_rmsnorm_bwd_workspace(int64_t rows, int32_t D) {
+  return (size_t)bwd_blocks(rows) * (size_t)(D > 0 ? D : 0) * sizeof(float);
+}
+
+int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rstd,
+                    const void* dy, void* dx, void* dw, int32_t dw_dtype, int32_t dw_accumulate,
+                    float* workspace, int64_t rows, int32_t D, void* stream) {
+  int r = check_common(dtype, x, w, rows, D);
+  if (r) return r;
+  if (fxb::dtype_size(dw_dtype) == 0) return fxb::set_error(FXB_EINVAL, "rmsnorm bwd: bad dw dtype");
+  if (!fxb::aligned16(dy) || !fxb::aligned16(dx))
+    return fxb::set_error(FXB_EINVAL, "rmsnorm bwd: dy and dx must be 16-byte aligned");
+  if (!workspace || !dw) return fxb::set_error(FXB_EINVAL, "rmsnorm bwd: workspace/dw NULL");
+  cudaStream_t st = fxb::as_stream(stream);
+  if (rows == 0) {
+    if (dw_accumulate) return FXB_OK;
+    return fxb::check_cuda(cudaMemsetAsync(dw, 0, (size_t)D * fxb::dtype_size(dw_dtype), st),
+                           "rmsnorm bwd memset");
+  }
+  switch (dtype) {
+    case FXB_DTYPE_BF16:
+      return launch_bwd<__nv_bfloat16>(x, w, rstd, dy, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
+    case FXB_DTYPE_F16:
+      return launch_bwd<__half>(x, w, rstd, dy, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
+    default:
+      return launch_bwd<float>(x, w, rstd, dy, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,115 @@
+"""Thin tensor-level helpers over the C ABI (GEMM, embedding, axpy).
+
+These are the building blocks the reference-named ops (fxlm.*, fxgpu.*) call.
+Every function launches on torch's current stream, allocates outputs with
+torch (the library never allocates) and raises RuntimeError on failure.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import (EPI_STORE, EPI_RESIDUAL, EPI_GELU, EPI_DGELU, EPI_BIAS,  # noqa: F401
+                   EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_ACCUM_F32)
+
+_TC_DTYPES = (torch.bfloat16, torch.float16)
+
+
+def _rowmajor(t, name):
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D row-major view (stride(1) == 1)")
+    return t.stride(0)
+
+
+def gemm(A, B, out, *, a_trans=False, b_trans=False, epilogue=EPI_STORE, alpha=1.0,
+         R=None, Z=None, bias=None):
+    """out[M,N] = epilogue(opA(A) @ opB(B)^T) on tcgen05 tensor cores.
+
+    opA(A) = A (M,K) or, with a_trans, A stored (K,M); opB(B) = B (N,K) or,
+    with b_trans, B stored (K,N). A and B share one 16-bit dtype; `out`, R, Z
+    and bias share out's dtype (fp32 out is required for EPI_ACCUM_F32).
+    """
+    if A.dtype not in _TC_DTYPES or B.dtype != A.dtype:
+        raise TypeError(f"gemm operands must both be bf16 or fp16 ({A.dtype}, {B.dtype})")
+    if not (A.is_cuda and B.is_cuda and out.is_cuda):
+        raise TypeError("gemm operands must be cuda tensors")
+    lda = _rowmajor(A, "A")
+    ldb = _rowmajor(B, "B")
+    ldc = _rowmajor(out, "out")
+    M = A.shape[1] if a_trans else A.shape[0]
+    K = A.shape[0] if a_trans else A.shape[1]
+    N = B.shape[1] if b_trans else B.shape[0]
+    Kb = B.shape[0] if b_trans else B.shape[1]
+    if Kb != K or tuple(out.shape) != (M, N):
+        raise ValueError(f"gemm shape mismatch: A{tuple(A.shape)} B{tuple(B.shape)} "
+                         f"out{tuple(out.shape)} a_trans={a_trans} b_trans={b_trans}")
+    a = _lib.GemmArgs()
+    a.dtype = _lib.dtype_code(A.dtype)
+    a.M, a.N, a.K = M, N, K
+    a.A, a.lda, a.a_trans = A.data_ptr(), lda, int(a_trans)
+    a.B, a.ldb, a.b_trans = B.data_ptr(), ldb, int(b_trans)
+    a.C, a.ldc, a.c_dtype = out.data_ptr(), ldc, _lib.dtype_code(out.dtype)
+    a.epilogue = epilogue
+    a.alpha = float(alpha)
+    if R is not None:
+        a.R, a.ldr = R.data_ptr(), _rowmajor(R, "R")
+    if Z is not None:
+        a.Z, a.ldz = Z.data_ptr(), _rowmajor(Z, "Z")
+    if bias is not None:
+        a.bias = bias.data_ptr()
+    _lib.check(_lib.load().fxb_gemm(ctypes.byref(a), _lib.stream_ptr(A.device)), "fxb_gemm")
+    return out
+
+
+def linear_fwd(x2d, W, residual=None):
+    """y = x W^T (+ residual)."""
+    y = torch.empty(x2d.shape[0], W.shape[0], device=x2d.device, dtype=x2d.dtype)
+    if residual is None:
+        return gemm(x2d, W, y)
+    return gemm(x2d, W, y, epilogue=EPI_RESIDUAL, R=residual)
+
+
+def linear_dx(dy, W, out=None):
+    """dx = dy W   (dy (M,N), W (N,K) -> (M,K))."""
+    if out is None:
+        out = torch.empty(dy.shape[0], W.shape[1], device=dy.device, dtype=dy.dtype)
+    return gemm(dy, W, out, b_trans=True)
+
+
+def linear_dw_into(dy, x, dw32, alpha=1.0):
+    """dw32 (fp32, (N,K)) += alpha * dy^T x   (dy (M,N), x (M,K)); split-K red.add."""
+    return gemm(dy, x, dw32, a_trans=True, b_trans=True, epilogue=EPI_ACCUM_F32, alpha=alpha)
+
+
+def param_grad_sink(p):
+    """fp32 flat-gradient view of a parameter managed by FlatAdamW, or None."""
+    g = getattr(p, "_fxb_grad", None)
+    if g is not None:
+        owner = getattr(p, "_fxb_owner", None)
+        if owner is not None:
+            owner._grad_dirty = True
+    return g
+
+
+def weight_grad(dy, x, W):
+    """dW for y = x W^T: accumulated into W's flat fp32 slot when W belongs to
+    a FlatAdamW (returns None), else returned as a tensor of W's dtype."""
+    sink = param_grad_sink(W)
+    if sink is not None:
+        linear_dw_into(dy, x, sink.view(W.shape[0], W.shape[1]))
+        return None
+    tmp = torch.zeros(W.shape[0], W.shape[1], device=W.device, dtype=torch.float32)
+    linear_dw_into(dy, x, tmp)
+    return tmp.to(W.dtype)
+
+
+def axpy(dst, src, scale=None, accumulate=True):
+    """dst (+)= src * (*scale)  elementwise over numel (scale: 0-dim fp32 cuda tensor)."""
+    if dst.numel() != src.numel():
+        raise ValueError("axpy: size mismatch")
+    if not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("axpy: tensors must be contiguous")
+    _lib.call("fxb_axpy", _lib.dtype_code(dst.dtype), _lib.ptr(dst), _lib.dtype_code(src.dtype),
+              _lib.ptr(src), _lib.ptr(scale), 1 if accumulate else 0, dst.numel(),
+              _lib.stream_ptr(dst.device))
+    return dst

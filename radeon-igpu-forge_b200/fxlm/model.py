@@ -1,0 +1,192 @@
+"""fxlm.model: GPTConfig + GPT — pre-RMSNorm transformer (B200 build).
+
+Same architecture, parameter names, initialisation and forward signature as
+the reference (ml/fxlm/model.py:22-130): block = RMSNorm -> qkv Linear (no
+bias) -> causal attention on the (B,T,3,H,Dh) view -> proj -> residual;
+RMSNorm -> fc -> GELU(tanh) -> fc2 -> residual; final RMSNorm; tied LM head
+through linear_cross_entropy; init N(0, 0.02), proj/fc2 at 0.02/sqrt(2L),
+pos_emb zeros. State dicts are interchangeable with the reference's.
+
+Implementation switches keep the reference's names and add `linear_impl`:
+  attn_impl   "flash" (tcgen05 kernels) | "sdpa"
+  norm_impl   "fused" (sm_100a kernel)  | "torch"
+  ce_impl     "fused" (tcgen05 linear-CE) | "torch"
+  linear_impl "fused" (tcgen05 GEMM + fused epilogues) | "torch"
+The defaults select the sm_100a kernels everywhere (the reference defaults
+norm_impl to "torch" because its iGPU kernel was not faster,
+ml/fxlm/model.py:32); the "torch" settings reproduce the reference's own
+PyTorch path.
+"""
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+import torch.nn.functional as Fn
+
+from fxb200 import _lib
+from fxb200.ops import param_grad_sink
+from .attention import flash_attention_qkv
+from .norm import rms_norm
+from .cross_entropy import linear_cross_entropy
+from .linear import fused_linear, fused_mlp
+
+
+@dataclass
+class GPTConfig:
+    vocab_size: int
+    seq_len: int
+    n_layer: int
+    n_head: int
+    d_model: int
+    mlp_ratio: int = 4
+    tie_embeddings: bool = True
+    attn_impl: str = "flash"      # "flash" | "sdpa"
+    norm_impl: str = "fused"      # "fused" | "torch"
+    ce_impl: str = "fused"        # "fused" | "torch"
+    eps: float = 1e-6
+    linear_impl: str = "fused"    # "fused" | "torch"
+
+
+class _Embedding(torch.autograd.Function):
+    """x[b,t] = tok[idx[b,t]] + pos[t]; backward scatter-adds in fp32 (straight
+    into FlatAdamW's flat gradient when the weights are managed by it)."""
+
+    @staticmethod
+    def forward(ctx, idx, tok, pos):
+        if idx.dtype != torch.int64 or not idx.is_contiguous():
+            raise TypeError("idx must be contiguous int64")
+        B, T = idx.shape
+        V, D = tok.shape
+        out = torch.empty(B, T, D, device=tok.device, dtype=tok.dtype)
+        _lib.call("fxb_embedding_fwd", _lib.dtype_code(tok.dtype), _lib.ptr(idx), _lib.ptr(tok),
+                  _lib.ptr(pos), _lib.ptr(out), B, T, D, V, _lib.stream_ptr(tok.device))
+        ctx.save_for_backward(idx)
+        ctx.shapes = (tok, pos)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        (idx,) = ctx.saved_tensors
+        tok, pos = ctx.shapes
+        ctx.shapes = None
+        B, T = idx.shape
+        V, D = tok.shape
+        dout = dout.contiguous()
+        st = param_grad_sink(tok) if ctx.needs_input_grad[1] else None
+        sp = param_grad_sink(pos) if ctx.needs_input_grad[2] else None
+        gt = gp = None
+        wt = st if st is not None else (torch.zeros(V, D, device=tok.device, dtype=torch.float32)
+                                         if ctx.needs_input_grad[1] else None)
+        wp = sp if sp is not None else (torch.zeros(pos.shape, device=pos.device, dtype=torch.float32)
+                                         if ctx.needs_input_grad[2] else None)
+        _lib.call("fxb_embedding_bwd", _lib.dtype_code(dout.dtype), _lib.ptr(idx), _lib.ptr(dout),
+                  _lib.ptr(wt), _lib.ptr(wp), B, T, D, V, _lib.stream_ptr(dout.device))
+        if ctx.needs_input_grad[1] and st is None:
+            gt = wt.to(tok.dtype)
+        if ctx.needs_input_grad[2] and sp is None:
+            gp = wp.to(pos.dtype)
+        return None, gt, gp
+
+
+class Block(nn.Module):
+    def __init__(self, cfg):
+        super().__init__()
+        D, H = cfg.d_model, cfg.n_head
+        self.n_head = H
+        self.head_dim = D // H
+        self.attn_impl = cfg.attn_impl
+        self.norm_impl = cfg.norm_impl
+        self.linear_impl = cfg.linear_impl
+        self.eps = cfg.eps
+        self.ln1_w = nn.Parameter(torch.ones(D))
+        self.ln2_w = nn.Parameter(torch.ones(D))
+        self.qkv = nn.Linear(D, 3 * D, bias=False)
+        self.proj = nn.Linear(D, D, bias=False)
+        self.fc = nn.Linear(D, cfg.mlp_ratio * D, bias=False)
+        self.fc2 = nn.Linear(cfg.mlp_ratio * D, D, bias=False)
+
+    def _norm(self, x, w):
+        if self.norm_impl == "fused":
+            return rms_norm(x, w, self.eps)
+        return Fn.rms_norm(x, (x.shape[-1],), w, self.eps)
+
+    def forward(self, x):
+        B, T, D = x.shape
+        fused = self.linear_impl == "fused"
+        h = self._norm(x, self.ln1_w)
+        qkv = fused_linear(h, self.qkv.weight) if fused else self.qkv(h)
+        qkv = qkv.view(B, T, 3, self.n_head, self.head_dim)
+        if self.attn_impl == "flash":
+            y = flash_attention_qkv(qkv, causal=True)
+        else:
+            q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
+            y = Fn.scaled_dot_product_attention(q, k, v, is_causal=True)
+            y = y.transpose(1, 2)
+        y = y.reshape(B, T, D)
+        if fused:
+            x = fused_linear(y, self.proj.weight, residual=x)
+            h = self._norm(x, self.ln2_w)
+            return fused_mlp(h, self.fc.weight, self.fc2.weight, residual=x)
+        x = x + self.proj(y)
+        h = self._norm(x, self.ln2_w)
+        return x + self.fc2(Fn.gelu(self.fc(h), approximate="tanh"))
+
+
+class GPT(nn.Module):
+    def __init__(self, cfg: GPTConfig):
+        super().__init__()
+        if cfg.d_model % cfg.n_head:
+            raise ValueError("d_model must be a multiple of n_head")
+        self.cfg = cfg
+        D = cfg.d_model
+        self.tok_emb = nn.Embedding(cfg.vocab_size, D)
+        self.pos_emb = nn.Parameter(torch.zeros(cfg.seq_len, D))
+        self.blocks = nn.ModuleList(Block(cfg) for _ in range(cfg.n_layer))
+        self.lnf_w = nn.Parameter(torch.ones(D))
+        if not cfg.tie_embeddings:
+            self.head = nn.Linear(D, cfg.vocab_size, bias=False)
+        self.apply(self._init)
+        s = 0.02 / math.sqrt(2 * cfg.n_layer)
+        for b in self.blocks:
+            nn.init.normal_(b.proj.weight, std=s)
+            nn.init.normal_(b.fc2.weight, std=s)
+
+    @staticmethod
+    def _init(m):
+        if isinstance(m, nn.Linear):
+            nn.init.normal_(m.weight, std=0.02)
+        elif isinstance(m, nn.Embedding):
+            nn.init.normal_(m.weight, std=0.02)
+
+    def _norm_f(self, x):
+        if self.cfg.norm_impl == "fused":
+            return rms_norm(x, self.lnf_w, self.cfg.eps)
+        return Fn.rms_norm(x, (x.shape[-1],), self.lnf_w, self.cfg.eps)
+
+    def _head_w(self):
+        return self.tok_emb.weight if self.cfg.tie_embeddings else self.head.weight
+
+    def num_params(self):
+        return sum(p.numel() for p in self.parameters())
+
+    def forward(self, idx, targets=None, grad_scale=1.0):
+        B, T = idx.shape
+        if T > self.cfg.seq_len:
+            raise ValueError(f"T={T} > seq_len={self.cfg.seq_len}")
+        if self.cfg.linear_impl == "fused" and self.tok_emb.weight.dtype != torch.float32:
+            x = _Embedding.apply(idx.contiguous(), self.tok_emb.weight, self.pos_emb)
+        else:
+            x = self.tok_emb(idx) + self.pos_emb[:T]
+        for blk in self.blocks:
+            x = blk(x)
+        x = self._norm_f(x)
+        if targets is None:
+            if self.cfg.linear_impl == "fused":
+                return fused_linear(x, self._head_w())
+            return Fn.linear(x, self._head_w())
+        if self.cfg.ce_impl == "fused":
+            return linear_cross_entropy(x.reshape(-1, x.shape[-1]), self._head_w(),
+                                        targets.reshape(-1), grad_scale=grad_scale)
+        logits = Fn.linear(x, self._head_w())
+        return Fn.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))

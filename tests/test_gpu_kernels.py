@@ -1,0 +1,270 @@
+"""GPU parity tests of the sm_100a kernels through the C ABI (ctypes).
+
+Each op is compared with an fp32 PyTorch computation on the same rounded
+inputs, with the reference's own tolerance rule (ml/fxlm/selftest.py:49-53):
+max|ours - fp32| <= 2 * max|torch_lowp - fp32| + 1e-3, where torch_lowp is the
+same op run by PyTorch in the low-precision dtype.
+"""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.bfloat16, torch.float16]
+
+
+def rule(ours, ref32, lowp):
+    e_our = (ours.float() - ref32).abs().max().item()
+    e_lp = (lowp.float() - ref32).abs().max().item()
+    return e_our <= 2 * e_lp + 1e-3, e_our, e_lp
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda")
+
+
+@pytest.fixture(autouse=True)
+def _no_expired_waits(dev):
+    """Every test must leave the device error word (expired bounded waits) at 0."""
+    yield
+    from fxb200 import _lib
+    code = _lib.device_error(clear=True)
+    assert code == 0, f"a kernel's bounded wait expired (device error word {code})"
+
+
+# ------------------------------------------------------------------ RMSNorm
+@pytest.mark.parametrize("dtype", DTYPES + [torch.float32])
+@pytest.mark.parametrize("N,D", [(4, 8), (37, 64), (129, 768), (1000, 512), (8192, 768), (33, 2048)])
+def test_rms_norm(dev, dtype, N, D):
+    from fxlm.norm import rms_norm
+    torch.manual_seed(N * 1000 + D)
+    x = (torch.randn(N, D, device=dev) * 3).to(dtype)
+    w = (torch.randn(D, device=dev) * 0.5 + 1).to(dtype)
+    g = torch.randn(N, D, device=dev).to(dtype)
+    if dtype == torch.float32 and D > 1024:
+        pytest.skip("fp32 backward supports D <= 1024")
+    xq, wq = x.detach().clone().requires_grad_(), w.detach().clone().requires_grad_()
+    xr, wr = x.detach().float().clone().requires_grad_(), w.detach().float().clone().requires_grad_()
+    xt, wt = x.detach().clone().requires_grad_(), w.detach().clone().requires_grad_()
+    y = rms_norm(xq, wq, 1e-6)
+    yr = F.rms_norm(xr, (D,), wr, 1e-6)
+    yt = F.rms_norm(xt, (D,), wt, 1e-6)
+    y.backward(g); yr.backward(g.float()); yt.backward(g)
+    for ours, ref, lp, nm in ((y, yr, yt, "y"), (xq.grad, xr.grad, xt.grad, "dx"),
+                              (wq.grad, wr.grad, wt.grad, "dw")):
+        ok, e, b = rule(ours, ref.detach(), lp)
+        if dtype == torch.float32:
+            ok = e <= 1e-5 * max(1.0, ref.abs().max().item())
+        assert ok, f"{nm}: err {e:.3e} vs torch-lowp {b:.3e}"
+
+
+# ------------------------------------------------------------------ fused CE
+@pytest.mark.parametrize("dtype", DTYPES + [torch.float32])
+@pytest.mark.parametrize("N,V", [(5, 32), (100, 512), (301, 8192), (64, 32768), (7, 50), (3, 40000)])
+def test_fused_ce(dev, dtype, N, V):
+    from fxlm.cross_entropy import fused_cross_entropy
+    torch.manual_seed(N + V)
+    lg = (torch.randn(N, V, device=dev) * 4).to(dtype)
+    tg = torch.randint(0, V, (N,), device=dev)
+    tg[::7] = -100
+    l32 = F.cross_entropy(lg.float(), tg, ignore_index=-100)
+    l16 = F.cross_entropy(lg, tg, ignore_index=-100)
+    lq = fused_cross_entropy(lg, tg, -100)
+    ok1, e1, b1 = rule(lq, l32, l16)
+    lg2 = lg.detach().clone().requires_grad_()
+    lg3 = lg.detach().float().clone().requires_grad_()
+    lg4 = lg.detach().clone().requires_grad_()
+    fused_cross_entropy(lg2, tg, -100).backward()
+    F.cross_entropy(lg3, tg, ignore_index=-100).backward()
+    F.cross_entropy(lg4, tg, ignore_index=-100).backward()
+    ok2, e2, b2 = rule(lg2.grad, lg3.grad, lg4.grad)
+    if dtype == torch.float32:
+        ok1 = e1 <= 1e-5 * max(1.0, l32.abs().item())
+        ok2 = e2 <= 1e-6
+    assert ok1, f"loss err {e1} vs {b1}"
+    assert ok2, f"grad err {e2} vs {b2}"
+
+
+# ------------------------------------------------------------------ GEMM
+def _gemm_ref(A, B, a_trans, b_trans):
+    Af = A.float().t() if a_trans else A.float()
+    Bf = B.float().t() if b_trans else B.float()
+    return Af @ Bf.t()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("a_trans,b_trans", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 512, 256), (200, 136, 72),
+                                   (1000, 768, 768), (8192, 2304, 768), (64, 3072, 8192)])
+def test_gemm_store(dev, dtype, a_trans, b_trans, M, N, K):
+    from fxb200 import ops
+    torch.manual_seed(M + N + K)
+    A = (torch.randn(K, M, device=dev) if a_trans else torch.randn(M, K, device=dev)).to(dtype)
+    B = (torch.randn(K, N, device=dev) if b_trans else torch.randn(N, K, device=dev)).to(dtype)
+    C = torch.empty(M, N, device=dev, dtype=dtype)
+    ops.gemm(A, B, C, a_trans=a_trans, b_trans=b_trans)
+    ref = _gemm_ref(A, B, a_trans, b_trans)
+    err = (C.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, f"rel err {err:.3e}"
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("M,N,K", [(300, 264, 136), (4096, 3072, 768)])
+def test_gemm_epilogues(dev, dtype, M, N, K):
+    from fxb200 import ops
+    torch.manual_seed(7)
+    A = (torch.randn(M, K, device=dev) / math.sqrt(K)).to(dtype)
+    B = torch.randn(N, K, device=dev).to(dtype)
+    acc = A.float() @ B.float().t()
+    tol = 1e-2 * acc.abs().max().item()
+    # residual (in place)
+    R = torch.randn(M, N, device=dev).to(dtype)
+    C = R.clone()
+    ops.gemm(A, B, C, epilogue=ops.EPI_RESIDUAL, R=C)
+    assert (C.float() - (acc + R.float())).abs().max().item() < tol + 1e-2
+    # gelu with pre-activation
+    Z = torch.empty(M, N, device=dev, dtype=dtype)
+    C = torch.empty(M, N, device=dev, dtype=dtype)
+    ops.gemm(A, B, C, epilogue=ops.EPI_GELU, Z=Z)
+    assert (Z.float() - acc).abs().max().item() < tol
+    assert (C.float() - F.gelu(Z.float(), approximate="tanh")).abs().max().item() < 2e-2
+    # dgelu
+    zz = torch.randn(M, N, device=dev).to(dtype)
+    ops.gemm(A, B, C, epilogue=ops.EPI_DGELU, R=zz)
+    zr = zz.float().requires_grad_()
+    F.gelu(zr, approximate="tanh").backward(acc)
+    assert (C.float() - zr.grad).abs().max().item() < 2e-2 * zr.grad.abs().max().item() + 1e-2
+    # bias + gelu / bias + silu
+    bias = torch.randn(N, device=dev).to(dtype)
+    ops.gemm(A, B, C, epilogue=ops.EPI_BIAS_GELU, Z=Z, bias=bias)
+    assert (Z.float() - (acc + bias.float())).abs().max().item() < tol + 2e-2
+    ops.gemm(A, B, C, epilogue=ops.EPI_BIAS_SILU, Z=Z, bias=bias)
+    assert (C.float() - F.silu(Z.float())).abs().max().item() < 2e-2
+    ops.gemm(A, B, C, epilogue=ops.EPI_BIAS, bias=bias)
+    assert (C.float() - (acc + bias.float())).abs().max().item() < tol + 2e-2
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("Mtok,N,K", [(8192, 768, 768), (8192, 3072, 768), (1000, 264, 72)])
+def test_gemm_dw_accum(dev, dtype, Mtok, N, K):
+    """dW (fp32) += dy^T x via split-K red.add, accumulating twice."""
+    from fxb200 import ops
+    torch.manual_seed(11)
+    dy = torch.randn(Mtok, N, device=dev).to(dtype)
+    x = torch.randn(Mtok, K, device=dev).to(dtype)
+    dW = torch.zeros(N, K, device=dev, dtype=torch.float32)
+    ops.linear_dw_into(dy, x, dW)
+    ops.linear_dw_into(dy, x, dW, alpha=0.5)
+    ref = 1.5 * (dy.float().t() @ x.float())
+    err = (dW - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-4, f"rel err {err:.3e}"
+
+
+# ------------------------------------------------------------------ attention
+def _ref_attn(q, k, v, causal, scale):
+    qt, kt, vt = (t.float().permute(0, 2, 1, 3) for t in (q, k, v))
+    s = qt @ kt.transpose(-1, -2) * scale
+    if causal:
+        T = q.shape[1]
+        mask = torch.ones(T, T, device=q.device, dtype=torch.bool).triu(1)
+        s = s.masked_fill(mask, float("-inf"))
+    return (torch.softmax(s, -1) @ vt).permute(0, 2, 1, 3)
+
+
+def _sdpa(q, k, v, causal, scale):
+    o = F.scaled_dot_product_attention(q.permute(0, 2, 1, 3), k.permute(0, 2, 1, 3),
+                                       v.permute(0, 2, 1, 3), is_causal=causal, scale=scale)
+    return o.permute(0, 2, 1, 3)
+
+
+ATTN_CASES = [(1, 1, 1, 64), (1, 17, 1, 64), (2, 64, 2, 64), (1, 100, 8, 64), (3, 256, 8, 64),
+              (2, 513, 2, 64), (1, 130, 4, 128), (2, 200, 8, 128), (1, 33, 1, 128),
+              (2, 1024, 12, 64)]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("B,T,H,Dh", ATTN_CASES)
+def test_attention(dev, dtype, causal, B, T, H, Dh):
+    from fxlm.attention import flash_attention
+    torch.manual_seed(B * 7 + T * 13 + Dh)
+    scale = 1.0 / math.sqrt(Dh)
+    qkv = torch.randn(B, T, 3, H, Dh, device=dev).to(dtype)
+    q, k, v = (qkv[:, :, i].requires_grad_() for i in range(3))
+    o = flash_attention(q, k, v, causal=causal, scale=scale)
+    oref = _ref_attn(q.detach(), k.detach(), v.detach(), causal, scale)
+    o16 = _sdpa(q.detach(), k.detach(), v.detach(), causal, scale)
+    ok, e, b = rule(o, oref, o16)
+    assert ok, f"fwd err {e} vs {b}"
+    if Dh != 64:
+        return  # tcgen05 backward of this build covers head_dim 64
+    g = torch.randn_like(o)
+    o.backward(g)
+    qr, kr, vr = (t.detach().float().requires_grad_() for t in (q, k, v))
+    _ref_attn(qr, kr, vr, causal, scale).backward(g.float())
+    qt, kt, vt = (t.detach().clone().requires_grad_() for t in (q, k, v))
+    _sdpa(qt, kt, vt, causal, scale).backward(g)
+    for ours, ref, lp, nm in ((q.grad, qr.grad, qt.grad, "dq"), (k.grad, kr.grad, kt.grad, "dk"),
+                              (v.grad, vr.grad, vt.grad, "dv")):
+        ok, e, b = rule(ours, ref, lp)
+        assert ok, f"{nm}: err {e} vs {b}"
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_qkv_and_lse(dev, causal):
+    from fxlm.attention import flash_attention_qkv, _fwd
+    torch.manual_seed(5)
+    B, T, H, Dh = 2, 100, 4, 64
+    qkv = torch.randn(B, T, 3, H, Dh, device=dev).to(torch.bfloat16).requires_grad_()
+    o = flash_attention_qkv(qkv, causal=causal)
+    q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+    scale = 1.0 / math.sqrt(Dh)
+    oref = _ref_attn(q.detach(), k.detach(), v.detach(), causal, scale)
+    o16 = _sdpa(q.detach(), k.detach(), v.detach(), causal, scale)
+    assert rule(o, oref, o16)[0]
+    g = torch.randn_like(o)
+    o.backward(g)
+    qr, kr, vr = (t.detach().float().requires_grad_() for t in (q, k, v))
+    _ref_attn(qr, kr, vr, causal, scale).backward(g.float())
+    qt, kt, vt = (t.detach().clone().requires_grad_() for t in (q, k, v))
+    _sdpa(qt, kt, vt, causal, scale).backward(g)
+    for i, (rg, tg) in enumerate(((qr, qt), (kr, kt), (vr, vt))):
+        assert rule(qkv.grad[:, :, i], rg.grad, tg.grad)[0], f"grad {i}"
+    # logsumexp of the scaled scores, natural log
+    _o, lse = _fwd(q.detach(), k.detach(), v.detach(), causal, scale)
+    s = (q.detach().float().permute(0, 2, 1, 3) @ k.detach().float().permute(0, 2, 3, 1)) * scale
+    if causal:
+        s = s.masked_fill(torch.ones(T, T, device=dev, dtype=torch.bool).triu(1), float("-inf"))
+    assert (lse - torch.logsumexp(s, -1)).abs().max().item() < 1e-2
+
+
+# ------------------------------------------------------------------ embedding / axpy
+def test_embedding(dev):
+    from fxlm.model import _Embedding
+    torch.manual_seed(3)
+    V, D, B, T = 300, 64, 4, 50
+    tok = torch.randn(V, D, device=dev).to(torch.bfloat16).requires_grad_()
+    pos = torch.randn(T + 6, D, device=dev).to(torch.bfloat16).requires_grad_()
+    idx = torch.randint(0, V, (B, T), device=dev)
+    out = _Embedding.apply(idx, tok, pos)
+    ref = tok.detach().float()[idx] + pos.detach().float()[:T]
+    assert (out.float() - ref).abs().max().item() < 2e-2
+    g = torch.randn(B, T, D, device=dev).to(torch.bfloat16)
+    out.backward(g)
+    gt = torch.zeros(V, D, device=dev).index_add_(0, idx.reshape(-1), g.float().reshape(-1, D))
+    gp = torch.zeros(T + 6, D, device=dev)
+    gp[:T] = g.float().sum(0)
+    assert (tok.grad.float() - gt).abs().max().item() < 3e-2 * max(1.0, gt.abs().max().item())
+    assert (pos.grad.float() - gp).abs().max().item() < 3e-2 * max(1.0, gp.abs().max().item())
+
+
+def test_device_error_word_clear(dev):
+    from fxb200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.device_error(clear=True) == 0
