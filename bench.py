@@ -1,0 +1,489 @@
+#!/usr/bin/env python
+"""Benchmark: GPT d768x12L training step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = forward + backward + FlatAdamW update of the reference GPT
+architecture (V32768, L12, D768, H12, T1024) on a per-GPU micro-batch of 8
+sequences of Zipf(1.1) tokens (seed 3 + rank), bf16 compute with fp32 master
+weights. For N > 1 the driver launches this under torchrun (one rank per GPU,
+NCCL); gradients are all-reduced in buckets that overlap backward.
+
+Printed (rank 0, one JSON line): `value` = tokens/s of the whole job with the
+token batch already in HBM, timed on the device with CUDA events (max over
+ranks); `e2e` = the same loop through the public API with the batch copied
+from pinned host memory and the loss read back every step; `roofline` for the
+dominant kernel (the tcgen05 GEMM: summed algorithmic FLOPs / summed event
+time of its launches in the timed region, against the measured sustained bf16
+peak); `cpu_baseline` = the reference's PyTorch path restated in oracle/gpt.py
+on the host cores (bounded sample); `clocks` sampled with nvidia-smi during
+the timed region; `gpu_launches` = kernels launched by libfxb200 in the timed
+region. `--impl reference` times only that CPU path (the reference arm).
+"""
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "radeon-igpu-forge_b200")
+for _p in (PKG, ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+CFG4 = dict(vocab_size=32768, seq_len=1024, n_layer=12, n_head=12, d_model=768)
+MB, SEQ = 8, 1024  # per-GPU micro-batch
+WORKLOAD = "gpt_d768x12L_v32768: per-GPU micro-batch 8 x seq 1024, bf16 + fp32-master FlatAdamW"
+
+
+def _metric():
+    try:
+        with open(os.path.join(ROOT, "BASELINE.json")) as f:
+            return json.load(f)["metric"]
+    except Exception:
+        return "GPT d768x12L train tokens/s"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops_sustained"]), "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
+    except Exception:
+        return 1400.0, "fallback 1.4 PFLOP/s sustained (of fallback)"
+
+
+def _gemm_traffic():
+    """Average DRAM bytes per GEMM launch of one step, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "gemm_tc_gpt_d768_step.md")
+    try:
+        with open(p) as f:
+            m = re.search(r"avg_dram_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+        return float(m.group(1)) if m else None
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_baseline(steps=3, warmup=1):
+    """The reference's PyTorch path (oracle/gpt.py) in fp32 on the host cores:
+    one 1024-token sequence per step, forward + backward + FlatAdamW step."""
+    import torch
+    from oracle import gpt as og
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(3)
+    m = og.RefGPT(**CFG4)
+    opt = og.OracleFlatAdamW(list(m.named_parameters()), lr=6e-4, weight_decay=0.1,
+                             max_grad_norm=1.0, init_scale=1.0)
+    x, y = og.zipf_tokens(CFG4["vocab_size"], 1, SEQ, seed=3)
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        m.zero_grad(set_to_none=True)
+        loss = m(x, y)
+        (loss * opt.scale).backward()
+        opt.step({n: p.grad for n, p in m.named_parameters()})
+        with torch.no_grad():
+            for n, p in m.named_parameters():
+                p.copy_(opt.master[n])
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    tps = SEQ / statistics.mean(times)
+    return {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"1 x {SEQ} tokens per step, {steps} timed steps after {warmup} warm-up "
+                      f"(fp32, oracle/gpt.py restating ml/fxlm/model.py torch path + FlatAdamW)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    base = cpu_baseline(steps=max(1, args.steps), warmup=max(1, args.warmup))
+    line = {"metric": _metric(), "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": SEQ / base["value"] * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic Zipf(1.1) tokens (seed 3)", "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": SEQ,
+                       "parallelism": "cpu", "sample": base["sample"]},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- attention microbench
+def attn_tflops(dev, iters=10):
+    """Config 2: causal flash attention fwd+bwd, B16 H12 S1024 D64 bf16."""
+    import math
+    import torch
+    from fxlm.attention import flash_attention
+    B, H, S, D = 16, 12, 1024, 64
+    g = torch.Generator(device=dev).manual_seed(1)
+    q, k, v, do = (torch.randn(B, S, H, D, device=dev, generator=g).mul_(1 / math.sqrt(D))
+                   .to(torch.bfloat16) for _ in range(4))
+    q.requires_grad_(); k.requires_grad_(); v.requires_grad_()
+    fwd_flops = 2 * B * H * S * S * D  # causal: half of 4*B*H*S^2*D
+    for _ in range(3):
+        o = flash_attention(q, k, v, causal=True)
+        o.backward(do)
+    torch.cuda.synchronize()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    tf, tb = 0.0, 0.0
+    for _ in range(iters):
+        q.grad = k.grad = v.grad = None
+        e0.record()
+        o = flash_attention(q, k, v, causal=True)
+        e1.record()
+        o.backward(do)
+        e2.record()
+        torch.cuda.synchronize()
+        tf += e0.elapsed_time(e1)
+        tb += e1.elapsed_time(e2)
+    tf, tb = tf / iters, tb / iters
+    return {"fwd_tflops": fwd_flops / tf / 1e9, "fwd_bwd_tflops": 3 * fwd_flops / (tf + tb) / 1e9,
+            "fwd_ms": tf, "bwd_ms": tb, "shape": "B16 H12 S1024 D64 causal bf16"}
+
+
+# ---------------------------------------------------------------- per-kernel microbenchmarks
+def _time_ms(fn, iters, warmup=3):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def run_micro(args):
+    """One JSON line per kernel: BASELINE configs 2 and 3 shapes, the block
+    GEMMs of config 4 and the AdamW pass over config 4's parameters. Inputs
+    are larger than L2 (126 MB) except where noted."""
+    import math
+    import torch
+    from fxb200 import _lib, ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    hbm = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        hbm, tc = float(pk["hbm_gbs"]), float(pk["bf16_tflops"])
+    except Exception:
+        hbm, tc = 6650.0, 1590.0
+    out = []
+    which = args.micro.split(",")
+    it = args.iters
+    bf = torch.bfloat16
+    if "gemm" in which or "gemm_fc" in which or "all" in which:
+        cases = [(8192, 3072, 768, ops.EPI_GELU, "fc+gelu"), (8192, 2304, 768, ops.EPI_STORE, "qkv"),
+                 (8192, 768, 3072, ops.EPI_RESIDUAL, "fc2+residual"),
+                 (65536, 32768, 768, ops.EPI_STORE, "lm_head cfg3")]
+        if "gemm_fc" in which:
+            cases = cases[:1]
+        for (M, N, K, epi, nm) in cases:
+            A = torch.randn(M, K, device=dev).to(bf)
+            B = (torch.randn(N, K, device=dev) / math.sqrt(K)).to(bf)
+            C = torch.empty(M, N, device=dev, dtype=bf)
+            Z = torch.empty(M, N, device=dev, dtype=bf) if epi == ops.EPI_GELU else None
+            R = torch.randn(M, N, device=dev).to(bf) if epi == ops.EPI_RESIDUAL else None
+            ms = _time_ms(lambda: ops.gemm(A, B, C, epilogue=epi, Z=Z, R=R), it)
+            tf = 2.0 * M * N * K / ms / 1e9
+            out.append({"kernel": "gemm_tc", "case": f"{nm} M{M} N{N} K{K}", "ms": ms, "tflops": tf,
+                        "frac_of_measured_burst": tf / tc})
+        for (Mt, N, K, nm) in ([] if "gemm_fc" in which else
+                               [(8192, 3072, 768, "dW fc"), (8192, 768, 768, "dW proj")]):
+            dy = torch.randn(Mt, N, device=dev).to(bf)
+            x = torch.randn(Mt, K, device=dev).to(bf)
+            dW = torch.zeros(N, K, device=dev)
+            ms = _time_ms(lambda: ops.linear_dw_into(dy, x, dW), it)
+            tf = 2.0 * Mt * N * K / ms / 1e9
+            out.append({"kernel": "gemm_tc (split-K, fp32 red.add)", "case": f"{nm} tokens{Mt} N{N} K{K}",
+                        "ms": ms, "tflops": tf, "frac_of_measured_burst": tf / tc})
+    if "attn" in which or "all" in which:
+        a = attn_tflops(dev, iters=it)
+        a.update({"kernel": "attn_fwd + attn_bwd", "case": "BASELINE config 2",
+                  "frac_of_measured_burst_fwd_bwd": a["fwd_bwd_tflops"] / tc})
+        out.append(a)
+    if "rmsnorm" in which or "all" in which:
+        from fxlm.norm import _RMSNorm  # noqa: F401
+        Nr, D = 65536, 768
+        g = torch.Generator(device=dev).manual_seed(2)
+        x = torch.randn(Nr, D, device=dev, generator=g).to(bf)
+        w = (1 + 0.02 * torch.randn(D, device=dev, generator=g)).to(bf)
+        y = torch.empty_like(x)
+        rstd = torch.empty(Nr, device=dev)
+        st = _lib.stream_ptr(dev)
+        f = lambda: _lib.call("fxb_rmsnorm_fwd", 2, _lib.ptr(x), _lib.ptr(w), _lib.ptr(y), _lib.ptr(rstd),  # noqa: E731
+                              Nr, D, 1e-6, st)
+        ms = _time_ms(f, it)
+        byt = 2 * Nr * D * 2 + Nr * 4
+        out.append({"kernel": "rmsnorm_fwd", "case": f"config 3 [{Nr},{D}] bf16", "ms": ms,
+                    "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm})
+        dy = torch.randn(Nr, D, device=dev, generator=g).to(bf)
+        dx = torch.empty_like(x)
+        dw = torch.zeros(D, device=dev)
+        ws = torch.empty(_lib.load().fxb_rmsnorm_bwd_workspace(Nr, D) // 4 + 1, device=dev)
+        fb = lambda: _lib.call("fxb_rmsnorm_bwd", 2, _lib.ptr(x), _lib.ptr(w), _lib.ptr(rstd), _lib.ptr(dy),  # noqa: E731
+                               _lib.ptr(dx), _lib.ptr(dw), 0, 0, _lib.ptr(ws), Nr, D, st)
+        ms = _time_ms(fb, it)
+        byt = 3 * Nr * D * 2 + Nr * 4
+        out.append({"kernel": "rmsnorm_bwd", "case": f"config 3 [{Nr},{D}] bf16", "ms": ms,
+                    "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm})
+    if "ce" in which or "all" in which:
+        Nr, V = 65536, 32768
+        g = torch.Generator(device=dev).manual_seed(2)
+        lg = torch.randn(Nr, V, device=dev, generator=g, dtype=bf)
+        tg = torch.randint(0, V, (Nr,), device=dev, generator=g)
+        grad = torch.empty_like(lg)
+        loss = torch.zeros(Nr, device=dev)  # per-row losses
+        mul = torch.full((), 1.0 / Nr, device=dev)
+        st = _lib.stream_ptr(dev)
+        f = lambda: _lib.call("fxb_ce_fwd_grad", 2, _lib.ptr(lg), V, _lib.ptr(tg), _lib.ptr(grad),  # noqa: E731
+                              _lib.ptr(loss), _lib.ptr(mul), Nr, V, -100, st)
+        ms = _time_ms(f, it)
+        byt = 2 * Nr * V * 2
+        out.append({"kernel": "ce_fwd_grad", "case": f"config 3 [{Nr},{V}] bf16 (read logits + write dlogits)",
+                    "ms": ms, "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm})
+        del lg, grad
+    if "adamw" in which or "all" in which:
+        n = 110_906_112 + 8 * 80
+        n -= n % 8
+        grad = torch.randn(n, device=dev) * 1e-3
+        master, m, v = torch.randn(n, device=dev) * 0.02, torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+        p16 = torch.empty(n, device=dev, dtype=bf)
+        seg_end = torch.tensor([n], device=dev, dtype=torch.int64)
+        seg_wd = torch.tensor([1], device=dev, dtype=torch.int32)
+        scratch = torch.zeros(2, device=dev); flags = torch.zeros((), device=dev, dtype=torch.int32)
+        step = torch.zeros((), device=dev, dtype=torch.int32); fi = torch.zeros((), device=dev)
+        norm = torch.zeros((), device=dev); scale = torch.ones((), device=dev)
+        st = _lib.stream_ptr(dev)
+        P = _lib.ptr
+
+        def f():
+            _lib.call("fxb_adamw_sumsq", 0, P(grad), n, P(scratch), P(flags), st)
+            _lib.call("fxb_adamw_final", P(scratch), P(flags), P(step), P(fi), P(norm), P(scale), 1.0, st)
+            _lib.call("fxb_adamw_update", 0, 2, P(grad), P(master), P(m), P(v), P(p16), n, P(seg_end),
+                      P(seg_wd), 1, P(scratch), P(fi), P(scale), P(step), 6e-4, 0.9, 0.95, 1e-8, 0.1, st)
+        ms = _time_ms(f, it)
+        byt = n * (4 + 4 + 4 + 24 + 2)
+        out.append({"kernel": "adamw_sumsq + adamw_final + adamw_update", "case": f"{n} params fp32 grad",
+                    "ms": ms, "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm,
+                    "bytes_per_param": 38})
+    for o in out:
+        print(json.dumps(o), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from fxb200 import _lib, ops
+    from fxb200.data import zipf_tokens
+    from fxlm import GPT, GPTConfig, FlatAdamW
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.load()
+
+    torch.manual_seed(3)
+    model = GPT(GPTConfig(**CFG4, eps=1e-6)).to(dev)
+    opt = FlatAdamW(model, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                    max_grad_norm=1.0, init_scale=1.0, param_dtype=torch.bfloat16)
+    if world > 1:
+        from fxb200.ddp import DataParallel
+        DataParallel(model, opt)
+    x_cpu, y_cpu = zipf_tokens(CFG4["vocab_size"], MB, SEQ, seed=3 + rank)
+    x_host, y_host = x_cpu.pin_memory(), y_cpu.pin_memory()
+    x_dev, y_dev = x_cpu.to(dev), y_cpu.to(dev)
+
+    def step(x, y):
+        loss = model(x, y, grad_scale=opt.scale)
+        opt.backward(loss)
+        opt.step(6e-4)
+        opt.zero_grad()
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step(x_dev, y_dev)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+
+    # ---- device-timed steps, inputs resident in HBM
+    clk = ClockSampler(local_rank)
+    clk.start()
+    time.sleep(0.3)
+    records = []
+    ops.set_gemm_timing(records)
+    n0 = _lib.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        loss = step(x_dev, y_dev)
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    ops.set_gemm_timing(None)
+    clocks = clk.stop()
+    barrier()
+    t_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    tokens = world * MB * SEQ * args.steps
+    value = tokens / (t_ms / 1e3)
+    g_flops = sum(r[0] for r in records)
+    g_ms = sum(r[1].elapsed_time(r[2]) for r in records)
+    n_gemm = len(records)
+    achieved = g_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else None
+    final_loss = float(loss.item())
+
+    # ---- end to end through the public API: H2D batch + D2H loss each step
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        y_dev.copy_(y_host, non_blocking=True)
+        loss = step(x_dev, y_dev)
+        _ = loss.item()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e = {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": x_host.numel() * 8 + y_host.numel() * 8, "d2h_bytes_per_step": 4}
+
+    attn = attn_tflops(dev) if (rank == 0 and not args.no_attn) else None
+    barrier()
+    derr = _lib.device_error(clear=True)
+
+    if rank == 0:
+        peak, peak_src = _peaks()
+        traffic = _gemm_traffic()
+        line = {
+            "metric": _metric(), "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic Zipf(1.1) tokens, seed 3 + rank; reference init (seed 3)",
+            "config": {"workload": WORKLOAD, "global_batch": MB * world, "seq_len": SEQ,
+                       "parallelism": f"dp{world}", "model": "GPT d768x12L tied, V32768",
+                       "l2": "no flush: one step moves several GB (> 126 MB L2)"},
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (all GEMM launches of the step)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (achieved / peak) if achieved else None,
+                         "traffic": traffic, "peak_source": peak_src,
+                         "gemm_launches": n_gemm, "gemm_flops_per_step": g_flops / args.steps,
+                         "gemm_ms_per_step": g_ms / args.steps},
+            "model_tflops": value * 717e6 / 1e12,  # 717 MFLOP/token (6 x 110.1M matmul params + attention)
+            "clocks": clocks,
+            "final_loss": final_loss,
+            "device_error_word": derr,
+        }
+        if attn is not None:
+            line["attn"] = attn
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-attn", action="store_true", help="skip the attention microbench")
+    ap.add_argument("--micro", default=None,
+                    help="per-kernel microbenchmarks instead of the step: all or a comma list "
+                         "of gemm,attn,rmsnorm,ce,adamw")
+    ap.add_argument("--iters", type=int, default=20, help="iterations per microbenchmark")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.micro:
+        return run_micro(args)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

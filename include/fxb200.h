@@ -53,6 +53,9 @@ int fxb_device_error(int32_t* code, int32_t clear);
 /* Number of streaming multiprocessors of the current device (grid sizing). */
 int fxb_num_sms(int32_t* out);
 
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t fxb_launch_count(void);
+
 /* ABI self-check for bindings: sizeof(fxb_gemm_args) for which == 0,
  * sizeof(fxb_attn_args) for which == 1, 0 otherwise. */
 size_t fxb_abi_struct_size(int32_t which);
@@ -84,16 +87,18 @@ int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rs
 /* ------------------------------------------------------------------ cross entropy */
 
 /* Row-wise softmax cross entropy with the gradient written in the same pass.
- *   loss_sum += sum over valid rows of (logsumexp(row) - row[target])
- *   grad[r,:] = (softmax(row) - onehot(target)) * (*mul)   (0 for ignored rows)
- * A row is valid when target != ignore_index and 0 <= target < V.
+ *   row_loss[r] = logsumexp(row) - row[target]   (0 for rows that are not valid)
+ *   grad[r,:]   = (softmax(row) - onehot(target)) * (*mul)   (0 for ignored rows)
+ * A row is valid when target != ignore_index and 0 <= target < V. The caller
+ * sums row_loss (fixed order, deterministic) where the reference accumulated
+ * one scalar with atomics.
  * grad may be NULL (loss only) or equal to logits (in place).
  * logits/grad: (rows, V) with row stride ld (elements); target int64 (rows,);
- * loss_sum and mul are fp32 device scalars (no host sync).
+ * row_loss fp32 (rows,); mul is an fp32 device scalar (no host sync).
  * Replaces ce_fwd_grad (ml/fxlm/kernels/ce.hip:32) as launched by _ce_rows
  * (ml/fxlm/cross_entropy.py:47-59). */
 int fxb_ce_fwd_grad(int32_t dtype, const void* logits, int64_t ld, const int64_t* target,
-                    void* grad, float* loss_sum, const float* mul, int64_t rows, int32_t V,
+                    void* grad, float* row_loss, const float* mul, int64_t rows, int32_t V,
                     int64_t ignore_index, void* stream);
 
 /* ------------------------------------------------------------------ FlatAdamW */
@@ -139,6 +144,7 @@ int fxb_adamw_update(int32_t gdtype, int32_t pdtype, const void* grad, float* ma
 #define FXB_EPI_BIAS_GELU 5 /* Z = acc + bias[n] ; C = gelu_tanh(Z) */
 #define FXB_EPI_BIAS_SILU 6 /* Z = acc + bias[n] ; C = silu(Z) */
 #define FXB_EPI_ACCUM_F32 7 /* C(fp32) += alpha*acc (red.add; enables split-K) */
+#define FXB_EPI_DSILU 8     /* C = acc * silu'(R)        (R = pre-activation) */
 
 typedef struct fxb_gemm_args {
   int32_t dtype;     /* A/B dtype: FXB_DTYPE_BF16 or FXB_DTYPE_F16 */
@@ -223,6 +229,22 @@ int fxb_embedding_bwd(int32_t dtype, const int64_t* idx, const void* dout, float
  * Carries the linear-CE backward rescale (ml/fxlm/cross_entropy.py:140-149). */
 int fxb_axpy(int32_t ddtype, void* dst, int32_t sdtype, const void* src, const float* scale,
              int32_t accumulate, int64_t n, void* stream);
+
+/* ------------------------------------------------------------------ fxgpu window model */
+
+/* Xg[b, :] = X[idx[b] : idx[b] + window, :] flattened window-major (K = window*F),
+ * i.e. Xg[b, w*F + f] = X[idx[b] + w, f]. X (R, F) 16-bit row-major, F % 8 == 0,
+ * idx int32; windows that leave [0, R) are written as zeros.
+ * Replaces the A-operand gather and the Xg write-out of gather_gemm
+ * (ml/fxgpu/gather_gemm.hip:17-180, launched by ml/fxgpu/fused_linear.py:76-85);
+ * the GEMM itself runs through fxb_gemm with FXB_EPI_BIAS*. */
+int fxb_gather_windows(int32_t dtype, const void* X, int64_t R, int32_t F, const int32_t* idx,
+                       int32_t B, int32_t window, void* Xg, void* stream);
+
+/* out[c] (fp32) = (accumulate ? out[c] : 0) + sum_r g[r, c]; g (rows, cols) row-major.
+ * The bias gradient db = g.sum(0) of ml/fxgpu/fused_linear.py:95. */
+int fxb_colsum(int32_t dtype, const void* g, int64_t rows, int32_t cols, float* out,
+               int32_t accumulate, void* stream);
 
 #ifdef __cplusplus
 }

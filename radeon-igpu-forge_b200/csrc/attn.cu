@@ -318,26 +318,32 @@ __global__ void attn_bwd_prep_kernel(const T16* __restrict__ o, int64_t o_sb, in
                                      int64_t o_sh, const T16* __restrict__ dout, int64_t do_sb,
                                      int64_t do_st, int64_t do_sh, float* __restrict__ delta,
                                      float* __restrict__ dq_acc, int B, int T, int H) {
-  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (b*H + h)*T + t
-  if (row >= (int64_t)B * H * T) return;
-  const int t = (int)(row % T);
-  const int bh = (int)(row / T);
-  const int b = bh / H, h = bh - b * H;
-  const T16* orow = o + b * o_sb + (int64_t)t * o_st + h * o_sh;
-  const T16* grow = dout + b * do_sb + (int64_t)t * do_st + h * do_sh;
+  // DH/8 lanes per row (8 bf16 each): coalesced 128-byte row reads
+  constexpr int LPR = DH / 8;
+  const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = gtid / LPR;  // (b*H + h)*T + t
+  const int sub = (int)(gtid % LPR);
+  const bool ok = row < (int64_t)B * H * T;
   float s = 0.f;
-#pragma unroll
-  for (int d = 0; d < DH; d += 8) {
+  if (ok) {
+    const int t = (int)(row % T);
+    const int bh = (int)(row / T);
+    const int b = bh / H, h = bh - b * H;
+    const T16* orow = o + b * o_sb + (int64_t)t * o_st + h * o_sh + sub * 8;
+    const T16* grow = dout + b * do_sb + (int64_t)t * do_st + h * do_sh + sub * 8;
     float a[8], g[8];
-    unpack8<T16>(*reinterpret_cast<const uint4*>(orow + d), a);
-    unpack8<T16>(*reinterpret_cast<const uint4*>(grow + d), g);
+    unpack8<T16>(*reinterpret_cast<const uint4*>(orow), a);
+    unpack8<T16>(*reinterpret_cast<const uint4*>(grow), g);
 #pragma unroll
     for (int i = 0; i < 8; ++i) s += a[i] * g[i];
   }
-  delta[row] = s;
-  float4* z = reinterpret_cast<float4*>(dq_acc + row * DH);
 #pragma unroll
-  for (int d = 0; d < DH / 4; ++d) z[d] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int off = LPR / 2; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (!ok) return;
+  if (sub == 0) delta[row] = s;
+  float4* z = reinterpret_cast<float4*>(dq_acc + row * DH + sub * 8);
+  z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // dq = dq_acc * scale in the caller's layout
@@ -709,7 +715,7 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
   const int64_t rows = (int64_t)a->B * a->H * a->T;
   float* delta = a->workspace;
   float* dq_acc = a->workspace + ((rows + 3) / 4) * 4;
-  attn_bwd_prep_kernel<T16, DH><<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(
+  attn_bwd_prep_kernel<T16, DH><<<(unsigned)((rows * (DH / 8) + 255) / 256), 256, 0, st>>>(
       static_cast<const T16*>(a->o), a->o_sb, a->o_st, a->o_sh, static_cast<const T16*>(a->dout),
       a->do_sb, a->do_st, a->do_sh, delta, dq_acc, a->B, a->T, a->H);
   int r = fxb::check_launch("attn_bwd_prep");

@@ -1,5 +1,6 @@
 // Library-wide C ABI: version, error reporting, device error word, SM count,
 // and the tensor-map encoder used by the TMA-fed kernels.
+#include <atomic>
 #include <mutex>
 #include "common.cuh"
 #include "internal.h"
@@ -10,6 +11,9 @@ __device__ int g_fxb_dev_error = 0;
 namespace fxb {
 
 static thread_local std::string t_last_error;
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int set_error(int code, const char* fmt, ...) {
   char buf[1024];
@@ -121,6 +125,8 @@ int fxb_device_error(int32_t* code, int32_t clear) {
   }
   return r;
 }
+
+uint64_t fxb_launch_count(void) { return fxb::g_launches.load(std::memory_order_relaxed); }
 
 size_t fxb_abi_struct_size(int32_t which) {
   if (which == 0) return sizeof(fxb_gemm_args);

@@ -1,9 +1,11 @@
 // Fused softmax cross-entropy forward + gradient for sm_100a (HBM-bound).
 //
 // Semantics follow ce_fwd_grad (ml/fxlm/kernels/ce.hip:32-116): per row,
-// logsumexp in fp32, loss_sum += lse - x[target] for valid rows (atomic, like
-// ce.hip:89-92), grad = (softmax - onehot) * (*mul), zero for rows whose target
-// is ignore_index or out of [0, V) (ce.hip:43,97-115). The B200 layout keeps
+// logsumexp in fp32, row loss lse - x[target] for valid rows (the reference
+// atomically adds it into one scalar, ce.hip:89-92; here each row's loss is
+// stored and the caller sums them in a fixed order, so the result does not
+// depend on scheduling), grad = (softmax - onehot) * (*mul), zero for rows
+// whose target is ignore_index or out of [0, V) (ce.hip:43,97-115). The B200 layout keeps
 // the whole row in registers (16-byte vectors), so logits are read from HBM
 // once and the gradient written once; the gradient may overwrite the logits.
 #include "common.cuh"
@@ -65,7 +67,7 @@ template <int NT> FXB_DEV float block_sum(float v, float* red) {
 template <typename T, int NT, int VPT>
 __global__ void __launch_bounds__(NT == 32 ? 256 : NT)
 ce_cached_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
-                 T* grad, float* __restrict__ loss_sum, const float* __restrict__ mul,
+                 T* grad, float* __restrict__ row_loss, const float* __restrict__ mul,
                  int64_t rows, int V, int64_t ignore_index) {
   constexpr int E = CEVec<T>::N;
   __shared__ float red[32];
@@ -109,7 +111,8 @@ ce_cached_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __rest
     s = block_sum<NT>(s, red);
     // the logit of the target comes from registers: with grad == logits the
     // row in memory is being overwritten by other threads below
-    if (valid && owner) atomicAdd(loss_sum, mx + log2f(s) * kLn2 - xt);
+    if (valid && owner) row_loss[r] = mx + log2f(s) * kLn2 - xt;
+    if (!valid && tid == 0) row_loss[r] = 0.f;
     if (grad) {
       const float scale = valid ? gm / s : 0.f;
       const float sub = valid ? gm : 0.f;
@@ -136,7 +139,7 @@ ce_cached_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __rest
 template <typename T>
 __global__ void __launch_bounds__(256)
 ce_generic_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
-                  T* grad, float* __restrict__ loss_sum, const float* __restrict__ mul,
+                  T* grad, float* __restrict__ row_loss, const float* __restrict__ mul,
                   int64_t rows, int V, int64_t ignore_index) {
   __shared__ float red[32];
   const float gm = grad ? *mul : 0.f;
@@ -153,7 +156,7 @@ ce_generic_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __res
     float s = 0.f;
     for (int d = threadIdx.x; d < V; d += 256) s += exp2f(fmaf(to_f<T>(row[d]), kLog2e, -mxl));
     s = block_sum<256>(s, red);
-    if (valid && threadIdx.x == 0) atomicAdd(loss_sum, mx + log2f(s) * kLn2 - xt);
+    if (threadIdx.x == 0) row_loss[r] = valid ? mx + log2f(s) * kLn2 - xt : 0.f;
     if (grad) {
       const float scale = valid ? gm / s : 0.f;
       T* grow = grad + r * ld;
@@ -207,23 +210,23 @@ int launch_ce(const void* lg, int64_t ld, const int64_t* tg, void* gr, float* lo
 }  // namespace
 
 extern "C" int fxb_ce_fwd_grad(int32_t dtype, const void* logits, int64_t ld,
-                               const int64_t* target, void* grad, float* loss_sum,
+                               const int64_t* target, void* grad, float* row_loss,
                                const float* mul, int64_t rows, int32_t V, int64_t ignore_index,
                                void* stream) {
   if (fxb::dtype_size(dtype) == 0) return fxb::set_error(FXB_EINVAL, "ce: bad dtype %d", dtype);
   if (V <= 0 || rows < 0 || ld < V)
     return fxb::set_error(FXB_EINVAL, "ce: bad shape rows=%lld V=%d ld=%lld", (long long)rows, V,
                           (long long)ld);
-  if (!logits || !target || !loss_sum || (grad && !mul))
+  if (!logits || !target || !row_loss || (grad && !mul))
     return fxb::set_error(FXB_EINVAL, "ce: NULL pointer");
   if (rows == 0) return FXB_OK;
   cudaStream_t st = fxb::as_stream(stream);
   switch (dtype) {
     case FXB_DTYPE_BF16:
-      return launch_ce<__nv_bfloat16>(logits, ld, target, grad, loss_sum, mul, rows, V, ignore_index, st);
+      return launch_ce<__nv_bfloat16>(logits, ld, target, grad, row_loss, mul, rows, V, ignore_index, st);
     case FXB_DTYPE_F16:
-      return launch_ce<__half>(logits, ld, target, grad, loss_sum, mul, rows, V, ignore_index, st);
+      return launch_ce<__half>(logits, ld, target, grad, row_loss, mul, rows, V, ignore_index, st);
     default:
-      return launch_ce<float>(logits, ld, target, grad, loss_sum, mul, rows, V, ignore_index, st);
+      return launch_ce<float>(logits, ld, target, grad, row_loss, mul, rows, V, ignore_index, st);
   }
 }

@@ -17,6 +17,7 @@
 //     all read their operands in place.
 // Every mbarrier wait is bounded (common.cuh); on expiry the kernel records
 // FXB_DERR_GEMM_WAIT, drains what it issued and frees its tensor memory.
+#include <cstdlib>
 #include "common.cuh"
 #include "internal.h"
 
@@ -24,7 +25,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 
 struct GemmParams {
   int M, N, K;
@@ -176,6 +177,17 @@ FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v) {
       store32<CT>(crow, v, n8);
       break;
     }
+    case FXB_EPI_DSILU: {
+      float z[32];
+      load32_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, z, n8);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float s = 1.f / (1.f + __expf(-z[i]));
+        v[i] *= s * (1.f + z[i] * (1.f - s));
+      }
+      store32<CT>(crow, v, n8);
+      break;
+    }
     default: {  // FXB_EPI_ATOMIC_F32: red.add into fp32 C
       float* c32 = static_cast<float*>(p.C) + (int64_t)m * p.ldc + n0;
 #pragma unroll
@@ -216,7 +228,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull_bar(b), 1);
-      mbar_init(tempty_bar(b), 128);
+      mbar_init(tempty_bar(b), 8);  // one arrival per epilogue warp
     }
     mbar_init(final_bar, 1);
     fence_mbar_init();
@@ -319,8 +331,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------ epilogue (warps 2..9)
+    // two warps per TMEM lane quarter, each taking half of the tile's columns
     const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     int abuf = 0;
     uint32_t aphase = 0;
@@ -332,7 +346,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int m = tm * BM + row_in_tile;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         uint32_t r[32];
         tmem_ld32(tbase + c * 32, r);
         tmem_wait_ld();
@@ -349,7 +363,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
       tc_fence_before();
-      mbar_arrive(tempty_bar(abuf));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(abuf));
       if (++abuf == 2) { abuf = 0; aphase ^= 1; }
     }
   }
@@ -362,55 +377,292 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
 }
 
+// ---------------------------------------------------------------- 2-SM kernel
+// CTA pair (cluster of 2) computing 256 x BN tiles with tcgen05.mma
+// cta_group::2: each CTA loads its own 128 rows of A and its half (BN/2 rows)
+// of B with plain (non-multicast) TMA whose completion is counted on the
+// leader CTA's full barrier; the leader's single MMA thread reads both CTAs'
+// shared memory and writes both CTAs' tensor memory, and commits to the
+// barriers of both CTAs (tcgen05.commit multicast). Shared-memory operand
+// traffic per SM is half of the 1-SM kernel's for the same tile width, which
+// is what lets the tensor pipe run at full rate.
+template <int BN> struct Cfg2 {
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+FXB_DEV void tile_coords2(int unit, const GemmParams& p, int& tm, int& tn, int& split) {
+  tile_coords(unit, p, tm, tn, split);  // tm counts 256-row tiles here
+}
+
+template <int BN, bool A_MN, bool B_MN, int AB_FMT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmParams p) {
+  using C = Cfg2<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + C::STAGES * C::STAGE_BYTES;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+  auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + b); };
+  auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + 2 + b); };
+  const uint32_t final_bar = bar0 + 8u * (2 * C::STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + 8 * (2 * C::STAGES + 5));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs)
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 16);  // 8 epilogue warps x 2 CTAs
+    }
+    mbar_init(final_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and tensor memory allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_units = p.tiles_m * p.tiles_n * p.splits;
+  constexpr uint32_t IDESC = umma_idesc_f16(AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, 256, BN);
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_parity = 0;
+      bool ok = true;
+      for (int unit = pair; unit < total_units && ok; unit += npairs) {
+        int tm, tn, split;
+        tile_coords2(unit, p, tm, tn, split);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        const int arow = tm * 256 + (int)rank * 128;
+        const int brow = tn * BN + (int)rank * (BN / 2);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
+          const uint32_t sa = base + stage * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+          const uint32_t fb = mapa_shared(full_bar(stage), 0);
+          if (rank == 0) {
+            mbar_expect_tx(full_bar(stage), 2 * C::STAGE_BYTES);
+            armed |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          }
+          const int k0 = kb * BK;
+          if (A_MN) {
+            tma_load_2d_pair(sa, &tmA, fb, arow, k0);
+            tma_load_2d_pair(sa + 8192, &tmA, fb, arow + 64, k0);
+          } else {
+            tma_load_2d_pair(sa, &tmA, fb, k0, arow);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d_pair(sb + j * 8192, &tmB, fb, brow + 64 * j, k0);
+          } else {
+            tma_load_2d_pair(sb, &tmB, fb, k0, brow);
+          }
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // the leader's full barriers count both CTAs' bytes: draining them
+      // means every copy of the pair has landed
+      if (rank == 0)
+        for (int s = 0; s < C::STAGES; ++s)
+          if (armed & (1u << s)) mbar_wait(full_bar(s), (armed_parity >> s) & 1u, p.err, FXB_DERR_GEMM_WAIT);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (leader CTA)
+    if (lane == 0) {
+      if (rank == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        int abuf = 0;
+        uint32_t aphase = 0;
+        bool ok = true;
+        for (int unit = pair; unit < total_units && ok; unit += npairs) {
+          int tm, tn, split;
+          tile_coords2(unit, p, tm, tn, split);
+          const int kb0 = split * p.kb_per_split;
+          const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+          if (!mbar_wait(tempty_bar(abuf), aphase ^ 1, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t dcol = tmem_base + abuf * BN;
+          for (int kb = kb0; kb < kb1; ++kb) {
+            if (!mbar_wait(full_bar(stage), phase, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = base + stage * C::STAGE_BYTES;
+            const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t ad = A_MN ? umma_desc_sw128(sa + kk * 2048, 8192, 1024)
+                                       : umma_desc_sw128(sa + kk * 32, 16, 1024);
+              const uint64_t bd = B_MN ? umma_desc_sw128(sb + kk * 2048, 8192, 1024)
+                                       : umma_desc_sw128(sb + kk * 32, 16, 1024);
+              umma_f16_pair(dcol, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit_pair(empty_bar(stage), 0x3);
+            if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+          }
+          if (!ok) break;
+          umma_commit_pair(tfull_bar(abuf), 0x3);
+          if (++abuf == 2) { abuf = 0; aphase ^= 1; }
+        }
+        // completes (in both CTAs) once every MMA of the pair is done
+        umma_commit_pair(final_bar, 0x3);
+      }
+      mbar_wait(final_bar, 0, p.err, FXB_DERR_GEMM_WAIT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..9, both CTAs)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = (int)rank * 128 + quarter * 32 + lane;
+    int abuf = 0;
+    uint32_t aphase = 0;
+    for (int unit = pair; unit < total_units; unit += npairs) {
+      int tm, tn, split;
+      tile_coords2(unit, p, tm, tn, split);
+      if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
+      tc_fence_after();
+      const int m = tm * 256 + row_in_tile;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
+#pragma unroll 1
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        tmem_wait_ld();
+        const int n0 = tn * BN + c * 32;
+        if (m < p.M && n0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          switch (p.c_dtype) {
+            case FXB_DTYPE_BF16: epilogue_chunk<__nv_bfloat16>(p, m, n0, v); break;
+            case FXB_DTYPE_F16: epilogue_chunk<__half>(p, m, n0, v); break;
+            default: epilogue_chunk<float>(p, m, n0, v); break;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(abuf), 0));
+      if (++abuf == 2) { abuf = 0; aphase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's smem / tensor memory are no longer in use
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 constexpr int FXB_EPI_ATOMIC_F32 = FXB_EPI_ACCUM_F32;
 
-template <int BN, bool A_MN, bool B_MN, int AB_FMT>
+template <int BN, bool A_MN, bool B_MN, int AB_FMT, bool PAIR>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
                cudaStream_t st) {
-  auto k = gemm_tc_kernel<BN, A_MN, B_MN, AB_FMT>;
+  void (*k)(const CUtensorMap, const CUtensorMap, const GemmParams) =
+      PAIR ? gemm_tc2_kernel<BN, A_MN, B_MN, AB_FMT> : gemm_tc_kernel<BN, A_MN, B_MN, AB_FMT>;
+  constexpr int smem = PAIR ? Cfg2<BN>::SMEM : Cfg<BN>::SMEM;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    int r = fxb::check_cuda(
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM),
-        "gemm smem attribute");
+    int r = fxb::check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                            "gemm smem attribute");
     if (r) return r;
     attr_set[dev] = true;
   }
-  k<<<grid, kThreads, Cfg<BN>::SMEM, st>>>(ta, tb, p);
-  return fxb::check_launch("gemm_tc");
+  k<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  return fxb::check_launch(PAIR ? "gemm_tc2" : "gemm_tc");
 }
 
-template <int BN, int AB_FMT>
+template <int BN, int AB_FMT, bool PAIR>
 int launch_layout(bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb,
                   const GemmParams& p, int grid, cudaStream_t st) {
-  if (!amn && !bmn) return launch_one<BN, false, false, AB_FMT>(ta, tb, p, grid, st);
-  if (!amn && bmn) return launch_one<BN, false, true, AB_FMT>(ta, tb, p, grid, st);
-  if (amn && bmn) return launch_one<BN, true, true, AB_FMT>(ta, tb, p, grid, st);
-  return launch_one<BN, true, false, AB_FMT>(ta, tb, p, grid, st);
+  if (!amn && !bmn) return launch_one<BN, false, false, AB_FMT, PAIR>(ta, tb, p, grid, st);
+  if (!amn && bmn) return launch_one<BN, false, true, AB_FMT, PAIR>(ta, tb, p, grid, st);
+  if (amn && bmn) return launch_one<BN, true, true, AB_FMT, PAIR>(ta, tb, p, grid, st);
+  return launch_one<BN, true, false, AB_FMT, PAIR>(ta, tb, p, grid, st);
 }
 
-// Pick BN (128 or 256) and split-K to minimise waves x per-tile work.
-void plan(int M, int N, int K, bool allow_split, int sms, int& BN, int& splits) {
-  const int tm = (M + BM - 1) / BM;
+struct Plan {
+  bool pair;   // 2-SM (cta_group::2, 256-row tiles) or 1-SM (128-row tiles)
+  int BN;      // tile width
+  int splits;  // split-K factor (fp32 accumulate epilogue only)
+};
+
+// Choose tile shape and split-K by a cost model of the persistent schedule:
+// waves x per-unit time, where a unit's k-block time is bounded by the
+// shared-memory traffic of its MMA operands plus the TMA writes (128 B/clk
+// per SM) and the epilogue of a tile overlaps the next tile's mainloop.
+// Per-SM cycles per 64-deep k-block: 1-SM 128x128: 512, 1-SM 128x256: 768,
+// 2-SM 256x128: 384, 2-SM 256x256: 512 (the last one is tensor-bound).
+// `mode` (FXB_GEMM_FORCE=1sm|2sm, tests) restricts the choice.
+Plan plan(int M, int N, int K, bool allow_split, int sms, int mode) {
   const int nkb = (K + BK - 1) / BK;
   double best = 1e30;
-  BN = 128;
-  splits = 1;
-  for (int bn : {256, 128}) {
-    const int tn = (N + bn - 1) / bn;
-    for (int s = 1; s <= (allow_split ? 16 : 1); s *= 2) {
-      if (s > 1 && nkb / s < 4) break;  // keep >= 4 k-blocks per split
-      const int kbs = (nkb + s - 1) / s;
-      const long units = (long)tm * tn * s;
-      const long waves = (units + sms - 1) / sms;
-      // cost: waves x (k-blocks per unit x tile width + fixed epilogue/fill cost)
-      const double cost = (double)waves * ((double)kbs * bn + 6.0 * bn) + (s > 1 ? 0.02 * units : 0);
-      if (cost < best - 1e-9) { best = cost; BN = bn; splits = s; }
+  Plan out{false, 128, 1};
+  for (int pair = 1; pair >= 0; --pair) {
+    if ((mode == 1 && pair) || (mode == 2 && !pair)) continue;
+    const int rows = pair ? 256 : 128;
+    const int slots = pair ? sms / 2 : sms;
+    const int tm = (M + rows - 1) / rows;
+    for (int bn : {256, 128}) {
+      const int tn = (N + bn - 1) / bn;
+      const double t_kb = pair ? (bn == 256 ? 512.0 : 384.0) : (bn == 256 ? 768.0 : 512.0);
+      for (int s = 1; s <= (allow_split ? 16 : 1); s *= 2) {
+        if (s > 1 && nkb / s < 4) break;  // keep >= 4 k-blocks per split
+        const int kbs = (nkb + s - 1) / s;
+        const long units = (long)tm * tn * s;
+        const long waves = (units + slots - 1) / slots;
+        const double mainloop = kbs * t_kb + 600.0;  // + pipeline fill
+        const double epi = bn * 6.0;                  // TMEM -> registers -> global per tile
+        const double cost = (double)waves * (mainloop > epi ? mainloop : epi) + (s > 1 ? 0.5 * units : 0);
+        if (cost < best - 1e-9) { best = cost; out = Plan{pair != 0, bn, s}; }
+      }
     }
   }
+  return out;
+}
+
+int force_mode() {
+  const char* e = getenv("FXB_GEMM_FORCE");
+  if (!e) return 0;
+  if (e[0] == '1') return 1;
+  if (e[0] == '2') return 2;
+  return 0;
 }
 
 int make_map(CUtensorMap* map, int ab_dtype, const void* ptr, uint64_t inner, uint64_t outer,
@@ -446,7 +698,7 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
     return set_error(FXB_EINVAL, "gemm: B needs 16-byte rows and ldb >= row");
   if ((a->lda % 8) || (a->ldb % 8)) return set_error(FXB_EINVAL, "gemm: lda/ldb must be multiples of 8");
   if (a->ldc < N) return set_error(FXB_EINVAL, "gemm: ldc < N");
-  const bool needs_r = (epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU);
+  const bool needs_r = (epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU);
   if (needs_r && (!a->R || !aligned16(a->R) || (a->ldr * csz) % 16))
     return set_error(FXB_EINVAL, "gemm: epilogue needs an aligned R");
   const bool has_bias = (epi == FXB_EPI_BIAS || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU);
@@ -456,16 +708,18 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
     return set_error(FXB_EINVAL, "gemm: Z misaligned");
   if (epi == FXB_EPI_ATOMIC_F32 && a->c_dtype != FXB_DTYPE_F32)
     return set_error(FXB_EINVAL, "gemm: accumulate epilogue needs fp32 C");
-  if (epi < 0 || epi > FXB_EPI_ATOMIC_F32) return set_error(FXB_EINVAL, "gemm: bad epilogue %d", epi);
+  if (epi < 0 || epi > FXB_EPI_DSILU) return set_error(FXB_EINVAL, "gemm: bad epilogue %d", epi);
   if (M == 0 || N == 0) return FXB_OK;
   if (K == 0) return set_error(FXB_EUNSUPPORTED, "gemm: K == 0");
 
   int* err = dev_error_ptr();
   if (!err) return FXB_ECUDA;
   const int sms = num_sms();
-  int BN, splits;
-  plan(M, N, K, epi == FXB_EPI_ATOMIC_F32, sms, BN, splits);
+  Plan pl = plan(M, N, K, epi == FXB_EPI_ATOMIC_F32, sms, force_mode());
+  const int BN = pl.BN;
+  int splits = pl.splits;
   if (force_splits > 0 && epi == FXB_EPI_ATOMIC_F32) splits = force_splits;
+  const int rows = pl.pair ? 256 : 128;
 
   CUtensorMap ta, tb;
   int r;
@@ -473,12 +727,13 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
   else r = make_map(&ta, a->dtype, a->A, (uint64_t)K, (uint64_t)M, a->lda, 64, 128);
   if (r) return r;
   if (a->b_trans) r = make_map(&tb, a->dtype, a->B, (uint64_t)N, (uint64_t)K, a->ldb, 64, 64);
-  else r = make_map(&tb, a->dtype, a->B, (uint64_t)K, (uint64_t)N, a->ldb, 64, (uint32_t)BN);
+  else r = make_map(&tb, a->dtype, a->B, (uint64_t)K, (uint64_t)N, a->ldb, 64,
+                    (uint32_t)(pl.pair ? BN / 2 : BN));
   if (r) return r;
 
   GemmParams p;
   p.M = M; p.N = N; p.K = K;
-  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_m = (M + rows - 1) / rows;
   p.tiles_n = (N + BN - 1) / BN;
   p.num_kb = (K + BK - 1) / BK;
   p.splits = splits;
@@ -493,14 +748,22 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
   p.bias = a->bias;
   p.err = err;
   const long units = (long)p.tiles_m * p.tiles_n * p.splits;
-  const int grid = (int)(units < sms ? units : sms);
   const bool amn = a->a_trans != 0, bmn = a->b_trans != 0;
-  if (a->dtype == FXB_DTYPE_BF16) {
-    return BN == 256 ? launch_layout<256, 1>(amn, bmn, ta, tb, p, grid, st)
-                     : launch_layout<128, 1>(amn, bmn, ta, tb, p, grid, st);
+  if (pl.pair) {
+    const long pairs = units < sms / 2 ? units : sms / 2;
+    const int grid = (int)(2 * pairs);
+    if (a->dtype == FXB_DTYPE_BF16)
+      return BN == 256 ? launch_layout<256, 1, true>(amn, bmn, ta, tb, p, grid, st)
+                       : launch_layout<128, 1, true>(amn, bmn, ta, tb, p, grid, st);
+    return BN == 256 ? launch_layout<256, 0, true>(amn, bmn, ta, tb, p, grid, st)
+                     : launch_layout<128, 0, true>(amn, bmn, ta, tb, p, grid, st);
   }
-  return BN == 256 ? launch_layout<256, 0>(amn, bmn, ta, tb, p, grid, st)
-                   : launch_layout<128, 0>(amn, bmn, ta, tb, p, grid, st);
+  const int grid = (int)(units < sms ? units : sms);
+  if (a->dtype == FXB_DTYPE_BF16)
+    return BN == 256 ? launch_layout<256, 1, false>(amn, bmn, ta, tb, p, grid, st)
+                     : launch_layout<128, 1, false>(amn, bmn, ta, tb, p, grid, st);
+  return BN == 256 ? launch_layout<256, 0, false>(amn, bmn, ta, tb, p, grid, st)
+                   : launch_layout<128, 0, false>(amn, bmn, ta, tb, p, grid, st);
 }
 }  // namespace fxb
 

@@ -16,8 +16,15 @@ int set_error(int code, const char* fmt, ...);
 // Wraps a CUDA runtime status; FXB_OK when success.
 int check_cuda(cudaError_t e, const char* what);
 
-// Launch-time check: picks up configuration errors of the launch just made.
-inline int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+// Counts kernel launches made by this library (fxb_launch_count).
+void count_launch();
+
+// Launch-time check: picks up configuration errors of the launch just made
+// and counts the launch.
+inline int check_launch(const char* what) {
+  count_launch();
+  return check_cuda(cudaGetLastError(), what);
+}
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

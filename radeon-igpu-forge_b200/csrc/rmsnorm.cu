@@ -159,13 +159,22 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
 template <typename T>
 __global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ part, int nparts, int D,
                                          T* __restrict__ dw, int accumulate) {
-  // (dw dtype is independent of the activation dtype)
-  int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d >= D) return;
+  // block (32 columns) x (8 row groups); each row group sums a fixed stride of
+  // partials, then the 8 group sums are added in a fixed order (deterministic)
+  __shared__ float grp[8][33];
+  const int d = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  for (int b = 0; b < nparts; ++b) s += part[(int64_t)b * D + d];
-  if (accumulate) s += to_f<T>(dw[d]);
-  dw[d] = from_f<T>(s);
+  if (d < D)
+    for (int b = threadIdx.y; b < nparts; b += 8) s += part[(int64_t)b * D + d];
+  grp[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && d < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += grp[k][threadIdx.x];
+    if (accumulate) t += to_f<T>(dw[d]);
+    dw[d] = from_f<T>(t);
+  }
 }
 
 template <typename T>
@@ -231,16 +240,16 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
 #undef FXB_RMS_BWD
   int r = fxb::check_launch("rmsnorm_bwd");
   if (r) return r;
-  const int g = (D + 255) / 256;
+  const dim3 g((D + 31) / 32), blk(32, 8);
   switch (dw_dtype) {
     case FXB_DTYPE_BF16:
-      rmsnorm_dw_reduce_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(ws, blocks, D, static_cast<__nv_bfloat16*>(dw), acc);
+      rmsnorm_dw_reduce_kernel<__nv_bfloat16><<<g, blk, 0, st>>>(ws, blocks, D, static_cast<__nv_bfloat16*>(dw), acc);
       break;
     case FXB_DTYPE_F16:
-      rmsnorm_dw_reduce_kernel<__half><<<g, 256, 0, st>>>(ws, blocks, D, static_cast<__half*>(dw), acc);
+      rmsnorm_dw_reduce_kernel<__half><<<g, blk, 0, st>>>(ws, blocks, D, static_cast<__half*>(dw), acc);
       break;
     default:
-      rmsnorm_dw_reduce_kernel<float><<<g, 256, 0, st>>>(ws, blocks, D, static_cast<float*>(dw), acc);
+      rmsnorm_dw_reduce_kernel<float><<<g, blk, 0, st>>>(ws, blocks, D, static_cast<float*>(dw), acc);
   }
   return fxb::check_launch("rmsnorm_dw_reduce");
 }

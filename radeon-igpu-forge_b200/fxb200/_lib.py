@@ -21,7 +21,7 @@ FXB_OK = 0
 DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 EPI_STORE, EPI_RESIDUAL, EPI_GELU, EPI_DGELU = 0, 1, 2, 3
-EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_ACCUM_F32 = 4, 5, 6, 7
+EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_ACCUM_F32, EPI_DSILU = 4, 5, 6, 7, 8
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -69,6 +69,7 @@ SIGNATURES = {
     "fxb_device_error": (ctypes.c_int, [ctypes.POINTER(_i32), _i32]),
     "fxb_num_sms": (ctypes.c_int, [ctypes.POINTER(_i32)]),
     "fxb_abi_struct_size": (ctypes.c_size_t, [_i32]),
+    "fxb_launch_count": (ctypes.c_uint64, []),
     "fxb_rmsnorm_fwd": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _vp]),
     "fxb_rmsnorm_bwd_workspace": (ctypes.c_size_t, [_i64, _i32]),
     "fxb_rmsnorm_bwd": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
@@ -87,6 +88,8 @@ SIGNATURES = {
     "fxb_embedding_fwd": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _vp]),
     "fxb_embedding_bwd": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i64, _vp]),
     "fxb_axpy": (ctypes.c_int, [_i32, _vp, _i32, _vp, _vp, _i32, _i64, _vp]),
+    "fxb_gather_windows": (ctypes.c_int, [_i32, _vp, _i64, _i32, _vp, _i32, _i32, _vp, _vp]),
+    "fxb_colsum": (ctypes.c_int, [_i32, _vp, _i64, _i32, _vp, _i32, _vp]),
 }
 
 _LIB = None
@@ -140,6 +143,11 @@ def dtype_code(dt):
         return DTYPE_CODE[dt]
     except KeyError:
         raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def launch_count():
+    """Kernels launched by libfxb200 so far in this process."""
+    return int(load().fxb_launch_count())
 
 
 def device_error(clear=True):

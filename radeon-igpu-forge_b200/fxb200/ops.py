@@ -10,9 +10,20 @@ import torch
 
 from . import _lib
 from ._lib import (EPI_STORE, EPI_RESIDUAL, EPI_GELU, EPI_DGELU, EPI_BIAS,  # noqa: F401
-                   EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_ACCUM_F32)
+                   EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_ACCUM_F32, EPI_DSILU)
 
 _TC_DTYPES = (torch.bfloat16, torch.float16)
+
+# Optional per-launch timing of the GEMM (bench.py's live roofline): when a
+# list is installed here, every gemm() appends (flops, start, end) with CUDA
+# events recorded on the launching stream around the C-ABI call.
+_GEMM_TIMING = None
+
+
+def set_gemm_timing(records):
+    """Install a list to collect (flops, start_event, end_event) per GEMM, or None."""
+    global _GEMM_TIMING
+    _GEMM_TIMING = records
 
 
 def _rowmajor(t, name):
@@ -57,6 +68,14 @@ def gemm(A, B, out, *, a_trans=False, b_trans=False, epilogue=EPI_STORE, alpha=1
         a.Z, a.ldz = Z.data_ptr(), _rowmajor(Z, "Z")
     if bias is not None:
         a.bias = bias.data_ptr()
+    if _GEMM_TIMING is not None:
+        st = torch.cuda.current_stream(A.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        _lib.check(_lib.load().fxb_gemm(ctypes.byref(a), _lib.stream_ptr(A.device)), "fxb_gemm")
+        e1.record(st)
+        _GEMM_TIMING.append((2.0 * M * N * K, e0, e1))
+        return out
     _lib.check(_lib.load().fxb_gemm(ctypes.byref(a), _lib.stream_ptr(A.device)), "fxb_gemm")
     return out
 

@@ -25,11 +25,12 @@ def _inv_nvalid(target, ignore_index):
     return torch.where(nv > 0, nv.reciprocal(), nv)
 
 
-def _ce_rows(logits, target, grad, loss_sum, mul, ignore_index):
-    """One launch: loss_sum += sum CE(rows); grad (may alias logits) written."""
+def _ce_rows(logits, target, grad, row_loss, mul, ignore_index):
+    """One launch: row_loss[r] = CE of row r (0 if ignored); grad (may alias
+    logits) written. The caller sums row_loss in a fixed order."""
     N, V = logits.shape
     _lib.call("fxb_ce_fwd_grad", _lib.dtype_code(logits.dtype), _lib.ptr(logits),
-              logits.stride(0), _lib.ptr(target), _lib.ptr(grad), _lib.ptr(loss_sum),
+              logits.stride(0), _lib.ptr(target), _lib.ptr(grad), _lib.ptr(row_loss),
               _lib.ptr(mul), N, V, int(ignore_index), _lib.stream_ptr(logits.device))
 
 
@@ -55,11 +56,11 @@ class _FusedCE(torch.autograd.Function):
         N, V = logits.shape
         dev = logits.device
         inv_n = _inv_nvalid(target, ignore_index)
-        loss_sum = torch.zeros((), device=dev, dtype=torch.float32)
+        row_loss = torch.empty(N, device=dev, dtype=torch.float32)
         grad = torch.empty(N, V, device=dev, dtype=logits.dtype)
-        _ce_rows(logits, target, grad, loss_sum, inv_n, ignore_index)
+        _ce_rows(logits, target, grad, row_loss, inv_n, ignore_index)
         ctx.save_for_backward(grad)
-        return loss_sum * inv_n
+        return row_loss.sum() * inv_n
 
     @staticmethod
     def backward(ctx, g):
@@ -113,7 +114,7 @@ class _LinearCE(torch.autograd.Function):
         gs_t = (grad_scale if torch.is_tensor(grad_scale)
                 else torch.tensor(float(grad_scale), device=dev, dtype=torch.float32))
         mul = inv_n * gs_t.float()
-        loss_sum = torch.zeros((), device=dev, dtype=torch.float32)
+        row_loss = torch.empty(N, device=dev, dtype=torch.float32)
         dx = torch.empty(N, D, device=dev, dtype=x.dtype)
         dW = torch.zeros(V, D, device=dev, dtype=torch.float32)
         dl_buf = torch.empty(min(chunk_rows, N), V, device=dev, dtype=x.dtype)
@@ -122,13 +123,13 @@ class _LinearCE(torch.autograd.Function):
             xc = x[r0:r1]
             dl = dl_buf[:r1 - r0]
             ops.gemm(xc, weight, dl)                          # logits chunk
-            _ce_rows(dl, target[r0:r1], dl, loss_sum, mul, ignore_index)  # in place
+            _ce_rows(dl, target[r0:r1], dl, row_loss[r0:r1], mul, ignore_index)  # in place
             ops.gemm(dl, weight, dx[r0:r1], b_trans=True)     # dx chunk
             ops.linear_dw_into(dl, xc, dW)                    # dW += dl^T x (fp32)
         ctx.save_for_backward(dx, dW)
         ctx.grad_scale = grad_scale
         ctx.weight = weight
-        return loss_sum * inv_n
+        return row_loss.sum() * inv_n
 
     @staticmethod
     def backward(ctx, g):
@@ -158,14 +159,14 @@ def _linear_ce_loss_only(x, weight, target, ignore_index, chunk_rows):
     if chunk_rows is None:
         chunk_rows = _auto_chunk(N, D, V)
     inv_n = _inv_nvalid(target, ignore_index)
-    loss_sum = torch.zeros((), device=dev, dtype=torch.float32)
+    row_loss = torch.empty(N, device=dev, dtype=torch.float32)
     buf = torch.empty(min(chunk_rows, N), V, device=dev, dtype=x.dtype)
     for r0 in range(0, N, chunk_rows):
         r1 = min(r0 + chunk_rows, N)
         lg = buf[:r1 - r0]
         ops.gemm(x[r0:r1], weight, lg)
-        _ce_rows(lg, target[r0:r1], None, loss_sum, inv_n, ignore_index)
-    return loss_sum * inv_n
+        _ce_rows(lg, target[r0:r1], None, row_loss[r0:r1], inv_n, ignore_index)
+    return row_loss.sum() * inv_n
 
 
 def linear_cross_entropy(x, weight, target, grad_scale=1.0, ignore_index=-100,

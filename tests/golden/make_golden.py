@@ -50,7 +50,7 @@ def bf16r(t):
 
 
 def np32(t):
-    return t.detach().float().cpu().numpy()
+    return t.detach().float().cpu().numpy().copy()
 
 
 def zipf(V, B, T, seed, s=1.1):
@@ -201,31 +201,39 @@ def make_gpt_tiny(ref_model):
     print("gpt_tiny.npz: loss", loss.item())
 
 
-def make_curve_tiny(ref_model, steps):
-    """200-step loss curve of config 1 with the selftest's FlatAdamW oracle
-    (torch AdamW, wd on ndim >= 2, clip 1.0, selftest.py:228-250), lr 3e-4."""
+def _curve(ref_model, steps, batch_seed):
+    """Loss per step of config 1 with the selftest's FlatAdamW oracle (torch
+    AdamW, wd on ndim >= 2, clip 1.0, selftest.py:228-250), lr 3e-4.
+    batch_seed(s) -> Zipf seed of step s's batch."""
     cfg = _cfg_tiny()
     torch.manual_seed(0)
     m = _ref_gpt(ref_model, cfg, 1e-5)
     opt = torch.optim.AdamW([{"params": [p for p in m.parameters() if p.dim() >= 2], "weight_decay": 0.1},
                              {"params": [p for p in m.parameters() if p.dim() < 2], "weight_decay": 0.0}],
                             lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
-    x, y = zipf(256, 32, 256, seed=0)
     losses = []
     t0 = time.time()
     for s in range(steps):
+        x, y = zipf(256, 32, 256, seed=batch_seed(s))
         opt.zero_grad(set_to_none=True)
         loss = m(x, y)
         loss.backward()
         torch.nn.utils.clip_grad_norm_(list(m.parameters()), 1.0)
         opt.step()
-        losses.append(float(loss))
-        if s % 20 == 0:
+        losses.append(float(loss.detach()))
+        if s % 40 == 0:
             print(f"  curve step {s} loss {losses[-1]:.4f} ({time.time() - t0:.0f}s)", flush=True)
+    return losses
+
+
+def make_curve_tiny(ref_model, steps):
+    fixed = _curve(ref_model, steps, lambda s: 0)
+    stream = _curve(ref_model, steps, lambda s: 1000 + s)
     with open(os.path.join(HERE, "curve_tiny.json"), "w") as f:
-        json.dump({"config": "V256 L4 D256 H4 eps1e-5, B32 T256, zipf seed 0, init seed 0, "
-                             "AdamW lr3e-4 b(0.9,0.95) wd0.1 clip1.0, same batch every step",
-                   "losses": losses}, f)
+        json.dump({"config": "V256 L4 D256 H4 eps1e-5, B32 T256, init seed 0, AdamW lr3e-4 "
+                             "b(0.9,0.95) wd0.1 clip1.0",
+                   "losses": fixed, "fixed_batch": "zipf seed 0 every step",
+                   "losses_stream": stream, "stream": "step s uses zipf seed 1000+s"}, f)
 
 
 def make_d768(ref_model):

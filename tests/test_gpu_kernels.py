@@ -92,6 +92,13 @@ def test_fused_ce(dev, dtype, N, V):
 
 
 # ------------------------------------------------------------------ GEMM
+@pytest.fixture(params=["1sm", "2sm"])
+def gemm_mode(request, monkeypatch):
+    """Run each GEMM case through the 1-SM and the 2-SM (cta_group::2) kernel."""
+    monkeypatch.setenv("FXB_GEMM_FORCE", request.param)
+    return request.param
+
+
 def _gemm_ref(A, B, a_trans, b_trans):
     Af = A.float().t() if a_trans else A.float()
     Bf = B.float().t() if b_trans else B.float()
@@ -102,7 +109,7 @@ def _gemm_ref(A, B, a_trans, b_trans):
 @pytest.mark.parametrize("a_trans,b_trans", [(False, False), (False, True), (True, True), (True, False)])
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 512, 256), (200, 136, 72),
                                    (1000, 768, 768), (8192, 2304, 768), (64, 3072, 8192)])
-def test_gemm_store(dev, dtype, a_trans, b_trans, M, N, K):
+def test_gemm_store(dev, gemm_mode, dtype, a_trans, b_trans, M, N, K):
     from fxb200 import ops
     torch.manual_seed(M + N + K)
     A = (torch.randn(K, M, device=dev) if a_trans else torch.randn(M, K, device=dev)).to(dtype)
@@ -116,7 +123,7 @@ def test_gemm_store(dev, dtype, a_trans, b_trans, M, N, K):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("M,N,K", [(300, 264, 136), (4096, 3072, 768)])
-def test_gemm_epilogues(dev, dtype, M, N, K):
+def test_gemm_epilogues(dev, gemm_mode, dtype, M, N, K):
     from fxb200 import ops
     torch.manual_seed(7)
     A = (torch.randn(M, K, device=dev) / math.sqrt(K)).to(dtype)
@@ -152,7 +159,7 @@ def test_gemm_epilogues(dev, dtype, M, N, K):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("Mtok,N,K", [(8192, 768, 768), (8192, 3072, 768), (1000, 264, 72)])
-def test_gemm_dw_accum(dev, dtype, Mtok, N, K):
+def test_gemm_dw_accum(dev, gemm_mode, dtype, Mtok, N, K):
     """dW (fp32) += dy^T x via split-K red.add, accumulating twice."""
     from fxb200 import ops
     torch.manual_seed(11)
