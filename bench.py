@@ -247,8 +247,11 @@ def run_micro(args):
             R = torch.randn(M, N, device=dev).to(bf) if epi == ops.EPI_RESIDUAL else None
             ms = _time_ms(lambda: ops.gemm(A, B, C, epilogue=epi, Z=Z, R=R), it)
             tf = 2.0 * M * N * K / ms / 1e9
+            # same plain product through cuBLAS (sanity reference only)
+            ms_cb = _time_ms(lambda: torch.matmul(A, B.t(), out=C), it)
             out.append({"kernel": "gemm_tc", "case": f"{nm} M{M} N{N} K{K}", "ms": ms, "tflops": tf,
-                        "frac_of_measured_burst": tf / tc})
+                        "frac_of_measured_burst": tf / tc,
+                        "cublas_plain_tflops": 2.0 * M * N * K / ms_cb / 1e9})
         for (Mt, N, K, nm) in ([] if "gemm_fc" in which else
                                [(8192, 3072, 768, "dW fc"), (8192, 768, 768, "dW proj")]):
             dy = torch.randn(Mt, N, device=dev).to(bf)
@@ -258,6 +261,54 @@ def run_micro(args):
             tf = 2.0 * Mt * N * K / ms / 1e9
             out.append({"kernel": "gemm_tc (split-K, fp32 red.add)", "case": f"{nm} tokens{Mt} N{N} K{K}",
                         "ms": ms, "tflops": tf, "frac_of_measured_burst": tf / tc})
+    if "gemm_layer" in which or "all" in which:
+        # the 12 GEMMs of one config-4 transformer layer (M tokens = 8192), each
+        # with the planner's tile choice and a plain cuBLAS reference
+        T_, D, F_ = 8192, 768, 3072
+        shapes = [  # name, M, N, K, a_trans, b_trans, epilogue
+            ("fwd qkv", T_, 3 * D, D, False, False, ops.EPI_STORE),
+            ("fwd proj+res", T_, D, D, False, False, ops.EPI_RESIDUAL),
+            ("fwd fc+gelu", T_, F_, D, False, False, ops.EPI_GELU),
+            ("fwd fc2+res", T_, D, F_, False, False, ops.EPI_RESIDUAL),
+            ("bwd dz=dout.W2 (dgelu)", T_, F_, D, False, True, ops.EPI_DGELU),
+            ("bwd dh=dz.W1", T_, D, F_, False, True, ops.EPI_STORE),
+            ("bwd dy=dx.Wproj", T_, D, D, False, True, ops.EPI_STORE),
+            ("bwd dh=dqkv.Wqkv", T_, D, 3 * D, False, True, ops.EPI_STORE),
+            ("bwd dW2", D, F_, T_, True, True, ops.EPI_ACCUM_F32),
+            ("bwd dW1", F_, D, T_, True, True, ops.EPI_ACCUM_F32),
+            ("bwd dWproj", D, D, T_, True, True, ops.EPI_ACCUM_F32),
+            ("bwd dWqkv", 3 * D, D, T_, True, True, ops.EPI_ACCUM_F32),
+        ]
+        tot_f, tot_ms = 0.0, 0.0
+        for nm, M, N, K, at, bt, epi in shapes:
+            A = (torch.randn(K, M, device=dev) if at else torch.randn(M, K, device=dev)).to(bf)
+            B = ((torch.randn(K, N, device=dev) if bt else torch.randn(N, K, device=dev)) / math.sqrt(K)).to(bf)
+            acc = epi == ops.EPI_ACCUM_F32
+            C = torch.zeros(M, N, device=dev, dtype=torch.float32 if acc else bf)
+            R = torch.randn(M, N, device=dev).to(bf) if epi in (ops.EPI_RESIDUAL, ops.EPI_DGELU) else None
+            Z = torch.empty(M, N, device=dev, dtype=bf) if epi == ops.EPI_GELU else None
+            ms = _time_ms(lambda: ops.gemm(A, B, C, a_trans=at, b_trans=bt, epilogue=epi, R=R, Z=Z), it)
+            Ar = A.t() if at else A
+            Br = B if bt else B.t()
+            Cc = torch.empty(M, N, device=dev, dtype=bf)
+            ms_cb = _time_ms(lambda: torch.matmul(Ar, Br, out=Cc), it)
+            fl = 2.0 * M * N * K
+            tot_f += fl
+            tot_ms += ms
+            pair, bn, sp = _lib.gemm_plan(M, N, K, epi)
+            out.append({"kernel": "gemm_tc" + ("2" if pair else ""), "case": f"layer {nm} M{M} N{N} K{K}",
+                        "tile": f"{'256' if pair else '128'}x{bn} splitK{sp}", "ms": ms,
+                        "tflops": fl / ms / 1e9, "cublas_plain_tflops": fl / ms_cb / 1e9})
+        out.append({"kernel": "gemm_tc (one layer, 12 GEMMs)", "ms": tot_ms, "tflops": tot_f / tot_ms / 1e9,
+                    "frac_of_measured_burst": tot_f / tot_ms / 1e9 / tc})
+    if "gemm_big" in which:
+        M, N, K = 16384, 16384, 768
+        A = torch.randn(M, K, device=dev).to(bf)
+        B = (torch.randn(N, K, device=dev) / math.sqrt(K)).to(bf)
+        C = torch.empty(M, N, device=dev, dtype=bf)
+        ms = _time_ms(lambda: ops.gemm(A, B, C), it)
+        out.append({"kernel": "gemm_tc", "case": f"big M{M} N{N} K{K}", "ms": ms,
+                    "tflops": 2.0 * M * N * K / ms / 1e9})
     if "attn" in which or "all" in which:
         a = attn_tflops(dev, iters=it)
         a.update({"kernel": "attn_fwd + attn_bwd", "case": "BASELINE config 2",
@@ -283,7 +334,7 @@ def run_micro(args):
         dw = torch.zeros(D, device=dev)
         ws = torch.empty(_lib.load().fxb_rmsnorm_bwd_workspace(Nr, D) // 4 + 1, device=dev)
         fb = lambda: _lib.call("fxb_rmsnorm_bwd", 2, _lib.ptr(x), _lib.ptr(w), _lib.ptr(rstd), _lib.ptr(dy),  # noqa: E731
-                               _lib.ptr(dx), _lib.ptr(dw), 0, 0, _lib.ptr(ws), Nr, D, st)
+                               None, _lib.ptr(dx), _lib.ptr(dw), 0, 0, _lib.ptr(ws), Nr, D, st)
         ms = _time_ms(fb, it)
         byt = 3 * Nr * D * 2 + Nr * 4
         out.append({"kernel": "rmsnorm_bwd", "case": f"config 3 [{Nr},{D}] bf16", "ms": ms,

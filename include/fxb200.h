@@ -72,7 +72,9 @@ int fxb_rmsnorm_fwd(int32_t dtype, const void* x, const void* w, void* y, float*
 /* Bytes of fp32 workspace fxb_rmsnorm_bwd needs for the dw partial sums. */
 size_t fxb_rmsnorm_bwd_workspace(int64_t rows, int32_t D);
 
-/* dx = rstd*w*dy - x*rstd^3*sum(x*w*dy)/D ; dw = sum_rows x*rstd*dy.
+/* dx = rstd*w*dy - x*rstd^3*sum(x*w*dy)/D (+ dres when dres != NULL: the
+ * gradient reaching x through a residual connection, summed in the same pass);
+ * dw = sum_rows x*rstd*dy.
  * dw (dtype dw_dtype, e.g. an fp32 flat-gradient slot) is written
  * (dw_accumulate == 0) or added to (dw_accumulate != 0). D <= 2048 for 16-bit
  * dtypes (1024 for fp32). Deterministic: per-block partials, then a
@@ -80,7 +82,7 @@ size_t fxb_rmsnorm_bwd_workspace(int64_t rows, int32_t D);
  * Replaces rms_norm_bwd_dx + rms_norm_bwd_dw + part.sum(0)
  * (ml/fxlm/kernels/norm.hip:64,102; ml/fxlm/norm.py:62-84). */
 int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rstd,
-                    const void* dy, void* dx, void* dw, int32_t dw_dtype,
+                    const void* dy, const void* dres, void* dx, void* dw, int32_t dw_dtype,
                     int32_t dw_accumulate, float* workspace, int64_t rows, int32_t D,
                     void* stream);
 
@@ -175,6 +177,13 @@ typedef struct fxb_gemm_args {
  * (ml/fxlm/cross_entropy.py:131-135,180) and the fxgpu dW mm
  * (ml/fxgpu/fused_linear.py:94). */
 int fxb_gemm(const fxb_gemm_args* args, void* stream);
+
+/* The tile configuration fxb_gemm would use for this problem on the current
+ * device: *pair = 1 for the CTA-pair (cta_group::2, 256-row) kernel, 0 for the
+ * single-CTA (128-row) kernel; *bn = tile width; *splits = split-K factor
+ * (> 1 only for FXB_EPI_ACCUM_F32). Diagnostic; no reference counterpart. */
+int fxb_gemm_plan(int32_t M, int32_t N, int32_t K, int32_t epilogue, int32_t* pair,
+                  int32_t* bn, int32_t* splits);
 
 /* ------------------------------------------------------------------ attention */
 

@@ -95,7 +95,7 @@ constexpr int kMaxSeg = 1024;
 
 template <typename G, typename P>
 __global__ void __launch_bounds__(256)
-adamw_update_kernel(const G* g, float* __restrict__ master, float* __restrict__ m,
+adamw_update_kernel(G* __restrict__ g, float* __restrict__ master, float* __restrict__ m,
                     float* __restrict__ v, P* __restrict__ p, int64_t n,
                     const int64_t* __restrict__ seg_end, const int* __restrict__ seg_wd, int nseg,
                     const float* __restrict__ scratch, const float* __restrict__ found_inf,
@@ -107,7 +107,7 @@ adamw_update_kernel(const G* g, float* __restrict__ master, float* __restrict__ 
     // step skipped: master / m / v untouched, the gradient is still consumed
     for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < ngroups; gi += stride) {
       const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      store8<G>(const_cast<G*>(g) + gi * 8, z);
+      store8<G>(g + gi * 8, z);
     }
     return;
   }
@@ -122,40 +122,53 @@ adamw_update_kernel(const G* g, float* __restrict__ master, float* __restrict__ 
   const int step = *step_p;
   const float bc1 = 1.f - powf(b1, (float)step);
   const float bc2 = 1.f - powf(b2, (float)step);
+  const float inv_bc1 = 1.f / bc1, inv_bc2 = 1.f / bc2;
   const float b1c = 1.f - b1, b2c = 1.f - b2;
   const float lrwd = lr * wd;
   const float zero8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < ngroups; gi += stride) {
-    const int64_t e0 = gi * 8;
-    // segment containing e0: first index with s_end > e0
-    int lo = 0, hi = nseg - 1;
-    while (lo < hi) {
-      int mid = (lo + hi) >> 1;
-      if (s_end[mid] > e0) hi = mid; else lo = mid + 1;
-    }
-    const bool wd_on = s_wd[lo] != 0;
+  // Each thread walks its 8-element groups in increasing order, so the
+  // segment cursor only moves forward. Two groups per iteration keep more
+  // loads in flight.
+  int seg = 0;
+  auto update8 = [&](int64_t e0, bool wd_on) {
     float gv[8], mw[8], mv[8], vv[8];
     load8<G>(g + e0, gv);
-    store8<G>(const_cast<G*>(g) + e0, zero8);  // gradient consumed
     load8<float>(master + e0, mw);
     load8<float>(m + e0, mv);
     load8<float>(v + e0, vv);
+    store8<G>(g + e0, zero8);  // gradient consumed
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float gg = gv[j] * inv;
+      const float gg = gv[j] * inv;
       float w = mw[j];
       if (wd_on) w -= lrwd * w;
-      float a = mv[j] * b1 + b1c * gg;
-      float b = vv[j] * b2 + b2c * gg * gg;
+      const float a = mv[j] * b1 + b1c * gg;
+      const float b = vv[j] * b2 + b2c * gg * gg;
       mv[j] = a;
       vv[j] = b;
-      w -= lr * (a / bc1) / (sqrtf(b / bc2) + eps);
+      w -= lr * (a * inv_bc1) / (sqrtf(b * inv_bc2) + eps);
       mw[j] = w;
     }
     store8<float>(master + e0, mw);
     store8<float>(m + e0, mv);
     store8<float>(v + e0, vv);
     store8<P>(p + e0, mw);
+  };
+  for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < ngroups; gi += 2 * stride) {
+    const int64_t e0 = gi * 8;
+    while (seg < nseg - 1 && s_end[seg] <= e0) ++seg;
+    const bool wd0 = s_wd[seg] != 0;
+    const int64_t gi1 = gi + stride;
+    if (gi1 < ngroups) {
+      const int64_t e1 = gi1 * 8;
+      int seg1 = seg;
+      while (seg1 < nseg - 1 && s_end[seg1] <= e1) ++seg1;
+      update8(e0, wd0);
+      update8(e1, s_wd[seg1] != 0);
+      seg = seg1;
+    } else {
+      update8(e0, wd0);
+    }
   }
 }
 
@@ -169,7 +182,7 @@ int launch_update(const void* g, float* master, float* m, float* v, void* p, int
   int64_t cap = (int64_t)fxb::num_sms() * 8;
   int blocks = (int)(want < cap ? want : cap);
   if (blocks < 1) blocks = 1;
-  adamw_update_kernel<G, P><<<blocks, 256, 0, st>>>(static_cast<const G*>(g), master, m, v,
+  adamw_update_kernel<G, P><<<blocks, 256, 0, st>>>(static_cast<G*>(const_cast<void*>(g)), master, m, v,
                                                     static_cast<P*>(p), n, se, sw, nseg, scratch,
                                                     fi, sc, stp, lr, b1, b2, eps, wd);
   return fxb::check_launch("adamw_update");

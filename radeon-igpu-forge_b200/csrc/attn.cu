@@ -9,12 +9,16 @@
 //                      dV = P^T dO, dK = dS^T Q, dQ = dS K.
 // B200 design (new): 128x128 tiles; TMA (4-D maps over the strided (B,T,H,D)
 // views, no copies, no multicast) feeds shared memory; one thread issues
-// tcgen05.mma into tensor memory; softmax warps own one row each and read
-// scores with tcgen05.ld. Forward keeps O in registers and receives each P.V
-// product from TMEM (online-softmax rescale in registers). Backward works per
-// key tile: S^T and dP^T land in TMEM, dV and dK accumulate in TMEM across
-// query tiles, and each dQ partial is reduced into an fp32 workspace with
-// vector red.add. Every wait is bounded (FXB_DERR_ATTN_WAIT).
+// tcgen05.mma into tensor memory; eight softmax warps read scores with
+// tcgen05.ld, two warps per TMEM lane quarter, each owning half of a tile's
+// columns (forward: row maxima exchanged through shared memory once per tile,
+// row sums combined at the end). Forward keeps O in registers and receives
+// each P.V product from TMEM (online-softmax rescale in registers). Backward
+// works per key tile: S^T and dP^T land in TMEM, dV and dK accumulate in TMEM
+// across query tiles, and each dQ partial is reduced into an fp32 workspace
+// with vector red.add. Every wait is bounded (FXB_DERR_ATTN_WAIT); after an
+// expired wait a thread keeps stepping through its loop without work so that
+// named barriers are always met by every participant.
 #include "common.cuh"
 #include "internal.h"
 
@@ -23,7 +27,7 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int TILE = 128;
-constexpr int kThreads = 192;  // warps 0-3 softmax, 4 MMA, 5 TMA
+constexpr int kFwdThreads = 320;  // warps 0-7 softmax, 8 MMA, 9 TMA (forward and backward)
 
 struct FwdParams {
   int B, T, H, nqt, nkt, causal;
@@ -72,13 +76,23 @@ FXB_DEV uint64_t mnmajor_desc(uint32_t base, int kk) {
 }
 
 // ============================================================ forward
+FXB_DEV float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Warp roles (320 threads): warps 0-7 softmax (warp w owns TMEM lane quarter
+// w & 3, i.e. 32 query rows, and column half w >> 2 of every S tile: 64 of the
+// 128 keys, and DH/2 of the output columns), warp 8 MMA issuer, warp 9 TMA.
 template <int DH, int FMT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
   constexpr int QB = TILE * DH * 2;  // bytes of one [128][DH] tile
   constexpr int NBOX = DH / 64;
+  constexpr int OC = DH / 2;         // output columns per thread
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -87,7 +101,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t sK = sQ + QB;          // 2 stages
   const uint32_t sV = sK + 2 * QB;      // 2 stages
   const uint32_t sP = sV + 2 * QB;      // [128][128] 16-bit
-  const uint32_t bars = sP + 32768;
+  const uint32_t sX = sP + 32768;       // row-statistics exchange: [2 buf][2 half][128] fp32
+  float* xch = reinterpret_cast<float*>(gbase + (sX - base));
+  const uint32_t bars = sX + 2048;
   const uint32_t q_full = bars;
   auto k_full = [&](int s) { return bars + 8u * (1 + s); };
   auto v_full = [&](int s) { return bars + 8u * (3 + s); };
@@ -113,14 +129,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(v_full(s), 1);
       mbar_init(kv_empty(s), 1);
       mbar_init(s_full(s), 1);
-      mbar_init(s_empty(s), 128);
+      mbar_init(s_empty(s), 256);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(pv_full, 1);
     mbar_init(final_bar, 1);
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -131,7 +147,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tS = tmem;         // S buffers at columns 0 and 128
   const uint32_t tPV = tmem + 256;  // P.V product, DH columns
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -154,7 +170,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           tma_load_4d(sV + st * QB + c * 16384, &tmV, v_full(st), 64 * c, j * TILE, h, b);
         armed = j + 1;
       }
-      // drain what was issued
       mbar_wait(q_full, 0, p.err, FXB_DERR_ATTN_WAIT);
       for (int j = (armed > 2 ? armed - 2 : 0); j < armed; ++j) {
         mbar_wait(k_full(j & 1), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
@@ -162,7 +177,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
     }
     __syncwarp();
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
@@ -197,78 +212,84 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------ softmax warps: row r
-    const int r = warp * 32 + lane;
+    // ------------------------------------------------ softmax warps 0..7
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;  // query row within the tile
     const int q = q0 + r;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    float o[DH];
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int col0 = half * 64;         // this thread's key columns within a tile
+    float o[OC];
 #pragma unroll
-    for (int d = 0; d < DH; ++d) o[d] = 0.f;
+    for (int d = 0; d < OC; ++d) o[d] = 0.f;
     float m = -INFINITY, l = 0.f, a_prev = 0.f;
     bool ok = true;
+    uint8_t* pbase = gbase + (sP - base);
+    // After a failed (timed-out) wait a thread keeps stepping through the
+    // tiles without waiting or computing, so that both warps of a pair always
+    // meet at the same named barriers.
     for (int j = 0; j < n_kv; ++j) {
       const int st = j & 1;
-      if (!mbar_wait(s_full(st), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-      tc_fence_after();
-      const int kv0 = j * TILE;
-      const uint32_t sAddr = tS + st * TILE + lane_off;
-      const bool need_mask = (kv0 + TILE > p.T) || (p.causal && kv0 + TILE > q0);
-      // pass 1: row max
+      if (ok && !mbar_wait(s_full(st), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) ok = false;
+      const int kv0 = j * TILE + col0;
+      float sv[64];
       float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(sAddr + c * 32, rr);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = kv0 + c * 32 + i;
-          float y = __uint_as_float(rr[i]) * p.scale_log2;
-          if (need_mask && (col >= p.T || (p.causal && col > q))) y = -INFINITY;
-          mx = fmaxf(mx, y);
-        }
-      }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = exp2f(m - m_new);
-      // P.V of the previous tile must be folded in before P is overwritten
-      if (j > 0) {
-        if (!mbar_wait(pv_full, (j - 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      if (ok) {
         tc_fence_after();
+        uint32_t sr[64];
+        tmem_ld32(tS + st * TILE + lane_off + col0, sr);
+        tmem_ld32(tS + st * TILE + lane_off + col0 + 32, sr + 32);
+        tmem_wait_ld();
+        const bool need_mask = (kv0 + 64 > p.T) || (p.causal && kv0 + 64 > q0);
+        if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < DH / 32; ++c) {
-          uint32_t rr[32];
-          tmem_ld32(tPV + lane_off + c * 32, rr);
-          tmem_wait_ld();
+          for (int i = 0; i < 64; ++i) {
+            const int col = kv0 + i;
+            sv[i] = (col >= p.T || (p.causal && col > q)) ? -INFINITY : __uint_as_float(sr[i]);
+            mx = fmaxf(mx, sv[i]);
+          }
+        } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * a_prev + __uint_as_float(rr[i]);
+          for (int i = 0; i < 64; ++i) {
+            sv[i] = __uint_as_float(sr[i]);
+            mx = fmaxf(mx, sv[i]);
+          }
         }
       }
-      // pass 2: probabilities -> P (16-bit, swizzled) and row sum
-      float rs = 0.f;
-      uint8_t* pbase = gbase + (sP - base);
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(sAddr + c * 32, rr);
-        tmem_wait_ld();
-        float pv[32];
+      // exchange the half-row maxima with the partner warp (double-buffered by tile parity)
+      float* xb = xch + (j & 1) * 256;
+      xb[half * 128 + r] = mx;
+      named_bar_sync(1 + quarter, 64);
+      mx = fmaxf(mx, xb[(half ^ 1) * 128 + r]);
+      if (!ok) continue;
+      const float m_new = fmaxf(m, mx * p.scale_log2);
+      const float alpha = ex2_ftz(m - m_new);
+      // P.V of the previous tile is folded in before P is overwritten
+      if (j > 0) {
+        if (!mbar_wait(pv_full, (j - 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; continue; }
+        tc_fence_after();
+        uint32_t pr[OC];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = kv0 + c * 32 + i;
-          float y = __uint_as_float(rr[i]) * p.scale_log2;
-          if (need_mask && (col >= p.T || (p.causal && col > q))) y = -INFINITY;
-          pv[i] = exp2f(y - m_new);
+        for (int c = 0; c < OC / 32; ++c) tmem_ld32(tPV + lane_off + half * OC + c * 32, pr + c * 32);
+        tmem_wait_ld();
+#pragma unroll
+        for (int d = 0; d < OC; ++d) o[d] = o[d] * a_prev + __uint_as_float(pr[d]);
+      }
+      // probabilities -> P (16-bit, 128B-swizzled) and the partial row sum
+      float rs = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float pv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          pv[i] = ex2_ftz(fmaf(sv[8 * u + i], p.scale_log2, -m_new));
           rs += pv[i];
         }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          uint4 w;
-          w.x = pack2<T16>(pv[8 * u + 0], pv[8 * u + 1]);
-          w.y = pack2<T16>(pv[8 * u + 2], pv[8 * u + 3]);
-          w.z = pack2<T16>(pv[8 * u + 4], pv[8 * u + 5]);
-          w.w = pack2<T16>(pv[8 * u + 6], pv[8 * u + 7]);
-          *reinterpret_cast<uint4*>(pbase + sw128_offset(r, c * 4 + u)) = w;
-        }
+        uint4 w;
+        w.x = pack2<T16>(pv[0], pv[1]);
+        w.y = pack2<T16>(pv[2], pv[3]);
+        w.z = pack2<T16>(pv[4], pv[5]);
+        w.w = pack2<T16>(pv[6], pv[7]);
+        *reinterpret_cast<uint4*>(pbase + sw128_offset(r, half * 8 + u)) = w;
       }
       tc_fence_before();
       mbar_arrive(s_empty(st));
@@ -278,34 +299,38 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       m = m_new;
       a_prev = alpha;
     }
-    if (ok && mbar_wait(pv_full, (n_kv - 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) {
+    const bool done = ok && mbar_wait(pv_full, (n_kv - 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+    if (done) {
       tc_fence_after();
+      uint32_t pr[OC];
 #pragma unroll
-      for (int c = 0; c < DH / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(tPV + lane_off + c * 32, rr);
-        tmem_wait_ld();
+      for (int c = 0; c < OC / 32; ++c) tmem_ld32(tPV + lane_off + half * OC + c * 32, pr + c * 32);
+      tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * a_prev + __uint_as_float(rr[i]);
+      for (int d = 0; d < OC; ++d) o[d] = o[d] * a_prev + __uint_as_float(pr[d]);
+    }
+    // combine the two half-row sums (every softmax thread reaches this barrier)
+    float* xs = xch + 512;
+    xs[half * 128 + r] = l;
+    named_bar_sync(1 + quarter, 64);
+    l += xs[(half ^ 1) * 128 + r];
+    if (done && q < p.T) {
+      const float inv = 1.f / l;
+      T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh + half * OC;
+#pragma unroll
+      for (int d = 0; d < OC; d += 8) {
+        float f[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = o[d + i] * inv;
+        *reinterpret_cast<uint4*>(orow + d) = pack8<T16>(f);
       }
-      if (q < p.T) {
-        const float inv = 1.f / l;
-        T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh;
-#pragma unroll
-        for (int d = 0; d < DH; d += 8) {
-          float f[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = o[d + i] * inv;
-          *reinterpret_cast<uint4*>(orow + d) = pack8<T16>(f);
-        }
-        p.lse[(int64_t)bh * p.T + q] = (m + log2f(l)) * kLn2;
-      }
+      if (half == 0) p.lse[(int64_t)bh * p.T + q] = (m + log2f(l)) * kLn2;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -373,7 +398,7 @@ FXB_DEV void red_add_v4f(float* addr, float a, float b, float c, float d) {
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                 const BwdParams p) {
@@ -420,14 +445,14 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(qdo_empty(s), 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 128);
-    mbar_init(ds_full, 128);
+    mbar_init(s_empty, 256);
+    mbar_init(ds_full, 256);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 128);
+    mbar_init(dq_empty, 256);
     mbar_init(acc_full, 1);
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -437,7 +462,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tmem = *tmem_slot;
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK);
@@ -460,7 +485,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         mbar_wait(qdo_full(it & 1), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
     }
     __syncwarp();
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t I_SS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);  // S^T, dP^T
@@ -501,107 +526,110 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------ softmax / dS warps
-    const int r = warp * 32 + lane;  // kv row for S^T/dP^T, q row for dQ
+    // ------------------------------------------------ softmax / dS warps 0..7
+    // warp w: TMEM lane quarter w & 3 (32 key rows for S^T / dP^T, 32 query
+    // rows for the dQ partial), column half w >> 2 (64 of the 128 queries of
+    // S^T / dP^T, 32 of the 64 head dims of dQ / dK / dV)
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
     const int kv = kv0 + r;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int qc0 = half * 64;
     uint8_t* pt = gbase + (sPT - base);
     uint8_t* ds = gbase + (sDS - base);
     bool ok = true;
+    // After a failed (timed-out) wait a thread keeps stepping through the
+    // iterations without waiting or computing, so that all 256 threads always
+    // meet at the same named barriers.
     for (int it = 0; it < n_it; ++it) {
       const int q0 = (i0 + it) * TILE;
       const int sb = it & 1;
-      {
-        const int q = q0 + r;
+      if (threadIdx.x < 128) {
+        const int q = q0 + (int)threadIdx.x;
         const bool v = q < p.T;
-        lse_s[sb * 128 + r] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
-        del_s[sb * 128 + r] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
+        lse_s[sb * 128 + threadIdx.x] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
+        del_s[sb * 128 + threadIdx.x] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
       }
-      named_bar_sync(1, 128);
-      if (!mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      named_bar_sync(1, 256);
+      if (!ok) continue;
+      if (!mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; continue; }
       tc_fence_after();
       const bool diag = p.causal && (q0 < kv0 + TILE);
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tST + lane_off + c * 32, sr);
-        tmem_ld32(tDPT + lane_off + c * 32, dr);
-        tmem_wait_ld();
-        float pv[32], dsv[32];
+      uint32_t sr[64], dr[64];
+      tmem_ld32(tST + lane_off + qc0, sr);
+      tmem_ld32(tST + lane_off + qc0 + 32, sr + 32);
+      tmem_ld32(tDPT + lane_off + qc0, dr);
+      tmem_ld32(tDPT + lane_off + qc0 + 32, dr + 32);
+      tmem_wait_ld();
+      const float* ls = lse_s + sb * 128 + qc0;
+      const float* dl = del_s + sb * 128 + qc0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qc = c * 32 + i;
-          const int q = q0 + qc;
-          float pp = exp2f(__uint_as_float(sr[i]) * p.scale_log2 - lse_s[sb * 128 + qc]);
-          if (kv >= p.T || (diag && q < kv)) pp = 0.f;
+      for (int u = 0; u < 8; ++u) {
+        float pv[8], dsv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int qc = 8 * u + i;
+          float pp = ex2_ftz(fmaf(__uint_as_float(sr[qc]), p.scale_log2, -ls[qc]));
+          if (kv >= p.T || (diag && q0 + qc0 + qc < kv)) pp = 0.f;
           pv[i] = pp;
-          dsv[i] = pp * (__uint_as_float(dr[i]) - del_s[sb * 128 + qc]);
+          dsv[i] = pp * (__uint_as_float(dr[qc]) - dl[qc]);
         }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          uint4 w, x;
-          w.x = pack2<T16>(pv[8 * u + 0], pv[8 * u + 1]);
-          w.y = pack2<T16>(pv[8 * u + 2], pv[8 * u + 3]);
-          w.z = pack2<T16>(pv[8 * u + 4], pv[8 * u + 5]);
-          w.w = pack2<T16>(pv[8 * u + 6], pv[8 * u + 7]);
-          x.x = pack2<T16>(dsv[8 * u + 0], dsv[8 * u + 1]);
-          x.y = pack2<T16>(dsv[8 * u + 2], dsv[8 * u + 3]);
-          x.z = pack2<T16>(dsv[8 * u + 4], dsv[8 * u + 5]);
-          x.w = pack2<T16>(dsv[8 * u + 6], dsv[8 * u + 7]);
-          // P^T / dS^T smem is free: the previous iteration's dQ commit was waited below
-          *reinterpret_cast<uint4*>(pt + sw128_offset(r, c * 4 + u)) = w;
-          *reinterpret_cast<uint4*>(ds + sw128_offset(r, c * 4 + u)) = x;
-        }
+        uint4 w, x;
+        w.x = pack2<T16>(pv[0], pv[1]);
+        w.y = pack2<T16>(pv[2], pv[3]);
+        w.z = pack2<T16>(pv[4], pv[5]);
+        w.w = pack2<T16>(pv[6], pv[7]);
+        x.x = pack2<T16>(dsv[0], dsv[1]);
+        x.y = pack2<T16>(dsv[2], dsv[3]);
+        x.z = pack2<T16>(dsv[4], dsv[5]);
+        x.w = pack2<T16>(dsv[6], dsv[7]);
+        // P^T / dS^T smem is free: the previous iteration's dQ commit was waited below
+        *reinterpret_cast<uint4*>(pt + sw128_offset(r, half * 8 + u)) = w;
+        *reinterpret_cast<uint4*>(ds + sw128_offset(r, half * 8 + u)) = x;
       }
       tc_fence_before();
       mbar_arrive(s_empty);
       fence_proxy_async_smem();
       mbar_arrive(ds_full);
-      // dQ partial of this query tile: row r is query q0 + r
-      if (!mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      // dQ partial of this query tile: row r is query q0 + r, head dims half*32..+32
+      if (!mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; continue; }
       tc_fence_after();
       {
         const int q = q0 + r;
-        float* dst = p.dq_acc + ((int64_t)bh * p.T + q) * DH;
+        uint32_t rr[32];
+        tmem_ld32(tDQ + lane_off + half * 32, rr);
+        tmem_wait_ld();
+        if (q < p.T) {
+          float* dst = p.dq_acc + ((int64_t)bh * p.T + q) * DH + half * 32;
 #pragma unroll
-        for (int c = 0; c < DH / 32; ++c) {
-          uint32_t rr[32];
-          tmem_ld32(tDQ + lane_off + c * 32, rr);
-          tmem_wait_ld();
-          if (q < p.T) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              red_add_v4f(dst + c * 32 + 4 * u, __uint_as_float(rr[4 * u]), __uint_as_float(rr[4 * u + 1]),
-                          __uint_as_float(rr[4 * u + 2]), __uint_as_float(rr[4 * u + 3]));
-          }
+          for (int u = 0; u < 8; ++u)
+            red_add_v4f(dst + 4 * u, __uint_as_float(rr[4 * u]), __uint_as_float(rr[4 * u + 1]),
+                        __uint_as_float(rr[4 * u + 2]), __uint_as_float(rr[4 * u + 3]));
         }
       }
       tc_fence_before();
       mbar_arrive(dq_empty);
     }
-    // final dK (scaled) and dV for key row kv
+    // final dK (scaled) and dV for key row kv, head dims half*32..+32
     if (ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT)) {
       tc_fence_after();
+      uint32_t rk[32], rv[32];
+      tmem_ld32(tDK + lane_off + half * 32, rk);
+      tmem_ld32(tDV + lane_off + half * 32, rv);
+      tmem_wait_ld();
+      if (kv < p.T) {
+        T16* krow = static_cast<T16*>(p.dk) + b * p.dk_sb + (int64_t)kv * p.dk_st + h * p.dk_sh + half * 32;
+        T16* vrow = static_cast<T16*>(p.dv) + b * p.dv_sb + (int64_t)kv * p.dv_st + h * p.dv_sh + half * 32;
 #pragma unroll
-      for (int c = 0; c < DH / 32; ++c) {
-        uint32_t rk[32], rv[32];
-        tmem_ld32(tDK + lane_off + c * 32, rk);
-        tmem_ld32(tDV + lane_off + c * 32, rv);
-        tmem_wait_ld();
-        if (kv < p.T) {
-          T16* krow = static_cast<T16*>(p.dk) + b * p.dk_sb + (int64_t)kv * p.dk_st + h * p.dk_sh + c * 32;
-          T16* vrow = static_cast<T16*>(p.dv) + b * p.dv_sb + (int64_t)kv * p.dv_st + h * p.dv_sh + c * 32;
+        for (int u = 0; u < 4; ++u) {
+          float fk[8], fv[8];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float fk[8], fv[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              fk[i] = __uint_as_float(rk[8 * u + i]) * p.scale;
-              fv[i] = __uint_as_float(rv[8 * u + i]);
-            }
-            *reinterpret_cast<uint4*>(krow + 8 * u) = pack8<T16>(fk);
-            *reinterpret_cast<uint4*>(vrow + 8 * u) = pack8<T16>(fv);
+          for (int i = 0; i < 8; ++i) {
+            fk[i] = __uint_as_float(rk[8 * u + i]) * p.scale;
+            fv[i] = __uint_as_float(rv[8 * u + i]);
           }
+          *reinterpret_cast<uint4*>(krow + 8 * u) = pack8<T16>(fk);
+          *reinterpret_cast<uint4*>(vrow + 8 * u) = pack8<T16>(fv);
         }
       }
     }
@@ -609,7 +637,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -621,8 +649,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 // 228 KB so a second CTA of any TMEM-using kernel can never be co-scheduled.
 constexpr int kOneCtaPerSm = 120 * 1024;
 template <int DH> constexpr int fwd_smem() {
-  return (5 * TILE * DH * 2 + 32768 + 1024 + 256) > kOneCtaPerSm
-             ? (5 * TILE * DH * 2 + 32768 + 1024 + 256)
+  return (5 * TILE * DH * 2 + 32768 + 2048 + 1024 + 256) > kOneCtaPerSm
+             ? (5 * TILE * DH * 2 + 32768 + 2048 + 1024 + 256)
              : kOneCtaPerSm;
 }
 constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 2 * 32768 + 2048 + 1024 + 256; }
@@ -704,7 +732,7 @@ int launch_fwd(const fxb_attn_args* a, cudaStream_t st) {
     once[dev & 63] = true;
   }
   dim3 grid(p.nqt, a->B * a->H);
-  k<<<grid, kThreads, fwd_smem<DH>(), st>>>(mq, mk, mv, p);
+  k<<<grid, kFwdThreads, fwd_smem<DH>(), st>>>(mq, mk, mv, p);
   return fxb::check_launch("attn_fwd");
 }
 
@@ -748,7 +776,7 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
     once[dev & 63] = true;
   }
   dim3 grid(p.nkt, a->B * a->H);
-  k<<<grid, kThreads, bwd_smem(), st>>>(mq, mk, mv, mdo, p);
+  k<<<grid, kFwdThreads, bwd_smem(), st>>>(mq, mk, mv, mdo, p);
   if ((r = fxb::check_launch("attn_bwd"))) return r;
   const int64_t n = rows * (DH / 8);
   attn_bwd_post_kernel<T16, DH><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(

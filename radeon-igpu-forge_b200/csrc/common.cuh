@@ -250,10 +250,11 @@ FXB_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
 }
-// arrive on an mbarrier that may live in another CTA of the cluster
+// arrive on an mbarrier that may live in another CTA of the cluster (default
+// .release.cta semantics: orders this thread's prior shared / tensor-memory
+// accesses, without waiting for its global stores to become cluster-visible)
 FXB_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // TMA load into this CTA's smem whose completion is signalled on an mbarrier
 // of either CTA of the pair (no multicast)

@@ -119,8 +119,38 @@ FXB_DEV void red_add_v4(float* addr, float a, float b, float c, float d) {
                : "memory");
 }
 
+// epilogues that read a second (m, n) input from R
+FXB_DEV bool epi_reads_r(int epi) {
+  return epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU;
+}
+
+// Issue the loads of one 32-column chunk of R (16-bit) into registers; called
+// before the accumulator is ready so that their latency overlaps the mainloop.
+FXB_DEV void prefetch_r16(const GemmParams& p, int m, int n0, uint4* pre) {
+  const int n8 = min(4, (p.N - n0) >> 3);
+  const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.R) +
+                                                    (int64_t)m * p.ldr + n0);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) pre[q] = (q < n8) ? src[q] : make_uint4(0, 0, 0, 0);
+}
+
+// R values of one chunk: from the prefetched registers (16-bit C) or loaded now
 template <typename CT>
-FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v) {
+FXB_DEV void chunk_r(const GemmParams& p, int m, int n0, int n8, bool use_pre,
+                     const uint4 (&pre)[4], float* r) {
+  if constexpr (sizeof(CT) == 2) {
+    if (use_pre) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) unpack8<CT>(pre[q], r + 8 * q);
+      return;
+    }
+  }
+  load32_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, r, n8);
+}
+
+template <typename CT>
+FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v, bool use_pre,
+                            const uint4 (&pre)[4]) {
   const int n8 = min(4, (p.N - n0) >> 3);  // groups of 8 valid columns (N % 8 == 0)
   if (n8 <= 0) return;
   CT* crow = static_cast<CT*>(p.C) + (int64_t)m * p.ldc + n0;
@@ -133,7 +163,7 @@ FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v) {
     }
     case FXB_EPI_RESIDUAL: {
       float r[32];
-      load32_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, r, n8);
+      chunk_r<CT>(p, m, n0, n8, use_pre, pre, r);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = v[i] * p.alpha + r[i];
       store32<CT>(crow, v, n8);
@@ -171,7 +201,7 @@ FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v) {
     }
     case FXB_EPI_DGELU: {
       float z[32];
-      load32_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, z, n8);
+      chunk_r<CT>(p, m, n0, n8, use_pre, pre, z);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] *= gelu_tanh_grad(z[i]);
       store32<CT>(crow, v, n8);
@@ -179,7 +209,7 @@ FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v) {
     }
     case FXB_EPI_DSILU: {
       float z[32];
-      load32_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, z, n8);
+      chunk_r<CT>(p, m, n0, n8, use_pre, pre, z);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float s = 1.f / (1.f + __expf(-z[i]));
@@ -198,6 +228,49 @@ FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v) {
     }
   }
 }
+
+// One epilogue warp's share of an accumulator tile. The warp reads TMEM lanes
+// of its quarter (row m for this lane) and the columns [half*BN/2, (half+1)*BN/2)
+// of the tile, i.e. NCH = BN/64 chunks of 32 columns.
+template <int BN>
+struct EpiWarp {
+  static constexpr int NCH = BN / 64;
+  uint4 pre[NCH][4];  // R (16-bit) prefetched before the accumulator is ready
+  bool use_pre;
+
+  FXB_DEV void prefetch(const GemmParams& p, int m, int ntile0, int half) {
+    use_pre = epi_reads_r(p.epi) && p.c_dtype != FXB_DTYPE_F32 && m < p.M;
+    if (!use_pre) return;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int n0 = ntile0 + (half * NCH + c) * 32;
+      if (n0 < p.N) prefetch_r16(p, m, n0, pre[c]);
+    }
+  }
+
+  FXB_DEV void run(const GemmParams& p, int m, int ntile0, int half, uint32_t tbase) {
+#pragma unroll
+    for (int cc = 0; cc < NCH; ++cc) {
+      const int c = half * NCH + cc;
+      uint32_t r[32];
+      tmem_ld32(tbase + c * 32, r);
+      tmem_wait_ld();
+      const int n0 = ntile0 + c * 32;
+      if (m < p.M && n0 < p.N) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        switch (p.c_dtype) {
+          case FXB_DTYPE_BF16:
+            epilogue_chunk<__nv_bfloat16>(p, m, n0, v, use_pre, pre[cc]);
+            break;
+          case FXB_DTYPE_F16: epilogue_chunk<__half>(p, m, n0, v, use_pre, pre[cc]); break;
+          default: epilogue_chunk<float>(p, m, n0, v, false, pre[cc]); break;
+        }
+      }
+    }
+  }
+};
 
 // ---------------------------------------------------------------- kernel
 template <int BN, bool A_MN, bool B_MN, int AB_FMT>
@@ -341,27 +414,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x) {
       int tm, tn, split;
       tile_coords(unit, p, tm, tn, split);
+      const int m = tm * BM + row_in_tile;
+      EpiWarp<BN> ew;
+      ew.prefetch(p, m, tn * BN, half);
       if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
       tc_fence_after();
-      const int m = tm * BM + row_in_tile;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
-#pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c * 32, r);
-        tmem_wait_ld();
-        const int n0 = tn * BN + c * 32;
-        if (m < p.M && n0 < p.N) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          switch (p.c_dtype) {
-            case FXB_DTYPE_BF16: epilogue_chunk<__nv_bfloat16>(p, m, n0, v); break;
-            case FXB_DTYPE_F16: epilogue_chunk<__half>(p, m, n0, v); break;
-            default: epilogue_chunk<float>(p, m, n0, v); break;
-          }
-        }
-      }
+      ew.run(p, m, tn * BN, half, tbase);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(abuf));
@@ -549,27 +608,13 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     for (int unit = pair; unit < total_units; unit += npairs) {
       int tm, tn, split;
       tile_coords2(unit, p, tm, tn, split);
+      const int m = tm * 256 + row_in_tile;
+      EpiWarp<BN> ew;
+      ew.prefetch(p, m, tn * BN, half);
       if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
       tc_fence_after();
-      const int m = tm * 256 + row_in_tile;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
-#pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c * 32, r);
-        tmem_wait_ld();
-        const int n0 = tn * BN + c * 32;
-        if (m < p.M && n0 < p.N) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          switch (p.c_dtype) {
-            case FXB_DTYPE_BF16: epilogue_chunk<__nv_bfloat16>(p, m, n0, v); break;
-            case FXB_DTYPE_F16: epilogue_chunk<__half>(p, m, n0, v); break;
-            default: epilogue_chunk<float>(p, m, n0, v); break;
-          }
-        }
-      }
+      ew.run(p, m, tn * BN, half, tbase);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(abuf), 0));
@@ -770,4 +815,15 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
 extern "C" int fxb_gemm(const fxb_gemm_args* args, void* stream) {
   if (!args) return fxb::set_error(FXB_EINVAL, "gemm: args is NULL");
   return fxb::gemm_launch(args, args->epilogue, 0, fxb::as_stream(stream));
+}
+
+extern "C" int fxb_gemm_plan(int32_t M, int32_t N, int32_t K, int32_t epilogue, int32_t* pair,
+                             int32_t* bn, int32_t* splits) {
+  if (!pair || !bn || !splits || M < 0 || N < 0 || K < 0)
+    return fxb::set_error(FXB_EINVAL, "gemm_plan: bad arguments");
+  Plan pl = plan(M, N, K, epilogue == FXB_EPI_ACCUM_F32, fxb::num_sms(), force_mode());
+  *pair = pl.pair ? 1 : 0;
+  *bn = pl.BN;
+  *splits = pl.splits;
+  return FXB_OK;
 }

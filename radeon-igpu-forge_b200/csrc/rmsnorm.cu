@@ -88,7 +88,8 @@ rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restri
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
-                   const float* __restrict__ rstd, const T* __restrict__ dy, T* __restrict__ dx,
+                   const float* __restrict__ rstd, const T* __restrict__ dy,
+                   const T* __restrict__ dres, T* __restrict__ dx,
                    float* __restrict__ part, int64_t rows, int D) {
   constexpr int E = Vec<T>::N;
   extern __shared__ float sdw[];  // kWarps x D
@@ -132,6 +133,12 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
         for (int j = 0; j < E; ++j) {
           o[j] = rs * wv[i][j] * gv[i][j] - xv[i][j] * corr;
           acc[i][j] += xv[i][j] * rs * gv[i][j];
+        }
+        if (dres) {  // gradient arriving through the residual path
+          float rr[E];
+          load_vec<T>(dres + r * D + (int64_t)v * E, rr);
+#pragma unroll
+          for (int j = 0; j < E; ++j) o[j] += rr[j];
         }
         store_vec<T>(dr + (int64_t)v * E, o);
       }
@@ -213,7 +220,8 @@ int bwd_blocks(int64_t rows) {
 }
 
 template <typename T>
-int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, void* dx, void* dw,
+int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* dres,
+               void* dx, void* dw,
                int dw_dtype, int acc, float* ws, int64_t rows, int D, cudaStream_t st) {
   constexpr int E = Vec<T>::N;
   const int vpl = (D / E + 31) / 32;
@@ -228,7 +236,7 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
     auto k = rmsnorm_bwd_kernel<T, V>;                                                   \
     if (smem > 48 * 1024)                                                                \
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
-    k<<<blocks, kWarps * 32, smem, st>>>(X, W, rstd, G, DX, ws, rows, D);                \
+    k<<<blocks, kWarps * 32, smem, st>>>(X, W, rstd, G, static_cast<const T*>(dres), DX, ws, rows, D); \
     break;                                                                               \
   }
   switch (vpl) {
@@ -287,13 +295,14 @@ size_t fxb_rmsnorm_bwd_workspace(int64_t rows, int32_t D) {
 }
 
 int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rstd,
-                    const void* dy, void* dx, void* dw, int32_t dw_dtype, int32_t dw_accumulate,
+                    const void* dy, const void* dres, void* dx, void* dw, int32_t dw_dtype,
+                    int32_t dw_accumulate,
                     float* workspace, int64_t rows, int32_t D, void* stream) {
   int r = check_common(dtype, x, w, rows, D);
   if (r) return r;
   if (fxb::dtype_size(dw_dtype) == 0) return fxb::set_error(FXB_EINVAL, "rmsnorm bwd: bad dw dtype");
-  if (!fxb::aligned16(dy) || !fxb::aligned16(dx))
-    return fxb::set_error(FXB_EINVAL, "rmsnorm bwd: dy and dx must be 16-byte aligned");
+  if (!fxb::aligned16(dy) || !fxb::aligned16(dx) || (dres && !fxb::aligned16(dres)))
+    return fxb::set_error(FXB_EINVAL, "rmsnorm bwd: dy, dres and dx must be 16-byte aligned");
   if (!workspace || !dw) return fxb::set_error(FXB_EINVAL, "rmsnorm bwd: workspace/dw NULL");
   cudaStream_t st = fxb::as_stream(stream);
   if (rows == 0) {
@@ -303,11 +312,11 @@ int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rs
   }
   switch (dtype) {
     case FXB_DTYPE_BF16:
-      return launch_bwd<__nv_bfloat16>(x, w, rstd, dy, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
+      return launch_bwd<__nv_bfloat16>(x, w, rstd, dy, dres, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
     case FXB_DTYPE_F16:
-      return launch_bwd<__half>(x, w, rstd, dy, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
+      return launch_bwd<__half>(x, w, rstd, dy, dres, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
     default:
-      return launch_bwd<float>(x, w, rstd, dy, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
+      return launch_bwd<float>(x, w, rstd, dy, dres, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
   }
 }
 

@@ -72,7 +72,7 @@ SIGNATURES = {
     "fxb_launch_count": (ctypes.c_uint64, []),
     "fxb_rmsnorm_fwd": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _vp]),
     "fxb_rmsnorm_bwd_workspace": (ctypes.c_size_t, [_i64, _i32]),
-    "fxb_rmsnorm_bwd": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
+    "fxb_rmsnorm_bwd": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
                                        _vp, _i64, _i32, _vp]),
     "fxb_ce_fwd_grad": (ctypes.c_int, [_i32, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32,
                                        _i64, _vp]),
@@ -82,6 +82,8 @@ SIGNATURES = {
                                         _i32, _vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32,
                                         _f32, _vp]),
     "fxb_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _vp]),
+    "fxb_gemm_plan": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.POINTER(_i32),
+                                     ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "fxb_attn_fwd": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
     "fxb_attn_bwd_workspace": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "fxb_attn_bwd": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
@@ -143,6 +145,14 @@ def dtype_code(dt):
         return DTYPE_CODE[dt]
     except KeyError:
         raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def gemm_plan(M, N, K, epilogue=EPI_STORE):
+    """(pair, tile_n, splits) that fxb_gemm would use for this problem."""
+    a, b, c = _i32(), _i32(), _i32()
+    check(load().fxb_gemm_plan(M, N, K, epilogue, ctypes.byref(a), ctypes.byref(b),
+                               ctypes.byref(c)), "fxb_gemm_plan")
+    return bool(a.value), b.value, c.value
 
 
 def launch_count():

@@ -30,6 +30,7 @@ from .attention import flash_attention_qkv
 from .norm import rms_norm
 from .cross_entropy import linear_cross_entropy
 from .linear import fused_linear, fused_mlp
+from .block import attn_block, mlp_block
 
 
 @dataclass
@@ -114,6 +115,12 @@ class Block(nn.Module):
     def forward(self, x):
         B, T, D = x.shape
         fused = self.linear_impl == "fused"
+        if (fused and self.attn_impl == "flash" and self.norm_impl == "fused"
+                and self.head_dim == 64 and x.dtype != torch.float32):
+            # both halves of the block as single Functions (residual-path
+            # gradients summed inside the RMSNorm backward kernel)
+            x = attn_block(x, self.ln1_w, self.qkv.weight, self.proj.weight, self.eps, self.n_head)
+            return mlp_block(x, self.ln2_w, self.fc.weight, self.fc2.weight, self.eps)
         h = self._norm(x, self.ln1_w)
         qkv = fused_linear(h, self.qkv.weight) if fused else self.qkv(h)
         qkv = qkv.view(B, T, 3, self.n_head, self.head_dim)

@@ -30,16 +30,45 @@ def _check(x, w):
     return D
 
 
+def rmsnorm_fwd(x2, w, eps):
+    """(y, rstd) for a (rows, D) contiguous input."""
+    N, D = x2.shape
+    y = torch.empty_like(x2)
+    rstd = torch.empty(N, device=x2.device, dtype=torch.float32)
+    _lib.call("fxb_rmsnorm_fwd", _lib.dtype_code(x2.dtype), _lib.ptr(x2), _lib.ptr(w),
+              _lib.ptr(y), _lib.ptr(rstd), N, D, float(eps), _lib.stream_ptr(x2.device))
+    return y, rstd
+
+
+def rmsnorm_bwd(x2, w, rstd, dy2, dres=None, need_dw=True):
+    """dx (+ dres, the residual-path gradient, in the same pass) and dw.
+
+    dw goes into w's FlatAdamW fp32 slot when it has one (returned as None),
+    else it is returned in w's dtype (None when need_dw is False)."""
+    N, D = x2.shape
+    dx = torch.empty_like(x2)
+    lib = _lib.load()
+    ws = torch.empty(max(1, lib.fxb_rmsnorm_bwd_workspace(N, D) // 4), device=x2.device,
+                     dtype=torch.float32)
+    sink = param_grad_sink(w) if need_dw else None
+    if sink is not None:
+        dw, dw_ret, acc = sink, None, 1
+    else:
+        dw = torch.empty_like(w)
+        dw_ret, acc = (dw if need_dw else None), 0
+    _lib.call("fxb_rmsnorm_bwd", _lib.dtype_code(x2.dtype), _lib.ptr(x2), _lib.ptr(w),
+              _lib.ptr(rstd), _lib.ptr(dy2), _lib.ptr(dres), _lib.ptr(dx), _lib.ptr(dw),
+              _lib.dtype_code(dw.dtype), acc, _lib.ptr(ws), N, D, _lib.stream_ptr(x2.device))
+    return dx, dw_ret
+
+
 class _RMSNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, eps):
         D = _check(x, w)
         N = x.numel() // D
         x2 = x.view(N, D)
-        y = torch.empty_like(x2)
-        rstd = torch.empty(N, device=x.device, dtype=torch.float32)
-        _lib.call("fxb_rmsnorm_fwd", _lib.dtype_code(x.dtype), _lib.ptr(x2), _lib.ptr(w),
-                  _lib.ptr(y), _lib.ptr(rstd), N, D, float(eps), _lib.stream_ptr(x.device))
+        y, rstd = rmsnorm_fwd(x2, w, eps)
         ctx.save_for_backward(x2, w, rstd)
         ctx.oshape = x.shape
         return y.view(x.shape)
@@ -48,24 +77,9 @@ class _RMSNorm(torch.autograd.Function):
     def backward(ctx, dy):
         x2, w, rstd = ctx.saved_tensors
         N, D = x2.shape
-        dy2 = dy.contiguous().view(N, D)
-        dx = torch.empty_like(x2)
-        lib = _lib.load()
-        ws = torch.empty(max(1, lib.fxb_rmsnorm_bwd_workspace(N, D) // 4), device=x2.device,
-                         dtype=torch.float32)
-        sink = param_grad_sink(w) if ctx.needs_input_grad[1] else None
-        if sink is not None:
-            dw, dw_ret, acc = sink, None, 1
-        else:
-            dw = torch.empty_like(w)
-            dw_ret, acc = dw, 0
-        _lib.call("fxb_rmsnorm_bwd", _lib.dtype_code(x2.dtype), _lib.ptr(x2), _lib.ptr(w),
-                  _lib.ptr(rstd), _lib.ptr(dy2), _lib.ptr(dx), _lib.ptr(dw),
-                  _lib.dtype_code(dw.dtype), acc, _lib.ptr(ws), N, D,
-                  _lib.stream_ptr(x2.device))
-        if not ctx.needs_input_grad[1]:
-            dw_ret = None
-        return dx.view(ctx.oshape), dw_ret, None
+        dx, dw = rmsnorm_bwd(x2, w, rstd, dy.contiguous().view(N, D),
+                             need_dw=ctx.needs_input_grad[1])
+        return dx.view(ctx.oshape), dw, None
 
 
 def rms_norm(x, weight, eps=1e-6):
