@@ -86,6 +86,31 @@ int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rs
                     int32_t dw_accumulate, float* workspace, int64_t rows, int32_t D,
                     void* stream);
 
+/* fxb_rmsnorm_bwd without a workspace argument: the call allocates nothing.
+ * No counterpart in the reference (its rms_norm backward allocates the dw
+ * partials with torch, ml/fxlm/norm.py:75-84); this entry exists for callers
+ * that cannot allocate device memory on the call path, e.g. a host runtime
+ * with a fixed memory budget that owns no allocator, or code that must not
+ * call cudaMalloc / cudaFree (which synchronise the device).
+ * Same math, arguments and results as fxb_rmsnorm_bwd (identical block count,
+ * so identical dw). The dw partials live in a file-scope device array of
+ * fxb_rmsnorm_bwd_static_max_bytes() bytes (4 MiB), one per device:
+ *  - the first call on a device looks up that array's address
+ *    (cudaGetSymbolAddress) and caches it; make that first call before any
+ *    stream capture;
+ *  - a call whose partials need more than the array holds
+ *    (fxb_rmsnorm_bwd_workspace(rows, D) > the maximum) returns FXB_EINVAL;
+ *  - nothing in the array has to start at zero (each block writes all of its
+ *    partials before they are read);
+ *  - every call on a device shares the array, so two calls that overlap in
+ *    time (different streams or host threads) race on it: issue them in order
+ *    on one stream. */
+size_t fxb_rmsnorm_bwd_static_max_bytes(void);
+int fxb_rmsnorm_bwd_static(int32_t dtype, const void* x, const void* w, const float* rstd,
+                           const void* dy, const void* dres, void* dx, void* dw,
+                           int32_t dw_dtype, int32_t dw_accumulate, int64_t rows, int32_t D,
+                           void* stream);
+
 /* ------------------------------------------------------------------ cross entropy */
 
 /* Row-wise softmax cross entropy with the gradient written in the same pass.

@@ -5,6 +5,8 @@
 // inputs. Layout differs: one warp owns a row, the row lives in registers as
 // 16-byte vectors (one HBM read of x, one write of y), and the dw reduction is
 // a per-block partial followed by a fixed-order column sum (deterministic).
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -262,6 +264,37 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
   return fxb::check_launch("rmsnorm_dw_reduce");
 }
 
+// ---------------------------------------------------------------- static scratch
+// fxb_rmsnorm_bwd_static keeps its dw partials in this file-scope array (one
+// copy per device) instead of a caller-provided workspace. Every call on a
+// device shares it. Nothing in it has to start at zero: each backward block
+// writes all D of its partials before the column reduction reads them.
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
+__device__ __align__(256) float g_rms_scratch[kStaticScratchBytes / sizeof(float)];
+
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[64] = {nullptr};
+
+// Address of g_rms_scratch on the current device; looked up once per device
+// (the first call there), never allocated.
+int static_scratch(float** out) {
+  int dev = 0;
+  int r = fxb::check_cuda(cudaGetDevice(&dev), "rmsnorm bwd static: cudaGetDevice");
+  if (r) return r;
+  if (dev < 0 || dev >= 64)
+    return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm bwd static: device ordinal %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    r = fxb::check_cuda(cudaGetSymbolAddress(&p, g_rms_scratch),
+                        "rmsnorm bwd static: cudaGetSymbolAddress(scratch)");
+    if (r) return r;
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return FXB_OK;
+}
+
 int check_common(int32_t dtype, const void* x, const void* w, int64_t rows, int32_t D) {
   if (fxb::dtype_size(dtype) == 0) return fxb::set_error(FXB_EINVAL, "rmsnorm: bad dtype %d", dtype);
   if (D <= 0 || D % 8 != 0 || D > 8192)
@@ -318,6 +351,27 @@ int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rs
     default:
       return launch_bwd<float>(x, w, rstd, dy, dres, dx, dw, dw_dtype, dw_accumulate, workspace, rows, D, st);
   }
+}
+
+size_t fxb_rmsnorm_bwd_static_max_bytes(void) { return kStaticScratchBytes; }
+
+int fxb_rmsnorm_bwd_static(int32_t dtype, const void* x, const void* w, const float* rstd,
+                           const void* dy, const void* dres, void* dx, void* dw,
+                           int32_t dw_dtype, int32_t dw_accumulate, int64_t rows, int32_t D,
+                           void* stream) {
+  int r = check_common(dtype, x, w, rows, D);
+  if (r) return r;
+  const size_t need = fxb_rmsnorm_bwd_workspace(rows, D);
+  if (need > kStaticScratchBytes)
+    return fxb::set_error(FXB_EINVAL,
+                          "rmsnorm bwd static: rows=%lld D=%d need %zu bytes of scratch, the "
+                          "static array holds %zu; use fxb_rmsnorm_bwd with a workspace",
+                          (long long)rows, D, need, kStaticScratchBytes);
+  float* scratch = nullptr;
+  r = static_scratch(&scratch);
+  if (r) return r;
+  return fxb_rmsnorm_bwd(dtype, x, w, rstd, dy, dres, dx, dw, dw_dtype, dw_accumulate, scratch,
+                         rows, D, stream);
 }
 
 }  // extern "C"

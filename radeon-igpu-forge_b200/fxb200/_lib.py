@@ -74,6 +74,9 @@ SIGNATURES = {
     "fxb_rmsnorm_bwd_workspace": (ctypes.c_size_t, [_i64, _i32]),
     "fxb_rmsnorm_bwd": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
                                        _vp, _i64, _i32, _vp]),
+    "fxb_rmsnorm_bwd_static_max_bytes": (ctypes.c_size_t, []),
+    "fxb_rmsnorm_bwd_static": (ctypes.c_int, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
+                                              _i32, _i64, _i32, _vp]),
     "fxb_ce_fwd_grad": (ctypes.c_int, [_i32, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32,
                                        _i64, _vp]),
     "fxb_adamw_sumsq": (ctypes.c_int, [_i32, _vp, _i64, _vp, _vp, _vp]),
