@@ -46,12 +46,26 @@ template <typename T> FXB_DEV void unpack8(const uint4& u, float* f) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) f[i] = to_f<T>(h[i]);
 }
+// two floats -> two 16-bit values in one word (a in the low half), one paired
+// round-to-nearest conversion instruction
+template <typename T> FXB_DEV uint32_t pack2(float a, float b);
+template <> FXB_DEV uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> FXB_DEV uint32_t pack2<__half>(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
 template <typename T> FXB_DEV uint4 pack8(const float* f) {
-  uint4 u;
-  T* h = reinterpret_cast<T*>(&u);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) h[i] = from_f<T>(f[i]);
-  return u;
+  return make_uint4(pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]), pack2<T>(f[4], f[5]),
+                    pack2<T>(f[6], f[7]));
+}
+
+// two 16-bit values in one 32-bit word (element 0 in the low half)
+template <typename T> FXB_DEV float2 unpack2(uint32_t u) {
+  const T* h = reinterpret_cast<const T*>(&u);
+  return make_float2(to_f<T>(h[0]), to_f<T>(h[1]));
 }
 
 FXB_DEV float warp_sum(float v) {
@@ -163,6 +177,31 @@ FXB_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+// shared -> global tile store and fp32 add-reduction (bulk-group completion);
+// the coordinates are never negative here
+FXB_DEV void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+FXB_DEV void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::
+          "l"(reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1)
+      : "memory");
+}
+FXB_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// this thread's bulk groups have finished reading shared memory
+FXB_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... and their global writes are complete
+FXB_DEV void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+FXB_DEV void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
 }
 // named barrier over `count` threads (ids 1..15; 0 is __syncthreads)
 FXB_DEV void named_bar_sync(int id, int count) {

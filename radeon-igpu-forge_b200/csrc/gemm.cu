@@ -7,10 +7,12 @@
 // ml/fxgpu/fused_linear.py:94). Design (B200-first, no reference analogue):
 //   - persistent CTAs (one per SM), static tile schedule grouped along M for
 //     L2 reuse; optional split-K for skinny outputs (dW), reduced with fp32
-//     red.add into the destination;
+//     TMA add-reductions into the destination;
 //   - warp 0: TMA producer (128B-swizzled boxes, no multicast), warp 1: MMA
 //     issuer (one thread, tcgen05.mma cta_group::1 M=128 N=BN K=16) and TMEM
-//     owner, warps 2-5: epilogue (tcgen05.ld 32x32b -> fused op -> global);
+//     owner, warps 2-9: epilogue (tcgen05.ld 32x32b -> fused op -> 64B-swizzled
+//     staging in shared memory -> TMA store / add-reduction, so global writes
+//     are whole coalesced boxes issued asynchronously);
 //   - STAGES-deep smem ring (full/empty mbarriers), two TMEM accumulators so
 //     the epilogue of tile i overlaps the mainloop of tile i+1;
 //   - operands K-major or MN-major (transposed) so forward, dX and dW GEMMs
@@ -26,6 +28,11 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = 128 bytes = one swizzle row
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+// Per-epilogue-warp output staging: two 2 KB buffers after the operand ring;
+// the warp's lane 0 issues the TMA stores (or fp32 add-reductions) and owns
+// their bulk groups.
+constexpr int kEpiWarpBytes = 4096;
+constexpr int kEpiBytes = 8 * kEpiWarpBytes;
 
 struct GemmParams {
   int M, N, K;
@@ -49,7 +56,7 @@ template <int BN> struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + kEpiBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 FXB_DEV void tile_coords(int unit, const GemmParams& p, int& tm, int& tn, int& split) {
@@ -68,60 +75,36 @@ FXB_DEV void tile_coords(int unit, const GemmParams& p, int& tm, int& tn, int& s
 }
 
 // ---------------------------------------------------------------- epilogue helpers
+// The epilogue works on 16-column pieces of one row per lane: v[16] holds the
+// accumulator values, n8 (0..2) counts the piece's valid groups of 8 columns
+// (N % 8 == 0).
 FXB_DEV float silu_f(float x) { return x / (1.f + __expf(-x)); }
 
-template <typename T> FXB_DEV void load32(const T* p, float* f) {
+// 16 values of row p (first n8 groups of 8; the rest zero)
+template <typename T> FXB_DEV void load16_part(const T* p, float* f, int n8) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) f[i] = 0.f;
   if constexpr (sizeof(T) == 4) {
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      float4 u = reinterpret_cast<const float4*>(p)[q];
-      f[4 * q] = u.x; f[4 * q + 1] = u.y; f[4 * q + 2] = u.z; f[4 * q + 3] = u.w;
-    }
-  } else {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) unpack8<T>(reinterpret_cast<const uint4*>(p)[q], f + 8 * q);
-  }
-}
-// store the first `n8` groups of 8 columns
-template <typename T> FXB_DEV void store32(T* p, const float* f, int n8) {
-  if constexpr (sizeof(T) == 4) {
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      if (q < 2 * n8)
-        reinterpret_cast<float4*>(p)[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
-  } else {
 #pragma unroll
     for (int q = 0; q < 4; ++q)
-      if (q < n8) reinterpret_cast<uint4*>(p)[q] = pack8<T>(f + 8 * q);
-  }
-}
-template <typename T> FXB_DEV void load32_part(const T* p, float* f, int n8) {
-  if (n8 >= 4) { load32<T>(p, f); return; }
-#pragma unroll
-  for (int i = 0; i < 32; ++i) f[i] = 0.f;
-  if constexpr (sizeof(T) == 4) {
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
       if (q < 2 * n8) {
         float4 u = reinterpret_cast<const float4*>(p)[q];
         f[4 * q] = u.x; f[4 * q + 1] = u.y; f[4 * q + 2] = u.z; f[4 * q + 3] = u.w;
       }
   } else {
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
+    for (int q = 0; q < 2; ++q)
       if (q < n8) unpack8<T>(reinterpret_cast<const uint4*>(p)[q], f + 8 * q);
   }
-}
-
-FXB_DEV void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
-               "f"(c), "f"(d)
-               : "memory");
 }
 
 // epilogues that read a second (m, n) input from R
 FXB_DEV bool epi_reads_r(int epi) {
   return epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU;
+}
+// epilogues that also write the rounded pre-activation to Z (when Z is given)
+FXB_DEV bool epi_writes_z(const GemmParams& p) {
+  return p.Z && (p.epi == FXB_EPI_GELU || p.epi == FXB_EPI_BIAS_GELU || p.epi == FXB_EPI_BIAS_SILU);
 }
 
 // Issue the loads of one 32-column chunk of R (16-bit) into registers; called
@@ -134,39 +117,38 @@ FXB_DEV void prefetch_r16(const GemmParams& p, int m, int n0, uint4* pre) {
   for (int q = 0; q < 4; ++q) pre[q] = (q < n8) ? src[q] : make_uint4(0, 0, 0, 0);
 }
 
-// R values of one chunk: from the prefetched registers (16-bit C) or loaded now
+// R values of one 16-column piece: from the prefetched registers (16-bit C),
+// loaded now (fp32 C), or zero for rows past M (their results are clipped by
+// the store)
 template <typename CT>
-FXB_DEV void chunk_r(const GemmParams& p, int m, int n0, int n8, bool use_pre,
-                     const uint4 (&pre)[4], float* r) {
+FXB_DEV void piece_r(const GemmParams& p, int m, int n0, int n8, bool use_pre, const uint4* pre2,
+                     float* r) {
   if constexpr (sizeof(CT) == 2) {
     if (use_pre) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) unpack8<CT>(pre[q], r + 8 * q);
+      unpack8<CT>(pre2[0], r);
+      unpack8<CT>(pre2[1], r + 8);
       return;
     }
   }
-  load32_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, r, n8);
+  if (m < p.M) {
+    load16_part<CT>(static_cast<const CT*>(p.R) + (int64_t)m * p.ldr + n0, r, n8);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = 0.f;
+  }
 }
 
+// Epilogue arithmetic of one 16-column piece of row m, in place on v: the
+// value written to C (or added to it, FXB_EPI_ACCUM_F32). z receives the
+// rounded pre-activation of the epilogues that also write Z.
 template <typename CT>
-FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v, bool use_pre,
-                            const uint4 (&pre)[4]) {
-  const int n8 = min(4, (p.N - n0) >> 3);  // groups of 8 valid columns (N % 8 == 0)
-  if (n8 <= 0) return;
-  CT* crow = static_cast<CT*>(p.C) + (int64_t)m * p.ldc + n0;
+FXB_DEV void epilogue_math(const GemmParams& p, int m, int n0, int n8, float* v, float* z,
+                           bool use_pre, const uint4* pre2) {
   switch (p.epi) {
-    case FXB_EPI_STORE: {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
-      store32<CT>(crow, v, n8);
-      break;
-    }
     case FXB_EPI_RESIDUAL: {
-      float r[32];
-      chunk_r<CT>(p, m, n0, n8, use_pre, pre, r);
+      piece_r<CT>(p, m, n0, n8, use_pre, pre2, z);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = v[i] * p.alpha + r[i];
-      store32<CT>(crow, v, n8);
+      for (int i = 0; i < 16; ++i) v[i] = v[i] * p.alpha + z[i];
       break;
     }
     case FXB_EPI_GELU:
@@ -174,100 +156,170 @@ FXB_DEV void epilogue_chunk(const GemmParams& p, int m, int n0, float* v, bool u
     case FXB_EPI_BIAS_SILU:
     case FXB_EPI_BIAS: {
       if (p.epi != FXB_EPI_GELU) {
-        float b[32];
-        load32_part<CT>(static_cast<const CT*>(p.bias) + n0, b, n8);
+        load16_part<CT>(static_cast<const CT*>(p.bias) + n0, z, n8);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += b[i];
+        for (int i = 0; i < 16; ++i) v[i] += z[i];
       }
-      if (p.epi == FXB_EPI_BIAS) {
-        store32<CT>(crow, v, n8);
-        break;
-      }
+      if (p.epi == FXB_EPI_BIAS) break;
       // round the pre-activation once; the activation is computed from the
       // stored value so that backward (which reads Z) sees the same input
-      float zr[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) zr[i] = to_f<CT>(from_f<CT>(v[i]));
-      if (p.Z) store32<CT>(static_cast<CT*>(p.Z) + (int64_t)m * p.ldz + n0, zr, n8);
+      for (int i = 0; i < 16; ++i) z[i] = to_f<CT>(from_f<CT>(v[i]));
       if (p.epi == FXB_EPI_BIAS_SILU) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = silu_f(zr[i]);
+        for (int i = 0; i < 16; ++i) v[i] = silu_f(z[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(zr[i]);
+        for (int i = 0; i < 16; ++i) v[i] = gelu_tanh(z[i]);
       }
-      store32<CT>(crow, v, n8);
       break;
     }
     case FXB_EPI_DGELU: {
-      float z[32];
-      chunk_r<CT>(p, m, n0, n8, use_pre, pre, z);
+      piece_r<CT>(p, m, n0, n8, use_pre, pre2, z);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= gelu_tanh_grad(z[i]);
-      store32<CT>(crow, v, n8);
+      for (int i = 0; i < 16; ++i) v[i] *= gelu_tanh_grad(z[i]);
       break;
     }
     case FXB_EPI_DSILU: {
-      float z[32];
-      chunk_r<CT>(p, m, n0, n8, use_pre, pre, z);
+      piece_r<CT>(p, m, n0, n8, use_pre, pre2, z);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const float s = 1.f / (1.f + __expf(-z[i]));
         v[i] *= s * (1.f + z[i] * (1.f - s));
       }
-      store32<CT>(crow, v, n8);
       break;
     }
-    default: {  // FXB_EPI_ATOMIC_F32: red.add into fp32 C
-      float* c32 = static_cast<float*>(p.C) + (int64_t)m * p.ldc + n0;
+    default: {  // FXB_EPI_STORE, FXB_EPI_ACCUM_F32
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (q < 2 * n8)
-          red_add_v4(c32 + 4 * q, v[4 * q] * p.alpha, v[4 * q + 1] * p.alpha,
-                     v[4 * q + 2] * p.alpha, v[4 * q + 3] * p.alpha);
+      for (int i = 0; i < 16; ++i) v[i] *= p.alpha;
     }
   }
 }
 
+// Staging buffers: 32 rows x 64 bytes (one row per lane) in the layout of a
+// 64-byte-swizzled TMA box: 16-byte chunk q of row r sits at q ^ ((r >> 1) & 3),
+// which also keeps each quarter-warp's 16-byte stores on distinct banks.
+// stage_piece writes 16 values of row `lane`: 16-byte chunks 2h, 2h+1 of the
+// row for 16-bit types, the whole 64-byte row for fp32 (h unused).
+template <typename CT> FXB_DEV void stage_piece(uint32_t buf, int lane, int h, const float* f) {
+  const uint32_t row = buf + (uint32_t)lane * 64u;
+  const int sw = (lane >> 1) & 3;
+  if constexpr (sizeof(CT) == 4) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      st_shared_v4(row + (uint32_t)((q ^ sw) << 4),
+                   make_uint4(__float_as_uint(f[4 * q]), __float_as_uint(f[4 * q + 1]),
+                              __float_as_uint(f[4 * q + 2]), __float_as_uint(f[4 * q + 3])));
+  } else {
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+      st_shared_v4(row + (uint32_t)(((2 * h + q) ^ sw) << 4), pack8<CT>(f + 8 * q));
+  }
+}
+
+// before writing the staging buffers: the pieces issued last have been read
+FXB_DEV void stage_begin(int lane) {
+  if (lane == 0) bulk_wait_read0();
+  __syncwarp();
+}
+
+// Issue the staged pieces (rows y..y+31): buffer 0 to map0 at column x0 and,
+// when map1 is given, buffer 1 to map1 at x1. TMA clips rows >= M and
+// columns >= N.
+FXB_DEV void stage_issue(const CUtensorMap* map0, int x0, const CUtensorMap* map1, int x1, int y,
+                         bool reduce, uint32_t sbuf, int lane) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (reduce) {
+      tma_reduce_add_2d(map0, sbuf, x0, y);
+      if (map1) tma_reduce_add_2d(map1, sbuf + 2048, x1, y);
+    } else {
+      tma_store_2d(map0, sbuf, x0, y);
+      if (map1) tma_store_2d(map1, sbuf + 2048, x1, y);
+    }
+    bulk_commit();
+  }
+}
+
 // One epilogue warp's share of an accumulator tile. The warp reads TMEM lanes
-// of its quarter (row m for this lane) and the columns [half*BN/2, (half+1)*BN/2)
-// of the tile, i.e. NCH = BN/64 chunks of 32 columns.
+// of its quarter (row m for this lane; rows m0..m0+31 for the warp) and the
+// columns [half*BN/2, (half+1)*BN/2) of the tile, i.e. NCH = BN/64 chunks of
+// 32 columns, and writes them through its staging buffers.
 template <int BN>
 struct EpiWarp {
   static constexpr int NCH = BN / 64;
-  uint4 pre[NCH][4];  // R (16-bit) prefetched before the accumulator is ready
+  // R (16-bit) of two chunks in flight: chunks 0 and 1 are loaded before the
+  // accumulator is ready, chunk c + 2 into slot c & 1 once chunk c is done
+  uint4 pre[2][4];
   bool use_pre;
 
   FXB_DEV void prefetch(const GemmParams& p, int m, int ntile0, int half) {
     use_pre = epi_reads_r(p.epi) && p.c_dtype != FXB_DTYPE_F32 && m < p.M;
     if (!use_pre) return;
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) {
+    for (int c = 0; c < 2; ++c) {
       const int n0 = ntile0 + (half * NCH + c) * 32;
       if (n0 < p.N) prefetch_r16(p, m, n0, pre[c]);
     }
   }
 
-  FXB_DEV void run(const GemmParams& p, int m, int ntile0, int half, uint32_t tbase) {
+  // one 16-column piece: TMEM -> registers -> epilogue math
+  template <typename CT>
+  FXB_DEV int piece(const GemmParams& p, int m, int n0, uint32_t taddr, const uint4* pre2,
+                    float* v, float* z) {
+    uint32_t r[16];
+    tmem_ld16(taddr, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    const int n8 = max(0, min(2, (p.N - n0) >> 3));
+    epilogue_math<CT>(p, m, n0, n8, v, z, sizeof(CT) == 2 && use_pre, pre2);
+    return n8;
+  }
+
+  template <typename CT>
+  FXB_DEV void chunk(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmZ, int m,
+                     int m0, int n0, uint32_t taddr, int cc, uint32_t sbuf, int lane) {
+    const bool wz = epi_writes_z(p);
+    float v[16], z[16];
+    if constexpr (sizeof(CT) == 2) {
+      stage_begin(lane);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        piece<CT>(p, m, n0 + 16 * h, taddr + 16 * h, &pre[cc & 1][2 * h], v, z);
+        stage_piece<CT>(sbuf, lane, h, v);
+        if (wz) stage_piece<CT>(sbuf + 2048, lane, h, z);
+      }
+      stage_issue(tmC, n0, wz ? tmZ : nullptr, n0, m0, false, sbuf, lane);
+    } else {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n8 = piece<CT>(p, m, n0 + 16 * h, taddr + 16 * h, &pre[cc & 1][2 * h], v, z);
+        if (n8 == 0) continue;  // warp-uniform
+        stage_begin(lane);
+        stage_piece<CT>(sbuf, lane, 0, v);
+        if (wz) stage_piece<CT>(sbuf + 2048, lane, 0, z);
+        stage_issue(tmC, n0 + 16 * h, wz ? tmZ : nullptr, n0 + 16 * h, m0,
+                    p.epi == FXB_EPI_ACCUM_F32, sbuf, lane);
+      }
+    }
+  }
+
+  FXB_DEV void run(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmZ, int m,
+                   int m0, int ntile0, int half, uint32_t tbase, uint32_t sbuf, int lane) {
 #pragma unroll
     for (int cc = 0; cc < NCH; ++cc) {
       const int c = half * NCH + cc;
-      uint32_t r[32];
-      tmem_ld32(tbase + c * 32, r);
-      tmem_wait_ld();
       const int n0 = ntile0 + c * 32;
-      if (m < p.M && n0 < p.N) {
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        switch (p.c_dtype) {
-          case FXB_DTYPE_BF16:
-            epilogue_chunk<__nv_bfloat16>(p, m, n0, v, use_pre, pre[cc]);
-            break;
-          case FXB_DTYPE_F16: epilogue_chunk<__half>(p, m, n0, v, use_pre, pre[cc]); break;
-          default: epilogue_chunk<float>(p, m, n0, v, false, pre[cc]); break;
-        }
+      if (n0 >= p.N) continue;  // warp-uniform
+      const uint32_t taddr = tbase + c * 32;
+      switch (p.c_dtype) {
+        case FXB_DTYPE_BF16: chunk<__nv_bfloat16>(p, tmC, tmZ, m, m0, n0, taddr, cc, sbuf, lane); break;
+        case FXB_DTYPE_F16: chunk<__half>(p, tmC, tmZ, m, m0, n0, taddr, cc, sbuf, lane); break;
+        default: chunk<float>(p, tmC, tmZ, m, m0, n0, taddr, cc, sbuf, lane); break;
       }
+      if (cc + 2 < NCH && use_pre && n0 + 64 < p.N) prefetch_r16(p, m, n0 + 64, pre[cc & 1]);
     }
   }
 };
@@ -276,20 +328,22 @@ struct EpiWarp {
 template <int BN, bool A_MN, bool B_MN, int AB_FMT>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmZ,
                const GemmParams p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // 1024B aligned for 128B swizzle
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t bar0 = base + C::STAGES * C::STAGE_BYTES;
+  const uint32_t epi0 = base + C::STAGES * C::STAGE_BYTES;  // output staging
+  const uint32_t bar0 = epi0 + kEpiBytes;
   // barrier layout: full[S], empty[S], tfull[2], tempty[2], final, then tmem slot
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
   auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + b); };
   auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + 2 + b); };
   const uint32_t final_bar = bar0 + 8u * (2 * C::STAGES + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + 8 * (2 * C::STAGES + 5));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bar0 - base) + 8 * (2 * C::STAGES + 5));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -307,6 +361,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -409,6 +464,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
+    const uint32_t sbuf = epi0 + (uint32_t)(warp - 2) * kEpiWarpBytes;
     int abuf = 0;
     uint32_t aphase = 0;
     for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x) {
@@ -420,12 +476,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
-      ew.run(p, m, tn * BN, half, tbase);
+      ew.run(p, &tmC, &tmZ, m, tm * BM + quarter * 32, tn * BN, half, tbase, sbuf, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(abuf));
       if (++abuf == 2) { abuf = 0; aphase ^= 1; }
     }
+    if (lane == 0) bulk_wait_all0();  // stores done before the staging smem goes away
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -451,7 +509,7 @@ template <int BN> struct Cfg2 {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + kEpiBytes + 1024 + 256;
 };
 
 FXB_DEV void tile_coords2(int unit, const GemmParams& p, int& tm, int& tn, int& split) {
@@ -461,19 +519,21 @@ FXB_DEV void tile_coords2(int unit, const GemmParams& p, int& tm, int& tn, int& 
 template <int BN, bool A_MN, bool B_MN, int AB_FMT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmZ,
                 const GemmParams p) {
   using C = Cfg2<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t bar0 = base + C::STAGES * C::STAGE_BYTES;
+  const uint32_t epi0 = base + C::STAGES * C::STAGE_BYTES;  // output staging
+  const uint32_t bar0 = epi0 + kEpiBytes;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
   auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + b); };
   auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + 2 + b); };
   const uint32_t final_bar = bar0 + 8u * (2 * C::STAGES + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + 8 * (2 * C::STAGES + 5));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bar0 - base) + 8 * (2 * C::STAGES + 5));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -494,6 +554,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -603,6 +664,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = (int)rank * 128 + quarter * 32 + lane;
+    const uint32_t sbuf = epi0 + (uint32_t)(warp - 2) * kEpiWarpBytes;
     int abuf = 0;
     uint32_t aphase = 0;
     for (int unit = pair; unit < total_units; unit += npairs) {
@@ -614,12 +676,15 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
-      ew.run(p, m, tn * BN, half, tbase);
+      ew.run(p, &tmC, &tmZ, m, tm * 256 + (int)rank * 128 + quarter * 32, tn * BN, half, tbase,
+             sbuf, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(abuf), 0));
       if (++abuf == 2) { abuf = 0; aphase ^= 1; }
     }
+    if (lane == 0) bulk_wait_all0();  // stores done before the staging smem goes away
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -634,12 +699,17 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 // ---------------------------------------------------------------- host side
 constexpr int FXB_EPI_ATOMIC_F32 = FXB_EPI_ACCUM_F32;
 
+struct Maps {
+  CUtensorMap a, b, c, z;  // operands, output C, pre-activation Z (= c when unused)
+};
+
 template <int BN, bool A_MN, bool B_MN, int AB_FMT, bool PAIR>
-int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
-               cudaStream_t st) {
-  void (*k)(const CUtensorMap, const CUtensorMap, const GemmParams) =
+int launch_one(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
+  void (*k)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+            const GemmParams) =
       PAIR ? gemm_tc2_kernel<BN, A_MN, B_MN, AB_FMT> : gemm_tc_kernel<BN, A_MN, B_MN, AB_FMT>;
   constexpr int smem = PAIR ? Cfg2<BN>::SMEM : Cfg<BN>::SMEM;
+  static_assert(smem <= 232448, "shared memory budget");
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -649,17 +719,17 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
     if (r) return r;
     attr_set[dev] = true;
   }
-  k<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  k<<<grid, kThreads, smem, st>>>(mp.a, mp.b, mp.c, mp.z, p);
   return fxb::check_launch(PAIR ? "gemm_tc2" : "gemm_tc");
 }
 
 template <int BN, int AB_FMT, bool PAIR>
-int launch_layout(bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb,
-                  const GemmParams& p, int grid, cudaStream_t st) {
-  if (!amn && !bmn) return launch_one<BN, false, false, AB_FMT, PAIR>(ta, tb, p, grid, st);
-  if (!amn && bmn) return launch_one<BN, false, true, AB_FMT, PAIR>(ta, tb, p, grid, st);
-  if (amn && bmn) return launch_one<BN, true, true, AB_FMT, PAIR>(ta, tb, p, grid, st);
-  return launch_one<BN, true, false, AB_FMT, PAIR>(ta, tb, p, grid, st);
+int launch_layout(bool amn, bool bmn, const Maps& mp, const GemmParams& p, int grid,
+                  cudaStream_t st) {
+  if (!amn && !bmn) return launch_one<BN, false, false, AB_FMT, PAIR>(mp, p, grid, st);
+  if (!amn && bmn) return launch_one<BN, false, true, AB_FMT, PAIR>(mp, p, grid, st);
+  if (amn && bmn) return launch_one<BN, true, true, AB_FMT, PAIR>(mp, p, grid, st);
+  return launch_one<BN, true, false, AB_FMT, PAIR>(mp, p, grid, st);
 }
 
 struct Plan {
@@ -720,6 +790,20 @@ int make_map(CUtensorMap* map, int ab_dtype, const void* ptr, uint64_t inner, ui
   return fxb::encode_tiled(map, dt, 2, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Output map (C or Z): 32 rows x 64 bytes per box (32 16-bit or 16 fp32
+// columns), 64-byte swizzle to match the epilogue's staging layout.
+int make_out_map(CUtensorMap* map, int c_dtype, const void* ptr, uint64_t cols, uint64_t rows,
+                 int64_t ld) {
+  const int esz = fxb::dtype_size(c_dtype);
+  uint64_t dims[2] = {cols, rows};
+  uint64_t strides[1] = {(uint64_t)ld * esz};
+  uint32_t box[2] = {(uint32_t)(64 / esz), 32};
+  CUtensorMapDataType dt = c_dtype == FXB_DTYPE_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                           : c_dtype == FXB_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  return fxb::encode_tiled(map, dt, 2, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 }  // namespace
 
 namespace fxb {
@@ -766,15 +850,23 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
   if (force_splits > 0 && epi == FXB_EPI_ATOMIC_F32) splits = force_splits;
   const int rows = pl.pair ? 256 : 128;
 
-  CUtensorMap ta, tb;
+  Maps mp;
   int r;
-  if (a->a_trans) r = make_map(&ta, a->dtype, a->A, (uint64_t)M, (uint64_t)K, a->lda, 64, 64);
-  else r = make_map(&ta, a->dtype, a->A, (uint64_t)K, (uint64_t)M, a->lda, 64, 128);
+  if (a->a_trans) r = make_map(&mp.a, a->dtype, a->A, (uint64_t)M, (uint64_t)K, a->lda, 64, 64);
+  else r = make_map(&mp.a, a->dtype, a->A, (uint64_t)K, (uint64_t)M, a->lda, 64, 128);
   if (r) return r;
-  if (a->b_trans) r = make_map(&tb, a->dtype, a->B, (uint64_t)N, (uint64_t)K, a->ldb, 64, 64);
-  else r = make_map(&tb, a->dtype, a->B, (uint64_t)K, (uint64_t)N, a->ldb, 64,
+  if (a->b_trans) r = make_map(&mp.b, a->dtype, a->B, (uint64_t)N, (uint64_t)K, a->ldb, 64, 64);
+  else r = make_map(&mp.b, a->dtype, a->B, (uint64_t)K, (uint64_t)N, a->ldb, 64,
                     (uint32_t)(pl.pair ? BN / 2 : BN));
   if (r) return r;
+  r = make_out_map(&mp.c, a->c_dtype, a->C, (uint64_t)N, (uint64_t)M, a->ldc);
+  if (r) return r;
+  if (a->Z) {
+    r = make_out_map(&mp.z, a->c_dtype, a->Z, (uint64_t)N, (uint64_t)M, a->ldz);
+    if (r) return r;
+  } else {
+    mp.z = mp.c;
+  }
 
   GemmParams p;
   p.M = M; p.N = N; p.K = K;
@@ -798,17 +890,17 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
     const long pairs = units < sms / 2 ? units : sms / 2;
     const int grid = (int)(2 * pairs);
     if (a->dtype == FXB_DTYPE_BF16)
-      return BN == 256 ? launch_layout<256, 1, true>(amn, bmn, ta, tb, p, grid, st)
-                       : launch_layout<128, 1, true>(amn, bmn, ta, tb, p, grid, st);
-    return BN == 256 ? launch_layout<256, 0, true>(amn, bmn, ta, tb, p, grid, st)
-                     : launch_layout<128, 0, true>(amn, bmn, ta, tb, p, grid, st);
+      return BN == 256 ? launch_layout<256, 1, true>(amn, bmn, mp, p, grid, st)
+                       : launch_layout<128, 1, true>(amn, bmn, mp, p, grid, st);
+    return BN == 256 ? launch_layout<256, 0, true>(amn, bmn, mp, p, grid, st)
+                     : launch_layout<128, 0, true>(amn, bmn, mp, p, grid, st);
   }
   const int grid = (int)(units < sms ? units : sms);
   if (a->dtype == FXB_DTYPE_BF16)
-    return BN == 256 ? launch_layout<256, 1, false>(amn, bmn, ta, tb, p, grid, st)
-                     : launch_layout<128, 1, false>(amn, bmn, ta, tb, p, grid, st);
-  return BN == 256 ? launch_layout<256, 0, false>(amn, bmn, ta, tb, p, grid, st)
-                   : launch_layout<128, 0, false>(amn, bmn, ta, tb, p, grid, st);
+    return BN == 256 ? launch_layout<256, 1, false>(amn, bmn, mp, p, grid, st)
+                     : launch_layout<128, 1, false>(amn, bmn, mp, p, grid, st);
+  return BN == 256 ? launch_layout<256, 0, false>(amn, bmn, mp, p, grid, st)
+                   : launch_layout<128, 0, false>(amn, bmn, mp, p, grid, st);
 }
 }  // namespace fxb
 

@@ -158,6 +158,37 @@ def test_gemm_epilogues(dev, gemm_mode, dtype, M, N, K):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("M,N,K", [(333, 200, 96), (1024, 1032, 256)])
+def test_gemm_output_layouts(dev, gemm_mode, dtype, M, N, K):
+    """Outputs written through strided views (column slices of wider buffers),
+    fp32 C with alpha, and ragged M / N tails; cells outside the view stay
+    untouched."""
+    from fxb200 import ops
+    torch.manual_seed(M * 7 + N)
+    A = (torch.randn(M, K, device=dev) / math.sqrt(K)).to(dtype)
+    B = torch.randn(N, K, device=dev).to(dtype)
+    acc = A.float() @ B.float().t()
+    tol = 1e-2 * acc.abs().max().item()
+    wide = torch.full((M, N + 72), 7.0, device=dev, dtype=dtype)
+    zwide = torch.full((M, N + 24), 7.0, device=dev, dtype=dtype)
+    C, Z = wide[:, 8:8 + N], zwide[:, 16:16 + N]
+    ops.gemm(A, B, C, epilogue=ops.EPI_GELU, Z=Z)
+    assert (Z.float() - acc).abs().max().item() < tol
+    assert (C.float() - F.gelu(Z.float(), approximate="tanh")).abs().max().item() < 2e-2
+    assert (wide[:, :8] == 7).all() and (wide[:, 8 + N:] == 7).all()
+    assert (zwide[:, :16] == 7).all() and (zwide[:, 16 + N:] == 7).all()
+    R = torch.randn(M, N, device=dev).to(dtype)
+    ops.gemm(A, B, C, epilogue=ops.EPI_RESIDUAL, R=R)
+    assert (C.float() - (acc + R.float())).abs().max().item() < tol + 1e-2
+    assert (wide[:, :8] == 7).all() and (wide[:, 8 + N:] == 7).all()
+    C32w = torch.full((M, N + 4), 7.0, device=dev)
+    C32 = C32w[:, :N]
+    ops.gemm(A, B, C32, alpha=0.25)
+    assert (C32 - 0.25 * acc).abs().max().item() < 1e-3 * acc.abs().max().item()
+    assert (C32w[:, N:] == 7).all()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("Mtok,N,K", [(8192, 768, 768), (8192, 3072, 768), (1000, 264, 72)])
 def test_gemm_dw_accum(dev, gemm_mode, dtype, Mtok, N, K):
     """dW (fp32) += dy^T x via split-K red.add, accumulating twice."""
