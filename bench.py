@@ -6,8 +6,11 @@
 One step = forward + backward + FlatAdamW update of the reference GPT
 architecture (V32768, L12, D768, H12, T1024) on a per-GPU micro-batch of 8
 sequences of Zipf(1.1) tokens (seed 3 + rank), bf16 compute with fp32 master
-weights. For N > 1 the driver launches this under torchrun (one rank per GPU,
-NCCL); gradients are all-reduced in buckets that overlap backward.
+weights. On one GPU the step is captured once in a CUDA graph
+(fxlm.GraphedStep, after the warm-up steps) and replayed; `--no-graph` runs it
+eagerly. For N > 1 the driver launches this under torchrun (one rank per GPU,
+NCCL) and the step runs eagerly; gradients are all-reduced in buckets that
+overlap backward.
 
 Printed (rank 0, one JSON line): `value` = tokens/s of the whole job with the
 token batch already in HBM, timed on the device with CUDA events (max over
@@ -18,8 +21,8 @@ time of its launches over a second pass of the same steps, run after the timed
 region so that its events do not perturb it, against the measured sustained
 bf16 peak); `cpu_baseline` = the reference's PyTorch path restated in oracle/gpt.py
 on the host cores (bounded sample); `clocks` sampled with nvidia-smi during
-the timed region; `gpu_launches` = kernels launched by libfxb200 in the timed
-region. `--impl reference` times only that CPU path (the reference arm).
+the timed region; `gpu_launches` = kernels of libfxb200 in the timed region
+(for a replayed graph: the library kernels captured in one step x steps). `--impl reference` times only that CPU path (the reference arm).
 """
 import argparse
 import datetime
@@ -374,7 +377,7 @@ def run_micro(args):
             _lib.call("fxb_adamw_sumsq", 0, P(grad), n, P(scratch), P(flags), st)
             _lib.call("fxb_adamw_final", P(scratch), P(flags), P(step), P(fi), P(norm), P(scale), 1.0, st)
             _lib.call("fxb_adamw_update", 0, 2, P(grad), P(master), P(m), P(v), P(p16), n, P(seg_end),
-                      P(seg_wd), 1, P(scratch), P(fi), P(scale), P(step), 6e-4, 0.9, 0.95, 1e-8, 0.1, st)
+                      P(seg_wd), 1, P(scratch), P(fi), P(scale), P(step), 6e-4, None, 0.9, 0.95, 1e-8, 0.1, st)
         ms = _time_ms(f, it)
         byt = n * (4 + 4 + 4 + 24 + 2)
         out.append({"kernel": "adamw_sumsq + adamw_final + adamw_update", "case": f"{n} params fp32 grad",
@@ -409,7 +412,7 @@ def run_ours(args, rank, world, local_rank):
     x_host, y_host = x_cpu.pin_memory(), y_cpu.pin_memory()
     x_dev, y_dev = x_cpu.to(dev), y_cpu.to(dev)
 
-    def step(x, y):
+    def eager_step(x, y):
         loss = model(x, y, grad_scale=opt.scale)
         opt.backward(loss)
         opt.step(6e-4)
@@ -427,8 +430,19 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        step(x_dev, y_dev)
+    # one process per GPU: the step is captured in a CUDA graph (fxlm.GraphedStep,
+    # warm-up steps run before capture); data-parallel runs step eagerly
+    graphed = None
+    if world == 1 and not args.no_graph:
+        from fxlm import GraphedStep
+        graphed = GraphedStep(model, opt, x_dev, y_dev, warmup=args.warmup)
+
+        def step(x, y):
+            return graphed()  # x, y already are the graph's static inputs
+    else:
+        step = eager_step
+        for _ in range(args.warmup):
+            step(x_dev, y_dev)
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -444,7 +458,8 @@ def run_ours(args, rank, world, local_rank):
         loss = step(x_dev, y_dev)
     ev1.record()
     torch.cuda.synchronize()
-    launches = _lib.launch_count() - n0
+    launches = (graphed.launches_per_step * args.steps if graphed is not None
+                else _lib.launch_count() - n0)
     clocks = clk.stop()
     barrier()
     t_ms = max_over_ranks(ev0.elapsed_time(ev1))
@@ -457,7 +472,7 @@ def run_ours(args, rank, world, local_rank):
     records = []
     ops.set_gemm_timing(records)
     for _ in range(args.steps):
-        step(x_dev, y_dev)
+        eager_step(x_dev, y_dev)
     torch.cuda.synchronize()
     ops.set_gemm_timing(None)
     barrier()
@@ -471,10 +486,11 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    xin, yin = (graphed.x, graphed.y) if graphed is not None else (x_dev, y_dev)
     for _ in range(args.steps):
-        x_dev.copy_(x_host, non_blocking=True)
-        y_dev.copy_(y_host, non_blocking=True)
-        loss = step(x_dev, y_dev)
+        xin.copy_(x_host, non_blocking=True)
+        yin.copy_(y_host, non_blocking=True)
+        loss = step(xin, yin)
         _ = loss.item()
     e1.record()
     torch.cuda.synchronize()
@@ -497,6 +513,7 @@ def run_ours(args, rank, world, local_rank):
             "data": "synthetic Zipf(1.1) tokens, seed 3 + rank; reference init (seed 3)",
             "config": {"workload": WORKLOAD, "global_batch": MB * world, "seq_len": SEQ,
                        "parallelism": f"dp{world}", "model": "GPT d768x12L tied, V32768",
+                       "step": "CUDA graph replay" if graphed is not None else "eager",
                        "l2": "no flush: one step moves several GB (> 126 MB L2)"},
             "e2e": e2e,
             "gpu_launches": launches,
@@ -529,6 +546,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-attn", action="store_true", help="skip the attention microbench")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="run the 1-GPU step eagerly instead of replaying a captured CUDA graph")
     ap.add_argument("--micro", default=None,
                     help="per-kernel microbenchmarks instead of the step: all or a comma list "
                          "of gemm,attn,rmsnorm,ce,adamw")

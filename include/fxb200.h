@@ -152,13 +152,16 @@ int fxb_adamw_final(float* scratch, int32_t* flags, int32_t* step, float* found_
  *   when the step is skipped, so the buffer is ready for the next backward).
  * Segments: seg_end[i] (exclusive, device int64, ascending, multiples of 8) and
  * seg_wd[i] (device int32), nseg <= 1024.
+ * lr_dev: when non-NULL the learning rate is read from this device fp32
+ * scalar and `lr` is ignored, so a captured CUDA graph can follow a schedule
+ * (the host updates the scalar between replays).
  * Replaces adamw_update (ml/fxlm/kernels/optim.hip:96-162). */
 int fxb_adamw_update(int32_t gdtype, int32_t pdtype, const void* grad, float* master,
                      float* m, float* v, void* param, int64_t n, const int64_t* seg_end,
                      const int32_t* seg_wd, int32_t nseg, const float* scratch,
                      const float* found_inf, const float* scale, const int32_t* step,
-                     float lr, float beta1, float beta2, float eps, float weight_decay,
-                     void* stream);
+                     float lr, const float* lr_dev, float beta1, float beta2, float eps,
+                     float weight_decay, void* stream);
 
 /* ------------------------------------------------------------------ GEMM */
 

@@ -6,29 +6,31 @@
 // params, m/v update, bias correction with powf, fp32 master + low-precision
 // copy). The reference walks a list of per-parameter gradient tensors; here
 // gradients live in one flat buffer with the same offsets as the master, so
-// each kernel is a single grid-stride pass of 16-byte vectors, and the
+// each kernel is a single grid-stride pass over 4-element vectors, and the
 // per-parameter weight-decay flag becomes a sorted segment table.
 #include "common.cuh"
 #include "internal.h"
 
 namespace {
 
-template <typename G> FXB_DEV void load8(const G* p, float* f) {
+// Four consecutive elements per access (16 bytes fp32, 8 bytes 16-bit): the
+// 32 lanes of a warp touch 32 consecutive 4-element units, so every warp
+// instruction covers one contiguous 512 (or 256) byte span.
+template <typename G> FXB_DEV void load4(const G* p, float* f) {
   if constexpr (sizeof(G) == 4) {
     float4 a = *reinterpret_cast<const float4*>(p);
-    float4 b = *reinterpret_cast<const float4*>(p + 4);
     f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
   } else {
-    unpack8<G>(*reinterpret_cast<const uint4*>(p), f);
+    uint2 u = *reinterpret_cast<const uint2*>(p);
+    float2 a = unpack2<G>(u.x), b = unpack2<G>(u.y);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
   }
 }
-template <typename P> FXB_DEV void store8(P* p, const float* f) {
+template <typename P> FXB_DEV void store4(P* p, const float* f) {
   if constexpr (sizeof(P) == 4) {
     *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
-    *reinterpret_cast<float4*>(p + 4) = make_float4(f[4], f[5], f[6], f[7]);
   } else {
-    *reinterpret_cast<uint4*>(p) = pack8<P>(f);
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack2<P>(f[0], f[1]), pack2<P>(f[2], f[3]));
   }
 }
 
@@ -38,20 +40,33 @@ adamw_sumsq_kernel(const G* __restrict__ g, int64_t n, float* __restrict__ scrat
                    int* __restrict__ flags) {
   float ss = 0.f;
   int bad = 0;
-  const int64_t ngroups = n >> 3;
+  const int64_t nunits = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += stride) {
-    float f[8];
-    load8<G>(g + i * 8, f);
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < nunits; i += 4 * stride) {  // four loads in flight
+    float f[4][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int k = 0; k < 4; ++k) load4<G>(g + (i + k * stride) * 4, f[k]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ss += f[k][j] * f[k][j];
+        bad |= !isfinite(f[k][j]);
+      }
+  }
+  for (; i < nunits; i += stride) {
+    float f[4];
+    load4<G>(g + i * 4, f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
       ss += f[j] * f[j];
       bad |= !isfinite(f[j]);
     }
   }
-  // tail (n not a multiple of 8)
+  // tail (n not a multiple of 4)
   if (blockIdx.x == 0) {
-    for (int64_t i = ngroups * 8 + threadIdx.x; i < n; i += blockDim.x) {
+    for (int64_t i = nunits * 4 + threadIdx.x; i < n; i += blockDim.x) {
       float f = to_f<G>(g[i]);
       ss += f * f;
       bad |= !isfinite(f);
@@ -99,16 +114,16 @@ adamw_update_kernel(G* __restrict__ g, float* __restrict__ master, float* __rest
                     float* __restrict__ v, P* __restrict__ p, int64_t n,
                     const int64_t* __restrict__ seg_end, const int* __restrict__ seg_wd, int nseg,
                     const float* __restrict__ scratch, const float* __restrict__ found_inf,
-                    const float* __restrict__ scale_p, const int* __restrict__ step_p, float lr,
+                    const float* __restrict__ scale_p, const int* __restrict__ step_p, float lr_arg,
+                    const float* __restrict__ lr_dev,
                     float b1, float b2, float eps, float wd) {
-  const int64_t ngroups = n >> 3;
+  const int64_t nunits = n >> 2;  // n % 8 == 0
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
   if (*found_inf != 0.f) {
     // step skipped: master / m / v untouched, the gradient is still consumed
-    for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < ngroups; gi += stride) {
-      const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      store8<G>(g + gi * 8, z);
-    }
+    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < nunits; u += stride)
+      store4<G>(g + u * 4, zero4);
     return;
   }
   __shared__ int64_t s_end[kMaxSeg];
@@ -124,21 +139,19 @@ adamw_update_kernel(G* __restrict__ g, float* __restrict__ master, float* __rest
   const float bc2 = 1.f - powf(b2, (float)step);
   const float inv_bc1 = 1.f / bc1, inv_bc2 = 1.f / bc2;
   const float b1c = 1.f - b1, b2c = 1.f - b2;
+  const float lr = lr_dev ? *lr_dev : lr_arg;
   const float lrwd = lr * wd;
-  const float zero8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  // Each thread walks its 8-element groups in increasing order, so the
-  // segment cursor only moves forward. Two groups per iteration keep more
-  // loads in flight.
+  // Each thread walks its units in increasing order, so the segment cursor
+  // only moves forward (segment boundaries are multiples of 8 elements). Two
+  // units per iteration: all eight loads are issued before any arithmetic.
   int seg = 0;
-  auto update8 = [&](int64_t e0, bool wd_on) {
-    float gv[8], mw[8], mv[8], vv[8];
-    load8<G>(g + e0, gv);
-    load8<float>(master + e0, mw);
-    load8<float>(m + e0, mv);
-    load8<float>(v + e0, vv);
-    store8<G>(g + e0, zero8);  // gradient consumed
+  auto wd_of = [&](int64_t e0) {
+    while (seg < nseg - 1 && s_end[seg] <= e0) ++seg;
+    return s_wd[seg] != 0;
+  };
+  auto update4 = [&](int64_t e0, bool wd_on, float* gv, float* mw, float* mv, float* vv) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 4; ++j) {
       const float gg = gv[j] * inv;
       float w = mw[j];
       if (wd_on) w -= lrwd * w;
@@ -149,57 +162,61 @@ adamw_update_kernel(G* __restrict__ g, float* __restrict__ master, float* __rest
       w -= lr * (a * inv_bc1) / (sqrtf(b * inv_bc2) + eps);
       mw[j] = w;
     }
-    store8<float>(master + e0, mw);
-    store8<float>(m + e0, mv);
-    store8<float>(v + e0, vv);
-    store8<P>(p + e0, mw);
+    store4<G>(g + e0, zero4);  // gradient consumed
+    store4<float>(master + e0, mw);
+    store4<float>(m + e0, mv);
+    store4<float>(v + e0, vv);
+    store4<P>(p + e0, mw);
   };
-  for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < ngroups; gi += 2 * stride) {
-    const int64_t e0 = gi * 8;
-    while (seg < nseg - 1 && s_end[seg] <= e0) ++seg;
-    const bool wd0 = s_wd[seg] != 0;
-    const int64_t gi1 = gi + stride;
-    if (gi1 < ngroups) {
-      const int64_t e1 = gi1 * 8;
-      int seg1 = seg;
-      while (seg1 < nseg - 1 && s_end[seg1] <= e1) ++seg1;
-      update8(e0, wd0);
-      update8(e1, s_wd[seg1] != 0);
-      seg = seg1;
-    } else {
-      update8(e0, wd0);
-    }
+  int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; u + stride < nunits; u += 2 * stride) {
+    const int64_t e0 = u * 4, e1 = (u + stride) * 4;
+    float g0[4], w0[4], m0[4], v0[4], g1[4], w1[4], m1[4], v1[4];
+    load4<G>(g + e0, g0); load4<float>(master + e0, w0); load4<float>(m + e0, m0); load4<float>(v + e0, v0);
+    load4<G>(g + e1, g1); load4<float>(master + e1, w1); load4<float>(m + e1, m1); load4<float>(v + e1, v1);
+    const bool wd0 = wd_of(e0);
+    update4(e0, wd0, g0, w0, m0, v0);
+    const bool wd1 = wd_of(e1);
+    update4(e1, wd1, g1, w1, m1, v1);
+  }
+  if (u < nunits) {
+    const int64_t e0 = u * 4;
+    float g0[4], w0[4], m0[4], v0[4];
+    load4<G>(g + e0, g0); load4<float>(master + e0, w0); load4<float>(m + e0, m0); load4<float>(v + e0, v0);
+    update4(e0, wd_of(e0), g0, w0, m0, v0);
   }
 }
 
 template <typename G, typename P>
 int launch_update(const void* g, float* master, float* m, float* v, void* p, int64_t n,
                   const int64_t* se, const int* sw, int nseg, const float* scratch,
-                  const float* fi, const float* sc, const int* stp, float lr, float b1, float b2,
+                  const float* fi, const float* sc, const int* stp, float lr, const float* lrd,
+                  float b1, float b2,
                   float eps, float wd, cudaStream_t st) {
-  int64_t groups = n >> 3;
-  int64_t want = (groups + 255) / 256;
+  int64_t units = n >> 2;
+  int64_t want = (units + 255) / 256;
   int64_t cap = (int64_t)fxb::num_sms() * 8;
   int blocks = (int)(want < cap ? want : cap);
   if (blocks < 1) blocks = 1;
   adamw_update_kernel<G, P><<<blocks, 256, 0, st>>>(static_cast<G*>(const_cast<void*>(g)), master, m, v,
                                                     static_cast<P*>(p), n, se, sw, nseg, scratch,
-                                                    fi, sc, stp, lr, b1, b2, eps, wd);
+                                                    fi, sc, stp, lr, lrd, b1, b2, eps, wd);
   return fxb::check_launch("adamw_update");
 }
 
 template <typename G>
 int dispatch_update_p(int32_t pdtype, const void* g, float* master, float* m, float* v, void* p,
                       int64_t n, const int64_t* se, const int* sw, int nseg, const float* scratch,
-                      const float* fi, const float* sc, const int* stp, float lr, float b1,
+                      const float* fi, const float* sc, const int* stp, float lr, const float* lrd,
+                      float b1,
                       float b2, float eps, float wd, cudaStream_t st) {
   switch (pdtype) {
     case FXB_DTYPE_BF16:
-      return launch_update<G, __nv_bfloat16>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, b1, b2, eps, wd, st);
+      return launch_update<G, __nv_bfloat16>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, lrd, b1, b2, eps, wd, st);
     case FXB_DTYPE_F16:
-      return launch_update<G, __half>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, b1, b2, eps, wd, st);
+      return launch_update<G, __half>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, lrd, b1, b2, eps, wd, st);
     default:
-      return launch_update<G, float>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, b1, b2, eps, wd, st);
+      return launch_update<G, float>(g, master, m, v, p, n, se, sw, nseg, scratch, fi, sc, stp, lr, lrd, b1, b2, eps, wd, st);
   }
 }
 
@@ -214,7 +231,7 @@ int fxb_adamw_sumsq(int32_t gdtype, const void* grad, int64_t n, float* scratch,
   if (n == 0) return FXB_OK;
   if (!fxb::aligned16(grad)) return fxb::set_error(FXB_EINVAL, "adamw_sumsq: grad not 16-byte aligned");
   cudaStream_t st = fxb::as_stream(stream);
-  int64_t want = ((n >> 3) + 255) / 256;
+  int64_t want = ((n >> 2) + 255) / 256;
   int64_t cap = (int64_t)fxb::num_sms() * 8;
   int blocks = (int)(want < cap ? want : cap);
   if (blocks < 1) blocks = 1;
@@ -244,6 +261,7 @@ int fxb_adamw_update(int32_t gdtype, int32_t pdtype, const void* grad, float* ma
                      float* v, void* param, int64_t n, const int64_t* seg_end,
                      const int32_t* seg_wd, int32_t nseg, const float* scratch,
                      const float* found_inf, const float* scale, const int32_t* step, float lr,
+                     const float* lr_dev,
                      float beta1, float beta2, float eps, float weight_decay, void* stream) {
   if (fxb::dtype_size(gdtype) == 0 || fxb::dtype_size(pdtype) == 0)
     return fxb::set_error(FXB_EINVAL, "adamw_update: bad dtype");
@@ -260,11 +278,11 @@ int fxb_adamw_update(int32_t gdtype, int32_t pdtype, const void* grad, float* ma
   cudaStream_t st = fxb::as_stream(stream);
   switch (gdtype) {
     case FXB_DTYPE_BF16:
-      return dispatch_update_p<__nv_bfloat16>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, beta1, beta2, eps, weight_decay, st);
+      return dispatch_update_p<__nv_bfloat16>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, lr_dev, beta1, beta2, eps, weight_decay, st);
     case FXB_DTYPE_F16:
-      return dispatch_update_p<__half>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, beta1, beta2, eps, weight_decay, st);
+      return dispatch_update_p<__half>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, lr_dev, beta1, beta2, eps, weight_decay, st);
     default:
-      return dispatch_update_p<float>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, beta1, beta2, eps, weight_decay, st);
+      return dispatch_update_p<float>(pdtype, grad, master, m, v, param, n, seg_end, seg_wd, nseg, scratch, found_inf, scale, step, lr, lr_dev, beta1, beta2, eps, weight_decay, st);
   }
 }
 

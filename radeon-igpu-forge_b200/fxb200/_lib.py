@@ -82,8 +82,8 @@ SIGNATURES = {
     "fxb_adamw_sumsq": (ctypes.c_int, [_i32, _vp, _i64, _vp, _vp, _vp]),
     "fxb_adamw_final": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _f32, _vp]),
     "fxb_adamw_update": (ctypes.c_int, [_i32, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp,
-                                        _i32, _vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32,
-                                        _f32, _vp]),
+                                        _i32, _vp, _vp, _vp, _vp, _f32, _vp, _f32, _f32,
+                                        _f32, _f32, _vp]),
     "fxb_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _vp]),
     "fxb_gemm_plan": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.POINTER(_i32),
                                      ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),

@@ -20,6 +20,7 @@ __all__ = [
     "FlatAdamW",
     "GPT",
     "GPTConfig",
+    "GraphedStep",
 ]
 
 
@@ -42,6 +43,9 @@ def __getattr__(name):
     if name == "FlatAdamW":
         from .optim import FlatAdamW
         return FlatAdamW
+    if name == "GraphedStep":
+        from .graph import GraphedStep
+        return GraphedStep
     if name in ("GPT", "GPTConfig"):
         from . import model as _m
         return getattr(_m, name)

@@ -1,0 +1,73 @@
+"""fxlm.graph: one whole training step (forward, backward, FlatAdamW update)
+captured in a CUDA graph and replayed.
+
+The reference runs its step eagerly from Python (ml/fxlm/train_lm.py training
+loop; no compiler on its hot path). A step of the B200 build is ~300 kernel
+launches, each a ctypes call; at B200 speeds the host then becomes the
+bound. Capturing the step once and replaying it removes the per-launch host
+work without changing a single kernel or its arguments.
+
+    step = GraphedStep(model, opt, x_example, y_example)   # runs `warmup` real steps, then captures
+    loss = step(x, y, lr=3e-4)    # copies the batch into the static inputs, replays; loss stays on device
+
+Conditions (checked where cheap): fixed batch shape; the optimizer is a
+FlatAdamW whose gradient buffer is consumed by its update (so no zeroing op
+is needed between replays); the learning rate is read from `opt.lr_dev`, a
+device scalar written before each replay; no data-parallel hooks (the
+NCCL bucket path runs eagerly). The warm-up steps before capture are real
+training steps (they also trigger every lazy initialisation: library load,
+tensor-map encoders, shared-memory attributes).
+"""
+import torch
+
+from fxb200 import _lib
+
+
+class GraphedStep:
+    def __init__(self, model, opt, x_example, y_example, warmup=3):
+        if getattr(opt, "pre_step_hooks", None):
+            raise ValueError("GraphedStep: optimizer has pre-step hooks (data parallel); "
+                             "run the step eagerly")
+        if warmup < 1:
+            raise ValueError("GraphedStep: warmup >= 1 (lazy initialisation must happen "
+                             "before capture)")
+        self.model, self.opt = model, opt
+        dev = opt.grad.device
+        self.x = torch.empty_like(x_example, device=dev)
+        self.y = torch.empty_like(y_example, device=dev)
+        self.x.copy_(x_example)
+        self.y.copy_(y_example)
+        if opt.lr_dev is None:
+            opt.lr_dev = torch.full((), float(opt.lr), device=dev, dtype=torch.float32)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = _lib.launch_count()
+        with torch.cuda.graph(self.graph):
+            self.loss = self._step()
+        # kernels of this library inside one replay
+        self.launches_per_step = _lib.launch_count() - n0
+
+    def _step(self):
+        loss = self.model(self.x, self.y, grad_scale=self.opt.scale)
+        self.opt.backward(loss)
+        self.opt.step()
+        self.opt.zero_grad()
+        return loss.detach()
+
+    def __call__(self, x=None, y=None, lr=None):
+        """Copy (x, y) into the static inputs (when given), set the learning
+        rate (when given) and replay; returns the step's loss (device)."""
+        if x is not None:
+            self.x.copy_(x, non_blocking=True)
+        if y is not None:
+            self.y.copy_(y, non_blocking=True)
+        if lr is not None:
+            self.opt.lr_dev.fill_(float(lr))
+        self.graph.replay()
+        return self.loss

@@ -92,6 +92,10 @@ class FlatAdamW:
         self._norm = torch.zeros((), device=dev, dtype=torch.float32)
         self.scale = torch.full((), float(init_scale), device=dev, dtype=torch.float32)
         self._growth = torch.zeros((), device=dev, dtype=torch.int32)
+        # optional fp32 device scalar holding the learning rate; when set, the
+        # update reads it instead of the `lr` argument (a captured CUDA graph
+        # follows a schedule by writing this scalar between replays)
+        self.lr_dev = None
         self._grad_dirty = False
         # hooks run after the gradient is complete and before the update
         # (data-parallel reduction of self.grad registers one here)
@@ -133,6 +137,7 @@ class FlatAdamW:
                   P(self.master), P(self.m), P(self.v), P(self.flat16), self.numel,
                   P(self._seg_end), P(self._seg_wd), len(self._info), P(self.scratch),
                   P(self._found_inf), P(self.scale), P(self._step_ctr), lr_v,
+                  P(self.lr_dev) if self.lr_dev is not None else None,
                   float(self.betas[0]), float(self.betas[1]), float(self.eps),
                   float(self.weight_decay), st)
         torch._amp_update_scale_(self.scale, self._growth, self._found_inf, 2.0, 0.5,

@@ -64,7 +64,7 @@ def test_einval_paths_without_gpu(lib):
     assert rc == -1 and "ce" in _lib.last_error()
     # AdamW: n not a multiple of 8
     rc = lib.fxb_adamw_update(0, 2, None, None, None, None, None, 9, None, None, 1, None, None,
-                              None, None, 1e-3, 0.9, 0.95, 1e-8, 0.1, None)
+                              None, None, 1e-3, None, 0.9, 0.95, 1e-8, 0.1, None)
     assert rc == -1 and "multiple of 8" in _lib.last_error()
     # GEMM: N not a multiple of 8
     a = _lib.GemmArgs()

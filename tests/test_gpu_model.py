@@ -317,3 +317,39 @@ def test_gpt_d768_first_step_loss(dev):
     gn = opt.grad.double().norm().item()
     assert abs(loss.item() - ref["loss"]) <= 1e-3 * ref["loss"], (loss.item(), ref["loss"])
     assert abs(gn - ref["grad_norm"]) <= 2e-2 * ref["grad_norm"], (gn, ref["grad_norm"])
+
+
+def test_graphed_step_matches_eager(dev):
+    """fxlm.GraphedStep (one captured training step, replayed) follows the
+    eager step: same losses over a fresh batch per step and the same master
+    weights, including a learning-rate change between replays."""
+    from fxlm import FlatAdamW, GraphedStep
+    from oracle import gpt as og
+    batches = [og.zipf_tokens(256, 32, 256, seed=500 + s) for s in range(6)]
+    lrs = [3e-4, 3e-4, 3e-4, 1e-4, 1e-4, 5e-5]
+
+    def fresh():
+        m = _our_gpt(CFG1, 1e-5, 0, dev)
+        m.load_state_dict(og.init_state(CFG1, 0))
+        return m, FlatAdamW(m, lr=3e-4, init_scale=1.0)
+
+    me, oe = fresh()
+    eager = []
+    for (x, y), lr in zip(batches, lrs):
+        loss = me(x.to(dev), y.to(dev), grad_scale=oe.scale)
+        oe.backward(loss)
+        oe.step(lr=lr)
+        oe.zero_grad()
+        eager.append(float(loss.detach()))
+
+    mg, og_ = fresh()
+    x0, y0 = batches[0]
+    g = GraphedStep(mg, og_, x0.to(dev), y0.to(dev), warmup=1)  # step 0 runs eagerly here
+    assert g.launches_per_step > 0
+    graphed = []
+    for (x, y), lr in zip(batches[1:], lrs[1:]):
+        graphed.append(float(g(x.to(dev), y.to(dev), lr=lr)))
+    for a, b in zip(graphed, eager[1:]):
+        assert abs(a - b) <= 1e-3 * abs(b), (graphed, eager[1:])
+    r = rel(og_.master, oe.master)
+    assert r < 1e-2, f"master rel diff {r:.3e}"
