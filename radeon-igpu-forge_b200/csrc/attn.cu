@@ -28,6 +28,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int TILE = 128;
 constexpr int kFwdThreads = 320;  // warps 0-7 softmax, 8 MMA, 9 TMA (forward and backward)
+// Forward pipeline depths: K/V ring stages and Q buffers (shared memory:
+// (QN + 2 KS) DH-wide tiles + P + exchange)
+template <int DH> constexpr int fwd_kv_stages() { return DH <= 64 ? 4 : 2; }
+template <int DH> constexpr int fwd_q_bufs() { return DH <= 64 ? 2 : 1; }
 
 struct FwdParams {
   int B, T, H, nqt, nkt, causal;
@@ -60,12 +64,6 @@ FXB_DEV uint32_t sw128_offset(int r, int chunk) {
   return (uint32_t)(blk * 16384 + r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-template <typename T> FXB_DEV uint32_t pack2(float a, float b) {
-  T lo = from_f<T>(a), hi = from_f<T>(b);
-  return (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) |
-         ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
-}
-
 // K-major operand tile [128 rows][D] stored as D/64 swizzled column blocks
 FXB_DEV uint64_t kmajor_desc(uint32_t base, int kk) {
   return umma_desc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
@@ -82,6 +80,14 @@ FXB_DEV float ex2_ftz(float x) {
   return y;
 }
 
+// Persistent kernel: each CTA walks work items (query tile, batch*head) from
+// blockIdx.x in steps of gridDim.x; items are numbered heaviest first for
+// causal attention (the last query tiles see the most key tiles). Tensor
+// memory, barriers and tensor maps are set up once per CTA, Q is
+// double-buffered and the K/V ring and S buffers run on counters that
+// continue across items, so the next item's loads and first S = Q K^T
+// overlap the current item's final P.V and output store.
+//
 // Warp roles (320 threads): warps 0-7 softmax (warp w owns TMEM lane quarter
 // w & 3, i.e. 32 query rows, and column half w >> 2 of every S tile: 64 of the
 // 128 keys, and DH/2 of the output columns), warp 8 MMA issuer, warp 9 TMA.
@@ -93,43 +99,53 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   constexpr int QB = TILE * DH * 2;  // bytes of one [128][DH] tile
   constexpr int NBOX = DH / 64;
   constexpr int OC = DH / 2;         // output columns per thread
+  constexpr int KS = fwd_kv_stages<DH>();
+  constexpr int QN = fwd_q_bufs<DH>();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t sQ = base;
-  const uint32_t sK = sQ + QB;          // 2 stages
-  const uint32_t sV = sK + 2 * QB;      // 2 stages
-  const uint32_t sP = sV + 2 * QB;      // [128][128] 16-bit
+  const uint32_t sQ = base;             // QN buffers
+  const uint32_t sK = sQ + QN * QB;     // KS stages
+  const uint32_t sV = sK + KS * QB;     // KS stages
+  const uint32_t sP = sV + KS * QB;     // [128][128] 16-bit
   const uint32_t sX = sP + 32768;       // row-statistics exchange: [2 buf][2 half][128] fp32
   float* xch = reinterpret_cast<float*>(gbase + (sX - base));
   const uint32_t bars = sX + 2048;
-  const uint32_t q_full = bars;
-  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
-  auto v_full = [&](int s) { return bars + 8u * (3 + s); };
-  auto kv_empty = [&](int s) { return bars + 8u * (5 + s); };
-  auto s_full = [&](int s) { return bars + 8u * (7 + s); };
-  auto s_empty = [&](int s) { return bars + 8u * (9 + s); };
-  const uint32_t p_full = bars + 8u * 11;
-  const uint32_t pv_full = bars + 8u * 12;
-  const uint32_t final_bar = bars + 8u * 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * 14);
+  auto q_full = [&](int s) { return bars + 8u * s; };
+  auto q_empty = [&](int s) { return bars + 8u * (2 + s); };
+  auto k_full = [&](int s) { return bars + 8u * (4 + s); };
+  auto v_full = [&](int s) { return bars + 8u * (4 + KS + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (4 + 2 * KS + s); };
+  auto s_full = [&](int s) { return bars + 8u * (4 + 3 * KS + s); };
+  auto s_empty = [&](int s) { return bars + 8u * (6 + 3 * KS + s); };
+  const uint32_t p_full = bars + 8u * (8 + 3 * KS);
+  const uint32_t pv_full = bars + 8u * (9 + 3 * KS);
+  const uint32_t final_bar = bars + 8u * (10 + 3 * KS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (11 + 3 * KS));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = (p.causal ? (p.nqt - 1 - (int)blockIdx.x) : (int)blockIdx.x);
-  const int bh = blockIdx.y;
-  const int b = bh / p.H, h = bh - b * p.H;
-  const int q0 = qt * TILE;
-  const int n_kv = p.causal ? min(qt + 1, p.nkt) : p.nkt;
+  const int BH = p.B * p.H;
+  const int n_items = p.nqt * BH;
+  // item -> (query tile, batch*head), heaviest query tiles first when causal
+  auto item_coords = [&](int w, int& qt, int& bh, int& n_kv) {
+    const int t = w / BH;
+    bh = w - t * BH;
+    qt = p.causal ? (p.nqt - 1 - t) : t;
+    n_kv = p.causal ? min(qt + 1, p.nkt) : p.nkt;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(q_full(s), 1);
+      mbar_init(q_empty(s), 1);
+      mbar_init(s_full(s), 1);
+      mbar_init(s_empty(s), 256);
+    }
+    for (int s = 0; s < KS; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(v_full(s), 1);
       mbar_init(kv_empty(s), 1);
-      mbar_init(s_full(s), 1);
-      mbar_init(s_empty(s), 256);
     }
     mbar_init(p_full, 256);
     mbar_init(pv_full, 1);
@@ -153,27 +169,40 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_expect_tx(q_full, QB);
-#pragma unroll
-      for (int c = 0; c < NBOX; ++c) tma_load_4d(sQ + c * 16384, &tmQ, q_full, 64 * c, q0, h, b);
-      int armed = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(kv_empty(st), ((j >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
-        mbar_expect_tx(k_full(st), QB);
+      bool ok = true;
+      int t = 0;   // K/V tiles issued (all items)
+      int it = 0;  // items of this CTA
+      int q_armed = 0;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+        int qt, bh, n_kv;
+        item_coords(w, qt, bh, n_kv);
+        const int b = bh / p.H, h = bh - b * p.H;
+        const int qb = it % QN;
+        if (!mbar_wait(q_empty(qb), ((it / QN) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        mbar_expect_tx(q_full(qb), QB);
 #pragma unroll
         for (int c = 0; c < NBOX; ++c)
-          tma_load_4d(sK + st * QB + c * 16384, &tmK, k_full(st), 64 * c, j * TILE, h, b);
-        mbar_expect_tx(v_full(st), QB);
+          tma_load_4d(sQ + qb * QB + c * 16384, &tmQ, q_full(qb), 64 * c, qt * TILE, h, b);
+        q_armed = it + 1;
+        for (int j = 0; j < n_kv; ++j, ++t) {
+          const int st = t % KS;
+          if (!mbar_wait(kv_empty(st), ((t / KS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          mbar_expect_tx(k_full(st), QB);
 #pragma unroll
-        for (int c = 0; c < NBOX; ++c)
-          tma_load_4d(sV + st * QB + c * 16384, &tmV, v_full(st), 64 * c, j * TILE, h, b);
-        armed = j + 1;
+          for (int c = 0; c < NBOX; ++c)
+            tma_load_4d(sK + st * QB + c * 16384, &tmK, k_full(st), 64 * c, j * TILE, h, b);
+          mbar_expect_tx(v_full(st), QB);
+#pragma unroll
+          for (int c = 0; c < NBOX; ++c)
+            tma_load_4d(sV + st * QB + c * 16384, &tmV, v_full(st), 64 * c, j * TILE, h, b);
+        }
       }
-      mbar_wait(q_full, 0, p.err, FXB_DERR_ATTN_WAIT);
-      for (int j = (armed > 2 ? armed - 2 : 0); j < armed; ++j) {
-        mbar_wait(k_full(j & 1), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
-        mbar_wait(v_full(j & 1), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      // drain: every copy issued has landed before shared memory goes away
+      for (int i = (q_armed > QN ? q_armed - QN : 0); i < q_armed; ++i)
+        mbar_wait(q_full(i % QN), (i / QN) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      for (int u = (t > KS ? t - KS : 0); u < t; ++u) {
+        mbar_wait(k_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+        mbar_wait(v_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
       }
     }
     __syncwarp();
@@ -182,30 +211,43 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     if (lane == 0) {
       constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
       constexpr uint32_t IPV = umma_idesc_f16(FMT, 0, 1, TILE, DH);
-      bool ok = mbar_wait(q_full, 0, p.err, FXB_DERR_ATTN_WAIT);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(k_full(st), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
-        if (!mbar_wait(s_empty(st), ((j >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+      bool ok = true;
+      int ts = 0;  // S tiles issued (all items)
+      int tp = 0;  // P.V products issued (all items)
+      int it = 0;
+      // S = Q K^T of tile (item `it`, global tile ts) into S buffer ts & 1
+      auto issue_s = [&](uint32_t q_s) -> bool {
+        const int st = ts % KS, sb = ts & 1;
+        if (!mbar_wait(k_full(st), (ts / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(s_empty(sb), ((ts >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk)
-          umma_f16(tS + st * TILE, kmajor_desc(sQ, kk), kmajor_desc(sK + st * QB, kk), IS, kk > 0);
-        umma_commit(s_full(st));
+          umma_f16(tS + sb * TILE, kmajor_desc(q_s, kk), kmajor_desc(sK + st * QB, kk), IS, kk > 0);
+        umma_commit(s_full(sb));
+        ++ts;
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
-        const int st = j & 1;
-        if (!mbar_wait(p_full, j & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-        if (!mbar_wait(v_full(st), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-        tc_fence_after();
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+        int qt, bh, n_kv;
+        item_coords(w, qt, bh, n_kv);
+        const int qb = it % QN;
+        const uint32_t q_s = sQ + qb * QB;
+        if (!mbar_wait(q_full(qb), (it / QN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        if (!issue_s(q_s)) { ok = false; break; }
+        for (int j = 0; j < n_kv && ok; ++j, ++tp) {
+          if (j + 1 < n_kv && !issue_s(q_s)) { ok = false; break; }
+          if (j + 1 == n_kv) umma_commit(q_empty(qb));  // last S of the item read Q
+          const int st = tp % KS;
+          if (!mbar_wait(p_full, tp & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          if (!mbar_wait(v_full(st), (tp / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < TILE / 16; ++kk)
-          umma_f16(tPV, kmajor_desc(sP, kk), mnmajor_desc(sV + st * QB, kk), IPV, kk > 0);
-        umma_commit(pv_full);
-        umma_commit(kv_empty(st));
+          for (int kk = 0; kk < TILE / 16; ++kk)
+            umma_f16(tPV, kmajor_desc(sP, kk), mnmajor_desc(sV + st * QB, kk), IPV, kk > 0);
+          umma_commit(pv_full);
+          umma_commit(kv_empty(st));
+        }
       }
       umma_commit(final_bar);
       mbar_wait(final_bar, 0, p.err, FXB_DERR_ATTN_WAIT);
@@ -215,57 +257,98 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     // ------------------------------------------------ softmax warps 0..7
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;  // query row within the tile
-    const int q = q0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int col0 = half * 64;         // this thread's key columns within a tile
-    float o[OC];
-#pragma unroll
-    for (int d = 0; d < OC; ++d) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f, a_prev = 0.f;
-    bool ok = true;
     uint8_t* pbase = gbase + (sP - base);
+    bool ok = true;
+    int t = 0;  // tiles consumed (all items)
     // After a failed (timed-out) wait a thread keeps stepping through the
     // tiles without waiting or computing, so that both warps of a pair always
     // meet at the same named barriers.
-    for (int j = 0; j < n_kv; ++j) {
-      const int st = j & 1;
-      if (ok && !mbar_wait(s_full(st), (j >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) ok = false;
-      const int kv0 = j * TILE + col0;
-      float sv[64];
-      float mx = -INFINITY;
-      if (ok) {
-        tc_fence_after();
-        uint32_t sr[64];
-        tmem_ld32(tS + st * TILE + lane_off + col0, sr);
-        tmem_ld32(tS + st * TILE + lane_off + col0 + 32, sr + 32);
-        tmem_wait_ld();
-        const bool need_mask = (kv0 + 64 > p.T) || (p.causal && kv0 + 64 > q0);
-        if (need_mask) {
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+      int qt, bh, n_kv;
+      item_coords(w, qt, bh, n_kv);
+      const int q0 = qt * TILE;
+      const int q = q0 + r;
+      float o[OC];
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const int col = kv0 + i;
-            sv[i] = (col >= p.T || (p.causal && col > q)) ? -INFINITY : __uint_as_float(sr[i]);
-            mx = fmaxf(mx, sv[i]);
-          }
-        } else {
+      for (int d = 0; d < OC; ++d) o[d] = 0.f;
+      float m = -INFINITY, l = 0.f, a_prev = 0.f;
+      for (int j = 0; j < n_kv; ++j, ++t) {
+        const int sb = t & 1;
+        if (ok && !mbar_wait(s_full(sb), (t >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) ok = false;
+        const int kv0 = j * TILE + col0;
+        float sv[64];
+        float mx = -INFINITY;
+        if (ok) {
+          tc_fence_after();
+          uint32_t sr[64];
+          tmem_ld32(tS + sb * TILE + lane_off + col0, sr);
+          tmem_ld32(tS + sb * TILE + lane_off + col0 + 32, sr + 32);
+          tmem_wait_ld();
+          const bool need_mask = (kv0 + 64 > p.T) || (p.causal && kv0 + 64 > q0);
+          if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            sv[i] = __uint_as_float(sr[i]);
-            mx = fmaxf(mx, sv[i]);
+            for (int i = 0; i < 64; ++i) {
+              const int col = kv0 + i;
+              sv[i] = (col >= p.T || (p.causal && col > q)) ? -INFINITY : __uint_as_float(sr[i]);
+              mx = fmaxf(mx, sv[i]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+              sv[i] = __uint_as_float(sr[i]);
+              mx = fmaxf(mx, sv[i]);
+            }
           }
         }
+        // exchange the half-row maxima with the partner warp (double-buffered by tile parity)
+        float* xb = xch + (t & 1) * 256;
+        xb[half * 128 + r] = mx;
+        named_bar_sync(1 + quarter, 64);
+        mx = fmaxf(mx, xb[(half ^ 1) * 128 + r]);
+        if (!ok) continue;
+        const float m_new = fmaxf(m, mx * p.scale_log2);
+        const float alpha = ex2_ftz(m - m_new);
+        // P.V of the previous tile is folded in before P is overwritten
+        if (j > 0) {
+          if (!mbar_wait(pv_full, (t - 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; continue; }
+          tc_fence_after();
+          uint32_t pr[OC];
+#pragma unroll
+          for (int c = 0; c < OC / 32; ++c) tmem_ld32(tPV + lane_off + half * OC + c * 32, pr + c * 32);
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d < OC; ++d) o[d] = o[d] * a_prev + __uint_as_float(pr[d]);
+        }
+        // probabilities -> P (16-bit, 128B-swizzled) and the partial row sum
+        float rs = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          float pv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            pv[i] = ex2_ftz(fmaf(sv[8 * u + i], p.scale_log2, -m_new));
+            rs += pv[i];
+          }
+          uint4 wv;
+          wv.x = pack2<T16>(pv[0], pv[1]);
+          wv.y = pack2<T16>(pv[2], pv[3]);
+          wv.z = pack2<T16>(pv[4], pv[5]);
+          wv.w = pack2<T16>(pv[6], pv[7]);
+          *reinterpret_cast<uint4*>(pbase + sw128_offset(r, half * 8 + u)) = wv;
+        }
+        tc_fence_before();
+        mbar_arrive(s_empty(sb));
+        fence_proxy_async_smem();
+        mbar_arrive(p_full);
+        l = l * alpha + rs;
+        m = m_new;
+        a_prev = alpha;
       }
-      // exchange the half-row maxima with the partner warp (double-buffered by tile parity)
-      float* xb = xch + (j & 1) * 256;
-      xb[half * 128 + r] = mx;
-      named_bar_sync(1 + quarter, 64);
-      mx = fmaxf(mx, xb[(half ^ 1) * 128 + r]);
-      if (!ok) continue;
-      const float m_new = fmaxf(m, mx * p.scale_log2);
-      const float alpha = ex2_ftz(m - m_new);
-      // P.V of the previous tile is folded in before P is overwritten
-      if (j > 0) {
-        if (!mbar_wait(pv_full, (j - 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; continue; }
+      const bool done = ok && mbar_wait(pv_full, (t - 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      if (!done) ok = false;
+      if (done) {
         tc_fence_after();
         uint32_t pr[OC];
 #pragma unroll
@@ -274,57 +357,24 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 #pragma unroll
         for (int d = 0; d < OC; ++d) o[d] = o[d] * a_prev + __uint_as_float(pr[d]);
       }
-      // probabilities -> P (16-bit, 128B-swizzled) and the partial row sum
-      float rs = 0.f;
+      // combine the two half-row sums (every softmax thread reaches this barrier)
+      float* xs = xch + 512;
+      xs[half * 128 + r] = l;
+      named_bar_sync(1 + quarter, 64);
+      l += xs[(half ^ 1) * 128 + r];
+      if (done && q < p.T) {
+        const int b = bh / p.H, h = bh - b * p.H;
+        const float inv = 1.f / l;
+        T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh + half * OC;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float pv[8];
+        for (int d = 0; d < OC; d += 8) {
+          float f[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          pv[i] = ex2_ftz(fmaf(sv[8 * u + i], p.scale_log2, -m_new));
-          rs += pv[i];
+          for (int i = 0; i < 8; ++i) f[i] = o[d + i] * inv;
+          *reinterpret_cast<uint4*>(orow + d) = pack8<T16>(f);
         }
-        uint4 w;
-        w.x = pack2<T16>(pv[0], pv[1]);
-        w.y = pack2<T16>(pv[2], pv[3]);
-        w.z = pack2<T16>(pv[4], pv[5]);
-        w.w = pack2<T16>(pv[6], pv[7]);
-        *reinterpret_cast<uint4*>(pbase + sw128_offset(r, half * 8 + u)) = w;
+        if (half == 0) p.lse[(int64_t)bh * p.T + q] = (m + log2f(l)) * kLn2;
       }
-      tc_fence_before();
-      mbar_arrive(s_empty(st));
-      fence_proxy_async_smem();
-      mbar_arrive(p_full);
-      l = l * alpha + rs;
-      m = m_new;
-      a_prev = alpha;
-    }
-    const bool done = ok && mbar_wait(pv_full, (n_kv - 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
-    if (done) {
-      tc_fence_after();
-      uint32_t pr[OC];
-#pragma unroll
-      for (int c = 0; c < OC / 32; ++c) tmem_ld32(tPV + lane_off + half * OC + c * 32, pr + c * 32);
-      tmem_wait_ld();
-#pragma unroll
-      for (int d = 0; d < OC; ++d) o[d] = o[d] * a_prev + __uint_as_float(pr[d]);
-    }
-    // combine the two half-row sums (every softmax thread reaches this barrier)
-    float* xs = xch + 512;
-    xs[half * 128 + r] = l;
-    named_bar_sync(1 + quarter, 64);
-    l += xs[(half ^ 1) * 128 + r];
-    if (done && q < p.T) {
-      const float inv = 1.f / l;
-      T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh + half * OC;
-#pragma unroll
-      for (int d = 0; d < OC; d += 8) {
-        float f[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = o[d + i] * inv;
-        *reinterpret_cast<uint4*>(orow + d) = pack8<T16>(f);
-      }
-      if (half == 0) p.lse[(int64_t)bh * p.T + q] = (m + log2f(l)) * kLn2;
     }
   }
 
@@ -649,10 +699,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 // 228 KB so a second CTA of any TMEM-using kernel can never be co-scheduled.
 constexpr int kOneCtaPerSm = 120 * 1024;
 template <int DH> constexpr int fwd_smem() {
-  return (5 * TILE * DH * 2 + 32768 + 2048 + 1024 + 256) > kOneCtaPerSm
-             ? (5 * TILE * DH * 2 + 32768 + 2048 + 1024 + 256)
+  return ((fwd_q_bufs<DH>() + 2 * fwd_kv_stages<DH>()) * TILE * DH * 2 + 32768 + 2048 + 1024 + 256) >
+                 kOneCtaPerSm
+             ? ((fwd_q_bufs<DH>() + 2 * fwd_kv_stages<DH>()) * TILE * DH * 2 + 32768 + 2048 + 1024 + 256)
              : kOneCtaPerSm;
 }
+static_assert(fwd_smem<64>() <= 232448 && fwd_smem<128>() <= 232448, "forward shared memory");
 constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 2 * 32768 + 2048 + 1024 + 256; }
 
 int make_map4(CUtensorMap* map, int dtype, const void* ptr, int D, int T, int H, int B,
@@ -731,7 +783,8 @@ int launch_fwd(const fxb_attn_args* a, cudaStream_t st) {
     if ((r = set_smem(k, fwd_smem<DH>()))) return r;
     once[dev & 63] = true;
   }
-  dim3 grid(p.nqt, a->B * a->H);
+  const int64_t items = (int64_t)p.nqt * a->B * a->H;
+  const int grid = (int)(items < fxb::num_sms() ? items : fxb::num_sms());
   k<<<grid, kFwdThreads, fwd_smem<DH>(), st>>>(mq, mk, mv, p);
   return fxb::check_launch("attn_fwd");
 }
