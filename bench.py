@@ -65,7 +65,7 @@ def _peaks():
 
 def _gemm_traffic():
     """Average DRAM bytes per GEMM launch of one step, from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "gemm_tc_gpt_d768_step.md")
+    p = os.path.join(ROOT, "profiles", "gemm_tc_gpt_d768_layer.md")
     try:
         with open(p) as f:
             m = re.search(r"avg_dram_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
@@ -283,6 +283,9 @@ def run_micro(args):
             ("bwd dWproj", D, D, T_, True, True, ops.EPI_ACCUM_F32),
             ("bwd dWqkv", 3 * D, D, T_, True, True, ops.EPI_ACCUM_F32),
         ]
+        if args.only:
+            keep = args.only.split(",")
+            shapes = [s for s in shapes if any(k in s[0] for k in keep)]
         tot_f, tot_ms = 0.0, 0.0
         for nm, M, N, K, at, bt, epi in shapes:
             A = (torch.randn(K, M, device=dev) if at else torch.randn(M, K, device=dev)).to(bf)
@@ -552,6 +555,8 @@ def main():
                     help="per-kernel microbenchmarks instead of the step: all or a comma list "
                          "of gemm,attn,rmsnorm,ce,adamw")
     ap.add_argument("--iters", type=int, default=20, help="iterations per microbenchmark")
+    ap.add_argument("--only", default=None,
+                    help="gemm_layer: comma-separated substrings selecting shapes (profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -256,7 +256,8 @@ int fxb_embedding_fwd(int32_t dtype, const int64_t* idx, const void* tok, const 
                       void* out, int64_t B, int64_t T, int32_t D, int64_t V, void* stream);
 
 /* dtok_ws[idx[b,t],:] += dout[b,t,:], dpos_ws[t,:] += dout[b,t,:] (fp32
- * workspaces, zeroed by the caller). Backward of ml/fxlm/model.py:118. */
+ * workspaces, zeroed by the caller, 16-byte aligned; fp32 vector reductions).
+ * Backward of ml/fxlm/model.py:118. */
 int fxb_embedding_bwd(int32_t dtype, const int64_t* idx, const void* dout, float* dtok_ws,
                       float* dpos_ws, int64_t B, int64_t T, int32_t D, int64_t V,
                       void* stream);

@@ -38,6 +38,8 @@ template <typename G>
 __global__ void __launch_bounds__(256)
 adamw_sumsq_kernel(const G* __restrict__ g, int64_t n, float* __restrict__ scratch,
                    int* __restrict__ flags) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   float ss = 0.f;
   int bad = 0;
   const int64_t nunits = n >> 2;
@@ -95,6 +97,8 @@ adamw_sumsq_kernel(const G* __restrict__ g, int64_t n, float* __restrict__ scrat
 
 __global__ void adamw_final_kernel(float* scratch, int* flags, int* step, float* found_inf,
                                    float* norm_out, const float* scale, float max_norm) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   const int bad = (*flags != 0) || !isfinite(scratch[0]);
   *found_inf = bad ? 1.f : 0.f;
@@ -117,6 +121,8 @@ adamw_update_kernel(G* __restrict__ g, float* __restrict__ master, float* __rest
                     const float* __restrict__ scale_p, const int* __restrict__ step_p, float lr_arg,
                     const float* __restrict__ lr_dev,
                     float b1, float b2, float eps, float wd) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   const int64_t nunits = n >> 2;  // n % 8 == 0
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -198,7 +204,7 @@ int launch_update(const void* g, float* master, float* m, float* v, void* p, int
   int64_t cap = (int64_t)fxb::num_sms() * 8;
   int blocks = (int)(want < cap ? want : cap);
   if (blocks < 1) blocks = 1;
-  adamw_update_kernel<G, P><<<blocks, 256, 0, st>>>(static_cast<G*>(const_cast<void*>(g)), master, m, v,
+  fxb::pdl_launch(adamw_update_kernel<G, P>, blocks, 256, 0, st, static_cast<G*>(const_cast<void*>(g)), master, m, v,
                                                     static_cast<P*>(p), n, se, sw, nseg, scratch,
                                                     fi, sc, stp, lr, lrd, b1, b2, eps, wd);
   return fxb::check_launch("adamw_update");
@@ -237,13 +243,13 @@ int fxb_adamw_sumsq(int32_t gdtype, const void* grad, int64_t n, float* scratch,
   if (blocks < 1) blocks = 1;
   switch (gdtype) {
     case FXB_DTYPE_BF16:
-      adamw_sumsq_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(grad), n, scratch, flags);
+      fxb::pdl_launch(adamw_sumsq_kernel<__nv_bfloat16>, blocks, 256, 0, st, static_cast<const __nv_bfloat16*>(grad), n, scratch, flags);
       break;
     case FXB_DTYPE_F16:
-      adamw_sumsq_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(grad), n, scratch, flags);
+      fxb::pdl_launch(adamw_sumsq_kernel<__half>, blocks, 256, 0, st, static_cast<const __half*>(grad), n, scratch, flags);
       break;
     default:
-      adamw_sumsq_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(grad), n, scratch, flags);
+      fxb::pdl_launch(adamw_sumsq_kernel<float>, blocks, 256, 0, st, static_cast<const float*>(grad), n, scratch, flags);
   }
   return fxb::check_launch("adamw_sumsq");
 }
@@ -252,7 +258,7 @@ int fxb_adamw_final(float* scratch, int32_t* flags, int32_t* step, float* found_
                     float* norm_out, const float* scale, float max_norm, void* stream) {
   if (!scratch || !flags || !step || !found_inf || !norm_out || !scale)
     return fxb::set_error(FXB_EINVAL, "adamw_final: NULL pointer");
-  adamw_final_kernel<<<1, 32, 0, fxb::as_stream(stream)>>>(scratch, flags, step, found_inf,
+  fxb::pdl_launch(adamw_final_kernel, 1, 32, 0, fxb::as_stream(stream), scratch, flags, step, found_inf,
                                                           norm_out, scale, max_norm);
   return fxb::check_launch("adamw_final");
 }

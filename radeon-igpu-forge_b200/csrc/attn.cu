@@ -28,10 +28,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int TILE = 128;
 constexpr int kFwdThreads = 320;  // warps 0-7 softmax, 8 MMA, 9 TMA (forward and backward)
-// Forward pipeline depths: K/V ring stages and Q buffers (shared memory:
-// (QN + 2 KS) DH-wide tiles + P + exchange)
-template <int DH> constexpr int fwd_kv_stages() { return DH <= 64 ? 4 : 2; }
+// Forward pipeline depths: K/V ring stages, Q buffers and P buffers (shared
+// memory: (QN + 2 KS) DH-wide tiles + PN 32 KB P tiles + exchange)
+template <int DH> constexpr int fwd_kv_stages() { return DH <= 64 ? 3 : 2; }
 template <int DH> constexpr int fwd_q_bufs() { return DH <= 64 ? 2 : 1; }
+template <int DH> constexpr int fwd_p_bufs() { return DH <= 64 ? 2 : 1; }
+constexpr int kFwdXchBytes = 3072;  // softmax row-statistics exchange area
 
 struct FwdParams {
   int B, T, H, nqt, nkt, causal;
@@ -84,13 +86,23 @@ FXB_DEV float ex2_ftz(float x) {
 // blockIdx.x in steps of gridDim.x; items are numbered heaviest first for
 // causal attention (the last query tiles see the most key tiles). Tensor
 // memory, barriers and tensor maps are set up once per CTA, Q is
-// double-buffered and the K/V ring and S buffers run on counters that
-// continue across items, so the next item's loads and first S = Q K^T
-// overlap the current item's final P.V and output store.
+// double-buffered (Dh 64) and the K/V ring, S buffers and P buffers run on
+// counters that continue across items, so the next item's loads and first
+// S = Q K^T overlap the current item's tail.
+//
+// O accumulates in tensor memory across the key tiles of an item (P.V with
+// accumulate). The softmax keeps a reference maximum per row and computes P
+// against it; only when a tile's row maximum exceeds the reference by more
+// than 2^8 (P values stay <= 256) is the row's O rescaled in tensor memory
+// (tcgen05.ld / st by the owning warp, after that row's previous P.V has
+// completed) and the reference raised. P is double-buffered (Dh 64) in shared
+// memory, so the softmax of tile j does not wait for P.V of tile j-1.
 //
 // Warp roles (320 threads): warps 0-7 softmax (warp w owns TMEM lane quarter
 // w & 3, i.e. 32 query rows, and column half w >> 2 of every S tile: 64 of the
-// 128 keys, and DH/2 of the output columns), warp 8 MMA issuer, warp 9 TMA.
+// 128 keys, and DH/2 of the O columns), warp 8 MMA issuer, warp 9 TMA.
+constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
+
 template <int DH, int FMT>
 __global__ void __launch_bounds__(kFwdThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -98,9 +110,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
   constexpr int QB = TILE * DH * 2;  // bytes of one [128][DH] tile
   constexpr int NBOX = DH / 64;
-  constexpr int OC = DH / 2;         // output columns per thread
+  constexpr int OC = DH / 2;         // O columns per softmax warp
   constexpr int KS = fwd_kv_stages<DH>();
   constexpr int QN = fwd_q_bufs<DH>();
+  constexpr int PN = fwd_p_bufs<DH>();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -108,10 +121,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t sQ = base;             // QN buffers
   const uint32_t sK = sQ + QN * QB;     // KS stages
   const uint32_t sV = sK + KS * QB;     // KS stages
-  const uint32_t sP = sV + KS * QB;     // [128][128] 16-bit
-  const uint32_t sX = sP + 32768;       // row-statistics exchange: [2 buf][2 half][128] fp32
+  const uint32_t sP = sV + KS * QB;     // PN x [128][128] 16-bit
+  // row-statistics exchange: maxima [2 buf][2 half][128] fp32, then the row
+  // sums [2 half][128] fp32 (3 KB)
+  const uint32_t sX = sP + PN * 32768;
   float* xch = reinterpret_cast<float*>(gbase + (sX - base));
-  const uint32_t bars = sX + 2048;
+  const uint32_t bars = sX + kFwdXchBytes;
   auto q_full = [&](int s) { return bars + 8u * s; };
   auto q_empty = [&](int s) { return bars + 8u * (2 + s); };
   auto k_full = [&](int s) { return bars + 8u * (4 + s); };
@@ -119,10 +134,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   auto kv_empty = [&](int s) { return bars + 8u * (4 + 2 * KS + s); };
   auto s_full = [&](int s) { return bars + 8u * (4 + 3 * KS + s); };
   auto s_empty = [&](int s) { return bars + 8u * (6 + 3 * KS + s); };
-  const uint32_t p_full = bars + 8u * (8 + 3 * KS);
-  const uint32_t pv_full = bars + 8u * (9 + 3 * KS);
-  const uint32_t final_bar = bars + 8u * (10 + 3 * KS);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (11 + 3 * KS));
+  auto p_full = [&](int s) { return bars + 8u * (8 + 3 * KS + s); };
+  auto p_empty = [&](int s) { return bars + 8u * (10 + 3 * KS + s); };  // = P.V of that buffer done
+  const uint32_t final_bar = bars + 8u * (12 + 3 * KS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (13 + 3 * KS));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int BH = p.B * p.H;
@@ -141,14 +156,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(q_empty(s), 1);
       mbar_init(s_full(s), 1);
       mbar_init(s_empty(s), 256);
+      mbar_init(p_full(s), 256);
+      mbar_init(p_empty(s), 1);
     }
     for (int s = 0; s < KS; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(v_full(s), 1);
       mbar_init(kv_empty(s), 1);
     }
-    mbar_init(p_full, 256);
-    mbar_init(pv_full, 1);
     mbar_init(final_bar, 1);
     fence_mbar_init();
   }
@@ -160,8 +175,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;         // S buffers at columns 0 and 128
-  const uint32_t tPV = tmem + 256;  // P.V product, DH columns
+  pdl_trigger();
+  pdl_wait();  // q / k / v come from earlier kernels on the stream
+  const uint32_t tS = tmem;        // S buffers at columns 0 and 128
+  const uint32_t tO = tmem + 256;  // O accumulator, DH columns
 
   if (warp == 9) {
     // ------------------------------------------------ TMA producer
@@ -215,7 +232,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       int ts = 0;  // S tiles issued (all items)
       int tp = 0;  // P.V products issued (all items)
       int it = 0;
-      // S = Q K^T of tile (item `it`, global tile ts) into S buffer ts & 1
+      // S = Q K^T of the next tile (global tile ts) into S buffer ts & 1
       auto issue_s = [&](uint32_t q_s) -> bool {
         const int st = ts % KS, sb = ts & 1;
         if (!mbar_wait(k_full(st), (ts / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
@@ -238,14 +255,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int j = 0; j < n_kv && ok; ++j, ++tp) {
           if (j + 1 < n_kv && !issue_s(q_s)) { ok = false; break; }
           if (j + 1 == n_kv) umma_commit(q_empty(qb));  // last S of the item read Q
-          const int st = tp % KS;
-          if (!mbar_wait(p_full, tp & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          const int st = tp % KS, pb = tp % PN;
+          if (!mbar_wait(p_full(pb), (tp / PN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
           if (!mbar_wait(v_full(st), (tp / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < TILE / 16; ++kk)
-            umma_f16(tPV, kmajor_desc(sP, kk), mnmajor_desc(sV + st * QB, kk), IPV, kk > 0);
-          umma_commit(pv_full);
+            umma_f16(tO, kmajor_desc(sP + pb * 32768, kk), mnmajor_desc(sV + st * QB, kk), IPV,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(p_empty(pb));
           umma_commit(kv_empty(st));
         }
       }
@@ -259,9 +277,19 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int col0 = half * 64;         // this thread's key columns within a tile
+    const uint32_t tOw = tO + lane_off + half * OC;  // this warp's O columns
     uint8_t* pbase = gbase + (sP - base);
     bool ok = true;
     int t = 0;  // tiles consumed (all items)
+    // Waits are made warp-uniform: the tensor-memory accesses that follow are
+    // warp-collective.
+    auto uwait = [&](uint32_t bar, uint32_t parity) -> bool {
+      const bool r = mbar_wait(bar, parity, p.err, FXB_DERR_ATTN_WAIT);
+      return __all_sync(0xffffffffu, r);
+    };
+    // wait until P.V of global tile u has completed (its P buffer is free and
+    // its contribution is in O)
+    auto wait_pv = [&](int u) -> bool { return uwait(p_empty(u % PN), (u / PN) & 1); };
     // After a failed (timed-out) wait a thread keeps stepping through the
     // tiles without waiting or computing, so that both warps of a pair always
     // meet at the same named barriers.
@@ -270,13 +298,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       item_coords(w, qt, bh, n_kv);
       const int q0 = qt * TILE;
       const int q = q0 + r;
-      float o[OC];
-#pragma unroll
-      for (int d = 0; d < OC; ++d) o[d] = 0.f;
-      float m = -INFINITY, l = 0.f, a_prev = 0.f;
+      float m_ref = -INFINITY, l = 0.f;
       for (int j = 0; j < n_kv; ++j, ++t) {
         const int sb = t & 1;
-        if (ok && !mbar_wait(s_full(sb), (t >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) ok = false;
+        if (ok && !uwait(s_full(sb), (t >> 1) & 1)) ok = false;
         const int kv0 = j * TILE + col0;
         float sv[64];
         float mx = -INFINITY;
@@ -286,21 +311,29 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           tmem_ld32(tS + sb * TILE + lane_off + col0, sr);
           tmem_ld32(tS + sb * TILE + lane_off + col0 + 32, sr + 32);
           tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(s_empty(sb));  // the scores are in registers
           const bool need_mask = (kv0 + 64 > p.T) || (p.causal && kv0 + 64 > q0);
+          // eight independent running maxima (short dependency chains)
+          float mv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mv[i] = -INFINITY;
           if (need_mask) {
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
               const int col = kv0 + i;
               sv[i] = (col >= p.T || (p.causal && col > q)) ? -INFINITY : __uint_as_float(sr[i]);
-              mx = fmaxf(mx, sv[i]);
+              mv[i & 7] = fmaxf(mv[i & 7], sv[i]);
             }
           } else {
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
               sv[i] = __uint_as_float(sr[i]);
-              mx = fmaxf(mx, sv[i]);
+              mv[i & 7] = fmaxf(mv[i & 7], sv[i]);
             }
           }
+          mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])),
+                     fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
         }
         // exchange the half-row maxima with the partner warp (double-buffered by tile parity)
         float* xb = xch + (t & 1) * 256;
@@ -308,72 +341,89 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         named_bar_sync(1 + quarter, 64);
         mx = fmaxf(mx, xb[(half ^ 1) * 128 + r]);
         if (!ok) continue;
-        const float m_new = fmaxf(m, mx * p.scale_log2);
-        const float alpha = ex2_ftz(m - m_new);
-        // P.V of the previous tile is folded in before P is overwritten
-        if (j > 0) {
-          if (!mbar_wait(pv_full, (t - 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; continue; }
-          tc_fence_after();
-          uint32_t pr[OC];
+        const float m_new = fmaxf(m_ref, mx * p.scale_log2);
+        if (j == 0) {
+          m_ref = m_new;  // O is overwritten by this item's first P.V
+        } else {
+          // lazy rescale: raise the reference only when P would exceed 2^8
+          const bool need = m_new > m_ref + kRescaleLog2;
+          if (__any_sync(0xffffffffu, need)) {
+            if (!wait_pv(t - 1)) { ok = false; continue; }
+            tc_fence_after();
+            const float alpha = need ? ex2_ftz(m_ref - m_new) : 1.f;
 #pragma unroll
-          for (int c = 0; c < OC / 32; ++c) tmem_ld32(tPV + lane_off + half * OC + c * 32, pr + c * 32);
-          tmem_wait_ld();
+            for (int c = 0; c < OC / 32; ++c) {
+              uint32_t orr[32];
+              tmem_ld32(tOw + c * 32, orr);
+              tmem_wait_ld();
 #pragma unroll
-          for (int d = 0; d < OC; ++d) o[d] = o[d] * a_prev + __uint_as_float(pr[d]);
+              for (int d = 0; d < 32; ++d) orr[d] = __float_as_uint(__uint_as_float(orr[d]) * alpha);
+              tmem_st32(tOw + c * 32, orr);
+            }
+            tmem_wait_st();
+            l *= alpha;
+            if (need) m_ref = m_new;
+          }
         }
+        const float m_off = (m_ref == -INFINITY) ? 0.f : m_ref;  // fully masked rows: P = 0
+        // P buffer t % PN is free once P.V of tile t - PN has completed
+        const int pb = t % PN;
+        if (t >= PN && !wait_pv(t - PN)) { ok = false; continue; }
         // probabilities -> P (16-bit, 128B-swizzled) and the partial row sum
-        float rs = 0.f;
+        // (eight partial sums: short dependency chains)
+        uint8_t* pbuf = pbase + pb * 32768;
+        float rsv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rsv[i] = 0.f;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           float pv[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            pv[i] = ex2_ftz(fmaf(sv[8 * u + i], p.scale_log2, -m_new));
-            rs += pv[i];
+            pv[i] = ex2_ftz(fmaf(sv[8 * u + i], p.scale_log2, -m_off));
+            rsv[i] += pv[i];
           }
           uint4 wv;
           wv.x = pack2<T16>(pv[0], pv[1]);
           wv.y = pack2<T16>(pv[2], pv[3]);
           wv.z = pack2<T16>(pv[4], pv[5]);
           wv.w = pack2<T16>(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(pbase + sw128_offset(r, half * 8 + u)) = wv;
+          *reinterpret_cast<uint4*>(pbuf + sw128_offset(r, half * 8 + u)) = wv;
         }
         tc_fence_before();
-        mbar_arrive(s_empty(sb));
         fence_proxy_async_smem();
-        mbar_arrive(p_full);
-        l = l * alpha + rs;
-        m = m_new;
-        a_prev = alpha;
+        mbar_arrive(p_full(pb));
+        l += ((rsv[0] + rsv[1]) + (rsv[2] + rsv[3])) + ((rsv[4] + rsv[5]) + (rsv[6] + rsv[7]));
       }
-      const bool done = ok && mbar_wait(pv_full, (t - 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      const bool done = ok && wait_pv(t - 1);
       if (!done) ok = false;
-      if (done) {
-        tc_fence_after();
-        uint32_t pr[OC];
-#pragma unroll
-        for (int c = 0; c < OC / 32; ++c) tmem_ld32(tPV + lane_off + half * OC + c * 32, pr + c * 32);
-        tmem_wait_ld();
-#pragma unroll
-        for (int d = 0; d < OC; ++d) o[d] = o[d] * a_prev + __uint_as_float(pr[d]);
-      }
       // combine the two half-row sums (every softmax thread reaches this barrier)
       float* xs = xch + 512;
       xs[half * 128 + r] = l;
       named_bar_sync(1 + quarter, 64);
       l += xs[(half ^ 1) * 128 + r];
-      if (done && q < p.T) {
+      if (done) {
+        tc_fence_after();
         const int b = bh / p.H, h = bh - b * p.H;
         const float inv = 1.f / l;
         T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh + half * OC;
 #pragma unroll
-        for (int d = 0; d < OC; d += 8) {
-          float f[8];
+        for (int c = 0; c < OC / 32; ++c) {
+          uint32_t orr[32];
+          tmem_ld32(tOw + c * 32, orr);  // warp-collective: every lane loads
+          tmem_wait_ld();
+          if (q < p.T) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = o[d + i] * inv;
-          *reinterpret_cast<uint4*>(orow + d) = pack8<T16>(f);
+            for (int d = 0; d < 32; d += 8) {
+              float f[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(orr[d + i]) * inv;
+              *reinterpret_cast<uint4*>(orow + c * 32 + d) = pack8<T16>(f);
+            }
+          }
         }
-        if (half == 0) p.lse[(int64_t)bh * p.T + q] = (m + log2f(l)) * kLn2;
+        if (half == 0 && q < p.T) p.lse[(int64_t)bh * p.T + q] = (m_ref + log2f(l)) * kLn2;
+        tc_fence_before();
       }
     }
   }
@@ -393,6 +443,8 @@ __global__ void attn_bwd_prep_kernel(const T16* __restrict__ o, int64_t o_sb, in
                                      int64_t o_sh, const T16* __restrict__ dout, int64_t do_sb,
                                      int64_t do_st, int64_t do_sh, float* __restrict__ delta,
                                      float* __restrict__ dq_acc, int B, int T, int H) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   // DH/8 lanes per row (8 bf16 each): coalesced 128-byte row reads
   constexpr int LPR = DH / 8;
   const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -426,6 +478,8 @@ template <typename T16, int DH>
 __global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, T16* __restrict__ dq,
                                      int64_t dq_sb, int64_t dq_st, int64_t dq_sh, float scale,
                                      int B, int T, int H) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // row*DH/8 + chunk
   const int64_t rows = (int64_t)B * H * T;
   if (idx >= rows * (DH / 8)) return;
@@ -510,6 +564,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // q / k / v (and dO, lse) come from earlier kernels on the stream
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
 
   if (warp == 9) {
@@ -542,11 +598,13 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       constexpr uint32_t I_KV = umma_idesc_f16(FMT, 0, 1, TILE, DH);    // dV, dK
       constexpr uint32_t I_Q = umma_idesc_f16(FMT, 1, 1, TILE, DH);     // dQ
       bool ok = mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
-      for (int it = 0; it < n_it && ok; ++it) {
+      // S^T and dP^T of query tile `it` (once its Q / dO have landed and the
+      // previous S^T / dP^T have been read out of tensor memory)
+      auto issue_s = [&](int it) -> bool {
         const int st = it & 1;
         const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
-        if (!mbar_wait(qdo_full(st), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-        if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        if (!mbar_wait(qdo_full(st), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk)
@@ -555,6 +613,15 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int kk = 0; kk < DH / 16; ++kk)
           umma_f16(tDPT, kmajor_desc(sV, kk), kmajor_desc(do_s, kk), I_SS, kk > 0);
         umma_commit(s_full);
+        return true;
+      };
+      if (ok && n_it > 0) ok = issue_s(0);
+      for (int it = 0; it < n_it && ok; ++it) {
+        // the next tile's scores run on the tensor core while the softmax
+        // warps turn this tile's scores into P^T and dS^T
+        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
+        const int st = it & 1;
+        const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
         if (!mbar_wait(ds_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -588,6 +655,19 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     uint8_t* pt = gbase + (sPT - base);
     uint8_t* ds = gbase + (sDS - base);
     bool ok = true;
+    // LSE / delta of a query tile are loaded from global memory one iteration
+    // ahead (threads 0..127, one query each) and published through the
+    // double-buffered shared arrays at the start of their iteration.
+    float lse_next = INFINITY, del_next = 0.f;
+    auto load_stats = [&](int it2) {
+      if (threadIdx.x < 128 && it2 < n_it) {
+        const int q = (i0 + it2) * TILE + (int)threadIdx.x;
+        const bool v = q < p.T;
+        lse_next = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
+        del_next = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
+      }
+    };
+    load_stats(0);
     // After a failed (timed-out) wait a thread keeps stepping through the
     // iterations without waiting or computing, so that all 256 threads always
     // meet at the same named barriers.
@@ -595,14 +675,14 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       const int q0 = (i0 + it) * TILE;
       const int sb = it & 1;
       if (threadIdx.x < 128) {
-        const int q = q0 + (int)threadIdx.x;
-        const bool v = q < p.T;
-        lse_s[sb * 128 + threadIdx.x] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
-        del_s[sb * 128 + threadIdx.x] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
+        lse_s[sb * 128 + threadIdx.x] = lse_next;
+        del_s[sb * 128 + threadIdx.x] = del_next;
       }
       named_bar_sync(1, 256);
+      load_stats(it + 1);
       if (!ok) continue;
-      if (!mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; continue; }
+      // waits are made warp-uniform: the tensor-memory loads that follow are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
       tc_fence_after();
       const bool diag = p.causal && (q0 < kv0 + TILE);
       uint32_t sr[64], dr[64];
@@ -611,6 +691,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       tmem_ld32(tDPT + lane_off + qc0, dr);
       tmem_ld32(tDPT + lane_off + qc0 + 32, dr + 32);
       tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(s_empty);  // S^T / dP^T are in registers: the next tile's may overwrite them
       const float* ls = lse_s + sb * 128 + qc0;
       const float* dl = del_s + sb * 128 + qc0;
 #pragma unroll
@@ -637,12 +719,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         *reinterpret_cast<uint4*>(pt + sw128_offset(r, half * 8 + u)) = w;
         *reinterpret_cast<uint4*>(ds + sw128_offset(r, half * 8 + u)) = x;
       }
-      tc_fence_before();
-      mbar_arrive(s_empty);
       fence_proxy_async_smem();
       mbar_arrive(ds_full);
       // dQ partial of this query tile: row r is query q0 + r, head dims half*32..+32
-      if (!mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; continue; }
+      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
       tc_fence_after();
       {
         const int q = q0 + r;
@@ -661,7 +741,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_arrive(dq_empty);
     }
     // final dK (scaled) and dV for key row kv, head dims half*32..+32
-    if (ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT)) {
+    if (__all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT))) {
       tc_fence_after();
       uint32_t rk[32], rv[32];
       tmem_ld32(tDK + lane_off + half * 32, rk);
@@ -698,11 +778,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 // per SM: the dynamic shared memory request is padded above half of the SM's
 // 228 KB so a second CTA of any TMEM-using kernel can never be co-scheduled.
 constexpr int kOneCtaPerSm = 120 * 1024;
+template <int DH> constexpr int fwd_smem_raw() {
+  return (fwd_q_bufs<DH>() + 2 * fwd_kv_stages<DH>()) * TILE * DH * 2 + fwd_p_bufs<DH>() * 32768 +
+         kFwdXchBytes + 1024 + 256;
+}
 template <int DH> constexpr int fwd_smem() {
-  return ((fwd_q_bufs<DH>() + 2 * fwd_kv_stages<DH>()) * TILE * DH * 2 + 32768 + 2048 + 1024 + 256) >
-                 kOneCtaPerSm
-             ? ((fwd_q_bufs<DH>() + 2 * fwd_kv_stages<DH>()) * TILE * DH * 2 + 32768 + 2048 + 1024 + 256)
-             : kOneCtaPerSm;
+  return fwd_smem_raw<DH>() > kOneCtaPerSm ? fwd_smem_raw<DH>() : kOneCtaPerSm;
 }
 static_assert(fwd_smem<64>() <= 232448 && fwd_smem<128>() <= 232448, "forward shared memory");
 constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 2 * 32768 + 2048 + 1024 + 256; }
@@ -785,7 +866,7 @@ int launch_fwd(const fxb_attn_args* a, cudaStream_t st) {
   }
   const int64_t items = (int64_t)p.nqt * a->B * a->H;
   const int grid = (int)(items < fxb::num_sms() ? items : fxb::num_sms());
-  k<<<grid, kFwdThreads, fwd_smem<DH>(), st>>>(mq, mk, mv, p);
+  fxb::pdl_launch(k, grid, kFwdThreads, fwd_smem<DH>(), st, mq, mk, mv, p);
   return fxb::check_launch("attn_fwd");
 }
 
@@ -796,7 +877,7 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
   const int64_t rows = (int64_t)a->B * a->H * a->T;
   float* delta = a->workspace;
   float* dq_acc = a->workspace + ((rows + 3) / 4) * 4;
-  attn_bwd_prep_kernel<T16, DH><<<(unsigned)((rows * (DH / 8) + 255) / 256), 256, 0, st>>>(
+  fxb::pdl_launch(attn_bwd_prep_kernel<T16, DH>, (unsigned)((rows * (DH / 8) + 255) / 256), 256, 0, st, 
       static_cast<const T16*>(a->o), a->o_sb, a->o_st, a->o_sh, static_cast<const T16*>(a->dout),
       a->do_sb, a->do_st, a->do_sh, delta, dq_acc, a->B, a->T, a->H);
   int r = fxb::check_launch("attn_bwd_prep");
@@ -829,10 +910,10 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
     once[dev & 63] = true;
   }
   dim3 grid(p.nkt, a->B * a->H);
-  k<<<grid, kFwdThreads, bwd_smem(), st>>>(mq, mk, mv, mdo, p);
+  fxb::pdl_launch(k, grid, kFwdThreads, bwd_smem(), st, mq, mk, mv, mdo, p);
   if ((r = fxb::check_launch("attn_bwd"))) return r;
   const int64_t n = rows * (DH / 8);
-  attn_bwd_post_kernel<T16, DH><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+  fxb::pdl_launch(attn_bwd_post_kernel<T16, DH>, (unsigned)((n + 255) / 256), 256, 0, st, 
       dq_acc, static_cast<T16*>(a->dq), a->dq_sb, a->dq_st, a->dq_sh, a->scale, a->B, a->T, a->H);
   return fxb::check_launch("attn_bwd_post");
 }

@@ -1,6 +1,7 @@
 // Library-wide C ABI: version, error reporting, device error word, SM count,
 // and the tensor-map encoder used by the TMA-fed kernels.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include "common.cuh"
 #include "internal.h"
@@ -14,6 +15,14 @@ static thread_local std::string t_last_error;
 static std::atomic<unsigned long long> g_launches{0};
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("FXB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 int set_error(int code, const char* fmt, ...) {
   char buf[1024];

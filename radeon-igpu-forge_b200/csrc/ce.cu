@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(NT == 32 ? 256 : NT)
 ce_cached_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
                  T* grad, float* __restrict__ row_loss, const float* __restrict__ mul,
                  int64_t rows, int V, int64_t ignore_index) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   constexpr int E = CEVec<T>::N;
   __shared__ float red[32];
   const int nvec = V / E;
@@ -141,6 +143,8 @@ __global__ void __launch_bounds__(256)
 ce_generic_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
                   T* grad, float* __restrict__ row_loss, const float* __restrict__ mul,
                   int64_t rows, int V, int64_t ignore_index) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   __shared__ float red[32];
   const float gm = grad ? *mul : 0.f;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -184,7 +188,7 @@ int launch_ce(const void* lg, int64_t ld, const int64_t* tg, void* gr, float* lo
     int vpt = (nvec + 31) / 32;
     int64_t want = (rows + 7) / 8;
     int blocks = (int)(want < (int64_t)sms * 32 ? want : (int64_t)sms * 32);
-#define FXB_CE_W(VP) case VP: ce_cached_kernel<T, 32, VP><<<blocks, 256, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign); break;
+#define FXB_CE_W(VP) case VP: fxb::pdl_launch(ce_cached_kernel<T, 32, VP>, blocks, 256, 0, st, L, ld, tg, G, loss, mul, rows, V, ign); break;
     switch (vpt) { FXB_CE_W(1) FXB_CE_W(2) FXB_CE_W(3) FXB_CE_W(4) FXB_CE_W(5) FXB_CE_W(6) FXB_CE_W(7) FXB_CE_W(8) }
 #undef FXB_CE_W
     return fxb::check_launch("ce_fwd_grad(warp)");
@@ -192,18 +196,18 @@ int launch_ce(const void* lg, int64_t ld, const int64_t* tg, void* gr, float* lo
   if (vec_ok && nvec <= 512 * 16) {
     int vpt = (nvec + 511) / 512;
     int blocks = (int)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
-#define FXB_CE_B(VP) case VP: ce_cached_kernel<T, 512, VP><<<blocks, 512, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign); break;
+#define FXB_CE_B(VP) case VP: fxb::pdl_launch(ce_cached_kernel<T, 512, VP>, blocks, 512, 0, st, L, ld, tg, G, loss, mul, rows, V, ign); break;
     switch (vpt) {
       FXB_CE_B(1) FXB_CE_B(2) FXB_CE_B(3) FXB_CE_B(4) FXB_CE_B(5) FXB_CE_B(6) FXB_CE_B(7) FXB_CE_B(8)
       default:
-        if (vpt <= 12) { ce_cached_kernel<T, 512, 12><<<blocks, 512, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign); }
-        else { ce_cached_kernel<T, 512, 16><<<blocks, 512, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign); }
+        if (vpt <= 12) { fxb::pdl_launch(ce_cached_kernel<T, 512, 12>, blocks, 512, 0, st, L, ld, tg, G, loss, mul, rows, V, ign); }
+        else { fxb::pdl_launch(ce_cached_kernel<T, 512, 16>, blocks, 512, 0, st, L, ld, tg, G, loss, mul, rows, V, ign); }
     }
 #undef FXB_CE_B
     return fxb::check_launch("ce_fwd_grad(block)");
   }
   int blocks = (int)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
-  ce_generic_kernel<T><<<blocks, 256, 0, st>>>(L, ld, tg, G, loss, mul, rows, V, ign);
+  fxb::pdl_launch(ce_generic_kernel<T>, blocks, 256, 0, st, L, ld, tg, G, loss, mul, rows, V, ign);
   return fxb::check_launch("ce_fwd_grad(generic)");
 }
 

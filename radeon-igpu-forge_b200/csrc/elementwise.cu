@@ -9,10 +9,19 @@
 
 namespace {
 
+// fp32 vector reduction into global memory (four consecutive floats)
+FXB_DEV void red_add4(float* addr, const float* f) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(f[0]), "f"(f[1]),
+               "f"(f[2]), "f"(f[3])
+               : "memory");
+}
+
 template <typename T>
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const T* __restrict__ tok,
                                      const T* __restrict__ pos, T* __restrict__ out, int64_t rows,
                                      int64_t T_, int D, int64_t V) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   // one warp per token row, 8 elements per lane-step (D % 8 == 0)
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -39,6 +48,8 @@ template <typename T>
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const T* __restrict__ dout,
                                      float* __restrict__ dtok, float* __restrict__ dpos,
                                      int64_t rows, int64_t T_, int D, int64_t V) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -50,10 +61,13 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const T* _
     for (int d = lane * 8; d < D; d += 256) {
       float f[8];
       unpack8<T>(*reinterpret_cast<const uint4*>(g + d), f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (ok && dtok) atomicAdd(dtok + id * D + d + j, f[j]);
-        if (dpos) atomicAdd(dpos + t * D + d + j, f[j]);
+      if (ok && dtok) {
+        red_add4(dtok + id * D + d, f);
+        red_add4(dtok + id * D + d + 4, f + 4);
+      }
+      if (dpos) {
+        red_add4(dpos + t * D + d, f);
+        red_add4(dpos + t * D + d + 4, f + 4);
       }
     }
   }
@@ -62,6 +76,8 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const T* _
 template <typename DT, typename ST>
 __global__ void axpy_kernel(DT* __restrict__ dst, const ST* __restrict__ src,
                             const float* __restrict__ scale, int acc, int64_t n) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   const float s = scale ? *scale : 1.f;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -81,13 +97,13 @@ int axpy_src(int32_t sdt, void* dst, const void* src, const float* scale, int ac
   DT* d = static_cast<DT*>(dst);
   switch (sdt) {
     case FXB_DTYPE_BF16:
-      axpy_kernel<DT, __nv_bfloat16><<<blocks, 256, 0, st>>>(d, static_cast<const __nv_bfloat16*>(src), scale, acc, n);
+      fxb::pdl_launch(axpy_kernel<DT, __nv_bfloat16>, blocks, 256, 0, st, d, static_cast<const __nv_bfloat16*>(src), scale, acc, n);
       break;
     case FXB_DTYPE_F16:
-      axpy_kernel<DT, __half><<<blocks, 256, 0, st>>>(d, static_cast<const __half*>(src), scale, acc, n);
+      fxb::pdl_launch(axpy_kernel<DT, __half>, blocks, 256, 0, st, d, static_cast<const __half*>(src), scale, acc, n);
       break;
     default:
-      axpy_kernel<DT, float><<<blocks, 256, 0, st>>>(d, static_cast<const float*>(src), scale, acc, n);
+      fxb::pdl_launch(axpy_kernel<DT, float>, blocks, 256, 0, st, d, static_cast<const float*>(src), scale, acc, n);
   }
   return fxb::check_launch("axpy");
 }
@@ -115,11 +131,11 @@ int fxb_embedding_fwd(int32_t dtype, const int64_t* idx, const void* tok, const 
   if (rows == 0) return FXB_OK;
   cudaStream_t st = fxb::as_stream(stream);
   if (dtype == FXB_DTYPE_BF16)
-    embedding_fwd_kernel<__nv_bfloat16><<<emb_blocks(rows), 256, 0, st>>>(
+    fxb::pdl_launch(embedding_fwd_kernel<__nv_bfloat16>, emb_blocks(rows), 256, 0, st, 
         idx, static_cast<const __nv_bfloat16*>(tok), static_cast<const __nv_bfloat16*>(pos),
         static_cast<__nv_bfloat16*>(out), rows, T, D, V);
   else
-    embedding_fwd_kernel<__half><<<emb_blocks(rows), 256, 0, st>>>(
+    fxb::pdl_launch(embedding_fwd_kernel<__half>, emb_blocks(rows), 256, 0, st, 
         idx, static_cast<const __half*>(tok), static_cast<const __half*>(pos),
         static_cast<__half*>(out), rows, T, D, V);
   return fxb::check_launch("embedding_fwd");
@@ -131,15 +147,17 @@ int fxb_embedding_bwd(int32_t dtype, const int64_t* idx, const void* dout, float
     return fxb::set_error(FXB_EUNSUPPORTED, "embedding_bwd: dtype %d (16-bit only)", dtype);
   if (D <= 0 || D % 8 || B < 0 || T <= 0 || V <= 0)
     return fxb::set_error(FXB_EINVAL, "embedding_bwd: bad shape");
-  if (!fxb::aligned16(dout)) return fxb::set_error(FXB_EINVAL, "embedding_bwd: dout alignment");
+  if (!fxb::aligned16(dout) || (dtok_ws && !fxb::aligned16(dtok_ws)) ||
+      (dpos_ws && !fxb::aligned16(dpos_ws)))
+    return fxb::set_error(FXB_EINVAL, "embedding_bwd: dout / dtok_ws / dpos_ws must be 16-byte aligned");
   const int64_t rows = B * T;
   if (rows == 0) return FXB_OK;
   cudaStream_t st = fxb::as_stream(stream);
   if (dtype == FXB_DTYPE_BF16)
-    embedding_bwd_kernel<__nv_bfloat16><<<emb_blocks(rows), 256, 0, st>>>(
+    fxb::pdl_launch(embedding_bwd_kernel<__nv_bfloat16>, emb_blocks(rows), 256, 0, st, 
         idx, static_cast<const __nv_bfloat16*>(dout), dtok_ws, dpos_ws, rows, T, D, V);
   else
-    embedding_bwd_kernel<__half><<<emb_blocks(rows), 256, 0, st>>>(
+    fxb::pdl_launch(embedding_bwd_kernel<__half>, emb_blocks(rows), 256, 0, st, 
         idx, static_cast<const __half*>(dout), dtok_ws, dpos_ws, rows, T, D, V);
   return fxb::check_launch("embedding_bwd");
 }

@@ -16,6 +16,8 @@ template <typename T>
 __global__ void gather_windows_kernel(const T* __restrict__ X, int64_t R, int F,
                                       const int* __restrict__ idx, int B, int window,
                                       T* __restrict__ Xg) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   const int lane = threadIdx.x & 31;
   const int64_t K = (int64_t)window * F;
   const int64_t nvec = K / 8;
@@ -34,6 +36,8 @@ __global__ void gather_windows_kernel(const T* __restrict__ X, int64_t R, int F,
 template <typename T>
 __global__ void colsum_kernel(const T* __restrict__ g, int64_t rows, int cols,
                               float* __restrict__ out, int accumulate) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   __shared__ float part[8][33];
   const int c = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
@@ -69,10 +73,10 @@ int fxb_gather_windows(int32_t dtype, const void* X, int64_t R, int32_t F, const
   int blocks = (int)(want < cap ? want : cap);
   cudaStream_t st = fxb::as_stream(stream);
   if (dtype == FXB_DTYPE_F16)
-    gather_windows_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(X), R, F, idx, B,
+    fxb::pdl_launch(gather_windows_kernel<__half>, blocks, 256, 0, st, static_cast<const __half*>(X), R, F, idx, B,
                                                           window, static_cast<__half*>(Xg));
   else
-    gather_windows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+    fxb::pdl_launch(gather_windows_kernel<__nv_bfloat16>, blocks, 256, 0, st, 
         static_cast<const __nv_bfloat16*>(X), R, F, idx, B, window, static_cast<__nv_bfloat16*>(Xg));
   return fxb::check_launch("gather_windows");
 }
@@ -85,13 +89,13 @@ int fxb_colsum(int32_t dtype, const void* g, int64_t rows, int32_t cols, float* 
   cudaStream_t st = fxb::as_stream(stream);
   switch (dtype) {
     case FXB_DTYPE_F16:
-      colsum_kernel<__half><<<grid, block, 0, st>>>(static_cast<const __half*>(g), rows, cols, out, accumulate);
+      fxb::pdl_launch(colsum_kernel<__half>, grid, block, 0, st, static_cast<const __half*>(g), rows, cols, out, accumulate);
       break;
     case FXB_DTYPE_BF16:
-      colsum_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(static_cast<const __nv_bfloat16*>(g), rows, cols, out, accumulate);
+      fxb::pdl_launch(colsum_kernel<__nv_bfloat16>, grid, block, 0, st, static_cast<const __nv_bfloat16*>(g), rows, cols, out, accumulate);
       break;
     default:
-      colsum_kernel<float><<<grid, block, 0, st>>>(static_cast<const float*>(g), rows, cols, out, accumulate);
+      fxb::pdl_launch(colsum_kernel<float>, grid, block, 0, st, static_cast<const float*>(g), rows, cols, out, accumulate);
   }
   return fxb::check_launch("colsum");
 }

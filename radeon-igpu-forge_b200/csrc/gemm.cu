@@ -371,6 +371,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // operands come from the previous kernel on the stream
 
   const int total_units = p.tiles_m * p.tiles_n * p.splits;
   constexpr uint32_t IDESC = umma_idesc_f16(AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, BM, BN);
@@ -564,6 +566,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
   cluster_sync();  // barriers initialised and tensor memory allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // operands come from the previous kernel on the stream
 
   const int total_units = p.tiles_m * p.tiles_n * p.splits;
   constexpr uint32_t IDESC = umma_idesc_f16(AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, 256, BN);
@@ -719,7 +723,7 @@ int launch_one(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
     if (r) return r;
     attr_set[dev] = true;
   }
-  k<<<grid, kThreads, smem, st>>>(mp.a, mp.b, mp.c, mp.z, p);
+  fxb::pdl_launch(k, grid, kThreads, smem, st, mp.a, mp.b, mp.c, mp.z, p);
   return fxb::check_launch(PAIR ? "gemm_tc2" : "gemm_tc");
 }
 

@@ -28,6 +28,32 @@ inline int check_launch(const char* what) {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Programmatic dependent launch is on unless FXB_PDL=0 in the environment.
+bool pdl_enabled();
+
+// Launches kernel `k` with programmatic dependent launch allowed: its CTAs may
+// be scheduled (and run their prologue: barrier init, tensor-memory
+// allocation, descriptor prefetch) while the previous kernel on the stream is
+// draining. Every kernel of this library calls pdl_wait() (griddepcontrol.wait:
+// the previous kernel has completed and its writes are visible) before its
+// first global-memory access, so stream order is preserved.
+// A launch error is left for the check_launch() that follows every launch.
+template <typename... KArgs, typename... Args>
+void pdl_launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  (void)cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline int dtype_size(int32_t dt) {

@@ -45,6 +45,8 @@ template <typename T, int VPL>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
                    float* __restrict__ rstd, int64_t rows, int D, float eps) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   constexpr int E = Vec<T>::N;
   const int lane = threadIdx.x & 31;
   const int nvec = D / E;
@@ -93,6 +95,8 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
                    const float* __restrict__ rstd, const T* __restrict__ dy,
                    const T* __restrict__ dres, T* __restrict__ dx,
                    float* __restrict__ part, int64_t rows, int D) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   constexpr int E = Vec<T>::N;
   extern __shared__ float sdw[];  // kWarps x D
   const int lane = threadIdx.x & 31;
@@ -168,6 +172,8 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
 template <typename T>
 __global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ part, int nparts, int D,
                                          T* __restrict__ dw, int accumulate) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
   // block (32 columns) x (8 row groups); each row group sums a fixed stride of
   // partials, then the 8 group sums are added in a fixed order (deterministic)
   __shared__ float grp[8][33];
@@ -200,14 +206,14 @@ int launch_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows,
   auto Y = static_cast<T*>(y);
 #define FXB_RMS_FWD(V)                                                            \
   case V:                                                                         \
-    rmsnorm_fwd_kernel<T, V><<<blocks, kWarps * 32, 0, st>>>(X, W, Y, rstd, rows, D, eps); \
+    fxb::pdl_launch(rmsnorm_fwd_kernel<T, V>, blocks, kWarps * 32, 0, st, X, W, Y, rstd, rows, D, eps); \
     break;
   switch (vpl) {
     FXB_RMS_FWD(1) FXB_RMS_FWD(2) FXB_RMS_FWD(3) FXB_RMS_FWD(4) FXB_RMS_FWD(5) FXB_RMS_FWD(6)
     FXB_RMS_FWD(7) FXB_RMS_FWD(8)
     default:
-      if (vpl <= 16) { rmsnorm_fwd_kernel<T, 16><<<blocks, kWarps * 32, 0, st>>>(X, W, Y, rstd, rows, D, eps); }
-      else if (vpl <= 32) { rmsnorm_fwd_kernel<T, 32><<<blocks, kWarps * 32, 0, st>>>(X, W, Y, rstd, rows, D, eps); }
+      if (vpl <= 16) { fxb::pdl_launch(rmsnorm_fwd_kernel<T, 16>, blocks, kWarps * 32, 0, st, X, W, Y, rstd, rows, D, eps); }
+      else if (vpl <= 32) { fxb::pdl_launch(rmsnorm_fwd_kernel<T, 32>, blocks, kWarps * 32, 0, st, X, W, Y, rstd, rows, D, eps); }
       else return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm: D=%d too large", D);
   }
 #undef FXB_RMS_FWD
@@ -215,8 +221,10 @@ int launch_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows,
 }
 
 int bwd_blocks(int64_t rows) {
-  int64_t want = (rows + kWarps * 4 - 1) / (kWarps * 4);  // >= ~4 rows per warp
-  int cap = fxb::num_sms() * 2;
+  // ~2 rows per warp and up to 4 blocks per SM: the kernel is latency-bound
+  // at training sizes (8K rows), and the dw partials stay small
+  int64_t want = (rows + kWarps * 2 - 1) / (kWarps * 2);
+  int cap = fxb::num_sms() * 4;
   int b = (int)(want < cap ? want : cap);
   return b < 1 ? 1 : b;
 }
@@ -238,7 +246,7 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
     auto k = rmsnorm_bwd_kernel<T, V>;                                                   \
     if (smem > 48 * 1024)                                                                \
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
-    k<<<blocks, kWarps * 32, smem, st>>>(X, W, rstd, G, static_cast<const T*>(dres), DX, ws, rows, D); \
+    fxb::pdl_launch(k, blocks, kWarps * 32, smem, st, X, W, rstd, G, static_cast<const T*>(dres), DX, ws, rows, D); \
     break;                                                                               \
   }
   switch (vpl) {
@@ -253,13 +261,13 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
   const dim3 g((D + 31) / 32), blk(32, 8);
   switch (dw_dtype) {
     case FXB_DTYPE_BF16:
-      rmsnorm_dw_reduce_kernel<__nv_bfloat16><<<g, blk, 0, st>>>(ws, blocks, D, static_cast<__nv_bfloat16*>(dw), acc);
+      fxb::pdl_launch(rmsnorm_dw_reduce_kernel<__nv_bfloat16>, g, blk, 0, st, ws, blocks, D, static_cast<__nv_bfloat16*>(dw), acc);
       break;
     case FXB_DTYPE_F16:
-      rmsnorm_dw_reduce_kernel<__half><<<g, blk, 0, st>>>(ws, blocks, D, static_cast<__half*>(dw), acc);
+      fxb::pdl_launch(rmsnorm_dw_reduce_kernel<__half>, g, blk, 0, st, ws, blocks, D, static_cast<__half*>(dw), acc);
       break;
     default:
-      rmsnorm_dw_reduce_kernel<float><<<g, blk, 0, st>>>(ws, blocks, D, static_cast<float*>(dw), acc);
+      fxb::pdl_launch(rmsnorm_dw_reduce_kernel<float>, g, blk, 0, st, ws, blocks, D, static_cast<float*>(dw), acc);
   }
   return fxb::check_launch("rmsnorm_dw_reduce");
 }
