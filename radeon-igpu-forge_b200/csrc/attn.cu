@@ -66,14 +66,15 @@ FXB_DEV uint32_t sw128_offset(int r, int chunk) {
   return (uint32_t)(blk * 16384 + r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-// K-major operand tile [128 rows][D] stored as D/64 swizzled column blocks
-FXB_DEV uint64_t kmajor_desc(uint32_t base, int kk) {
-  return umma_desc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-}
+// K-major operand tile [128 rows][D] stored as D/64 swizzled column blocks:
+// descriptor of the tile and the byte offset of its K slice kk (16 elements)
+FXB_DEV uint64_t kmajor_desc0(uint32_t base) { return umma_desc_sw128(base, 16, 1024); }
+__host__ __device__ constexpr uint32_t kmajor_off(int kk) { return (kk >> 2) * 16384 + (kk & 3) * 32; }
+FXB_DEV uint64_t kmajor_desc(uint32_t base, int kk) { return desc_add(kmajor_desc0(base), kmajor_off(kk)); }
 // MN-major view of the same storage: MN along the columns, K along the rows
-FXB_DEV uint64_t mnmajor_desc(uint32_t base, int kk) {
-  return umma_desc_sw128(base + kk * 2048, 16384, 1024);
-}
+FXB_DEV uint64_t mnmajor_desc0(uint32_t base) { return umma_desc_sw128(base, 16384, 1024); }
+__host__ __device__ constexpr uint32_t mnmajor_off(int kk) { return kk * 2048; }
+FXB_DEV uint64_t mnmajor_desc(uint32_t base, int kk) { return desc_add(mnmajor_desc0(base), mnmajor_off(kk)); }
 
 // ============================================================ forward
 FXB_DEV float ex2_ftz(float x) {
@@ -238,9 +239,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         if (!mbar_wait(k_full(st), (ts / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         if (!mbar_wait(s_empty(sb), ((ts >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         tc_fence_after();
+        const uint64_t qd = kmajor_desc0(q_s), kd = kmajor_desc0(sK + st * QB);
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk)
-          umma_f16(tS + sb * TILE, kmajor_desc(q_s, kk), kmajor_desc(sK + st * QB, kk), IS, kk > 0);
+          umma_f16(tS + sb * TILE, desc_add(qd, kmajor_off(kk)), desc_add(kd, kmajor_off(kk)), IS,
+                   kk > 0);
         umma_commit(s_full(sb));
         ++ts;
         return true;
@@ -259,9 +262,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           if (!mbar_wait(p_full(pb), (tp / PN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
           if (!mbar_wait(v_full(st), (tp / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
           tc_fence_after();
+          const uint64_t pd = kmajor_desc0(sP + pb * 32768), vd = mnmajor_desc0(sV + st * QB);
 #pragma unroll
           for (int kk = 0; kk < TILE / 16; ++kk)
-            umma_f16(tO, kmajor_desc(sP + pb * 32768, kk), mnmajor_desc(sV + st * QB, kk), IPV,
+            umma_f16(tO, desc_add(pd, kmajor_off(kk)), desc_add(vd, mnmajor_off(kk)), IPV,
                      (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(p_empty(pb));
           umma_commit(kv_empty(st));
@@ -606,12 +610,14 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         if (!mbar_wait(qdo_full(st), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         tc_fence_after();
+        const uint64_t kd = kmajor_desc0(sK), qd = kmajor_desc0(q_s);
+        const uint64_t vd = kmajor_desc0(sV), dod = kmajor_desc0(do_s);
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk)
-          umma_f16(tST, kmajor_desc(sK, kk), kmajor_desc(q_s, kk), I_SS, kk > 0);
+          umma_f16(tST, desc_add(kd, kmajor_off(kk)), desc_add(qd, kmajor_off(kk)), I_SS, kk > 0);
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk)
-          umma_f16(tDPT, kmajor_desc(sV, kk), kmajor_desc(do_s, kk), I_SS, kk > 0);
+          umma_f16(tDPT, desc_add(vd, kmajor_off(kk)), desc_add(dod, kmajor_off(kk)), I_SS, kk > 0);
         umma_commit(s_full);
         return true;
       };
@@ -624,17 +630,22 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
         if (!mbar_wait(ds_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
+        const uint64_t ptd = kmajor_desc0(sPT), dsd = kmajor_desc0(sDS);
+        const uint64_t dom = mnmajor_desc0(do_s), qm = mnmajor_desc0(q_s);
 #pragma unroll
         for (int kk = 0; kk < TILE / 16; ++kk)
-          umma_f16(tDV, kmajor_desc(sPT, kk), mnmajor_desc(do_s, kk), I_KV, (it > 0 || kk > 0));
+          umma_f16(tDV, desc_add(ptd, kmajor_off(kk)), desc_add(dom, mnmajor_off(kk)), I_KV,
+                   (it > 0 || kk > 0));
 #pragma unroll
         for (int kk = 0; kk < TILE / 16; ++kk)
-          umma_f16(tDK, kmajor_desc(sDS, kk), mnmajor_desc(q_s, kk), I_KV, (it > 0 || kk > 0));
+          umma_f16(tDK, desc_add(dsd, kmajor_off(kk)), desc_add(qm, mnmajor_off(kk)), I_KV,
+                   (it > 0 || kk > 0));
         if (!mbar_wait(dq_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
+        const uint64_t dsm = mnmajor_desc0(sDS), km = mnmajor_desc0(sK);
 #pragma unroll
         for (int kk = 0; kk < TILE / 16; ++kk)
-          umma_f16(tDQ, mnmajor_desc(sDS, kk), mnmajor_desc(sK, kk), I_Q, kk > 0);
+          umma_f16(tDQ, desc_add(dsm, mnmajor_off(kk)), desc_add(km, mnmajor_off(kk)), I_Q, kk > 0);
         umma_commit(dq_full);
         umma_commit(qdo_empty(st));
       }

@@ -87,21 +87,25 @@ FXB_DEV float tanh_fast(float x) {
   return y;
 }
 
-// GELU with the tanh approximation (torch approximate="tanh")
+// GELU with the tanh approximation (torch approximate="tanh"):
+//   gelu(x) = 0.5 x (1 + tanh(u)),  u = sqrt(2/pi) (x + 0.044715 x^3)
+// written as fused multiply-adds: u = x (k0 + k0 k1 x^2), 0.5x + 0.5x tanh(u)
 FXB_DEV float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  const float k1 = 0.044715f;
-  float u = k0 * (x + k1 * x * x * x);
-  return 0.5f * x * (1.f + tanh_fast(u));
+  const float k0 = 0.7978845608028654f;        // sqrt(2/pi)
+  const float k01 = 0.7978845608028654f * 0.044715f;
+  const float u = x * fmaf(k01, x * x, k0);
+  const float hx = 0.5f * x;
+  return fmaf(hx, tanh_fast(u), hx);
 }
+// d gelu / dx = 0.5 (1 + t) + 0.5 x (1 - t^2) du/dx,  du/dx = k0 (1 + 3 k1 x^2)
 FXB_DEV float gelu_tanh_grad(float x) {
   const float k0 = 0.7978845608028654f;
-  const float k1 = 0.044715f;
-  float x2 = x * x;
-  float u = k0 * (x + k1 * x2 * x);
-  float t = tanh_fast(u);
-  float du = k0 * (1.f + 3.f * k1 * x2);
-  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * du;
+  const float k01 = 0.7978845608028654f * 0.044715f;
+  const float x2 = x * x;
+  const float t = tanh_fast(x * fmaf(k01, x2, k0));
+  const float du = fmaf(3.f * k01, x2, k0);
+  const float a = fmaf(-t, t, 1.f);  // 1 - t^2
+  return fmaf(0.5f, x * du * a, fmaf(0.5f, t, 0.5f));
 }
 
 // ---------------------------------------------------------------- smem / mbarrier
@@ -369,6 +373,11 @@ FXB_DEV uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sb
   d |= (uint64_t)2 << 61;  // SWIZZLE_128B
   return d;
 }
+// The same descriptor for an operand `byte_off` bytes further on: only the
+// start-address field (bits 0-13, address >> 4) changes, and it cannot carry
+// out because shared-memory addresses stay below 256 KB. MMA loops build one
+// descriptor per stage and step it with this single add per instruction.
+FXB_DEV uint64_t desc_add(uint64_t d, uint32_t byte_off) { return d + (uint64_t)(byte_off >> 4); }
 // Instruction descriptor for kind::f16 with f32 accumulation.
 // ab_fmt: 0 = f16, 1 = bf16. a_mn / b_mn: operand is MN-major (1) or K-major (0).
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int ab_fmt, int a_mn, int b_mn, int M, int N) {

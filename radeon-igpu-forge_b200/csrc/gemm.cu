@@ -163,8 +163,17 @@ FXB_DEV void epilogue_math(const GemmParams& p, int m, int n0, int n8, float* v,
       if (p.epi == FXB_EPI_BIAS) break;
       // round the pre-activation once; the activation is computed from the
       // stored value so that backward (which reads Z) sees the same input
+      if constexpr (sizeof(CT) == 2) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) z[i] = to_f<CT>(from_f<CT>(v[i]));
+        for (int i = 0; i < 16; i += 2) {  // paired conversions
+          const float2 f = unpack2<CT>(pack2<CT>(v[i], v[i + 1]));
+          z[i] = f.x;
+          z[i + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) z[i] = v[i];
+      }
       if (p.epi == FXB_EPI_BIAS_SILU) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = silu_f(z[i]);
@@ -440,14 +449,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           tc_fence_after();
           const uint32_t sa = base + stage * C::STAGE_BYTES;
           const uint32_t sb = sa + C::A_BYTES;
+          const uint64_t ad0 = A_MN ? umma_desc_sw128(sa, 8192, 1024) : umma_desc_sw128(sa, 16, 1024);
+          const uint64_t bd0 = B_MN ? umma_desc_sw128(sb, 8192, 1024) : umma_desc_sw128(sb, 16, 1024);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = A_MN ? umma_desc_sw128(sa + kk * 2048, 8192, 1024)
-                                     : umma_desc_sw128(sa + kk * 32, 16, 1024);
-            const uint64_t bd = B_MN ? umma_desc_sw128(sb + kk * 2048, 8192, 1024)
-                                     : umma_desc_sw128(sb + kk * 32, 16, 1024);
-            umma_f16(dcol, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16(dcol, desc_add(ad0, A_MN ? kk * 2048 : kk * 32),
+                     desc_add(bd0, B_MN ? kk * 2048 : kk * 32), IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
           umma_commit(empty_bar(stage));
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
@@ -642,14 +649,13 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             tc_fence_after();
             const uint32_t sa = base + stage * C::STAGE_BYTES;
             const uint32_t sb = sa + C::A_BYTES;
+            const uint64_t ad0 = A_MN ? umma_desc_sw128(sa, 8192, 1024) : umma_desc_sw128(sa, 16, 1024);
+            const uint64_t bd0 = B_MN ? umma_desc_sw128(sb, 8192, 1024) : umma_desc_sw128(sb, 16, 1024);
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-              const uint64_t ad = A_MN ? umma_desc_sw128(sa + kk * 2048, 8192, 1024)
-                                       : umma_desc_sw128(sa + kk * 32, 16, 1024);
-              const uint64_t bd = B_MN ? umma_desc_sw128(sb + kk * 2048, 8192, 1024)
-                                       : umma_desc_sw128(sb + kk * 32, 16, 1024);
-              umma_f16_pair(dcol, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
-            }
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_f16_pair(dcol, desc_add(ad0, A_MN ? kk * 2048 : kk * 32),
+                            desc_add(bd0, B_MN ? kk * 2048 : kk * 32), IDESC,
+                            (kb > kb0 || kk > 0) ? 1u : 0u);
             umma_commit_pair(empty_bar(stage), 0x3);
             if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
           }
