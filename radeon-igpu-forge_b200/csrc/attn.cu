@@ -12,8 +12,8 @@
 // tcgen05.mma into tensor memory; eight softmax warps read scores with
 // tcgen05.ld, two warps per TMEM lane quarter, each owning half of a tile's
 // columns (forward: row maxima exchanged through shared memory once per tile,
-// row sums combined at the end). Forward keeps O in registers and receives
-// each P.V product from TMEM (online-softmax rescale in registers). Backward
+// row sums combined at the end). Forward: persistent CTAs, P written to and
+// O accumulated in TMEM, lazily rescaled (details at the kernel). Backward
 // works per key tile: S^T and dP^T land in TMEM, dV and dK accumulate in TMEM
 // across query tiles, and each dQ partial is reduced into an fp32 workspace
 // with vector red.add. Every wait is bounded (FXB_DERR_ATTN_WAIT); after an
@@ -28,11 +28,11 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int TILE = 128;
 constexpr int kFwdThreads = 320;  // warps 0-7 softmax, 8 MMA, 9 TMA (forward and backward)
-// Forward pipeline depths: K/V ring stages, Q buffers and P buffers (shared
-// memory: (QN + 2 KS) DH-wide tiles + PN 32 KB P tiles + exchange)
-template <int DH> constexpr int fwd_kv_stages() { return DH <= 64 ? 3 : 2; }
-template <int DH> constexpr int fwd_q_bufs() { return DH <= 64 ? 2 : 1; }
-template <int DH> constexpr int fwd_p_bufs() { return DH <= 64 ? 2 : 1; }
+// Forward pipeline depths: K/V ring stages and Q buffers (shared memory:
+// (QN + 2 KS) DH-wide tiles + exchange) and P buffers (tensor memory)
+template <int DH> constexpr int fwd_kv_stages() { return DH <= 64 ? 5 : 2; }
+template <int DH> constexpr int fwd_q_bufs() { return 2; }
+template <int DH> constexpr int fwd_p_bufs() { return 2; }
 constexpr int kFwdXchBytes = 3072;  // softmax row-statistics exchange area
 
 struct FwdParams {
@@ -96,8 +96,10 @@ FXB_DEV float ex2_ftz(float x) {
 // against it; only when a tile's row maximum exceeds the reference by more
 // than 2^8 (P values stay <= 256) is the row's O rescaled in tensor memory
 // (tcgen05.ld / st by the owning warp, after that row's previous P.V has
-// completed) and the reference raised. P is double-buffered (Dh 64) in shared
-// memory, so the softmax of tile j does not wait for P.V of tile j-1.
+// completed) and the reference raised. P goes to tensor memory (tcgen05.st,
+// 16-bit pairs) and is double-buffered there: the P.V MMA reads its A operand
+// straight from tensor memory (only V comes from shared memory), and the
+// softmax of tile j does not wait for P.V of tile j-1.
 //
 // Warp roles (320 threads): warps 0-7 softmax (warp w owns TMEM lane quarter
 // w & 3, i.e. 32 query rows, and column half w >> 2 of every S tile: 64 of the
@@ -122,10 +124,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t sQ = base;             // QN buffers
   const uint32_t sK = sQ + QN * QB;     // KS stages
   const uint32_t sV = sK + KS * QB;     // KS stages
-  const uint32_t sP = sV + KS * QB;     // PN x [128][128] 16-bit
   // row-statistics exchange: maxima [2 buf][2 half][128] fp32, then the row
   // sums [2 half][128] fp32 (3 KB)
-  const uint32_t sX = sP + PN * 32768;
+  const uint32_t sX = sV + KS * QB;
   float* xch = reinterpret_cast<float*>(gbase + (sX - base));
   const uint32_t bars = sX + kFwdXchBytes;
   auto q_full = [&](int s) { return bars + 8u * s; };
@@ -178,8 +179,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tmem = *tmem_slot;
   pdl_trigger();
   pdl_wait();  // q / k / v come from earlier kernels on the stream
-  const uint32_t tS = tmem;        // S buffers at columns 0 and 128
-  const uint32_t tO = tmem + 256;  // O accumulator, DH columns
+  const uint32_t tS = tmem;        // S buffers (fp32) at columns 0 and 128
+  const uint32_t tP = tmem + 256;  // P buffers (16-bit, two per column): 64 columns each
+  const uint32_t tO = tmem + 384;  // O accumulator, DH columns
 
   if (warp == 9) {
     // ------------------------------------------------ TMA producer
@@ -262,11 +264,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           if (!mbar_wait(p_full(pb), (tp / PN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
           if (!mbar_wait(v_full(st), (tp / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t pd = kmajor_desc0(sP + pb * 32768), vd = mnmajor_desc0(sV + st * QB);
+          const uint64_t vd = mnmajor_desc0(sV + st * QB);
 #pragma unroll
-          for (int kk = 0; kk < TILE / 16; ++kk)
-            umma_f16(tO, desc_add(pd, kmajor_off(kk)), desc_add(vd, mnmajor_off(kk)), IPV,
-                     (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < TILE / 16; ++kk)  // A = P from tensor memory, 16 keys = 8 columns
+            umma_f16_ta(tO, tP + pb * 64 + kk * 8, desc_add(vd, mnmajor_off(kk)), IPV,
+                        (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(p_empty(pb));
           umma_commit(kv_empty(st));
         }
@@ -282,7 +284,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int col0 = half * 64;         // this thread's key columns within a tile
     const uint32_t tOw = tO + lane_off + half * OC;  // this warp's O columns
-    uint8_t* pbase = gbase + (sP - base);
     bool ok = true;
     int t = 0;  // tiles consumed (all items)
     // Waits are made warp-uniform: the tensor-memory accesses that follow are
@@ -373,12 +374,13 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         // P buffer t % PN is free once P.V of tile t - PN has completed
         const int pb = t % PN;
         if (t >= PN && !wait_pv(t - PN)) { ok = false; continue; }
-        // probabilities -> P (16-bit, 128B-swizzled) and the partial row sum
-        // (eight partial sums: short dependency chains)
-        uint8_t* pbuf = pbase + pb * 32768;
+        // probabilities -> P (16-bit pairs) in tensor memory: this thread's 64
+        // keys are the 32 columns half*32.. of P buffer pb in its lane; the
+        // row sum uses eight partial sums (short dependency chains)
         float rsv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) rsv[i] = 0.f;
+        uint32_t pw[32];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           float pv[8];
@@ -387,15 +389,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             pv[i] = ex2_ftz(fmaf(sv[8 * u + i], p.scale_log2, -m_off));
             rsv[i] += pv[i];
           }
-          uint4 wv;
-          wv.x = pack2<T16>(pv[0], pv[1]);
-          wv.y = pack2<T16>(pv[2], pv[3]);
-          wv.z = pack2<T16>(pv[4], pv[5]);
-          wv.w = pack2<T16>(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(pbuf + sw128_offset(r, half * 8 + u)) = wv;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) pw[4 * u + i] = pack2<T16>(pv[2 * i], pv[2 * i + 1]);
         }
+        tmem_st32(tP + pb * 64 + lane_off + half * 32, pw);
+        tmem_wait_st();
         tc_fence_before();
-        fence_proxy_async_smem();
         mbar_arrive(p_full(pb));
         l += ((rsv[0] + rsv[1]) + (rsv[2] + rsv[3])) + ((rsv[4] + rsv[5]) + (rsv[6] + rsv[7]));
       }
@@ -790,8 +789,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 // 228 KB so a second CTA of any TMEM-using kernel can never be co-scheduled.
 constexpr int kOneCtaPerSm = 120 * 1024;
 template <int DH> constexpr int fwd_smem_raw() {
-  return (fwd_q_bufs<DH>() + 2 * fwd_kv_stages<DH>()) * TILE * DH * 2 + fwd_p_bufs<DH>() * 32768 +
-         kFwdXchBytes + 1024 + 256;
+  return (fwd_q_bufs<DH>() + 2 * fwd_kv_stages<DH>()) * TILE * DH * 2 + kFwdXchBytes + 1024 + 256;
 }
 template <int DH> constexpr int fwd_smem() {
   return fwd_smem_raw<DH>() > kOneCtaPerSm ? fwd_smem_raw<DH>() : kOneCtaPerSm;
