@@ -183,30 +183,39 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tP = tmem + 256;  // P buffers (16-bit, two per column): 64 columns each
   const uint32_t tO = tmem + 384;  // O accumulator, DH columns
 
+  // The TMA and MMA warps run their loops in all 32 lanes (waits polled by
+  // lane 0 and broadcast) and issue copies / MMAs from one elected lane, so
+  // that the instructions' operands are warp-uniform.
   if (warp == 9) {
     // ------------------------------------------------ TMA producer
-    if (lane == 0) {
+    if (elect_one()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      bool ok = true;
-      int t = 0;   // K/V tiles issued (all items)
-      int it = 0;  // items of this CTA
-      int q_armed = 0;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
-        int qt, bh, n_kv;
-        item_coords(w, qt, bh, n_kv);
-        const int b = bh / p.H, h = bh - b * p.H;
-        const int qb = it % QN;
-        if (!mbar_wait(q_empty(qb), ((it / QN) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+    }
+    __syncwarp();
+    bool ok = true;
+    int t = 0;   // K/V tiles issued (all items)
+    int it = 0;  // items of this CTA
+    int q_armed = 0;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+      int qt, bh, n_kv;
+      item_coords(w, qt, bh, n_kv);
+      const int b = bh / p.H, h = bh - b * p.H;
+      const int qb = it % QN;
+      if (!mbar_wait_warp(q_empty(qb), ((it / QN) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      if (elect_one()) {
         mbar_expect_tx(q_full(qb), QB);
 #pragma unroll
         for (int c = 0; c < NBOX; ++c)
           tma_load_4d(sQ + qb * QB + c * 16384, &tmQ, q_full(qb), 64 * c, qt * TILE, h, b);
-        q_armed = it + 1;
-        for (int j = 0; j < n_kv; ++j, ++t) {
-          const int st = t % KS;
-          if (!mbar_wait(kv_empty(st), ((t / KS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      }
+      __syncwarp();
+      q_armed = it + 1;
+      for (int j = 0; j < n_kv; ++j, ++t) {
+        const int st = t % KS;
+        if (!mbar_wait_warp(kv_empty(st), ((t / KS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        if (elect_one()) {
           mbar_expect_tx(k_full(st), QB);
 #pragma unroll
           for (int c = 0; c < NBOX; ++c)
@@ -216,55 +225,58 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           for (int c = 0; c < NBOX; ++c)
             tma_load_4d(sV + st * QB + c * 16384, &tmV, v_full(st), 64 * c, j * TILE, h, b);
         }
-      }
-      // drain: every copy issued has landed before shared memory goes away
-      for (int i = (q_armed > QN ? q_armed - QN : 0); i < q_armed; ++i)
-        mbar_wait(q_full(i % QN), (i / QN) & 1, p.err, FXB_DERR_ATTN_WAIT);
-      for (int u = (t > KS ? t - KS : 0); u < t; ++u) {
-        mbar_wait(k_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
-        mbar_wait(v_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+        __syncwarp();
       }
     }
-    __syncwarp();
+    // drain: every copy issued has landed before shared memory goes away
+    for (int i = (q_armed > QN ? q_armed - QN : 0); i < q_armed; ++i)
+      mbar_wait_warp(q_full(i % QN), (i / QN) & 1, p.err, FXB_DERR_ATTN_WAIT);
+    for (int u = (t > KS ? t - KS : 0); u < t; ++u) {
+      mbar_wait_warp(k_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      mbar_wait_warp(v_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+    }
   } else if (warp == 8) {
     // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
-      constexpr uint32_t IPV = umma_idesc_f16(FMT, 0, 1, TILE, DH);
-      bool ok = true;
-      int ts = 0;  // S tiles issued (all items)
-      int tp = 0;  // P.V products issued (all items)
-      int it = 0;
-      // S = Q K^T of the next tile (global tile ts) into S buffer ts & 1
-      auto issue_s = [&](uint32_t q_s) -> bool {
-        const int st = ts % KS, sb = ts & 1;
-        if (!mbar_wait(k_full(st), (ts / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
-        if (!mbar_wait(s_empty(sb), ((ts >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
-        tc_fence_after();
-        const uint64_t qd = kmajor_desc0(q_s), kd = kmajor_desc0(sK + st * QB);
+    constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
+    constexpr uint32_t IPV = umma_idesc_f16(FMT, 0, 1, TILE, DH);
+    bool ok = true;
+    int ts = 0;  // S tiles issued (all items)
+    int tp = 0;  // P.V products issued (all items)
+    int it = 0;
+    // S = Q K^T of the next tile (global tile ts) into S buffer ts & 1
+    auto issue_s = [&](uint32_t q_s) -> bool {
+      const int st = ts % KS, sb = ts & 1;
+      if (!mbar_wait_warp(k_full(st), (ts / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+      if (!mbar_wait_warp(s_empty(sb), ((ts >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+      tc_fence_after();
+      const uint64_t qd = kmajor_desc0(q_s), kd = kmajor_desc0(sK + st * QB);
+      if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk)
           umma_f16(tS + sb * TILE, desc_add(qd, kmajor_off(kk)), desc_add(kd, kmajor_off(kk)), IS,
                    kk > 0);
         umma_commit(s_full(sb));
-        ++ts;
-        return true;
-      };
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
-        int qt, bh, n_kv;
-        item_coords(w, qt, bh, n_kv);
-        const int qb = it % QN;
-        const uint32_t q_s = sQ + qb * QB;
-        if (!mbar_wait(q_full(qb), (it / QN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-        if (!issue_s(q_s)) { ok = false; break; }
-        for (int j = 0; j < n_kv && ok; ++j, ++tp) {
-          if (j + 1 < n_kv && !issue_s(q_s)) { ok = false; break; }
-          if (j + 1 == n_kv) umma_commit(q_empty(qb));  // last S of the item read Q
-          const int st = tp % KS, pb = tp % PN;
-          if (!mbar_wait(p_full(pb), (tp / PN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-          if (!mbar_wait(v_full(st), (tp / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t vd = mnmajor_desc0(sV + st * QB);
+      }
+      __syncwarp();
+      ++ts;
+      return true;
+    };
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+      int qt, bh, n_kv;
+      item_coords(w, qt, bh, n_kv);
+      const int qb = it % QN;
+      const uint32_t q_s = sQ + qb * QB;
+      if (!mbar_wait_warp(q_full(qb), (it / QN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+      if (!issue_s(q_s)) { ok = false; break; }
+      for (int j = 0; j < n_kv && ok; ++j, ++tp) {
+        if (j + 1 < n_kv && !issue_s(q_s)) { ok = false; break; }
+        const int st = tp % KS, pb = tp % PN;
+        if (!mbar_wait_warp(p_full(pb), (tp / PN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        if (!mbar_wait_warp(v_full(st), (tp / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t vd = mnmajor_desc0(sV + st * QB);
+        if (elect_one()) {
+          if (j + 1 == n_kv) umma_commit(q_empty(qb));  // the item's last S has read Q
 #pragma unroll
           for (int kk = 0; kk < TILE / 16; ++kk)  // A = P from tensor memory, 16 keys = 8 columns
             umma_f16_ta(tO, tP + pb * 64 + kk * 8, desc_add(vd, mnmajor_off(kk)), IPV,
@@ -272,11 +284,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           umma_commit(p_empty(pb));
           umma_commit(kv_empty(st));
         }
+        __syncwarp();
       }
-      umma_commit(final_bar);
-      mbar_wait(final_bar, 0, p.err, FXB_DERR_ATTN_WAIT);
     }
+    if (elect_one()) umma_commit(final_bar);
     __syncwarp();
+    mbar_wait_warp(final_bar, 0, p.err, FXB_DERR_ATTN_WAIT);
   } else {
     // ------------------------------------------------ softmax warps 0..7
     const int quarter = warp & 3, half = warp >> 2;

@@ -160,6 +160,28 @@ FXB_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int errcode) {
 FXB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 FXB_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Warp-wide bounded wait: lane 0 polls the barrier and the outcome is
+// broadcast, so the whole warp stays converged and every value it computes
+// afterwards (stage indices, descriptors) is warp-uniform.
+FXB_DEV bool mbar_wait_warp(uint32_t bar, uint32_t parity, int* err, int errcode) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, errcode) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+// true in exactly one lane of the (converged) warp: elect.sync. Producer and
+// MMA warps run their loops in all 32 lanes, so that the operands of the TMA
+// and tcgen05.mma instructions are warp-uniform, and issue those
+// instructions from the elected lane only.
+FXB_DEV bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "elect.sync _|P1, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // make generic-proxy smem writes visible to the async proxy (TMA store / MMA)
 FXB_DEV void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
