@@ -27,13 +27,15 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int TILE = 128;
-constexpr int kFwdThreads = 320;  // warps 0-7 softmax, 8 MMA, 9 TMA (forward and backward)
+constexpr int kFwdThreads = 576;  // forward: warps 0-15 softmax, 16 MMA, 17 TMA
+constexpr int kBwdThreads = 320;  // backward: warps 0-7 softmax / dS, 8 MMA, 9 TMA
+constexpr int kFwdWarpMma = 16, kFwdWarpTma = 17;
 // Forward pipeline depths: K/V ring stages and Q buffers (shared memory:
 // (QN + 2 KS) DH-wide tiles + exchange) and P buffers (tensor memory)
 template <int DH> constexpr int fwd_kv_stages() { return DH <= 64 ? 5 : 2; }
 template <int DH> constexpr int fwd_q_bufs() { return 2; }
 template <int DH> constexpr int fwd_p_bufs() { return 2; }
-constexpr int kFwdXchBytes = 3072;  // softmax row-statistics exchange area
+constexpr int kFwdXchBytes = 6144;  // softmax row-statistics exchange area
 
 struct FwdParams {
   int B, T, H, nqt, nkt, causal;
@@ -101,9 +103,10 @@ FXB_DEV float ex2_ftz(float x) {
 // straight from tensor memory (only V comes from shared memory), and the
 // softmax of tile j does not wait for P.V of tile j-1.
 //
-// Warp roles (320 threads): warps 0-7 softmax (warp w owns TMEM lane quarter
-// w & 3, i.e. 32 query rows, and column half w >> 2 of every S tile: 64 of the
-// 128 keys, and DH/2 of the O columns), warp 8 MMA issuer, warp 9 TMA.
+// Warp roles (576 threads): warps 0-15 softmax (warp w owns TMEM lane quarter
+// w & 3, i.e. 32 query rows, and column part w >> 2 of every S tile: 32 of the
+// 128 keys, and DH/4 of the O columns; four warps share each row's maximum and
+// sum through shared memory), warp 16 MMA issuer, warp 17 TMA.
 constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
 
 template <int DH, int FMT>
@@ -113,7 +116,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
   constexpr int QB = TILE * DH * 2;  // bytes of one [128][DH] tile
   constexpr int NBOX = DH / 64;
-  constexpr int OC = DH / 2;         // O columns per softmax warp
+  constexpr int OC = DH / 4;         // O columns per softmax warp
   constexpr int KS = fwd_kv_stages<DH>();
   constexpr int QN = fwd_q_bufs<DH>();
   constexpr int PN = fwd_p_bufs<DH>();
@@ -124,8 +127,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t sQ = base;             // QN buffers
   const uint32_t sK = sQ + QN * QB;     // KS stages
   const uint32_t sV = sK + KS * QB;     // KS stages
-  // row-statistics exchange: maxima [2 buf][2 half][128] fp32, then the row
-  // sums [2 half][128] fp32 (3 KB)
+  // row-statistics exchange: maxima [2 buf][4 part][128] fp32, then the row
+  // sums [4 part][128] fp32 (6 KB)
   const uint32_t sX = sV + KS * QB;
   float* xch = reinterpret_cast<float*>(gbase + (sX - base));
   const uint32_t bars = sX + kFwdXchBytes;
@@ -157,8 +160,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(q_full(s), 1);
       mbar_init(q_empty(s), 1);
       mbar_init(s_full(s), 1);
-      mbar_init(s_empty(s), 256);
-      mbar_init(p_full(s), 256);
+      mbar_init(s_empty(s), 512);  // every softmax thread
+      mbar_init(p_full(s), 512);
       mbar_init(p_empty(s), 1);
     }
     for (int s = 0; s < KS; ++s) {
@@ -169,7 +172,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     mbar_init(final_bar, 1);
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == kFwdWarpMma) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -186,7 +189,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   // The TMA and MMA warps run their loops in all 32 lanes (waits polled by
   // lane 0 and broadcast) and issue copies / MMAs from one elected lane, so
   // that the instructions' operands are warp-uniform.
-  if (warp == 9) {
+  if (warp == kFwdWarpTma) {
     // ------------------------------------------------ TMA producer
     if (elect_one()) {
       tma_prefetch_desc(&tmQ);
@@ -235,7 +238,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_wait_warp(k_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
       mbar_wait_warp(v_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
     }
-  } else if (warp == 8) {
+  } else if (warp == kFwdWarpMma) {
     // ------------------------------------------------ MMA issuer
     constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
     constexpr uint32_t IPV = umma_idesc_f16(FMT, 0, 1, TILE, DH);
@@ -291,12 +294,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     __syncwarp();
     mbar_wait_warp(final_bar, 0, p.err, FXB_DERR_ATTN_WAIT);
   } else {
-    // ------------------------------------------------ softmax warps 0..7
-    const int quarter = warp & 3, half = warp >> 2;
+    // ------------------------------------------------ softmax warps 0..15
+    const int quarter = warp & 3, part = warp >> 2;
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int col0 = half * 64;         // this thread's key columns within a tile
-    const uint32_t tOw = tO + lane_off + half * OC;  // this warp's O columns
+    const int col0 = part * 32;         // this thread's key columns within a tile
+    const uint32_t tOw = tO + lane_off + part * OC;  // this warp's O columns
     bool ok = true;
     int t = 0;  // tiles consumed (all items)
     // Waits are made warp-uniform: the tensor-memory accesses that follow are
@@ -308,9 +311,22 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     // wait until P.V of global tile u has completed (its P buffer is free and
     // its contribution is in O)
     auto wait_pv = [&](int u) -> bool { return uwait(p_empty(u % PN), (u / PN) & 1); };
+    // this warp's O columns: 16 at a time through registers
+    auto o_scale = [&](float alpha) {
+#pragma unroll
+      for (int c = 0; c < OC / 16; ++c) {
+        uint32_t orr[16];
+        tmem_ld16(tOw + c * 16, orr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int d = 0; d < 16; ++d) orr[d] = __float_as_uint(__uint_as_float(orr[d]) * alpha);
+        tmem_st16(tOw + c * 16, orr);
+      }
+      tmem_wait_st();
+    };
     // After a failed (timed-out) wait a thread keeps stepping through the
-    // tiles without waiting or computing, so that both warps of a pair always
-    // meet at the same named barriers.
+    // tiles without waiting or computing, so that the four warps of a row
+    // quarter always meet at the same named barriers.
     for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
       int qt, bh, n_kv;
       item_coords(w, qt, bh, n_kv);
@@ -321,31 +337,30 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const int sb = t & 1;
         if (ok && !uwait(s_full(sb), (t >> 1) & 1)) ok = false;
         const int kv0 = j * TILE + col0;
-        float sv[64];
+        float sv[32];
         float mx = -INFINITY;
         if (ok) {
           tc_fence_after();
-          uint32_t sr[64];
+          uint32_t sr[32];
           tmem_ld32(tS + sb * TILE + lane_off + col0, sr);
-          tmem_ld32(tS + sb * TILE + lane_off + col0 + 32, sr + 32);
           tmem_wait_ld();
           tc_fence_before();
           mbar_arrive(s_empty(sb));  // the scores are in registers
-          const bool need_mask = (kv0 + 64 > p.T) || (p.causal && kv0 + 64 > q0);
+          const bool need_mask = (kv0 + 32 > p.T) || (p.causal && kv0 + 32 > q0);
           // eight independent running maxima (short dependency chains)
           float mv[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) mv[i] = -INFINITY;
           if (need_mask) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
+            for (int i = 0; i < 32; ++i) {
               const int col = kv0 + i;
               sv[i] = (col >= p.T || (p.causal && col > q)) ? -INFINITY : __uint_as_float(sr[i]);
               mv[i & 7] = fmaxf(mv[i & 7], sv[i]);
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
+            for (int i = 0; i < 32; ++i) {
               sv[i] = __uint_as_float(sr[i]);
               mv[i & 7] = fmaxf(mv[i & 7], sv[i]);
             }
@@ -353,11 +368,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])),
                      fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
         }
-        // exchange the half-row maxima with the partner warp (double-buffered by tile parity)
-        float* xb = xch + (t & 1) * 256;
-        xb[half * 128 + r] = mx;
-        named_bar_sync(1 + quarter, 64);
-        mx = fmaxf(mx, xb[(half ^ 1) * 128 + r]);
+        // exchange the partial row maxima among the four warps of this row
+        // quarter (double-buffered by tile parity)
+        float* xb = xch + (t & 1) * 512;
+        xb[part * 128 + r] = mx;
+        named_bar_sync(1 + quarter, 128);
+        mx = fmaxf(fmaxf(xb[r], xb[128 + r]), fmaxf(xb[256 + r], xb[384 + r]));
         if (!ok) continue;
         const float m_new = fmaxf(m_ref, mx * p.scale_log2);
         if (j == 0) {
@@ -369,16 +385,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             if (!wait_pv(t - 1)) { ok = false; continue; }
             tc_fence_after();
             const float alpha = need ? ex2_ftz(m_ref - m_new) : 1.f;
-#pragma unroll
-            for (int c = 0; c < OC / 32; ++c) {
-              uint32_t orr[32];
-              tmem_ld32(tOw + c * 32, orr);
-              tmem_wait_ld();
-#pragma unroll
-              for (int d = 0; d < 32; ++d) orr[d] = __float_as_uint(__uint_as_float(orr[d]) * alpha);
-              tmem_st32(tOw + c * 32, orr);
-            }
-            tmem_wait_st();
+            o_scale(alpha);
             l *= alpha;
             if (need) m_ref = m_new;
           }
@@ -387,15 +394,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         // P buffer t % PN is free once P.V of tile t - PN has completed
         const int pb = t % PN;
         if (t >= PN && !wait_pv(t - PN)) { ok = false; continue; }
-        // probabilities -> P (16-bit pairs) in tensor memory: this thread's 64
-        // keys are the 32 columns half*32.. of P buffer pb in its lane; the
+        // probabilities -> P (16-bit pairs) in tensor memory: this thread's 32
+        // keys are the 16 columns part*16.. of P buffer pb in its lane; the
         // row sum uses eight partial sums (short dependency chains)
         float rsv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) rsv[i] = 0.f;
-        uint32_t pw[32];
+        uint32_t pw[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 4; ++u) {
           float pv[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -405,7 +412,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 #pragma unroll
           for (int i = 0; i < 4; ++i) pw[4 * u + i] = pack2<T16>(pv[2 * i], pv[2 * i + 1]);
         }
-        tmem_st32(tP + pb * 64 + lane_off + half * 32, pw);
+        tmem_st16(tP + pb * 64 + lane_off + part * 16, pw);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_full(pb));
@@ -413,32 +420,32 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
       const bool done = ok && wait_pv(t - 1);
       if (!done) ok = false;
-      // combine the two half-row sums (every softmax thread reaches this barrier)
-      float* xs = xch + 512;
-      xs[half * 128 + r] = l;
-      named_bar_sync(1 + quarter, 64);
-      l += xs[(half ^ 1) * 128 + r];
+      // combine the four partial row sums (every softmax thread reaches this barrier)
+      float* xs = xch + 1024;
+      xs[part * 128 + r] = l;
+      named_bar_sync(1 + quarter, 128);
+      l = (xs[r] + xs[128 + r]) + (xs[256 + r] + xs[384 + r]);
       if (done) {
         tc_fence_after();
         const int b = bh / p.H, h = bh - b * p.H;
         const float inv = 1.f / l;
-        T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh + half * OC;
+        T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh + part * OC;
 #pragma unroll
-        for (int c = 0; c < OC / 32; ++c) {
-          uint32_t orr[32];
-          tmem_ld32(tOw + c * 32, orr);  // warp-collective: every lane loads
+        for (int c = 0; c < OC / 16; ++c) {
+          uint32_t orr[16];
+          tmem_ld16(tOw + c * 16, orr);  // warp-collective: every lane loads
           tmem_wait_ld();
           if (q < p.T) {
 #pragma unroll
-            for (int d = 0; d < 32; d += 8) {
+            for (int d = 0; d < 16; d += 8) {
               float f[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(orr[d + i]) * inv;
-              *reinterpret_cast<uint4*>(orow + c * 32 + d) = pack8<T16>(f);
+              *reinterpret_cast<uint4*>(orow + c * 16 + d) = pack8<T16>(f);
             }
           }
         }
-        if (half == 0 && q < p.T) p.lse[(int64_t)bh * p.T + q] = (m_ref + log2f(l)) * kLn2;
+        if (part == 0 && q < p.T) p.lse[(int64_t)bh * p.T + q] = (m_ref + log2f(l)) * kLn2;
         tc_fence_before();
       }
     }
@@ -446,7 +453,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kFwdWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -518,7 +525,7 @@ FXB_DEV void red_add_v4f(float* addr, float a, float b, float c, float d) {
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                 const BwdParams p) {
@@ -932,7 +939,7 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
     once[dev & 63] = true;
   }
   dim3 grid(p.nkt, a->B * a->H);
-  fxb::pdl_launch(k, grid, kFwdThreads, bwd_smem(), st, mq, mk, mv, mdo, p);
+  fxb::pdl_launch(k, grid, kBwdThreads, bwd_smem(), st, mq, mk, mv, mdo, p);
   if ((r = fxb::check_launch("attn_bwd"))) return r;
   const int64_t n = rows * (DH / 8);
   fxb::pdl_launch(attn_bwd_post_kernel<T16, DH>, (unsigned)((n + 255) / 256), 256, 0, st, 
