@@ -9,16 +9,17 @@
 //                      dV = P^T dO, dK = dS^T Q, dQ = dS K.
 // B200 design (new): 128x128 tiles; TMA (4-D maps over the strided (B,T,H,D)
 // views, no copies, no multicast) feeds shared memory; one thread issues
-// tcgen05.mma into tensor memory; eight softmax warps read scores with
-// tcgen05.ld, two warps per TMEM lane quarter, each owning half of a tile's
-// columns (forward: row maxima exchanged through shared memory once per tile,
-// row sums combined at the end). Forward: persistent CTAs, P written to and
-// O accumulated in TMEM, lazily rescaled (details at the kernel). Backward
+// tcgen05.mma into tensor memory; softmax warps read scores with tcgen05.ld,
+// several warps per TMEM lane quarter, each owning a slice of a tile's columns
+// (forward: 16 warps, row maxima exchanged through shared memory once per
+// tile, row sums combined at the end; persistent CTAs, P written to and O
+// accumulated in TMEM, lazily rescaled: details at the kernel). Backward
 // works per key tile: S^T and dP^T land in TMEM, dV and dK accumulate in TMEM
-// across query tiles, and each dQ partial is reduced into an fp32 workspace
-// with vector red.add. Every wait is bounded (FXB_DERR_ATTN_WAIT); after an
-// expired wait a thread keeps stepping through its loop without work so that
-// named barriers are always met by every participant.
+// across query tiles, and each dQ partial is staged in shared memory and
+// added into an fp32 workspace with asynchronous TMA reductions. Every wait
+// is bounded (FXB_DERR_ATTN_WAIT); after an expired wait a thread keeps
+// stepping through its loop without work so that named barriers are always
+// met by every participant.
 #include "common.cuh"
 #include "internal.h"
 
@@ -186,113 +187,110 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tP = tmem + 256;  // P buffers (16-bit, two per column): 64 columns each
   const uint32_t tO = tmem + 384;  // O accumulator, DH columns
 
-  // The TMA and MMA warps run their loops in all 32 lanes (waits polled by
-  // lane 0 and broadcast) and issue copies / MMAs from one elected lane, so
-  // that the instructions' operands are warp-uniform.
+  // The TMA and MMA warps run their loops in lane 0 alone (the MMA issue is on
+  // the softmax's critical path: no warp-wide handshakes there).
   if (warp == kFwdWarpTma) {
     // ------------------------------------------------ TMA producer
-    if (elect_one()) {
+    if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      bool ok = true;
+      int t = 0;   // K/V tiles issued (all items)
+      int it = 0;  // items of this CTA
+      int q_armed = 0;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+        int qt, bh, n_kv;
+        item_coords(w, qt, bh, n_kv);
+        const int b = bh / p.H, h = bh - b * p.H;
+        const int qb = it % QN;
+        if (!mbar_wait(q_empty(qb), ((it / QN) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        {
+          mbar_expect_tx(q_full(qb), QB);
+  #pragma unroll
+          for (int c = 0; c < NBOX; ++c)
+            tma_load_4d(sQ + qb * QB + c * 16384, &tmQ, q_full(qb), 64 * c, qt * TILE, h, b);
+        }
+        q_armed = it + 1;
+        for (int j = 0; j < n_kv; ++j, ++t) {
+          const int st = t % KS;
+          if (!mbar_wait(kv_empty(st), ((t / KS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          {
+            mbar_expect_tx(k_full(st), QB);
+  #pragma unroll
+            for (int c = 0; c < NBOX; ++c)
+              tma_load_4d(sK + st * QB + c * 16384, &tmK, k_full(st), 64 * c, j * TILE, h, b);
+            mbar_expect_tx(v_full(st), QB);
+  #pragma unroll
+            for (int c = 0; c < NBOX; ++c)
+              tma_load_4d(sV + st * QB + c * 16384, &tmV, v_full(st), 64 * c, j * TILE, h, b);
+          }
+          }
+      }
+      // drain: every copy issued has landed before shared memory goes away
+      for (int i = (q_armed > QN ? q_armed - QN : 0); i < q_armed; ++i)
+        mbar_wait(q_full(i % QN), (i / QN) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      for (int u = (t > KS ? t - KS : 0); u < t; ++u) {
+        mbar_wait(k_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+        mbar_wait(v_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      }
     }
     __syncwarp();
-    bool ok = true;
-    int t = 0;   // K/V tiles issued (all items)
-    int it = 0;  // items of this CTA
-    int q_armed = 0;
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
-      int qt, bh, n_kv;
-      item_coords(w, qt, bh, n_kv);
-      const int b = bh / p.H, h = bh - b * p.H;
-      const int qb = it % QN;
-      if (!mbar_wait_warp(q_empty(qb), ((it / QN) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-      if (elect_one()) {
-        mbar_expect_tx(q_full(qb), QB);
-#pragma unroll
-        for (int c = 0; c < NBOX; ++c)
-          tma_load_4d(sQ + qb * QB + c * 16384, &tmQ, q_full(qb), 64 * c, qt * TILE, h, b);
-      }
-      __syncwarp();
-      q_armed = it + 1;
-      for (int j = 0; j < n_kv; ++j, ++t) {
-        const int st = t % KS;
-        if (!mbar_wait_warp(kv_empty(st), ((t / KS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-        if (elect_one()) {
-          mbar_expect_tx(k_full(st), QB);
-#pragma unroll
-          for (int c = 0; c < NBOX; ++c)
-            tma_load_4d(sK + st * QB + c * 16384, &tmK, k_full(st), 64 * c, j * TILE, h, b);
-          mbar_expect_tx(v_full(st), QB);
-#pragma unroll
-          for (int c = 0; c < NBOX; ++c)
-            tma_load_4d(sV + st * QB + c * 16384, &tmV, v_full(st), 64 * c, j * TILE, h, b);
-        }
-        __syncwarp();
-      }
-    }
-    // drain: every copy issued has landed before shared memory goes away
-    for (int i = (q_armed > QN ? q_armed - QN : 0); i < q_armed; ++i)
-      mbar_wait_warp(q_full(i % QN), (i / QN) & 1, p.err, FXB_DERR_ATTN_WAIT);
-    for (int u = (t > KS ? t - KS : 0); u < t; ++u) {
-      mbar_wait_warp(k_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
-      mbar_wait_warp(v_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
-    }
   } else if (warp == kFwdWarpMma) {
     // ------------------------------------------------ MMA issuer
-    constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
-    constexpr uint32_t IPV = umma_idesc_f16(FMT, 0, 1, TILE, DH);
-    bool ok = true;
-    int ts = 0;  // S tiles issued (all items)
-    int tp = 0;  // P.V products issued (all items)
-    int it = 0;
-    // S = Q K^T of the next tile (global tile ts) into S buffer ts & 1
-    auto issue_s = [&](uint32_t q_s) -> bool {
-      const int st = ts % KS, sb = ts & 1;
-      if (!mbar_wait_warp(k_full(st), (ts / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
-      if (!mbar_wait_warp(s_empty(sb), ((ts >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
-      tc_fence_after();
-      const uint64_t qd = kmajor_desc0(q_s), kd = kmajor_desc0(sK + st * QB);
-      if (elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < DH / 16; ++kk)
-          umma_f16(tS + sb * TILE, desc_add(qd, kmajor_off(kk)), desc_add(kd, kmajor_off(kk)), IS,
-                   kk > 0);
-        umma_commit(s_full(sb));
-      }
-      __syncwarp();
-      ++ts;
-      return true;
-    };
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
-      int qt, bh, n_kv;
-      item_coords(w, qt, bh, n_kv);
-      const int qb = it % QN;
-      const uint32_t q_s = sQ + qb * QB;
-      if (!mbar_wait_warp(q_full(qb), (it / QN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-      if (!issue_s(q_s)) { ok = false; break; }
-      for (int j = 0; j < n_kv && ok; ++j, ++tp) {
-        if (j + 1 < n_kv && !issue_s(q_s)) { ok = false; break; }
-        const int st = tp % KS, pb = tp % PN;
-        if (!mbar_wait_warp(p_full(pb), (tp / PN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-        if (!mbar_wait_warp(v_full(st), (tp / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+    if (lane == 0) {
+      constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
+      constexpr uint32_t IPV = umma_idesc_f16(FMT, 0, 1, TILE, DH);
+      bool ok = true;
+      int ts = 0;  // S tiles issued (all items)
+      int tp = 0;  // P.V products issued (all items)
+      int it = 0;
+      // S = Q K^T of the next tile (global tile ts) into S buffer ts & 1
+      auto issue_s = [&](uint32_t q_s) -> bool {
+        const int st = ts % KS, sb = ts & 1;
+        if (!mbar_wait(k_full(st), (ts / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(s_empty(sb), ((ts >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         tc_fence_after();
-        const uint64_t vd = mnmajor_desc0(sV + st * QB);
-        if (elect_one()) {
-          if (j + 1 == n_kv) umma_commit(q_empty(qb));  // the item's last S has read Q
-#pragma unroll
-          for (int kk = 0; kk < TILE / 16; ++kk)  // A = P from tensor memory, 16 keys = 8 columns
-            umma_f16_ta(tO, tP + pb * 64 + kk * 8, desc_add(vd, mnmajor_off(kk)), IPV,
-                        (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(p_empty(pb));
-          umma_commit(kv_empty(st));
+        const uint64_t qd = kmajor_desc0(q_s), kd = kmajor_desc0(sK + st * QB);
+        {
+  #pragma unroll
+          for (int kk = 0; kk < DH / 16; ++kk)
+            umma_f16(tS + sb * TILE, desc_add(qd, kmajor_off(kk)), desc_add(kd, kmajor_off(kk)), IS,
+                     kk > 0);
+          umma_commit(s_full(sb));
         }
-        __syncwarp();
+        ++ts;
+        return true;
+      };
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+        int qt, bh, n_kv;
+        item_coords(w, qt, bh, n_kv);
+        const int qb = it % QN;
+        const uint32_t q_s = sQ + qb * QB;
+        if (!mbar_wait(q_full(qb), (it / QN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        if (!issue_s(q_s)) { ok = false; break; }
+        for (int j = 0; j < n_kv && ok; ++j, ++tp) {
+          if (j + 1 < n_kv && !issue_s(q_s)) { ok = false; break; }
+          const int st = tp % KS, pb = tp % PN;
+          if (!mbar_wait(p_full(pb), (tp / PN) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          if (!mbar_wait(v_full(st), (tp / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t vd = mnmajor_desc0(sV + st * QB);
+          {
+            if (j + 1 == n_kv) umma_commit(q_empty(qb));  // the item's last S has read Q
+  #pragma unroll
+            for (int kk = 0; kk < TILE / 16; ++kk)  // A = P from tensor memory, 16 keys = 8 columns
+              umma_f16_ta(tO, tP + pb * 64 + kk * 8, desc_add(vd, mnmajor_off(kk)), IPV,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(p_empty(pb));
+            umma_commit(kv_empty(st));
+          }
+          }
       }
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, p.err, FXB_DERR_ATTN_WAIT);
     }
-    if (elect_one()) umma_commit(final_bar);
     __syncwarp();
-    mbar_wait_warp(final_bar, 0, p.err, FXB_DERR_ATTN_WAIT);
   } else {
     // ------------------------------------------------ softmax warps 0..15
     const int quarter = warp & 3, part = warp >> 2;
@@ -518,17 +516,12 @@ __global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, T16* __re
   *reinterpret_cast<uint4*>(dq + b * dq_sb + (int64_t)t * dq_st + h * dq_sh + d) = pack8<T16>(f);
 }
 
-FXB_DEV void red_add_v4f(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
-               "f"(c), "f"(d)
-               : "memory");
-}
 
 template <int FMT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                const BwdParams p) {
+                const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
   constexpr int DH = 64;
   using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
   constexpr int QB = TILE * DH * 2;  // 16 KB
@@ -542,7 +535,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t sDO = sQ + 2 * QB;   // 2 stages
   const uint32_t sPT = sDO + 2 * QB;  // [128 kv][128 q] 16-bit
   const uint32_t sDS = sPT + 32768;   // [128 kv][128 q] 16-bit
-  const uint32_t sStat = sDS + 32768; // lse2[2][128], delta[2][128] fp32
+  const uint32_t sDQ = sDS + 32768;   // dQ staging: 8 warps x [32 rows][32 fp32], 128B-swizzled
+  const uint32_t sStat = sDQ + 32768; // lse2[2][128], delta[2][128] fp32
   float* lse_s = reinterpret_cast<float*>(gbase + (sStat - base));
   float* del_s = lse_s + 256;
   const uint32_t bars = sStat + 2048;
@@ -568,7 +562,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(qdo_full(s), 1);
+      mbar_init(qdo_full(s), 1 + 32);  // TMA bytes + the producer warp's LSE / delta stores
       mbar_init(qdo_empty(s), 1);
     }
     mbar_init(s_full, 1);
@@ -592,23 +586,39 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
 
   if (warp == 9) {
-    // ------------------------------------------------ TMA producer
+    // ------------------------------------------------ producer: TMA (lane 0)
+    // plus the query tile's LSE (log2 units) and delta, four queries per lane,
+    // into the same double buffer as Q / dO
     if (lane == 0) {
       tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV); tma_prefetch_desc(&tmDO);
       mbar_expect_tx(kv_full, 2 * QB);
       tma_load_4d(sK, &tmK, kv_full, 0, kv0, h, b);
       tma_load_4d(sV, &tmV, kv_full, 0, kv0, h, b);
-      int armed = 0;
-      for (int it = 0; it < n_it; ++it) {
-        const int st = it & 1;
-        const int qq0 = (i0 + it) * TILE;
-        if (!mbar_wait(qdo_empty(st), ((it >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
+    }
+    __syncwarp();
+    int armed = 0;
+    for (int it = 0; it < n_it; ++it) {
+      const int st = it & 1;
+      const int qq0 = (i0 + it) * TILE;
+      if (!mbar_wait_warp(qdo_empty(st), ((it >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
+      if (lane == 0) {
         mbar_expect_tx(qdo_full(st), 2 * QB);
         tma_load_4d(sQ + st * QB, &tmQ, qdo_full(st), 0, qq0, h, b);
         tma_load_4d(sDO + st * QB, &tmDO, qdo_full(st), 0, qq0, h, b);
-        armed = it + 1;
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int qi = lane * 4 + i;
+        const int q = qq0 + qi;
+        const bool v = q < p.T;
+        lse_s[st * 128 + qi] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
+        del_s[st * 128 + qi] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
+      }
+      mbar_arrive(qdo_full(st));
+      armed = it + 1;
+    }
+    if (lane == 0) {
       mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
       for (int it = (armed > 2 ? armed - 2 : 0); it < armed; ++it)
         mbar_wait(qdo_full(it & 1), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
@@ -685,34 +695,16 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     uint8_t* pt = gbase + (sPT - base);
     uint8_t* ds = gbase + (sDS - base);
     bool ok = true;
-    // LSE / delta of a query tile are loaded from global memory one iteration
-    // ahead (threads 0..127, one query each) and published through the
-    // double-buffered shared arrays at the start of their iteration.
-    float lse_next = INFINITY, del_next = 0.f;
-    auto load_stats = [&](int it2) {
-      if (threadIdx.x < 128 && it2 < n_it) {
-        const int q = (i0 + it2) * TILE + (int)threadIdx.x;
-        const bool v = q < p.T;
-        lse_next = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
-        del_next = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
-      }
-    };
-    load_stats(0);
-    // After a failed (timed-out) wait a thread keeps stepping through the
-    // iterations without waiting or computing, so that all 256 threads always
-    // meet at the same named barriers.
+    // The query tile's LSE / delta were written to the double buffer by the
+    // producer warp before it arrived on qdo_full; waiting on that barrier here
+    // makes them visible.
     for (int it = 0; it < n_it; ++it) {
       const int q0 = (i0 + it) * TILE;
       const int sb = it & 1;
-      if (threadIdx.x < 128) {
-        lse_s[sb * 128 + threadIdx.x] = lse_next;
-        del_s[sb * 128 + threadIdx.x] = del_next;
-      }
-      named_bar_sync(1, 256);
-      load_stats(it + 1);
       if (!ok) continue;
       // waits are made warp-uniform: the tensor-memory loads that follow are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
+      if (!__all_sync(0xffffffffu, mbar_wait(qdo_full(sb), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) ||
+          !__all_sync(0xffffffffu, mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
       tc_fence_after();
       const bool diag = p.causal && (q0 < kv0 + TILE);
       uint32_t sr[64], dr[64];
@@ -751,25 +743,36 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
       fence_proxy_async_smem();
       mbar_arrive(ds_full);
-      // dQ partial of this query tile: row r is query q0 + r, head dims half*32..+32
+      // dQ partial of this query tile (row r is query q0 + r, head dims
+      // half*32..+32): tensor memory -> registers -> this warp's 128B-swizzled
+      // staging tile -> asynchronous fp32 TMA add-reduction into the dQ
+      // accumulator (rows past T are clipped by the tensor map)
       if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
       tc_fence_after();
       {
-        const int q = q0 + r;
         uint32_t rr[32];
         tmem_ld32(tDQ + lane_off + half * 32, rr);
         tmem_wait_ld();
-        if (q < p.T) {
-          float* dst = p.dq_acc + ((int64_t)bh * p.T + q) * DH + half * 32;
+        tc_fence_before();
+        mbar_arrive(dq_empty);  // the dQ partial is in registers
+        const uint32_t stg = sDQ + (uint32_t)warp * 4096u;
+        if (lane == 0) bulk_wait_read0();  // the previous reduction has read the staging tile
+        __syncwarp();
+        const uint32_t row = stg + (uint32_t)lane * 128u;
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            red_add_v4f(dst + 4 * u, __uint_as_float(rr[4 * u]), __uint_as_float(rr[4 * u + 1]),
-                        __uint_as_float(rr[4 * u + 2]), __uint_as_float(rr[4 * u + 3]));
+        for (int c = 0; c < 8; ++c)
+          st_shared_v4(row + (uint32_t)((c ^ (lane & 7)) << 4),
+                       make_uint4(rr[4 * c], rr[4 * c + 1], rr[4 * c + 2], rr[4 * c + 3]));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&tmDQ, stg, half * 32, q0 + quarter * 32, bh);
+          bulk_commit();
         }
       }
-      tc_fence_before();
-      mbar_arrive(dq_empty);
     }
+    if (lane == 0) bulk_wait_all0();  // dQ reductions complete before the kernel ends
+    __syncwarp();
     // final dK (scaled) and dV for key row kv, head dims half*32..+32
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT))) {
       tc_fence_after();
@@ -815,7 +818,7 @@ template <int DH> constexpr int fwd_smem() {
   return fwd_smem_raw<DH>() > kOneCtaPerSm ? fwd_smem_raw<DH>() : kOneCtaPerSm;
 }
 static_assert(fwd_smem<64>() <= 232448 && fwd_smem<128>() <= 232448, "forward shared memory");
-constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 2 * 32768 + 2048 + 1024 + 256; }
+constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 3 * 32768 + 2048 + 1024 + 256; }
 
 int make_map4(CUtensorMap* map, int dtype, const void* ptr, int D, int T, int H, int B,
               int64_t sb, int64_t st, int64_t sh) {
@@ -825,6 +828,16 @@ int make_map4(CUtensorMap* map, int dtype, const void* ptr, int D, int T, int H,
   CUtensorMapDataType dt =
       dtype == FXB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   return fxb::encode_tiled(map, dt, 4, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// fp32 dQ accumulator (B*H, T, D) for the backward's TMA add-reductions:
+// boxes of 32 rows x 32 columns (128 bytes, 128B swizzle)
+int make_map_dq(CUtensorMap* map, float* dq_acc, int D, int T, int BH) {
+  uint64_t dims[3] = {(uint64_t)D, (uint64_t)T, (uint64_t)BH};
+  uint64_t strides[2] = {(uint64_t)D * 4, (uint64_t)T * D * 4};
+  uint32_t box[3] = {32, 32, 1};
+  return fxb::encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_acc, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool strides_ok(int64_t sb, int64_t st, int64_t sh) {
@@ -916,6 +929,8 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
   if ((r = make_map4(&mk, a->dtype, a->k, DH, a->T, a->H, a->B, a->k_sb, a->k_st, a->k_sh))) return r;
   if ((r = make_map4(&mv, a->dtype, a->v, DH, a->T, a->H, a->B, a->v_sb, a->v_st, a->v_sh))) return r;
   if ((r = make_map4(&mdo, a->dtype, a->dout, DH, a->T, a->H, a->B, a->do_sb, a->do_st, a->do_sh))) return r;
+  CUtensorMap mdq;
+  if ((r = make_map_dq(&mdq, dq_acc, DH, a->T, a->B * a->H))) return r;
   BwdParams p;
   p.B = a->B; p.T = a->T; p.H = a->H;
   p.nqt = (a->T + TILE - 1) / TILE;
@@ -939,7 +954,7 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
     once[dev & 63] = true;
   }
   dim3 grid(p.nkt, a->B * a->H);
-  fxb::pdl_launch(k, grid, kBwdThreads, bwd_smem(), st, mq, mk, mv, mdo, p);
+  fxb::pdl_launch(k, grid, kBwdThreads, bwd_smem(), st, mq, mk, mv, mdo, mdq, p);
   if ((r = fxb::check_launch("attn_bwd"))) return r;
   const int64_t n = rows * (DH / 8);
   fxb::pdl_launch(attn_bwd_post_kernel<T16, DH>, (unsigned)((n + 255) / 256), 256, 0, st, 

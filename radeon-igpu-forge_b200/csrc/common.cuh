@@ -226,6 +226,13 @@ FXB_DEV void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int c0, int
       "r"(src), "r"(c0), "r"(c1)
       : "memory");
 }
+FXB_DEV void tma_reduce_add_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::
+          "l"(reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
 FXB_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // this thread's bulk groups have finished reading shared memory
 FXB_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
