@@ -692,9 +692,43 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const int kv = kv0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int qc0 = half * 64;
-    uint8_t* pt = gbase + (sPT - base);
-    uint8_t* ds = gbase + (sDS - base);
     bool ok = true;
+    // dQ partial of query tile it (row r is query row quarter*32 + lane of the
+    // tile, head dims half*32..+32): tensor memory -> registers -> this warp's
+    // 128B-swizzled staging tile -> asynchronous fp32 TMA add-reduction into
+    // the dQ accumulator (rows past T are clipped by the tensor map). Waiting
+    // for dq_full also means the tile's dV / dK / dQ MMAs no longer read P^T /
+    // dS^T in shared memory.
+    auto flush_dq = [&](int it) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) return false;
+      tc_fence_after();
+      const uint32_t stg = sDQ + (uint32_t)warp * 4096u;
+      if (lane == 0) bulk_wait_read0();  // the previous reduction has read the staging tile
+      __syncwarp();
+      const uint32_t row = stg + (uint32_t)lane * 128u;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {  // 16 columns at a time (register pressure)
+        uint32_t rr[16];
+        tmem_ld16(tDQ + lane_off + half * 32 + hh * 16, rr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          st_shared_v4(row + (uint32_t)(((4 * hh + c) ^ (lane & 7)) << 4),
+                       make_uint4(rr[4 * c], rr[4 * c + 1], rr[4 * c + 2], rr[4 * c + 3]));
+      }
+      tc_fence_before();
+      mbar_arrive(dq_empty);  // the dQ partial has left tensor memory
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_3d(&tmDQ, stg, half * 32, (i0 + it) * TILE + quarter * 32, bh);
+        bulk_commit();
+      }
+      return true;
+    };
+    // Software-pipelined: P^T / dS^T of tile it are computed in registers while
+    // the dV / dK / dQ MMAs of tile it-1 run; then tile it-1's dQ is flushed
+    // (which also frees the shared P^T / dS^T tiles) and tile it's are stored.
     // The query tile's LSE / delta were written to the double buffer by the
     // producer warp before it arrived on qdo_full; waiting on that barrier here
     // makes them visible.
@@ -707,70 +741,47 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           !__all_sync(0xffffffffu, mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
       tc_fence_after();
       const bool diag = p.causal && (q0 < kv0 + TILE);
-      uint32_t sr[64], dr[64];
-      tmem_ld32(tST + lane_off + qc0, sr);
-      tmem_ld32(tST + lane_off + qc0 + 32, sr + 32);
-      tmem_ld32(tDPT + lane_off + qc0, dr);
-      tmem_ld32(tDPT + lane_off + qc0 + 32, dr + 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(s_empty);  // S^T / dP^T are in registers: the next tile's may overwrite them
-      const float* ls = lse_s + sb * 128 + qc0;
-      const float* dl = del_s + sb * 128 + qc0;
+      uint32_t pw[32], dw[32];  // P^T and dS^T of this thread's 64 queries, 16-bit pairs
+#pragma unroll
+      for (int hq = 0; hq < 2; ++hq) {  // 32 queries at a time (register pressure)
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tST + lane_off + qc0 + hq * 32, sr);
+        tmem_ld32(tDPT + lane_off + qc0 + hq * 32, dr);
+        tmem_wait_ld();
+        if (hq == 1) {
+          tc_fence_before();
+          mbar_arrive(s_empty);  // S^T / dP^T are in registers: the next tile's may overwrite them
+        }
+        const float* ls = lse_s + sb * 128 + qc0 + hq * 32;
+        const float* dl = del_s + sb * 128 + qc0 + hq * 32;
+#pragma unroll
+        for (int qc = 0; qc < 32; qc += 2) {
+          float pp[2], dd[2];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            float e = ex2_ftz(fmaf(__uint_as_float(sr[qc + i]), p.scale_log2, -ls[qc + i]));
+            if (kv >= p.T || (diag && q0 + qc0 + hq * 32 + qc + i < kv)) e = 0.f;
+            pp[i] = e;
+            dd[i] = e * (__uint_as_float(dr[qc + i]) - dl[qc + i]);
+          }
+          pw[hq * 16 + (qc >> 1)] = pack2<T16>(pp[0], pp[1]);
+          dw[hq * 16 + (qc >> 1)] = pack2<T16>(dd[0], dd[1]);
+        }
+      }
+      if (it > 0 && !flush_dq(it - 1)) { ok = false; continue; }
+      uint8_t* pt = gbase + (sPT - base);
+      uint8_t* ds = gbase + (sDS - base);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        float pv[8], dsv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int qc = 8 * u + i;
-          float pp = ex2_ftz(fmaf(__uint_as_float(sr[qc]), p.scale_log2, -ls[qc]));
-          if (kv >= p.T || (diag && q0 + qc0 + qc < kv)) pp = 0.f;
-          pv[i] = pp;
-          dsv[i] = pp * (__uint_as_float(dr[qc]) - dl[qc]);
-        }
-        uint4 w, x;
-        w.x = pack2<T16>(pv[0], pv[1]);
-        w.y = pack2<T16>(pv[2], pv[3]);
-        w.z = pack2<T16>(pv[4], pv[5]);
-        w.w = pack2<T16>(pv[6], pv[7]);
-        x.x = pack2<T16>(dsv[0], dsv[1]);
-        x.y = pack2<T16>(dsv[2], dsv[3]);
-        x.z = pack2<T16>(dsv[4], dsv[5]);
-        x.w = pack2<T16>(dsv[6], dsv[7]);
-        // P^T / dS^T smem is free: the previous iteration's dQ commit was waited below
-        *reinterpret_cast<uint4*>(pt + sw128_offset(r, half * 8 + u)) = w;
-        *reinterpret_cast<uint4*>(ds + sw128_offset(r, half * 8 + u)) = x;
+        *reinterpret_cast<uint4*>(pt + sw128_offset(r, half * 8 + u)) =
+            make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
+        *reinterpret_cast<uint4*>(ds + sw128_offset(r, half * 8 + u)) =
+            make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
       }
       fence_proxy_async_smem();
       mbar_arrive(ds_full);
-      // dQ partial of this query tile (row r is query q0 + r, head dims
-      // half*32..+32): tensor memory -> registers -> this warp's 128B-swizzled
-      // staging tile -> asynchronous fp32 TMA add-reduction into the dQ
-      // accumulator (rows past T are clipped by the tensor map)
-      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
-      tc_fence_after();
-      {
-        uint32_t rr[32];
-        tmem_ld32(tDQ + lane_off + half * 32, rr);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(dq_empty);  // the dQ partial is in registers
-        const uint32_t stg = sDQ + (uint32_t)warp * 4096u;
-        if (lane == 0) bulk_wait_read0();  // the previous reduction has read the staging tile
-        __syncwarp();
-        const uint32_t row = stg + (uint32_t)lane * 128u;
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          st_shared_v4(row + (uint32_t)((c ^ (lane & 7)) << 4),
-                       make_uint4(rr[4 * c], rr[4 * c + 1], rr[4 * c + 2], rr[4 * c + 3]));
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_reduce_add_3d(&tmDQ, stg, half * 32, q0 + quarter * 32, bh);
-          bulk_commit();
-        }
-      }
     }
+    if (ok && n_it > 0 && !flush_dq(n_it - 1)) ok = false;
     if (lane == 0) bulk_wait_all0();  // dQ reductions complete before the kernel ends
     __syncwarp();
     // final dK (scaled) and dV for key row kv, head dims half*32..+32
