@@ -533,9 +533,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t sV = sK + QB;
   const uint32_t sQ = sV + QB;        // 2 stages
   const uint32_t sDO = sQ + 2 * QB;   // 2 stages
-  const uint32_t sPT = sDO + 2 * QB;  // [128 kv][128 q] 16-bit
-  const uint32_t sDS = sPT + 32768;   // [128 kv][128 q] 16-bit
-  const uint32_t sDQ = sDS + 32768;   // dQ staging: 8 warps x [32 rows][32 fp32], 128B-swizzled
+  const uint32_t sDS = sDO + 2 * QB;  // 2 buffers of dS^T [128 kv][128 q] 16-bit
+  const uint32_t sDQ = sDS + 65536;   // dQ staging: 8 warps x [32 rows][32 fp32], 128B-swizzled
   const uint32_t sStat = sDQ + 32768; // lse2[2][128], delta[2][128] fp32
   float* lse_s = reinterpret_cast<float*>(gbase + (sStat - base));
   float* del_s = lse_s + 256;
@@ -549,7 +548,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t dq_full = bars + 8u * 8;
   const uint32_t dq_empty = bars + 8u * 9;
   const uint32_t acc_full = bars + 8u * 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * 11);
+  const uint32_t pt_free = bars + 8u * 11;  // dV of the tile has read P^T from tensor memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x;
@@ -571,6 +571,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 256);
     mbar_init(acc_full, 1);
+    mbar_init(pt_free, 1);
     fence_mbar_init();
   }
   if (warp == 8) {
@@ -584,6 +585,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   pdl_trigger();
   pdl_wait();  // q / k / v (and dO, lse) come from earlier kernels on the stream
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
+  const uint32_t tPT = tmem + 448;  // P^T, 16-bit pairs (128 queries in 64 columns)
 
   if (warp == 9) {
     // ------------------------------------------------ producer: TMA (lane 0)
@@ -659,19 +661,20 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
         if (!mbar_wait(ds_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
-        const uint64_t ptd = kmajor_desc0(sPT), dsd = kmajor_desc0(sDS);
+        const uint32_t ds_s = sDS + (uint32_t)st * 32768u;
+        const uint64_t dsd = kmajor_desc0(ds_s);
         const uint64_t dom = mnmajor_desc0(do_s), qm = mnmajor_desc0(q_s);
 #pragma unroll
-        for (int kk = 0; kk < TILE / 16; ++kk)
-          umma_f16(tDV, desc_add(ptd, kmajor_off(kk)), desc_add(dom, mnmajor_off(kk)), I_KV,
-                   (it > 0 || kk > 0));
+        for (int kk = 0; kk < TILE / 16; ++kk)  // A = P^T from tensor memory, 16 queries = 8 columns
+          umma_f16_ta(tDV, tPT + kk * 8, desc_add(dom, mnmajor_off(kk)), I_KV, (it > 0 || kk > 0));
+        umma_commit(pt_free);
 #pragma unroll
         for (int kk = 0; kk < TILE / 16; ++kk)
           umma_f16(tDK, desc_add(dsd, kmajor_off(kk)), desc_add(qm, mnmajor_off(kk)), I_KV,
                    (it > 0 || kk > 0));
         if (!mbar_wait(dq_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
-        const uint64_t dsm = mnmajor_desc0(sDS), km = mnmajor_desc0(sK);
+        const uint64_t dsm = mnmajor_desc0(ds_s), km = mnmajor_desc0(sK);
 #pragma unroll
         for (int kk = 0; kk < TILE / 16; ++kk)
           umma_f16(tDQ, desc_add(dsm, mnmajor_off(kk)), desc_add(km, mnmajor_off(kk)), I_Q, kk > 0);
@@ -727,8 +730,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       return true;
     };
     // Software-pipelined: P^T / dS^T of tile it are computed in registers while
-    // the dV / dK / dQ MMAs of tile it-1 run; then tile it-1's dQ is flushed
-    // (which also frees the shared P^T / dS^T tiles) and tile it's are stored.
+    // the dV / dK / dQ MMAs of tile it-1 run; tile it's are stored (P^T to
+    // tensor memory, dS^T to a double-buffered shared tile), and tile it-1's
+    // dQ is flushed while tile it's dV / dK run.
     // The query tile's LSE / delta were written to the double buffer by the
     // producer warp before it arrived on qdo_full; waiting on that barrier here
     // makes them visible.
@@ -768,18 +772,26 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           dw[hq * 16 + (qc >> 1)] = pack2<T16>(dd[0], dd[1]);
         }
       }
-      if (it > 0 && !flush_dq(it - 1)) { ok = false; continue; }
-      uint8_t* pt = gbase + (sPT - base);
-      uint8_t* ds = gbase + (sDS - base);
+      // P^T -> tensor memory once dV of the previous tile has read it; dS^T ->
+      // shared buffer it & 1 (its previous user, tile it-2, finished with its
+      // dQ, which the flush of the previous iteration waited for)
+      if (it > 0 && !__all_sync(0xffffffffu, mbar_wait(pt_free, (it - 1) & 1, p.err, FXB_DERR_ATTN_WAIT))) {
+        ok = false;
+        continue;
+      }
+      tc_fence_after();
+      tmem_st32(tPT + lane_off + half * 32, pw);
+      uint8_t* ds = gbase + (sDS - base) + sb * 32768;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        *reinterpret_cast<uint4*>(pt + sw128_offset(r, half * 8 + u)) =
-            make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
+      for (int u = 0; u < 8; ++u)
         *reinterpret_cast<uint4*>(ds + sw128_offset(r, half * 8 + u)) =
             make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
-      }
+      tmem_wait_st();
       fence_proxy_async_smem();
+      tc_fence_before();
       mbar_arrive(ds_full);
+      // the previous tile's dQ is flushed while this tile's dV / dK run
+      if (it > 0 && !flush_dq(it - 1)) { ok = false; continue; }
     }
     if (ok && n_it > 0 && !flush_dq(n_it - 1)) ok = false;
     if (lane == 0) bulk_wait_all0();  // dQ reductions complete before the kernel ends
@@ -829,7 +841,7 @@ template <int DH> constexpr int fwd_smem() {
   return fwd_smem_raw<DH>() > kOneCtaPerSm ? fwd_smem_raw<DH>() : kOneCtaPerSm;
 }
 static_assert(fwd_smem<64>() <= 232448 && fwd_smem<128>() <= 232448, "forward shared memory");
-constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 3 * 32768 + 2048 + 1024 + 256; }
+constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 3 * 32768 + 2048 + 1024 + 256; }  // dS^T x2 + dQ staging
 
 int make_map4(CUtensorMap* map, int dtype, const void* ptr, int D, int T, int H, int B,
               int64_t sb, int64_t st, int64_t sh) {
