@@ -236,6 +236,8 @@ FXB_DEV void tma_reduce_add_3d(const CUtensorMap* map, uint32_t src, int c0, int
 FXB_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // this thread's bulk groups have finished reading shared memory
 FXB_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... all but the most recent one
+FXB_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // ... and their global writes are complete
 FXB_DEV void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 FXB_DEV void st_shared_v4(uint32_t addr, uint4 v) {

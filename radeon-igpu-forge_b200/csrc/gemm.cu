@@ -144,6 +144,23 @@ FXB_DEV void piece_r(const GemmParams& p, int m, int n0, int n8, bool use_pre, c
 template <typename CT>
 FXB_DEV void epilogue_math(const GemmParams& p, int m, int n0, int n8, float* v, float* z,
                            bool use_pre, const uint4* pre2) {
+  if constexpr (sizeof(CT) == 4) {
+    // fp32 C: store, accumulate, residual and bias only (the host rejects the
+    // activation epilogues), which keeps this instantiation small
+    if (p.epi == FXB_EPI_RESIDUAL) {
+      piece_r<CT>(p, m, n0, n8, false, pre2, z);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = v[i] * p.alpha + z[i];
+    } else if (p.epi == FXB_EPI_BIAS) {
+      load16_part<CT>(static_cast<const CT*>(p.bias) + n0, z, n8);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] += z[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] *= p.alpha;
+    }
+    return;
+  }
   switch (p.epi) {
     case FXB_EPI_RESIDUAL: {
       piece_r<CT>(p, m, n0, n8, use_pre, pre2, z);
@@ -226,9 +243,13 @@ template <typename CT> FXB_DEV void stage_piece(uint32_t buf, int lane, int h, c
   }
 }
 
-// before writing the staging buffers: the pieces issued last have been read
-FXB_DEV void stage_begin(int lane) {
-  if (lane == 0) bulk_wait_read0();
+// before writing a staging buffer: the group that last used it has been read
+// (all groups when both buffers are rewritten, else all but the newest)
+FXB_DEV void stage_begin(int lane, bool both) {
+  if (lane == 0) {
+    if (both) bulk_wait_read0();
+    else bulk_wait_read1();
+  }
   __syncwarp();
 }
 
@@ -258,77 +279,99 @@ FXB_DEV void stage_issue(const CUtensorMap* map0, int x0, const CUtensorMap* map
 template <int BN>
 struct EpiWarp {
   static constexpr int NCH = BN / 64;
-  // R (16-bit) of two chunks in flight: chunks 0 and 1 are loaded before the
-  // accumulator is ready, chunk c + 2 into slot c & 1 once chunk c is done
+  // R (16-bit) of two chunks in flight, as a ring that runs across tiles:
+  // chunk c of a tile sits in slot c & 1; once chunk c is done its slot is
+  // refilled with chunk c + 2, or with chunk c + 2 - NCH of the warp's next
+  // tile (NCH is even), so the next tile's first chunks load during this one.
   uint4 pre[2][4];
-  bool use_pre;
+  bool pre_ok[2];  // slot holds R of a row inside M (16-bit C, R-reading epilogue)
 
+  FXB_DEV void fill(const GemmParams& p, int slot, int m, int n0) {
+    pre_ok[slot] = epi_reads_r(p.epi) && p.c_dtype != FXB_DTYPE_F32 && m < p.M;
+    if (pre_ok[slot] && n0 < p.N) prefetch_r16(p, m, n0, pre[slot]);
+  }
+  // chunks 0 and 1 of the warp's first tile
   FXB_DEV void prefetch(const GemmParams& p, int m, int ntile0, int half) {
-    use_pre = epi_reads_r(p.epi) && p.c_dtype != FXB_DTYPE_F32 && m < p.M;
-    if (!use_pre) return;
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int n0 = ntile0 + (half * NCH + c) * 32;
-      if (n0 < p.N) prefetch_r16(p, m, n0, pre[c]);
-    }
+    for (int c = 0; c < 2; ++c) fill(p, c, m, ntile0 + (half * NCH + c) * 32);
   }
 
-  // one 16-column piece: TMEM -> registers -> epilogue math
+  // one 16-column piece: accumulator values (already loaded from tensor
+  // memory) -> epilogue math
   template <typename CT>
-  FXB_DEV int piece(const GemmParams& p, int m, int n0, uint32_t taddr, const uint4* pre2,
-                    float* v, float* z) {
-    uint32_t r[16];
-    tmem_ld16(taddr, r);
-    tmem_wait_ld();
+  FXB_DEV int piece(const GemmParams& p, int m, int n0, const uint32_t* r, int slot,
+                    const uint4* pre2, float* v, float* z) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
     const int n8 = max(0, min(2, (p.N - n0) >> 3));
-    epilogue_math<CT>(p, m, n0, n8, v, z, sizeof(CT) == 2 && use_pre, pre2);
+    epilogue_math<CT>(p, m, n0, n8, v, z, sizeof(CT) == 2 && pre_ok[slot], pre2);
     return n8;
   }
 
+  // Staging: an epilogue that writes only C alternates between the warp's two
+  // 2 KB buffers (one bulk group per piece, so a piece waits only for the
+  // group before last to have been read); one that also writes Z uses both
+  // buffers for every piece and waits for the previous group.
   template <typename CT>
   FXB_DEV void chunk(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmZ, int m,
-                     int m0, int n0, uint32_t taddr, int cc, uint32_t sbuf, int lane) {
+                     int m0, int n0, uint32_t taddr, int cc, uint32_t sbuf, int lane,
+                     uint32_t& cnt) {
     const bool wz = epi_writes_z(p);
     float v[16], z[16];
+    uint32_t acc[32];  // the chunk's 32 accumulator columns: one tensor-memory load
+    tmem_ld32(taddr, acc);
+    tmem_wait_ld();
     if constexpr (sizeof(CT) == 2) {
-      stage_begin(lane);
+      const uint32_t b = wz ? sbuf : sbuf + (cnt & 1u) * 2048u;
+      stage_begin(lane, wz);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        piece<CT>(p, m, n0 + 16 * h, taddr + 16 * h, &pre[cc & 1][2 * h], v, z);
-        stage_piece<CT>(sbuf, lane, h, v);
+        piece<CT>(p, m, n0 + 16 * h, acc + 16 * h, cc & 1, &pre[cc & 1][2 * h], v, z);
+        stage_piece<CT>(b, lane, h, v);
         if (wz) stage_piece<CT>(sbuf + 2048, lane, h, z);
       }
-      stage_issue(tmC, n0, wz ? tmZ : nullptr, n0, m0, false, sbuf, lane);
+      stage_issue(tmC, n0, wz ? tmZ : nullptr, n0, m0, false, b, lane);
+      ++cnt;
     } else {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int n8 = piece<CT>(p, m, n0 + 16 * h, taddr + 16 * h, &pre[cc & 1][2 * h], v, z);
+        const int n8 = piece<CT>(p, m, n0 + 16 * h, acc + 16 * h, cc & 1, &pre[cc & 1][2 * h], v, z);
         if (n8 == 0) continue;  // warp-uniform
-        stage_begin(lane);
-        stage_piece<CT>(sbuf, lane, 0, v);
+        const uint32_t b = wz ? sbuf : sbuf + (cnt & 1u) * 2048u;
+        stage_begin(lane, wz);
+        stage_piece<CT>(b, lane, 0, v);
         if (wz) stage_piece<CT>(sbuf + 2048, lane, 0, z);
         stage_issue(tmC, n0 + 16 * h, wz ? tmZ : nullptr, n0 + 16 * h, m0,
-                    p.epi == FXB_EPI_ACCUM_F32, sbuf, lane);
+                    p.epi == FXB_EPI_ACCUM_F32, b, lane);
+        ++cnt;
       }
     }
   }
 
+  // m_next / ntile0_next: this warp's row and first column in its next tile
+  // (has_next false when there is none)
   FXB_DEV void run(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmZ, int m,
-                   int m0, int ntile0, int half, uint32_t tbase, uint32_t sbuf, int lane) {
+                   int m0, int ntile0, int half, uint32_t tbase, uint32_t sbuf, int lane,
+                   uint32_t& cnt, bool has_next, int m_next, int ntile0_next) {
+    // unrolled by the prefetch ring's period (two chunks) only: the chunk
+    // body is large, and the instruction cache is shared with the MMA warp
+#pragma unroll 1
+    for (int cp = 0; cp < NCH; cp += 2)
 #pragma unroll
-    for (int cc = 0; cc < NCH; ++cc) {
+    for (int ci = 0; ci < 2; ++ci) {
+      const int cc = cp + ci;
       const int c = half * NCH + cc;
       const int n0 = ntile0 + c * 32;
-      if (n0 >= p.N) continue;  // warp-uniform
-      const uint32_t taddr = tbase + c * 32;
-      switch (p.c_dtype) {
-        case FXB_DTYPE_BF16: chunk<__nv_bfloat16>(p, tmC, tmZ, m, m0, n0, taddr, cc, sbuf, lane); break;
-        case FXB_DTYPE_F16: chunk<__half>(p, tmC, tmZ, m, m0, n0, taddr, cc, sbuf, lane); break;
-        default: chunk<float>(p, tmC, tmZ, m, m0, n0, taddr, cc, sbuf, lane); break;
+      if (n0 < p.N) {  // warp-uniform
+        const uint32_t taddr = tbase + c * 32;
+        switch (p.c_dtype) {
+          case FXB_DTYPE_BF16: chunk<__nv_bfloat16>(p, tmC, tmZ, m, m0, n0, taddr, ci, sbuf, lane, cnt); break;
+          case FXB_DTYPE_F16: chunk<__half>(p, tmC, tmZ, m, m0, n0, taddr, ci, sbuf, lane, cnt); break;
+          default: chunk<float>(p, tmC, tmZ, m, m0, n0, taddr, ci, sbuf, lane, cnt); break;
+        }
       }
-      if (cc + 2 < NCH && use_pre && n0 + 64 < p.N) prefetch_r16(p, m, n0 + 64, pre[cc & 1]);
+      if (cc + 2 < NCH) fill(p, ci, m, n0 + 64);
+      else if (has_next) fill(p, ci, m_next, ntile0_next + (half * NCH + cc + 2 - NCH) * 32);
     }
   }
 };
@@ -474,18 +517,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t sbuf = epi0 + (uint32_t)(warp - 2) * kEpiWarpBytes;
+    uint32_t ecnt = 0;  // staging pieces issued by this warp (buffer alternation)
     int abuf = 0;
     uint32_t aphase = 0;
+    EpiWarp<BN> ew;
+    if ((int)blockIdx.x < total_units) {
+      int tm, tn, split;
+      tile_coords(blockIdx.x, p, tm, tn, split);
+      ew.prefetch(p, tm * BM + row_in_tile, tn * BN, half);
+    }
     for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x) {
       int tm, tn, split;
       tile_coords(unit, p, tm, tn, split);
       const int m = tm * BM + row_in_tile;
-      EpiWarp<BN> ew;
-      ew.prefetch(p, m, tn * BN, half);
+      const int next = unit + gridDim.x;
+      int ntm = 0, ntn = 0, nsplit;
+      if (next < total_units) tile_coords(next, p, ntm, ntn, nsplit);
       if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
-      ew.run(p, &tmC, &tmZ, m, tm * BM + quarter * 32, tn * BN, half, tbase, sbuf, lane);
+      ew.run(p, &tmC, &tmZ, m, tm * BM + quarter * 32, tn * BN, half, tbase, sbuf, lane, ecnt,
+             next < total_units, ntm * BM + row_in_tile, ntn * BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(abuf));
@@ -675,19 +727,27 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     const int half = (warp - 2) >> 2;
     const int row_in_tile = (int)rank * 128 + quarter * 32 + lane;
     const uint32_t sbuf = epi0 + (uint32_t)(warp - 2) * kEpiWarpBytes;
+    uint32_t ecnt = 0;  // staging pieces issued by this warp (buffer alternation)
     int abuf = 0;
     uint32_t aphase = 0;
+    EpiWarp<BN> ew;
+    if (pair < total_units) {
+      int tm, tn, split;
+      tile_coords2(pair, p, tm, tn, split);
+      ew.prefetch(p, tm * 256 + row_in_tile, tn * BN, half);
+    }
     for (int unit = pair; unit < total_units; unit += npairs) {
       int tm, tn, split;
       tile_coords2(unit, p, tm, tn, split);
       const int m = tm * 256 + row_in_tile;
-      EpiWarp<BN> ew;
-      ew.prefetch(p, m, tn * BN, half);
+      const int next = unit + npairs;
+      int ntm = 0, ntn = 0, nsplit;
+      if (next < total_units) tile_coords2(next, p, ntm, ntn, nsplit);
       if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
       ew.run(p, &tmC, &tmZ, m, tm * 256 + (int)rank * 128 + quarter * 32, tn * BN, half, tbase,
-             sbuf, lane);
+             sbuf, lane, ecnt, next < total_units, ntm * 256 + row_in_tile, ntn * BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(abuf), 0));
@@ -847,6 +907,9 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
     return set_error(FXB_EINVAL, "gemm: Z misaligned");
   if (epi == FXB_EPI_ATOMIC_F32 && a->c_dtype != FXB_DTYPE_F32)
     return set_error(FXB_EINVAL, "gemm: accumulate epilogue needs fp32 C");
+  if (a->c_dtype == FXB_DTYPE_F32 && epi != FXB_EPI_STORE && epi != FXB_EPI_RESIDUAL &&
+      epi != FXB_EPI_BIAS && epi != FXB_EPI_ATOMIC_F32)
+    return set_error(FXB_EUNSUPPORTED, "gemm: epilogue %d with fp32 C (16-bit C only)", epi);
   if (epi < 0 || epi > FXB_EPI_DSILU) return set_error(FXB_EINVAL, "gemm: bad epilogue %d", epi);
   if (M == 0 || N == 0) return FXB_OK;
   if (K == 0) return set_error(FXB_EUNSUPPORTED, "gemm: K == 0");
