@@ -6,11 +6,11 @@
 One step = forward + backward + FlatAdamW update of the reference GPT
 architecture (V32768, L12, D768, H12, T1024) on a per-GPU micro-batch of 8
 sequences of Zipf(1.1) tokens (seed 3 + rank), bf16 compute with fp32 master
-weights. On one GPU the step is captured once in a CUDA graph
-(fxlm.GraphedStep, after the warm-up steps) and replayed; `--no-graph` runs it
-eagerly. For N > 1 the driver launches this under torchrun (one rank per GPU,
-NCCL) and the step runs eagerly; gradients are all-reduced in buckets that
-overlap backward.
+weights. The step is captured once in a CUDA graph (fxlm.GraphedStep, after
+the warm-up steps) and replayed; `--no-graph` runs it eagerly. For N > 1 the
+driver launches this under torchrun (one rank per GPU, NCCL); gradients are
+all-reduced in buckets that overlap backward, and those NCCL calls are part
+of the captured graph.
 
 Printed (rank 0, one JSON line): `value` = tokens/s of the whole job with the
 token batch already in HBM, timed on the device with CUDA events (max over
@@ -436,9 +436,10 @@ def run_ours(args, rank, world, local_rank):
         return float(t.item())
 
     # one process per GPU: the step is captured in a CUDA graph (fxlm.GraphedStep,
-    # warm-up steps run before capture); data-parallel runs step eagerly
+    # warm-up steps run before capture); with N > 1 the graph includes the
+    # bucketed NCCL gradient all-reduces
     graphed = None
-    if world == 1 and not args.no_graph:
+    if not args.no_graph:
         from fxlm import GraphedStep
         graphed = GraphedStep(model, opt, x_dev, y_dev, warmup=args.warmup)
 
@@ -538,6 +539,8 @@ def run_ours(args, rank, world, local_rank):
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
+    if graphed is not None:
+        graphed.release()  # a graph holding NCCL calls must go before the process group
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -552,7 +555,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-attn", action="store_true", help="skip the attention microbench")
     ap.add_argument("--no-graph", action="store_true",
-                    help="run the 1-GPU step eagerly instead of replaying a captured CUDA graph")
+                    help="run the step eagerly instead of replaying a captured CUDA graph")
     ap.add_argument("--micro", default=None,
                     help="per-kernel microbenchmarks instead of the step: all or a comma list "
                          "of gemm,attn,rmsnorm,ce,adamw")

@@ -136,6 +136,19 @@ int fxb_ce_fwd_grad(int32_t dtype, const void* logits, int64_t ld, const int64_t
 int fxb_adamw_sumsq(int32_t gdtype, const void* grad, int64_t n, float* scratch,
                     int32_t* flags, void* stream);
 
+/* Same result as fxb_adamw_sumsq, summed in a fixed order: per-block partial
+ * sums go to the workspace `ws` (fxb_adamw_sumsq_ws_bytes() bytes, 4-byte
+ * aligned, zero-filled once before its first use; every call leaves its
+ * ticket counter at zero) and the block that finishes last adds them in
+ * block order. The
+ * norm is then bitwise reproducible, so data-parallel ranks holding the same
+ * reduced gradient take bitwise identical optimizer steps. One workspace per
+ * stream (concurrent calls must not share it). No reference counterpart: the
+ * reference accumulates with atomicAdd (ml/fxlm/kernels/optim.hip:71). */
+size_t fxb_adamw_sumsq_ws_bytes(void);
+int fxb_adamw_sumsq_det(int32_t gdtype, const void* grad, int64_t n, float* scratch,
+                        int32_t* flags, void* ws, void* stream);
+
 /* One thread: found_inf = flags || !isfinite(scratch[0]);
  * norm = sqrt(scratch[0]) / scale; scratch[1] = clip coefficient
  * min(1, max_norm/(norm+1e-6)) (0 when found_inf); step += !found_inf;

@@ -34,10 +34,19 @@ template <typename P> FXB_DEV void store4(P* p, const float* f) {
   }
 }
 
+// Deterministic sum: per-block partials in a caller workspace, summed in
+// block order by the block that finishes last (ticket counter), so identical
+// gradients give a bitwise identical norm on every data-parallel rank.
+constexpr int kSumsqMaxBlocks = 2048;
+struct SumsqWs {
+  float part[kSumsqMaxBlocks];
+  unsigned int ticket;  // zero between calls
+};
+
 template <typename G>
 __global__ void __launch_bounds__(256)
 adamw_sumsq_kernel(const G* __restrict__ g, int64_t n, float* __restrict__ scratch,
-                   int* __restrict__ flags) {
+                   int* __restrict__ flags, SumsqWs* __restrict__ ws) {
   pdl_trigger();
   pdl_wait();  // inputs come from the previous kernel on the stream
   float ss = 0.f;
@@ -89,8 +98,34 @@ adamw_sumsq_kernel(const G* __restrict__ g, int64_t n, float* __restrict__ scrat
 #pragma unroll
     for (int o = 16; o; o >>= 1) bad |= __shfl_xor_sync(0xffffffffu, bad, o);
     if (lane == 0) {
-      if (ss != 0.f) atomicAdd(&scratch[0], ss);
       if (bad) atomicOr(flags, 1);
+      if (ws == nullptr) {
+        if (ss != 0.f) atomicAdd(&scratch[0], ss);
+      } else {
+        ws->part[blockIdx.x] = ss;
+      }
+    }
+  }
+  if (ws == nullptr) return;
+  __shared__ bool s_last;
+  if (threadIdx.x == 0) {
+    __threadfence();  // this block's partial before its ticket
+    s_last = atomicAdd(&ws->ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float t = 0.f;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) t += __ldcg(&ws->part[b]);
+  __shared__ float tred[8];
+  t = warp_sum(t);
+  if (lane == 0) tred[wid] = t;
+  __syncthreads();
+  if (wid == 0) {
+    t = warp_sum(lane < 8 ? tred[lane] : 0.f);
+    if (lane == 0) {
+      scratch[0] += t;
+      ws->ticket = 0u;  // ready for the next call
     }
   }
 }
@@ -230,8 +265,8 @@ int dispatch_update_p(int32_t pdtype, const void* g, float* master, float* m, fl
 
 extern "C" {
 
-int fxb_adamw_sumsq(int32_t gdtype, const void* grad, int64_t n, float* scratch, int32_t* flags,
-                    void* stream) {
+static int sumsq_launch(int32_t gdtype, const void* grad, int64_t n, float* scratch, int32_t* flags,
+                        SumsqWs* ws, void* stream) {
   if (fxb::dtype_size(gdtype) == 0) return fxb::set_error(FXB_EINVAL, "adamw_sumsq: bad dtype");
   if (n < 0 || !scratch || !flags) return fxb::set_error(FXB_EINVAL, "adamw_sumsq: bad args");
   if (n == 0) return FXB_OK;
@@ -239,19 +274,34 @@ int fxb_adamw_sumsq(int32_t gdtype, const void* grad, int64_t n, float* scratch,
   cudaStream_t st = fxb::as_stream(stream);
   int64_t want = ((n >> 2) + 255) / 256;
   int64_t cap = (int64_t)fxb::num_sms() * 8;
+  if (cap > kSumsqMaxBlocks) cap = kSumsqMaxBlocks;
   int blocks = (int)(want < cap ? want : cap);
   if (blocks < 1) blocks = 1;
   switch (gdtype) {
     case FXB_DTYPE_BF16:
-      fxb::pdl_launch(adamw_sumsq_kernel<__nv_bfloat16>, blocks, 256, 0, st, static_cast<const __nv_bfloat16*>(grad), n, scratch, flags);
+      fxb::pdl_launch(adamw_sumsq_kernel<__nv_bfloat16>, blocks, 256, 0, st, static_cast<const __nv_bfloat16*>(grad), n, scratch, flags, ws);
       break;
     case FXB_DTYPE_F16:
-      fxb::pdl_launch(adamw_sumsq_kernel<__half>, blocks, 256, 0, st, static_cast<const __half*>(grad), n, scratch, flags);
+      fxb::pdl_launch(adamw_sumsq_kernel<__half>, blocks, 256, 0, st, static_cast<const __half*>(grad), n, scratch, flags, ws);
       break;
     default:
-      fxb::pdl_launch(adamw_sumsq_kernel<float>, blocks, 256, 0, st, static_cast<const float*>(grad), n, scratch, flags);
+      fxb::pdl_launch(adamw_sumsq_kernel<float>, blocks, 256, 0, st, static_cast<const float*>(grad), n, scratch, flags, ws);
   }
   return fxb::check_launch("adamw_sumsq");
+}
+
+int fxb_adamw_sumsq(int32_t gdtype, const void* grad, int64_t n, float* scratch, int32_t* flags,
+                    void* stream) {
+  return sumsq_launch(gdtype, grad, n, scratch, flags, nullptr, stream);
+}
+
+size_t fxb_adamw_sumsq_ws_bytes(void) { return sizeof(SumsqWs); }
+
+int fxb_adamw_sumsq_det(int32_t gdtype, const void* grad, int64_t n, float* scratch,
+                        int32_t* flags, void* ws, void* stream) {
+  if (!ws || (reinterpret_cast<uintptr_t>(ws) & 3u))
+    return fxb::set_error(FXB_EINVAL, "adamw_sumsq_det: workspace NULL or not 4-byte aligned");
+  return sumsq_launch(gdtype, grad, n, scratch, flags, static_cast<SumsqWs*>(ws), stream);
 }
 
 int fxb_adamw_final(float* scratch, int32_t* flags, int32_t* step, float* found_inf,

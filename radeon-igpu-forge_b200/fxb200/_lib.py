@@ -80,6 +80,8 @@ SIGNATURES = {
     "fxb_ce_fwd_grad": (ctypes.c_int, [_i32, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32,
                                        _i64, _vp]),
     "fxb_adamw_sumsq": (ctypes.c_int, [_i32, _vp, _i64, _vp, _vp, _vp]),
+    "fxb_adamw_sumsq_ws_bytes": (ctypes.c_size_t, []),
+    "fxb_adamw_sumsq_det": (ctypes.c_int, [_i32, _vp, _i64, _vp, _vp, _vp, _vp]),
     "fxb_adamw_final": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _f32, _vp]),
     "fxb_adamw_update": (ctypes.c_int, [_i32, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp,
                                         _i32, _vp, _vp, _vp, _vp, _f32, _vp, _f32, _f32,

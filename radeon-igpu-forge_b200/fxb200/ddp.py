@@ -38,6 +38,10 @@ class DataParallel:
         self.world = dist.get_world_size(process_group)
         dev = opt.grad.device
         self.stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
+        # the hooks only enqueue work (events, NCCL on a side stream, stream
+        # waits) and never read results on the host, so a step that runs
+        # them can be captured in a CUDA graph (fxlm.GraphedStep)
+        self.graph_capturable = self.stream is not None
         self._pending = []      # (work, bucket) launched this backward
         self._done = set()
         # bucket = contiguous range of the flat gradient: one per block

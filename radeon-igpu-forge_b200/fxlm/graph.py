@@ -13,10 +13,14 @@ work without changing a single kernel or its arguments.
 Conditions (checked where cheap): fixed batch shape; the optimizer is a
 FlatAdamW whose gradient buffer is consumed by its update (so no zeroing op
 is needed between replays); the learning rate is read from `opt.lr_dev`, a
-device scalar written before each replay; no data-parallel hooks (the
-NCCL bucket path runs eagerly). The warm-up steps before capture are real
-training steps (they also trigger every lazy initialisation: library load,
-tensor-map encoders, shared-memory attributes).
+device scalar written before each replay; optimizer pre-step hooks only if
+their owner declares `graph_capturable` (fxb200.ddp.DataParallel does: its
+bucket all-reduces are NCCL calls on a side stream forked from the capturing
+stream, so they are recorded into the graph and replayed with it). The
+warm-up steps before capture are real training steps (they also trigger every
+lazy initialisation: library load, tensor-map encoders, shared-memory
+attributes, NCCL communicators). A graph that holds NCCL calls must be
+released (`release()`) before the process group is destroyed.
 """
 import torch
 
@@ -25,9 +29,10 @@ from fxb200 import _lib
 
 class GraphedStep:
     def __init__(self, model, opt, x_example, y_example, warmup=3):
-        if getattr(opt, "pre_step_hooks", None):
-            raise ValueError("GraphedStep: optimizer has pre-step hooks (data parallel); "
-                             "run the step eagerly")
+        for h in getattr(opt, "pre_step_hooks", None) or ():
+            if not getattr(getattr(h, "__self__", None), "graph_capturable", False):
+                raise ValueError("GraphedStep: optimizer has a pre-step hook that cannot be "
+                                 "captured; run the step eagerly")
         if warmup < 1:
             raise ValueError("GraphedStep: warmup >= 1 (lazy initialisation must happen "
                              "before capture)")
@@ -71,3 +76,11 @@ class GraphedStep:
             self.opt.lr_dev.fill_(float(lr))
         self.graph.replay()
         return self.loss
+
+    def release(self):
+        """Free the captured graph (required before destroy_process_group when
+        the step holds NCCL collectives)."""
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None

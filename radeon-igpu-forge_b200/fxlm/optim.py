@@ -86,6 +86,10 @@ class FlatAdamW:
             raise ValueError(f"{len(ends)} parameters > 1024 segments supported")
 
         self.scratch = torch.zeros(2, device=dev, dtype=torch.float32)
+        # per-block partial sums of the gradient norm, added in a fixed order
+        # (bitwise identical norms on data-parallel ranks); kept zeroed by the kernel
+        ws_words = (int(_lib.load().fxb_adamw_sumsq_ws_bytes()) + 3) // 4
+        self._sumsq_ws = torch.zeros(ws_words, device=dev, dtype=torch.int32)
         self._flags = torch.zeros((), device=dev, dtype=torch.int32)
         self._step_ctr = torch.zeros((), device=dev, dtype=torch.int32)
         self._found_inf = torch.zeros((), device=dev, dtype=torch.float32)
@@ -128,8 +132,8 @@ class FlatAdamW:
             hook(self)
         st = _lib.stream_ptr(self.grad.device)
         P = _lib.ptr
-        _lib.call("fxb_adamw_sumsq", 0, P(self.grad), self.numel, P(self.scratch),
-                  P(self._flags), st)
+        _lib.call("fxb_adamw_sumsq_det", 0, P(self.grad), self.numel, P(self.scratch),
+                  P(self._flags), P(self._sumsq_ws), st)
         _lib.call("fxb_adamw_final", P(self.scratch), P(self._flags), P(self._step_ctr),
                   P(self._found_inf), P(self._norm), P(self.scale),
                   float(self.max_grad_norm), st)

@@ -302,6 +302,41 @@ def test_embedding(dev):
     assert (pos.grad.float() - gp).abs().max().item() < 3e-2 * max(1.0, gp.abs().max().item())
 
 
+@pytest.mark.parametrize("n", [8, 1000, 110_906_112 // 4 + 8])
+def test_adamw_sumsq_deterministic(dev, n):
+    """fxb_adamw_sumsq_det: the sum of squares (fp64 reference, fp32 rounding
+    bound) and the non-finite flag of fxb_adamw_sumsq, bitwise identical on
+    every call, with the workspace's ticket counter reset."""
+    from fxb200 import _lib
+    P, st = _lib.ptr, _lib.stream_ptr(dev)
+    torch.manual_seed(11)
+    g = torch.randn(n, device=dev) * 3.0
+    ws = torch.zeros((int(_lib.load().fxb_adamw_sumsq_ws_bytes()) + 3) // 4, device=dev,
+                     dtype=torch.int32)
+    ref = float((g.double() ** 2).sum())
+    outs = []
+    for _ in range(3):
+        sc = torch.zeros(2, device=dev)
+        fl = torch.zeros((), device=dev, dtype=torch.int32)
+        _lib.call("fxb_adamw_sumsq_det", 0, P(g), n, P(sc), P(fl), P(ws), st)
+        torch.cuda.synchronize()
+        outs.append(sc[0].item())
+        assert int(fl) == 0
+        assert int(ws[-1]) == 0  # the ticket counter (last word) is reset
+    assert outs[0] == outs[1] == outs[2]
+    assert abs(outs[0] - ref) <= 1e-5 * ref
+    sc = torch.zeros(2, device=dev)
+    fl = torch.zeros((), device=dev, dtype=torch.int32)
+    _lib.call("fxb_adamw_sumsq", 0, P(g), n, P(sc), P(fl), st)
+    torch.cuda.synchronize()
+    assert abs(sc[0].item() - ref) <= 1e-5 * ref
+    g[n // 2] = float("nan")
+    sc.zero_()
+    _lib.call("fxb_adamw_sumsq_det", 0, P(g), n, P(sc), P(fl), P(ws), st)
+    torch.cuda.synchronize()
+    assert int(fl) == 1
+
+
 def test_device_error_word_clear(dev):
     from fxb200 import _lib
     torch.cuda.synchronize()
