@@ -208,6 +208,13 @@ typedef struct fxb_gemm_args {
   void* Z;           /* second output (pre-activation), dtype c_dtype, row stride ldz */
   int64_t ldz;
   const void* bias;  /* (N,), dtype c_dtype */
+  /* Optional scratch (NULL: none) of workspace_bytes >= fxb_gemm_workspace_size()
+   * bytes, 16-byte aligned, whose first 4096 bytes (arrival counters) are
+   * zero-filled once before its first use (the kernels leave them at zero). With it, tiles that would leave most of the
+   * last wave idle are split along K and their pieces reduced through it; it
+   * must not be shared by calls that can run concurrently (one per stream). */
+  void* workspace;
+  int64_t workspace_bytes;
 } fxb_gemm_args;
 
 /* tcgen05 / TMEM GEMM with TMA-fed operands. Requires K % 8 == 0 for K-major
@@ -219,10 +226,17 @@ typedef struct fxb_gemm_args {
  * (ml/fxgpu/fused_linear.py:94). */
 int fxb_gemm(const fxb_gemm_args* args, void* stream);
 
+/* Bytes of fxb_gemm_args.workspace that enable the tail split on the current
+ * device. No reference counterpart (the reference's rocBLAS calls own their
+ * scratch). */
+size_t fxb_gemm_workspace_size(void);
+
 /* The tile configuration fxb_gemm would use for this problem on the current
  * device: *pair = 1 for the CTA-pair (cta_group::2, 256-row) kernel, 0 for the
  * single-CTA (128-row) kernel; *bn = tile width; *splits = split-K factor
- * (> 1 only for FXB_EPI_ACCUM_F32). Diagnostic; no reference counterpart. */
+ * (> 1 for FXB_EPI_ACCUM_F32), or for the other epilogues the number of K
+ * pieces of each tail tile when a workspace is given (1: no tail split).
+ * Diagnostic; no reference counterpart. */
 int fxb_gemm_plan(int32_t M, int32_t N, int32_t K, int32_t epilogue, int32_t* pair,
                   int32_t* bn, int32_t* splits);
 

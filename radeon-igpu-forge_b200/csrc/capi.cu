@@ -114,7 +114,7 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, const 
 
 extern "C" {
 
-int fxb_version(void) { return 100; }  // 0.1.0
+int fxb_version(void) { return 200; }  // 0.2.0: fxb_gemm_args.workspace
 
 const char* fxb_last_error(void) { return fxb::t_last_error.c_str(); }
 

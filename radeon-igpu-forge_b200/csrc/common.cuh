@@ -153,6 +153,27 @@ FXB_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int errcode) {
   }
 }
 
+// Bounded spin until the global counter *c reaches `target` (acquire load at
+// GPU scope, so writes released before the increments are visible after it
+// returns true); false (and errcode ORed into *err) after FXB_WAIT_CYCLES.
+FXB_DEV unsigned ld_acquire_gpu(const unsigned* c) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+  return v;
+}
+FXB_DEV bool spin_until_geq(const unsigned* c, unsigned target, int* err, int errcode) {
+  if (ld_acquire_gpu(c) >= target) return true;
+  const long long t0 = clock64();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(c) >= target) return true;
+    if (clock64() - t0 > FXB_WAIT_CYCLES) {
+      atomicOr(err, errcode);
+      return false;
+    }
+  }
+}
+
 // Programmatic dependent launch: pdl_wait blocks until the previous kernel on
 // the stream has completed and its memory is visible (a no-op when the launch
 // had no programmatic dependency); pdl_trigger lets the next kernel's CTAs be

@@ -42,22 +42,37 @@ namespace {
 using namespace fxb::gk;
 
 struct Plan {
-  bool pair;   // 2-SM (cta_group::2, 256-row tiles) or 1-SM (128-row tiles)
-  int BN;      // tile width
-  int splits;  // split-K factor (fp32 accumulate epilogue only)
+  bool pair;        // 2-SM (cta_group::2, 256-row tiles) or 1-SM (128-row tiles)
+  int BN;           // tile width
+  int splits;       // split-K factor (fp32 accumulate epilogue only)
+  int tail_splits;  // K pieces per tail tile (1: no tail split)
 };
 
-// Choose tile shape and split-K by a cost model of the persistent schedule:
-// waves x per-unit time, where a unit's k-block time is bounded by the
-// shared-memory traffic of its MMA operands plus the TMA writes (128 B/clk
+// Workspace of the tail split: arrival counters, then the contributors' fp32
+// partial tiles (at most one 128 x 256 tile per SM: tail tiles x (pieces - 1)
+// never exceed the slots of one wave).
+constexpr size_t kWsCounterBytes = 4096;
+size_t workspace_bytes(int sms) { return kWsCounterBytes + (size_t)sms * 128 * 256 * 4; }
+
+// Choose tile shape, split-K and tail split by a cost model of the persistent
+// schedule: waves x per-unit time, where a unit's k-block time is bounded by
+// the shared-memory traffic of its MMA operands plus the TMA writes (128 B/clk
 // per SM) and the epilogue of a tile overlaps the next tile's mainloop.
 // Per-SM cycles per 64-deep k-block: 1-SM 128x128: 512, 1-SM 128x256: 768,
 // 2-SM 256x128: 384, 2-SM 256x256: 512 (the last one is tensor-bound).
-// `mode` (FXB_GEMM_FORCE=1sm|2sm, tests) restricts the choice.
-Plan plan(int M, int N, int K, bool allow_split, int sms, int mode) {
+// Epilogue per 128-row CTA tile (measured): ~18 cycles per column to store,
+// +10 when it reads R, +12 when it also writes Z. A tail split replaces the
+// last, partly filled wave of whole tiles by one wave of K pieces plus the
+// partial-tile exchange (~8 cycles per column per piece at ~64 B/clk of L2
+// traffic per SM). `mode` (FXB_GEMM_FORCE=1sm|2sm, tests) restricts the choice.
+Plan plan(int M, int N, int K, int epi, bool tail_ok, int sms, int mode) {
+  const bool allow_split = epi == FXB_EPI_ACCUM_F32;
+  const bool reads_r = epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU;
+  const bool writes_z = epi == FXB_EPI_GELU || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU;
+  const double epi_col = 18.0 + (reads_r ? 10.0 : 0.0) + (writes_z ? 12.0 : 0.0);
   const int nkb = (K + BK - 1) / BK;
   double best = 1e30;
-  Plan out{false, 128, 1};
+  Plan out{false, 128, 1, 1};
   for (int pair = 1; pair >= 0; --pair) {
     if ((mode == 1 && pair) || (mode == 2 && !pair)) continue;
     const int rows = pair ? 256 : 128;
@@ -66,16 +81,29 @@ Plan plan(int M, int N, int K, bool allow_split, int sms, int mode) {
     for (int bn : {256, 128}) {
       const int tn = (N + bn - 1) / bn;
       const double t_kb = pair ? (bn == 256 ? 512.0 : 384.0) : (bn == 256 ? 768.0 : 512.0);
+      const double epi_t = bn * epi_col;
       for (int s = 1; s <= (allow_split ? 16 : 1); s *= 2) {
         if (s > 1 && nkb / s < 4) break;  // keep >= 4 k-blocks per split
         const int kbs = (nkb + s - 1) / s;
         const long units = (long)tm * tn * s;
         const long waves = (units + slots - 1) / slots;
         const double mainloop = kbs * t_kb + 600.0;  // + pipeline fill
-        const double epi = bn * 6.0;                  // TMEM -> registers -> global per tile
-        const double cost = (double)waves * (mainloop > epi ? mainloop : epi) + (s > 1 ? 0.5 * units : 0);
-        if (cost < best - 1e-9) { best = cost; out = Plan{pair != 0, bn, s}; }
+        const double cost = (double)waves * (mainloop > epi_t ? mainloop : epi_t) + (s > 1 ? 0.5 * units : 0);
+        if (cost < best - 1e-9) { best = cost; out = Plan{pair != 0, bn, s, 1}; }
       }
+      if (allow_split || !tail_ok) continue;
+      const long tiles = (long)tm * tn;
+      const long full_waves = tiles / slots, tail = tiles % slots;
+      if (tail == 0) continue;
+      int S = (int)(slots / tail);
+      if (S > 8) S = 8;
+      if (S > nkb / 2) S = nkb / 2;
+      if (S < 2) continue;
+      const double main_full = nkb * t_kb + 600.0;
+      const double main_piece = ((nkb + S - 1) / S) * t_kb + 600.0;
+      const double cost = (double)full_waves * (main_full > epi_t ? main_full : epi_t) +
+                          (main_piece > epi_t ? main_piece : epi_t) + 8.0 * bn * S;
+      if (cost < best - 1e-9) { best = cost; out = Plan{pair != 0, bn, 1, S}; }
     }
   }
   return out;
@@ -163,7 +191,9 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
   int* err = dev_error_ptr();
   if (!err) return FXB_ECUDA;
   const int sms = num_sms();
-  Plan pl = plan(M, N, K, epi == FXB_EPI_ATOMIC_F32, sms, force_mode());
+  const bool tail_ok = a->workspace && aligned16(a->workspace) &&
+                       a->workspace_bytes >= (int64_t)workspace_bytes(sms);
+  Plan pl = plan(M, N, K, epi, tail_ok, sms, force_mode());
   const int BN = pl.BN;
   int splits = pl.splits;
   if (force_splits > 0 && epi == FXB_EPI_ATOMIC_F32) splits = force_splits;
@@ -195,6 +225,21 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
   p.splits = splits;
   p.kb_per_split = (p.num_kb + splits - 1) / splits;
   p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;  // no empty splits
+  const long slots = pl.pair ? sms / 2 : sms;
+  const long tiles = (long)p.tiles_m * p.tiles_n;
+  p.tail_splits = pl.tail_splits;
+  p.tail_kb = (p.num_kb + pl.tail_splits - 1) / pl.tail_splits;
+  if (pl.tail_splits > 1) {
+    p.tail_splits = (p.num_kb + p.tail_kb - 1) / p.tail_kb;  // no empty pieces
+    p.full_units = (int)((tiles / slots) * slots);
+    p.total_units = p.full_units + (int)(tiles - p.full_units) * p.tail_splits;
+  } else {
+    p.full_units = (int)(tiles * p.splits);
+    p.total_units = p.full_units;
+  }
+  p.ws_cnt = static_cast<unsigned*>(a->workspace);
+  p.ws = tail_ok ? reinterpret_cast<float*>(static_cast<char*>(a->workspace) + kWsCounterBytes)
+                 : nullptr;
   p.epi = epi;
   p.c_dtype = a->c_dtype;
   p.alpha = a->alpha;
@@ -203,9 +248,8 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
   p.Z = a->Z; p.ldz = a->ldz;
   p.bias = a->bias;
   p.err = err;
-  const long units = (long)p.tiles_m * p.tiles_n * p.splits;
+  const long units = p.total_units;
   const bool amn = a->a_trans != 0, bmn = a->b_trans != 0;
-  const long slots = pl.pair ? sms / 2 : sms;
   const long used = units < slots ? units : slots;
   const int grid = (int)(pl.pair ? 2 * used : used);
   const int fmt = a->dtype == FXB_DTYPE_BF16 ? 1 : 0;
@@ -223,13 +267,15 @@ extern "C" int fxb_gemm(const fxb_gemm_args* args, void* stream) {
   return fxb::gemm_launch(args, args->epilogue, 0, fxb::as_stream(stream));
 }
 
+extern "C" size_t fxb_gemm_workspace_size(void) { return workspace_bytes(fxb::num_sms()); }
+
 extern "C" int fxb_gemm_plan(int32_t M, int32_t N, int32_t K, int32_t epilogue, int32_t* pair,
                              int32_t* bn, int32_t* splits) {
   if (!pair || !bn || !splits || M < 0 || N < 0 || K < 0)
     return fxb::set_error(FXB_EINVAL, "gemm_plan: bad arguments");
-  Plan pl = plan(M, N, K, epilogue == FXB_EPI_ACCUM_F32, fxb::num_sms(), force_mode());
+  Plan pl = plan(M, N, K, epilogue, true, fxb::num_sms(), force_mode());
   *pair = pl.pair ? 1 : 0;
   *bn = pl.BN;
-  *splits = pl.splits;
+  *splits = epilogue == FXB_EPI_ACCUM_F32 ? pl.splits : pl.tail_splits;
   return FXB_OK;
 }

@@ -17,16 +17,19 @@
 //     the epilogue of tile i overlaps the mainloop of tile i+1;
 //   - operands K-major or MN-major (transposed) so forward, dX and dW GEMMs
 //     all read their operands in place.
-// Every mbarrier wait is bounded (common.cuh); on expiry the kernel records
+//   - tail split: when the tiles do not fill the last wave, the leftover tiles
+//     are cut along K into pieces run side by side; piece 0 of a tile waits
+//     (bounded) for the others' fp32 partial tiles, adds them and runs the
+//     epilogue, so the last wave is as short as a piece instead of a tile.
+// Every wait is bounded (common.cuh); on expiry the kernel records
 // FXB_DERR_GEMM_WAIT, drains what it issued and frees its tensor memory.
-#include "common.cuh"
-#include "internal.h"
-
 //
 // This header holds the device side (kernels, epilogues, launch templates);
 // gemm.cu holds the planner and the C entry, and gemm_k0..3.cu instantiate
 // one epilogue kind each (they compile in parallel).
 #pragma once
+#include "common.cuh"
+#include "internal.h"
 
 namespace fxb {
 namespace gk {
@@ -58,6 +61,11 @@ template <int AB_FMT> struct CType<EK_F32, AB_FMT> { using T = float; };
 struct GemmParams {
   int M, N, K;
   int tiles_m, tiles_n, splits, kb_per_split, num_kb;
+  // units = full_units whole tiles (or split-K (tile, split) pairs), then
+  // tail_splits pieces of tail_kb k-blocks for each remaining tile
+  int total_units, full_units, tail_splits, tail_kb;
+  float* ws;         // tail pieces' fp32 partial tiles
+  unsigned* ws_cnt;  // per (tail tile, CTA) arrival counters, zero between launches
   int epi;
   int c_dtype;
   float alpha;
@@ -93,6 +101,107 @@ FXB_DEV void tile_coords(int unit, const GemmParams& p, int& tm, int& tn, int& s
   const int r = t - g * per_group;
   tm = first_m + r % gs;
   tn = r / gs;
+}
+
+// What a unit of the persistent schedule covers: tile (tm, tn), k-blocks
+// [kb0, kb1), and for a tail piece its tail tile index and piece number
+// (piece -1 for whole tiles).
+struct UnitInfo {
+  int tm, tn, kb0, kb1, tail, piece;
+};
+FXB_DEV UnitInfo unit_info(int unit, const GemmParams& p) {
+  UnitInfo u;
+  int split;
+  if (unit < p.full_units) {
+    tile_coords(unit, p, u.tm, u.tn, split);
+    u.kb0 = split * p.kb_per_split;
+    u.kb1 = min(p.num_kb, u.kb0 + p.kb_per_split);
+    u.tail = -1;
+    u.piece = -1;
+  } else {
+    const int v = unit - p.full_units;
+    u.tail = v / p.tail_splits;
+    u.piece = v - u.tail * p.tail_splits;
+    tile_coords(p.full_units + u.tail, p, u.tm, u.tn, split);
+    u.kb0 = u.piece * p.tail_kb;
+    u.kb1 = min(p.num_kb, u.kb0 + p.tail_kb);
+  }
+  return u;
+}
+
+// The k-th unit of persistent slot `slot` (a CTA, or a CTA pair), -1 past its
+// last: its whole tiles slot, slot + nslots, ... and its tail piece (tail
+// unit v goes to slot v). A contributor runs its piece first, so its partial
+// tile is written while the owner is still on its whole tiles; the owner runs
+// its piece last. The owner's wait therefore depends only on units that wait
+// for nothing.
+FXB_DEV int unit_of(int slot, int k, const GemmParams& p, int nslots) {
+  const int npieces = p.total_units - p.full_units;
+  const bool has_piece = slot < npieces;
+  const bool contrib = has_piece && (slot % p.tail_splits) != 0;
+  if (contrib) {
+    if (k == 0) return p.full_units + slot;
+    --k;
+  }
+  const int nfull = slot < p.full_units ? (p.full_units - slot + nslots - 1) / nslots : 0;
+  if (k < nfull) return slot + k * nslots;
+  if (has_piece && !contrib && k == nfull) return p.full_units + slot;
+  return -1;
+}
+
+// Partial-tile exchange of a tail tile. A contributor (piece > 0) writes its
+// fp32 accumulator tile to the workspace and counts its epilogue warps in; the
+// owner (piece 0) waits for all of them and adds their tiles, in piece order,
+// to its own accumulator before the epilogue. Workspace layout per CTA tile:
+// float4 index ((chunk * 4 + quarter) * 8 + j) * 32 + lane holds values
+// 4j..4j+3 of the lane's 32-column chunk, so every warp access is one
+// contiguous 512-byte span.
+struct Red {
+  float4* out;       // contributor: this lane's slot in its partial tile
+  const float4* in;  // owner: this lane's slot in the first contributor's tile
+  int nin;           // owner: contributor tiles to add
+  int64_t stride4;   // float4 distance between consecutive contributors' tiles
+};
+template <int BN>
+FXB_DEV Red tail_red(const GemmParams& p, const UnitInfo& u, int cta, int nctas, int quarter,
+                     int lane) {
+  Red r{nullptr, nullptr, 0, 0};
+  if (u.piece < 0) return r;
+  constexpr int64_t kTile4 = 32 * BN;  // float4s per 128-row CTA tile
+  const int nc = p.tail_splits - 1;
+  float4* ws4 = reinterpret_cast<float4*>(p.ws);
+  const int64_t lane_off = (int64_t)quarter * 256 + lane;
+  if (u.piece > 0) {
+    r.out = ws4 + ((int64_t)(u.tail * nc + u.piece - 1) * nctas + cta) * kTile4 + lane_off;
+  } else {
+    r.in = ws4 + ((int64_t)u.tail * nc * nctas + cta) * kTile4 + lane_off;
+    r.nin = nc;
+    r.stride4 = (int64_t)nctas * kTile4;
+  }
+  return r;
+}
+// owner: wait (bounded) until every contributor warp of this CTA's tile is in
+FXB_DEV void tail_wait(const GemmParams& p, const UnitInfo& u, int cta, int nctas, int lane) {
+  if (u.piece != 0) return;
+  if (lane == 0)
+    spin_until_geq(p.ws_cnt + u.tail * nctas + cta, 8u * (unsigned)(p.tail_splits - 1), p.err,
+                   FXB_DERR_GEMM_WAIT);
+  __syncwarp();
+  __threadfence();
+}
+// after the warp's epilogue: a contributor publishes its partial; the owner's
+// last warp resets the counter for the next launch
+FXB_DEV void tail_done(const GemmParams& p, const UnitInfo& u, int cta, int nctas, int lane) {
+  if (u.piece < 0) return;
+  unsigned* c = p.ws_cnt + u.tail * nctas + cta;
+  if (u.piece > 0) {
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) atomicAdd(c, 1u);
+  } else if (lane == 0) {
+    const unsigned expect = 8u * (unsigned)(p.tail_splits - 1);
+    if (atomicAdd(c, 1u) == expect + 7u) atomicExch(c, 0u);
+  }
 }
 
 // ---------------------------------------------------------------- epilogue helpers
@@ -341,6 +450,60 @@ struct EpiWarp {
     }
   }
 
+  // Tail pieces (see Red). A contributor copies its accumulator columns to
+  // its partial tile; the owner adds the contributors' tiles into tensor
+  // memory before run(), so the epilogue's chunk loop is the same code for
+  // every unit.
+  FXB_DEV void write_partial(const GemmParams& p, int ntile0, int half, uint32_t tbase,
+                             const Red& rd) {
+#pragma unroll 1
+    for (int cc = 0; cc < NCH; ++cc) {
+      const int c = half * NCH + cc;
+      if (ntile0 + c * 32 >= p.N) break;  // warp-uniform
+      uint32_t acc[32];
+      tmem_ld32(tbase + c * 32, acc);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        rd.out[c * 1024 + j * 32] =
+            make_float4(__uint_as_float(acc[4 * j]), __uint_as_float(acc[4 * j + 1]),
+                        __uint_as_float(acc[4 * j + 2]), __uint_as_float(acc[4 * j + 3]));
+    }
+  }
+  FXB_DEV void fold_partials(const GemmParams& p, int ntile0, int half, uint32_t tbase,
+                             const Red& rd) {
+#pragma unroll 1
+    for (int cc = 0; cc < NCH; ++cc) {
+      const int c = half * NCH + cc;
+      if (ntile0 + c * 32 >= p.N) break;  // warp-uniform
+      uint32_t acc[32];
+      tmem_ld32(tbase + c * 32, acc);
+      tmem_wait_ld();
+#pragma unroll 1
+      for (int q = 0; q < rd.nin; q += 2) {  // two contributors' loads in flight
+        const float4* src = rd.in + q * rd.stride4 + c * 1024;
+        const bool two = q + 1 < rd.nin;
+        float4 x[2][8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          x[0][j] = __ldcg(src + j * 32);
+          x[1][j] = two ? __ldcg(src + rd.stride4 + j * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)  // in contributor order
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            acc[4 * j] = __float_as_uint(__uint_as_float(acc[4 * j]) + x[h][j].x);
+            acc[4 * j + 1] = __float_as_uint(__uint_as_float(acc[4 * j + 1]) + x[h][j].y);
+            acc[4 * j + 2] = __float_as_uint(__uint_as_float(acc[4 * j + 2]) + x[h][j].z);
+            acc[4 * j + 3] = __float_as_uint(__uint_as_float(acc[4 * j + 3]) + x[h][j].w);
+          }
+      }
+      tmem_st32(tbase + c * 32, acc);
+    }
+    tmem_wait_st();
+  }
+
   // m_next / ntile0_next: this warp's row and first column in its next tile
   // (has_next false when there is none)
   FXB_DEV void run(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmZ, int m,
@@ -415,7 +578,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   pdl_trigger();
   pdl_wait();  // operands come from the previous kernel on the stream
 
-  const int total_units = p.tiles_m * p.tiles_n * p.splits;
+
   constexpr uint32_t IDESC = umma_idesc_f16(AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, BM, BN);
 
   if (warp == 0) {
@@ -426,12 +589,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t armed = 0;          // bit s: stage s armed at least once
       uint32_t armed_parity = 0;   // bit s: parity of the last arming of stage s
       bool ok = true;
-      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
-        int tm, tn, split;
-        tile_coords(unit, p, tm, tn, split);
-        const int kb0 = split * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
+      for (int k = 0, unit; ok && (unit = unit_of(blockIdx.x, k, p, gridDim.x)) >= 0; ++k) {
+        const UnitInfo u = unit_info(unit, p);
+        const int tm = u.tm, tn = u.tn;
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
           const uint32_t sa = base + stage * C::STAGE_BYTES;
           const uint32_t sb = sa + C::A_BYTES;
@@ -468,11 +629,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int abuf = 0;
       uint32_t aphase = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
-        int tm, tn, split;
-        tile_coords(unit, p, tm, tn, split);
-        const int kb0 = split * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+      for (int k = 0, unit; ok && (unit = unit_of(blockIdx.x, k, p, gridDim.x)) >= 0; ++k) {
+        const UnitInfo u = unit_info(unit, p);
+        const int kb0 = u.kb0, kb1 = u.kb1;
         if (!mbar_wait(tempty_bar(abuf), aphase ^ 1, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
         tc_fence_after();
         const uint32_t dcol = tmem_base + abuf * BN;
@@ -510,23 +669,37 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int abuf = 0;
     uint32_t aphase = 0;
     EpiWarp<BN, typename CType<EK, AB_FMT>::T, EK> ew;
-    if ((int)blockIdx.x < total_units) {
-      int tm, tn, split;
-      tile_coords(blockIdx.x, p, tm, tn, split);
-      ew.prefetch(p, tm * BM + row_in_tile, tn * BN, half);
+    if (unit_of(blockIdx.x, 0, p, gridDim.x) >= 0) {
+      const UnitInfo u = unit_info(unit_of(blockIdx.x, 0, p, gridDim.x), p);
+      ew.prefetch(p, u.tm * BM + row_in_tile, u.tn * BN, half);
     }
-    for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x) {
-      int tm, tn, split;
-      tile_coords(unit, p, tm, tn, split);
+    for (int k = 0, unit; (unit = unit_of(blockIdx.x, k, p, gridDim.x)) >= 0; ++k) {
+      const UnitInfo u = unit_info(unit, p);
+      const int tm = u.tm, tn = u.tn;
       const int m = tm * BM + row_in_tile;
-      const int next = unit + gridDim.x;
-      int ntm = 0, ntn = 0, nsplit;
-      if (next < total_units) tile_coords(next, p, ntm, ntn, nsplit);
+      const int next = unit_of(blockIdx.x, k + 1, p, gridDim.x);
+      int ntm = 0, ntn = 0;
+      if (next >= 0) {
+        const UnitInfo nu = unit_info(next, p);
+        ntm = nu.tm;
+        ntn = nu.tn;
+      }
       if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
-      ew.run(p, &tmC, &tmZ, m, tm * BM + quarter * 32, tn * BN, half, tbase, sbuf, lane, ecnt,
-             next < total_units, ntm * BM + row_in_tile, ntn * BN);
+      if (u.piece > 0) {
+        ew.write_partial(p, tn * BN, half, tbase, tail_red<BN>(p, u, 0, 1, quarter, lane));
+        // the R prefetched for this unit is unused: load the next unit's
+        if (next >= 0) ew.prefetch(p, ntm * BM + row_in_tile, ntn * BN, half);
+      } else {
+        if (u.piece == 0) {
+          tail_wait(p, u, 0, 1, lane);
+          ew.fold_partials(p, tn * BN, half, tbase, tail_red<BN>(p, u, 0, 1, quarter, lane));
+        }
+        ew.run(p, &tmC, &tmZ, m, tm * BM + quarter * 32, tn * BN, half, tbase, sbuf, lane, ecnt,
+               next >= 0, ntm * BM + row_in_tile, ntn * BN);
+      }
+      tail_done(p, u, 0, 1, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(abuf));
@@ -561,10 +734,6 @@ template <int BN> struct Cfg2 {
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM = STAGES * STAGE_BYTES + kEpiBytes + 1024 + 256;
 };
-
-FXB_DEV void tile_coords2(int unit, const GemmParams& p, int& tm, int& tn, int& split) {
-  tile_coords(unit, p, tm, tn, split);  // tm counts 256-row tiles here
-}
 
 template <int BN, bool A_MN, bool B_MN, int AB_FMT, int EK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -617,7 +786,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
   pdl_trigger();
   pdl_wait();  // operands come from the previous kernel on the stream
 
-  const int total_units = p.tiles_m * p.tiles_n * p.splits;
+
   constexpr uint32_t IDESC = umma_idesc_f16(AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, 256, BN);
 
   if (warp == 0) {
@@ -627,11 +796,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       uint32_t phase = 0;
       uint32_t armed = 0, armed_parity = 0;
       bool ok = true;
-      for (int unit = pair; unit < total_units && ok; unit += npairs) {
-        int tm, tn, split;
-        tile_coords2(unit, p, tm, tn, split);
-        const int kb0 = split * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+      for (int k = 0, unit; ok && (unit = unit_of(pair, k, p, npairs)) >= 0; ++k) {
+        const UnitInfo u = unit_info(unit, p);  // tm counts 256-row tiles here
+        const int tm = u.tm, tn = u.tn, kb0 = u.kb0, kb1 = u.kb1;
         const int arow = tm * 256 + (int)rank * 128;
         const int brow = tn * BN + (int)rank * (BN / 2);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -677,11 +844,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         int abuf = 0;
         uint32_t aphase = 0;
         bool ok = true;
-        for (int unit = pair; unit < total_units && ok; unit += npairs) {
-          int tm, tn, split;
-          tile_coords2(unit, p, tm, tn, split);
-          const int kb0 = split * p.kb_per_split;
-          const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int k = 0, unit; ok && (unit = unit_of(pair, k, p, npairs)) >= 0; ++k) {
+          const UnitInfo u = unit_info(unit, p);
+          const int kb0 = u.kb0, kb1 = u.kb1;
           if (!mbar_wait(tempty_bar(abuf), aphase ^ 1, p.err, FXB_DERR_GEMM_WAIT)) { ok = false; break; }
           tc_fence_after();
           const uint32_t dcol = tmem_base + abuf * BN;
@@ -720,23 +885,37 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     int abuf = 0;
     uint32_t aphase = 0;
     EpiWarp<BN, typename CType<EK, AB_FMT>::T, EK> ew;
-    if (pair < total_units) {
-      int tm, tn, split;
-      tile_coords2(pair, p, tm, tn, split);
-      ew.prefetch(p, tm * 256 + row_in_tile, tn * BN, half);
+    if (unit_of(pair, 0, p, npairs) >= 0) {
+      const UnitInfo u = unit_info(unit_of(pair, 0, p, npairs), p);
+      ew.prefetch(p, u.tm * 256 + row_in_tile, u.tn * BN, half);
     }
-    for (int unit = pair; unit < total_units; unit += npairs) {
-      int tm, tn, split;
-      tile_coords2(unit, p, tm, tn, split);
+    for (int k = 0, unit; (unit = unit_of(pair, k, p, npairs)) >= 0; ++k) {
+      const UnitInfo u = unit_info(unit, p);
+      const int tm = u.tm, tn = u.tn;
       const int m = tm * 256 + row_in_tile;
-      const int next = unit + npairs;
-      int ntm = 0, ntn = 0, nsplit;
-      if (next < total_units) tile_coords2(next, p, ntm, ntn, nsplit);
+      const int next = unit_of(pair, k + 1, p, npairs);
+      int ntm = 0, ntn = 0;
+      if (next >= 0) {
+        const UnitInfo nu = unit_info(next, p);
+        ntm = nu.tm;
+        ntn = nu.tn;
+      }
       if (!mbar_wait(tfull_bar(abuf), aphase, p.err, FXB_DERR_GEMM_WAIT)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
-      ew.run(p, &tmC, &tmZ, m, tm * 256 + (int)rank * 128 + quarter * 32, tn * BN, half, tbase,
-             sbuf, lane, ecnt, next < total_units, ntm * 256 + row_in_tile, ntn * BN);
+      if (u.piece > 0) {
+        ew.write_partial(p, tn * BN, half, tbase, tail_red<BN>(p, u, (int)rank, 2, quarter, lane));
+        // the R prefetched for this unit is unused: load the next unit's
+        if (next >= 0) ew.prefetch(p, ntm * 256 + row_in_tile, ntn * BN, half);
+      } else {
+        if (u.piece == 0) {
+          tail_wait(p, u, (int)rank, 2, lane);
+          ew.fold_partials(p, tn * BN, half, tbase, tail_red<BN>(p, u, (int)rank, 2, quarter, lane));
+        }
+        ew.run(p, &tmC, &tmZ, m, tm * 256 + (int)rank * 128 + quarter * 32, tn * BN, half, tbase,
+               sbuf, lane, ecnt, next >= 0, ntm * 256 + row_in_tile, ntn * BN);
+      }
+      tail_done(p, u, (int)rank, 2, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(abuf), 0));

@@ -40,6 +40,7 @@ class GemmArgs(ctypes.Structure):
         ("R", _vp), ("ldr", _i64),
         ("Z", _vp), ("ldz", _i64),
         ("bias", _vp),
+        ("workspace", _vp), ("workspace_bytes", _i64),
     ]
 
 
@@ -87,6 +88,7 @@ SIGNATURES = {
                                         _i32, _vp, _vp, _vp, _vp, _f32, _vp, _f32, _f32,
                                         _f32, _f32, _vp]),
     "fxb_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), _vp]),
+    "fxb_gemm_workspace_size": (ctypes.c_size_t, []),
     "fxb_gemm_plan": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.POINTER(_i32),
                                      ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "fxb_attn_fwd": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),

@@ -26,6 +26,24 @@ def set_gemm_timing(records):
     _GEMM_TIMING = records
 
 
+# GEMM workspace (tail split, see fxb_gemm_args.workspace): one zero-filled
+# buffer per (device, stream), allocated on first use and kept, so that
+# captured CUDA graphs keep pointing at it.
+_GEMM_WS = {}
+
+
+def _gemm_workspace(device):
+    st = torch.cuda.current_stream(device)
+    key = (device.index, st.cuda_stream)
+    ws = _GEMM_WS.get(key)
+    if ws is None:
+        n = int(_lib.load().fxb_gemm_workspace_size())
+        ws = torch.empty(n, device=device, dtype=torch.uint8)
+        ws[:4096].zero_()  # the arrival counters; the partial tiles need no init
+        _GEMM_WS[key] = ws
+    return ws
+
+
 def _rowmajor(t, name):
     if t.dim() != 2 or t.stride(1) != 1:
         raise ValueError(f"{name} must be a 2-D row-major view (stride(1) == 1)")
@@ -68,6 +86,8 @@ def gemm(A, B, out, *, a_trans=False, b_trans=False, epilogue=EPI_STORE, alpha=1
         a.Z, a.ldz = Z.data_ptr(), _rowmajor(Z, "Z")
     if bias is not None:
         a.bias = bias.data_ptr()
+    ws = _gemm_workspace(A.device)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     if _GEMM_TIMING is not None:
         st = torch.cuda.current_stream(A.device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -121,6 +121,60 @@ def test_gemm_store(dev, gemm_mode, dtype, a_trans, b_trans, M, N, K):
     assert err < 1e-2, f"rel err {err:.3e}"
 
 
+@pytest.mark.parametrize("epi", ["store", "residual", "dgelu"])
+@pytest.mark.parametrize("M,N,K,b_trans", [(8192, 768, 3072, False), (8192, 768, 2304, True),
+                                           (512, 1024, 4096, False), (2000, 520, 1032, True)])
+def test_gemm_tail_split(dev, gemm_mode, epi, M, N, K, b_trans):
+    """Tail split: the tiles left over after the full waves are cut along K
+    and their fp32 partial tiles reduced through the workspace. Same result
+    as the reference within the tolerance, bitwise equal on a second call
+    (fixed reduction order, counters reset) and equal to the call without a
+    workspace (no split) to fp32 rounding."""
+    import ctypes
+    from fxb200 import _lib, ops
+    dtype = torch.bfloat16
+    pair, bn, sp = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    code = {"store": ops.EPI_STORE, "residual": ops.EPI_RESIDUAL, "dgelu": ops.EPI_DGELU}[epi]
+    _lib.call("fxb_gemm_plan", M, N, K, code, ctypes.byref(pair), ctypes.byref(bn), ctypes.byref(sp))
+    torch.manual_seed(M + K)
+    A = (torch.randn(M, K, device=dev) / math.sqrt(K)).to(dtype)
+    B = (torch.randn(K, N, device=dev) if b_trans else torch.randn(N, K, device=dev)).to(dtype)
+    R = torch.randn(M, N, device=dev).to(dtype)
+    kw = {} if epi == "store" else dict(epilogue=code, R=R)
+    C1 = torch.empty(M, N, device=dev, dtype=dtype)
+    C2 = torch.empty_like(C1)
+    ops.gemm(A, B, C1, b_trans=b_trans, **kw)
+    ops.gemm(A, B, C2, b_trans=b_trans, **kw)
+    acc = _gemm_ref(A, B, False, b_trans)
+    if epi == "residual":
+        ref = acc + R.float()
+    elif epi == "dgelu":
+        x = R.float()
+        t = torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3))
+        ref = acc * (0.5 * (1 + t) + 0.5 * x * (1 - t * t) * 0.7978845608028654 * (1 + 3 * 0.044715 * x * x))
+    else:
+        ref = acc
+    err = (C1.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, f"rel err {err:.3e}"
+    assert torch.equal(C1, C2), "second call differs (counters not reset or order not fixed)"
+    # the same GEMM without a workspace (no tail split)
+    a = _lib.GemmArgs()
+    a.dtype, a.M, a.N, a.K = _lib.dtype_code(dtype), M, N, K
+    a.A, a.lda, a.a_trans = A.data_ptr(), K, 0
+    a.B, a.ldb, a.b_trans = B.data_ptr(), (N if b_trans else K), int(b_trans)
+    C3 = torch.empty_like(C1)
+    a.C, a.ldc, a.c_dtype = C3.data_ptr(), N, _lib.dtype_code(dtype)
+    a.epilogue, a.alpha = code, 1.0
+    if epi != "store":
+        a.R, a.ldr = R.data_ptr(), N
+    _lib.check(_lib.load().fxb_gemm(ctypes.byref(a), _lib.stream_ptr(dev)), "fxb_gemm")
+    torch.cuda.synchronize()
+    d = (C1.float() - C3.float()).abs().max().item()
+    assert d <= 2e-2 * max(1.0, C3.float().abs().max().item()), d
+    if gemm_mode == "2sm" and (M, N, K) == (8192, 768, 3072):
+        assert sp.value > 1, "tail split expected for this shape"
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("M,N,K", [(300, 264, 136), (4096, 3072, 768)])
 def test_gemm_epilogues(dev, gemm_mode, dtype, M, N, K):
