@@ -348,6 +348,23 @@ def run_micro(args):
         byt = 3 * Nr * D * 2 + Nr * 4
         out.append({"kernel": "rmsnorm_bwd", "case": f"config 3 [{Nr},{D}] bf16", "ms": ms,
                     "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm})
+        # the config-4 step's shape: [8192, 768] with the residual gradient added
+        Ns = 8192
+        xs, dys, dres = x[:Ns], dy[:Ns], torch.randn(Ns, D, device=dev, generator=g).to(bf)
+        ys, dxs = y[:Ns], dx[:Ns]
+        fs = lambda: _lib.call("fxb_rmsnorm_fwd", 2, _lib.ptr(xs), _lib.ptr(w), _lib.ptr(ys),  # noqa: E731
+                               _lib.ptr(rstd), Ns, D, 1e-6, st)
+        ms = _time_ms(fs, it)
+        byt = 2 * Ns * D * 2 + Ns * 4
+        out.append({"kernel": "rmsnorm_fwd", "case": f"config 4 step [{Ns},{D}] bf16", "ms": ms,
+                    "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm})
+        fbs = lambda: _lib.call("fxb_rmsnorm_bwd", 2, _lib.ptr(xs), _lib.ptr(w), _lib.ptr(rstd),  # noqa: E731
+                                _lib.ptr(dys), _lib.ptr(dres), _lib.ptr(dxs), _lib.ptr(dw), 0, 0,
+                                _lib.ptr(ws), Ns, D, st)
+        ms = _time_ms(fbs, it)
+        byt = 4 * Ns * D * 2 + Ns * 4
+        out.append({"kernel": "rmsnorm_bwd (+dres, + dw reduce)", "case": f"config 4 step [{Ns},{D}] bf16",
+                    "ms": ms, "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm})
     if "ce" in which or "all" in which:
         Nr, V = 65536, 32768
         g = torch.Generator(device=dev).manual_seed(2)

@@ -88,7 +88,19 @@ rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restri
   }
 }
 
-// dx per row + per-block dw partial (part[blockIdx.x, :]).
+// dx per row + per-block dw partial (part[blockIdx.x, :]). Each warp takes
+// two rows at a time and issues all of their loads (x, dy, dres) before using
+// any, so that enough bytes are in flight to keep HBM busy with one block
+// per SM or two.
+template <typename T> FXB_DEV void unpack_vec(const uint4& u, float* f) {
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  } else {
+    unpack8<T>(u, f);
+  }
+}
+
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
@@ -107,46 +119,65 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
   for (int i = 0; i < VPL; ++i) {
     int v = i * 32 + lane;
 #pragma unroll
-    for (int j = 0; j < E; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < E; ++j) acc[i][j] = wv[i][j] = 0.f;  // lanes past D keep zeros
     if (v < nvec) load_vec<T>(w + (int64_t)v * E, wv[i]);
   }
   const float invD = 1.f / (float)D;
-  for (int64_t r = (int64_t)blockIdx.x * kWarps + wid; r < rows; r += (int64_t)gridDim.x * kWarps) {
-    const T* xr = x + r * D;
-    const T* gr = dy + r * D;
-    float xv[VPL][E], gv[VPL][E];
-    float t = 0.f;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  const int64_t stride = (int64_t)gridDim.x * kWarps * 2;
+  for (int64_t r0 = ((int64_t)blockIdx.x * kWarps + wid) * 2; r0 < rows; r0 += stride) {
+    const bool two = r0 + 1 < rows;  // warp-uniform
+    uint4 xp[2][VPL], gp[2][VPL], dp[2][VPL];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      int v = i * 32 + lane;
-      if (v < nvec) {
-        load_vec<T>(xr + (int64_t)v * E, xv[i]);
-        load_vec<T>(gr + (int64_t)v * E, gv[i]);
+    for (int k = 0; k < 2; ++k) {
+      const int64_t r = r0 + k;
+      const bool rv = k == 0 || two;
 #pragma unroll
-        for (int j = 0; j < E; ++j) t += xv[i][j] * wv[i][j] * gv[i][j];
+      for (int i = 0; i < VPL; ++i) {
+        const int v = i * 32 + lane;
+        const bool ok = rv && v < nvec;
+        xp[k][i] = ok ? *reinterpret_cast<const uint4*>(x + r * D + (int64_t)v * E) : zero;
+        gp[k][i] = ok ? *reinterpret_cast<const uint4*>(dy + r * D + (int64_t)v * E) : zero;
+        dp[k][i] = (ok && dres) ? *reinterpret_cast<const uint4*>(dres + r * D + (int64_t)v * E) : zero;
       }
     }
-    t = warp_sum(t);
-    const float rs = rstd[r];
-    const float corr = rs * rs * rs * t * invD;
-    T* dr = dx + r * D;
+    float rs[2], t[2];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      int v = i * 32 + lane;
-      if (v < nvec) {
-        float o[E];
+    for (int k = 0; k < 2; ++k) {
+      rs[k] = (k == 0 || two) ? rstd[r0 + k] : 0.f;
+      float tt = 0.f;
 #pragma unroll
-        for (int j = 0; j < E; ++j) {
-          o[j] = rs * wv[i][j] * gv[i][j] - xv[i][j] * corr;
-          acc[i][j] += xv[i][j] * rs * gv[i][j];
+      for (int i = 0; i < VPL; ++i) {
+        float xv[E], gv[E];
+        unpack_vec<T>(xp[k][i], xv);
+        unpack_vec<T>(gp[k][i], gv);
+#pragma unroll
+        for (int j = 0; j < E; ++j) tt += xv[j] * wv[i][j] * gv[j];
+      }
+      t[k] = tt;
+    }
+    t[0] = warp_sum(t[0]);
+    t[1] = warp_sum(t[1]);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (k == 1 && !two) break;
+      const int64_t r = r0 + k;
+      const float corr = rs[k] * rs[k] * rs[k] * t[k] * invD;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int v = i * 32 + lane;
+        if (v < nvec) {
+          float xv[E], gv[E], dv[E], o[E];
+          unpack_vec<T>(xp[k][i], xv);
+          unpack_vec<T>(gp[k][i], gv);
+          unpack_vec<T>(dp[k][i], dv);  // zero without a residual gradient
+#pragma unroll
+          for (int j = 0; j < E; ++j) {
+            o[j] = rs[k] * wv[i][j] * gv[j] - xv[j] * corr + dv[j];
+            acc[i][j] += xv[j] * rs[k] * gv[j];
+          }
+          store_vec<T>(dx + r * D + (int64_t)v * E, o);
         }
-        if (dres) {  // gradient arriving through the residual path
-          float rr[E];
-          load_vec<T>(dres + r * D + (int64_t)v * E, rr);
-#pragma unroll
-          for (int j = 0; j < E; ++j) o[j] += rr[j];
-        }
-        store_vec<T>(dr + (int64_t)v * E, o);
       }
     }
   }
@@ -179,8 +210,15 @@ __global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ part, int npa
   __shared__ float grp[8][33];
   const int d = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  if (d < D)
-    for (int b = threadIdx.y; b < nparts; b += 8) s += part[(int64_t)b * D + d];
+  if (d < D) {
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};  // four loads in flight, fixed assignment
+    int b = threadIdx.y;
+    for (; b + 24 < nparts; b += 32)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s4[u] += part[(int64_t)(b + 8 * u) * D + d];
+    for (; b < nparts; b += 8) s4[0] += part[(int64_t)b * D + d];
+    s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+  }
   grp[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
   if (threadIdx.y == 0 && d < D) {
@@ -221,10 +259,10 @@ int launch_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows,
 }
 
 int bwd_blocks(int64_t rows) {
-  // ~2 rows per warp and up to 4 blocks per SM: the kernel is latency-bound
-  // at training sizes (8K rows), and the dw partials stay small
+  // two blocks per SM, each warp two rows per pass with all their loads in
+  // flight: enough bytes outstanding for HBM, and few dw partials to reduce
   int64_t want = (rows + kWarps * 2 - 1) / (kWarps * 2);
-  int cap = fxb::num_sms() * 4;
+  int cap = fxb::num_sms() * 2;
   int b = (int)(want < cap ? want : cap);
   return b < 1 ? 1 : b;
 }
