@@ -40,6 +40,27 @@ template <typename T> FXB_DEV void st_vec(T* p, const float* f) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
+// 16-byte vector v of a row staged in shared memory, as floats / from floats
+template <typename T> FXB_DEV void unpack_row(const uint8_t* row, int v, float* f) {
+  const uint4 u = reinterpret_cast<const uint4*>(row)[v];
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  } else {
+    unpack8<T>(u, f);
+  }
+}
+template <typename T> FXB_DEV void pack_row(uint8_t* row, int v, const float* f) {
+  uint4 u;
+  if constexpr (sizeof(T) == 4) {
+    u = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                   __float_as_uint(f[3]));
+  } else {
+    u = pack8<T>(f);
+  }
+  reinterpret_cast<uint4*>(row)[v] = u;
+}
+
 // Block-wide (or warp-wide when NT == 32) max and sum.
 template <int NT> FXB_DEV float block_max(float v, float* red) {
   v = warp_max(v);
@@ -137,6 +158,123 @@ ce_cached_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __rest
   }
 }
 
+// Rows of up to kSmemRowMax bytes (V = 32768 in 16-bit is 64 KB): the row is
+// brought into shared memory by one bulk asynchronous copy, both passes run
+// out of shared memory (online max / sum-of-exp, then the gradient written
+// back in place), and one bulk copy stores the gradient row. Three blocks per
+// SM keep loads, arithmetic and stores of different rows overlapped; the
+// logits are read from HBM once and the gradient written once.
+constexpr int kSmemRowMax = 72 * 1024;
+constexpr int kSmemThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kSmemThreads)
+ce_smem_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
+               T* grad, float* __restrict__ row_loss, const float* __restrict__ mul,
+               int64_t rows, int V, int64_t ignore_index, int* err) {
+  constexpr int E = CEVec<T>::N;
+  constexpr int NW = kSmemThreads / 32;
+  extern __shared__ __align__(128) uint8_t srow_raw[];
+  __shared__ __align__(8) uint64_t full_bar;
+  __shared__ float red_m[NW], red_s[NW];
+  __shared__ float s_xt;
+  const uint32_t srow = smem_u32(srow_raw);
+  const uint32_t bar = smem_u32(&full_bar);
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int nvec = V / E;
+  const uint32_t row_bytes = (uint32_t)V * sizeof(T);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  const float gm = grad ? *mul : 0.f;
+  uint32_t phase = 0;
+  bool ok = true;
+  if (tid == 0 && (int64_t)blockIdx.x < rows) {
+    mbar_expect_tx(bar, row_bytes);
+    bulk_load_g2s(srow, logits + (int64_t)blockIdx.x * ld, row_bytes, bar);
+  }
+  for (int64_t r = blockIdx.x; r < rows && ok; r += gridDim.x) {
+    ok = mbar_wait(bar, phase, err, FXB_DERR_CE_WAIT);
+    phase ^= 1;
+    if (!ok) break;  // uniform: every thread saw the same barrier
+    // pass 1: online max and sum of exp2 over this thread's vectors
+    float m = -INFINITY, s = 0.f;
+    for (int v = tid; v < nvec; v += kSmemThreads) {
+      float f[E];
+      unpack_row<T>(srow_raw, v, f);
+      float vm = f[0];
+#pragma unroll
+      for (int j = 1; j < E; ++j) vm = fmaxf(vm, f[j]);
+      const float mn = fmaxf(m, vm);
+      if (mn == -INFINITY) continue;  // nothing but -inf so far: m, s unchanged
+      const float mnl = mn * kLog2e;
+      float add = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) add += exp2f(fmaf(f[j], kLog2e, -mnl));
+      s = s * exp2f((m - mn) * kLog2e) + add;  // m = -inf: s = 0 * 0 + add
+      m = mn;
+    }
+    // block combine of (m, s)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float mn = fmaxf(m, m2);
+      s = (mn == -INFINITY) ? 0.f : s * exp2f((m - mn) * kLog2e) + s2 * exp2f((m2 - mn) * kLog2e);
+      m = mn;
+    }
+    const int64_t t = target[r];
+    const bool valid = (t != ignore_index) && (t >= 0) && (t < (int64_t)V);
+    if (lane == 0) { red_m[wid] = m; red_s[wid] = s; }
+    if (tid == 0) s_xt = valid ? to_f<T>(reinterpret_cast<const T*>(srow_raw)[t]) : 0.f;
+    __syncthreads();
+    float M = red_m[0], S = red_s[0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) {
+      const float m2 = red_m[w], s2 = red_s[w];
+      const float mn = fmaxf(M, m2);
+      S = (mn == -INFINITY) ? 0.f : S * exp2f((M - mn) * kLog2e) + s2 * exp2f((m2 - mn) * kLog2e);
+      M = mn;
+    }
+    const float xt = s_xt;
+    if (tid == 0) row_loss[r] = valid ? M + log2f(S) * kLn2 - xt : 0.f;
+    if (grad) {
+      // pass 2: gradient in place in shared memory, then one bulk store
+      const float scale = valid ? gm / S : 0.f;
+      const float Ml = M * kLog2e;
+      for (int v = tid; v < nvec; v += kSmemThreads) {
+        float f[E];
+        unpack_row<T>(srow_raw, v, f);
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          f[j] = exp2f(fmaf(f[j], kLog2e, -Ml)) * scale;
+          if ((int64_t)(v * E + j) == t && valid) f[j] -= gm;
+        }
+        pack_row<T>(srow_raw, v, f);
+      }
+      fence_proxy_async_smem();
+    }
+    __syncthreads();  // row consumed (and the gradient staged)
+    if (tid == 0) {
+      if (grad) {
+        bulk_store_s2g(grad + r * ld, srow, row_bytes);
+        bulk_commit();
+        bulk_wait_read0();  // the buffer is free once the store has read it
+      }
+      const int64_t rn = r + gridDim.x;
+      if (rn < rows) {
+        mbar_expect_tx(bar, row_bytes);
+        bulk_load_g2s(srow, logits + rn * ld, row_bytes, bar);
+      }
+    }
+  }
+  if (tid == 0) bulk_wait_all0();
+}
+
 // Generic path (any V, any alignment): block per row, three streaming passes.
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -192,6 +330,24 @@ int launch_ce(const void* lg, int64_t ld, const int64_t* tg, void* gr, float* lo
     switch (vpt) { FXB_CE_W(1) FXB_CE_W(2) FXB_CE_W(3) FXB_CE_W(4) FXB_CE_W(5) FXB_CE_W(6) FXB_CE_W(7) FXB_CE_W(8) }
 #undef FXB_CE_W
     return fxb::check_launch("ce_fwd_grad(warp)");
+  }
+  const size_t row_bytes = (size_t)V * sizeof(T);
+  if (vec_ok && row_bytes > 32 * 1024 && row_bytes <= (size_t)kSmemRowMax && (ld * sizeof(T)) % 16 == 0) {
+    int* err = fxb::dev_error_ptr();
+    if (!err) return FXB_ECUDA;
+    auto k = ce_smem_kernel<T>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      int r = fxb::check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   kSmemRowMax), "ce smem attribute");
+      if (r) return r;
+      attr_set[dev] = true;
+    }
+    int blocks = (int)(rows < (int64_t)sms * 3 ? rows : (int64_t)sms * 3);
+    fxb::pdl_launch(k, blocks, kSmemThreads, row_bytes, st, L, ld, tg, G, loss, mul, rows, V, ign, err);
+    return fxb::check_launch("ce_fwd_grad(smem)");
   }
   if (vec_ok && nvec <= 512 * 16) {
     int vpt = (nvec + 511) / 512;

@@ -24,6 +24,7 @@ enum {
   FXB_DERR_GEMM_WAIT = 1,
   FXB_DERR_ATTN_WAIT = 2,
   FXB_DERR_GATHER_WAIT = 4,
+  FXB_DERR_CE_WAIT = 8,
 };
 
 // ~2-3 s at B200 clocks; legitimate waits here are microseconds
@@ -253,6 +254,19 @@ FXB_DEV void tma_reduce_add_3d(const CUtensorMap* map, uint32_t src, int c0, int
           "l"(reinterpret_cast<uint64_t>(map)),
       "r"(src), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+// Untiled bulk copies (no tensor map, no multicast): `bytes` a multiple of 16,
+// both addresses 16-byte aligned. The load completes on an mbarrier (tx
+// bytes); the store joins the thread's bulk group.
+FXB_DEV void bulk_load_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+FXB_DEV void bulk_store_s2g(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
 }
 FXB_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // this thread's bulk groups have finished reading shared memory

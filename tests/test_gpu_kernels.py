@@ -91,6 +91,45 @@ def test_fused_ce(dev, dtype, N, V):
     assert ok2, f"grad err {e2} vs {b2}"
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("N,V", [(1000, 32768), (445, 24576)])
+def test_ce_rows_in_shared_memory(dev, dtype, N, V):
+    """Rows of 48-72 KB go through shared memory (one bulk copy in, one out):
+    gradient written over the logits (in place, as the linear-CE chunk loop
+    does), ignored and out-of-range targets, masked (-inf) columns, leading
+    -inf vectors, loss-only calls; per-row losses against fp32 torch."""
+    from fxb200 import _lib
+    torch.manual_seed(N)
+    lg = (torch.randn(N, V, device=dev) * 4).to(dtype)
+    lg[:, :40] = float("-inf")          # a thread's first vectors all masked
+    lg[3, 1000:2000] = float("-inf")
+    tg = torch.randint(40, V, (N,), device=dev)
+    tg[::9] = -100
+    tg[5] = V + 3                       # out of range: treated as ignored
+    tg[3] = 3000                        # outside row 3's masked columns
+    valid = (tg >= 0) & (tg < V)
+    ref32 = torch.where(valid, F.cross_entropy(lg.float(), tg.clamp(0, V - 1), reduction="none"),
+                        torch.zeros((), device=dev))
+    p = torch.softmax(lg.float(), dim=1)
+    p[valid.nonzero().squeeze(1), tg[valid]] -= 1.0
+    gref = p * (valid.float() / N)[:, None]
+    st = _lib.stream_ptr(dev)
+    mul = torch.full((), 1.0 / N, device=dev)
+    loss = torch.empty(N, device=dev)
+    loss2 = torch.empty(N, device=dev)
+    _lib.call("fxb_ce_fwd_grad", _lib.dtype_code(dtype), _lib.ptr(lg), V, _lib.ptr(tg), None,
+              _lib.ptr(loss2), _lib.ptr(mul), N, V, -100, st)
+    buf = lg.clone()
+    _lib.call("fxb_ce_fwd_grad", _lib.dtype_code(dtype), _lib.ptr(buf), V, _lib.ptr(tg), _lib.ptr(buf),
+              _lib.ptr(loss), _lib.ptr(mul), N, V, -100, st)
+    torch.cuda.synchronize()
+    assert torch.equal(loss, loss2)
+    assert (loss - ref32).abs().max().item() <= 1e-4 * max(1.0, ref32.abs().max().item())
+    err = (buf.float() - gref).abs().max().item()
+    assert err <= 2e-2 * gref.abs().max().item(), err
+    assert not torch.isnan(buf.float()).any()
+
+
 # ------------------------------------------------------------------ GEMM
 @pytest.fixture(params=["1sm", "2sm"])
 def gemm_mode(request, monkeypatch):
