@@ -188,6 +188,9 @@ int fxb_adamw_update(int32_t gdtype, int32_t pdtype, const void* grad, float* ma
 #define FXB_EPI_BIAS_SILU 6 /* Z = acc + bias[n] ; C = silu(Z) */
 #define FXB_EPI_ACCUM_F32 7 /* C(fp32) += alpha*acc (red.add; enables split-K) */
 #define FXB_EPI_DSILU 8     /* C = acc * silu'(R)        (R = pre-activation) */
+#define FXB_EPI_GELU_DERIV 9 /* C = gelu_tanh(p) ; Z = gelu_tanh'(p), p = acc rounded to C's type */
+#define FXB_EPI_MUL 10      /* C = alpha*acc*R  (with Z of FXB_EPI_GELU_DERIV as R: the
+                               GELU backward without recomputing the activation) */
 
 typedef struct fxb_gemm_args {
   int32_t dtype;     /* A/B dtype: FXB_DTYPE_BF16 or FXB_DTYPE_F16 */

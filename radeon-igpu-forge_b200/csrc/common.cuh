@@ -109,6 +109,18 @@ FXB_DEV float gelu_tanh_grad(float x) {
   return fmaf(0.5f, x * du * a, fmaf(0.5f, t, 0.5f));
 }
 
+// both of the above from one tanh: *g = gelu(x), *d = gelu'(x)
+FXB_DEV void gelu_tanh_and_grad(float x, float* g, float* d) {
+  const float k0 = 0.7978845608028654f;
+  const float k01 = 0.7978845608028654f * 0.044715f;
+  const float x2 = x * x;
+  const float t = tanh_fast(x * fmaf(k01, x2, k0));
+  const float hx = 0.5f * x;
+  *g = fmaf(hx, t, hx);
+  const float du = fmaf(3.f * k01, x2, k0);
+  *d = fmaf(0.5f, x * du * fmaf(-t, t, 1.f), fmaf(0.5f, t, 0.5f));
+}
+
 // ---------------------------------------------------------------- smem / mbarrier
 FXB_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

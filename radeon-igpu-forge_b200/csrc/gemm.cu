@@ -67,8 +67,10 @@ size_t workspace_bytes(int sms) { return kWsCounterBytes + (size_t)sms * 128 * 2
 // traffic per SM). `mode` (FXB_GEMM_FORCE=1sm|2sm, tests) restricts the choice.
 Plan plan(int M, int N, int K, int epi, bool tail_ok, int sms, int mode) {
   const bool allow_split = epi == FXB_EPI_ACCUM_F32;
-  const bool reads_r = epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU;
-  const bool writes_z = epi == FXB_EPI_GELU || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU;
+  const bool reads_r = epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU ||
+                       epi == FXB_EPI_MUL;
+  const bool writes_z = epi == FXB_EPI_GELU || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU ||
+                        epi == FXB_EPI_GELU_DERIV;
   const double epi_col = 18.0 + (reads_r ? 10.0 : 0.0) + (writes_z ? 12.0 : 0.0);
   const int nkb = (K + BK - 1) / BK;
   double best = 1e30;
@@ -164,7 +166,8 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
     return set_error(FXB_EINVAL, "gemm: B needs 16-byte rows and ldb >= row");
   if ((a->lda % 8) || (a->ldb % 8)) return set_error(FXB_EINVAL, "gemm: lda/ldb must be multiples of 8");
   if (a->ldc < N) return set_error(FXB_EINVAL, "gemm: ldc < N");
-  const bool needs_r = (epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU);
+  const bool needs_r = (epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU ||
+                        epi == FXB_EPI_MUL);
   if (needs_r && (!a->R || !aligned16(a->R) || (a->ldr * csz) % 16))
     return set_error(FXB_EINVAL, "gemm: epilogue needs an aligned R");
   const bool has_bias = (epi == FXB_EPI_BIAS || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU);
@@ -179,9 +182,10 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
     return set_error(FXB_EUNSUPPORTED, "gemm: epilogue %d with fp32 C (16-bit C only)", epi);
   if (a->c_dtype != FXB_DTYPE_F32 && a->c_dtype != a->dtype)
     return set_error(FXB_EUNSUPPORTED, "gemm: C dtype %d must be fp32 or the A/B dtype", a->c_dtype);
-  if (epi < 0 || epi > FXB_EPI_DSILU) return set_error(FXB_EINVAL, "gemm: bad epilogue %d", epi);
+  if (epi < 0 || epi > FXB_EPI_MUL) return set_error(FXB_EINVAL, "gemm: bad epilogue %d", epi);
   const int kind = a->c_dtype == FXB_DTYPE_F32 ? EK_F32
-                   : (epi == FXB_EPI_GELU || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU)
+                   : (epi == FXB_EPI_GELU || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU ||
+                      epi == FXB_EPI_GELU_DERIV)
                        ? EK_ACT16
                    : (epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU) ? EK_DACT16
                                                                       : EK_LIN16;

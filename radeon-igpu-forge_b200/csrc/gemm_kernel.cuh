@@ -46,8 +46,8 @@ constexpr int kEpiBytes = 8 * kEpiWarpBytes;
 // Epilogue kinds: each kernel instantiation carries one, so that its
 // epilogue holds only the arithmetic of that kind (a runtime switch over every
 // epilogue made the per-chunk code several times larger than the path taken).
-constexpr int EK_LIN16 = 0;   // 16-bit C: store / residual / bias
-constexpr int EK_ACT16 = 1;   // 16-bit C: GELU / bias+GELU / bias+SiLU (+ Z)
+constexpr int EK_LIN16 = 0;   // 16-bit C: store / residual / bias / multiply
+constexpr int EK_ACT16 = 1;   // 16-bit C: GELU / bias+GELU / bias+SiLU / GELU+derivative (+ Z)
 constexpr int EK_DACT16 = 2;  // 16-bit C: dGELU / dSiLU (reads R)
 constexpr int EK_F32 = 3;     // fp32 C: store / residual / bias / accumulate
 
@@ -232,7 +232,7 @@ template <typename T> FXB_DEV void load16_part(const T* p, float* f, int n8) {
 template <int EK> FXB_DEV bool epi_reads_r(const GemmParams& p) {
   if constexpr (EK == EK_DACT16) return true;
   else if constexpr (EK == EK_ACT16) return false;
-  else return p.epi == FXB_EPI_RESIDUAL;
+  else return p.epi == FXB_EPI_RESIDUAL || p.epi == FXB_EPI_MUL;
 }
 // epilogues that also write the rounded pre-activation to Z (when Z is given)
 template <int EK> FXB_DEV bool epi_writes_z(const GemmParams& p) {
@@ -282,6 +282,10 @@ FXB_DEV void epilogue_math(const GemmParams& p, int m, int n0, int n8, float* v,
       piece_r<CT>(p, m, n0, n8, use_pre, pre2, z);
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = v[i] * p.alpha + z[i];
+    } else if (EK == EK_LIN16 && p.epi == FXB_EPI_MUL) {
+      piece_r<CT>(p, m, n0, n8, use_pre, pre2, z);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = v[i] * p.alpha * z[i];
     } else if (p.epi == FXB_EPI_BIAS) {
       load16_part<CT>(static_cast<const CT*>(p.bias) + n0, z, n8);
 #pragma unroll
@@ -291,7 +295,7 @@ FXB_DEV void epilogue_math(const GemmParams& p, int m, int n0, int n8, float* v,
       for (int i = 0; i < 16; ++i) v[i] *= p.alpha;
     }
   } else if constexpr (EK == EK_ACT16) {
-    if (p.epi != FXB_EPI_GELU) {
+    if (p.epi == FXB_EPI_BIAS_GELU || p.epi == FXB_EPI_BIAS_SILU) {
       load16_part<CT>(static_cast<const CT*>(p.bias) + n0, z, n8);
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] += z[i];
@@ -307,6 +311,9 @@ FXB_DEV void epilogue_math(const GemmParams& p, int m, int n0, int n8, float* v,
     if (p.epi == FXB_EPI_BIAS_SILU) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = silu_f(z[i]);
+    } else if (p.epi == FXB_EPI_GELU_DERIV) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) gelu_tanh_and_grad(z[i], &v[i], &z[i]);  // Z = gelu'
     } else {
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = gelu_tanh(z[i]);

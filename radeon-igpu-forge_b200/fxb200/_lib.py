@@ -22,6 +22,7 @@ DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 EPI_STORE, EPI_RESIDUAL, EPI_GELU, EPI_DGELU = 0, 1, 2, 3
 EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_ACCUM_F32, EPI_DSILU = 4, 5, 6, 7, 8
+EPI_GELU_DERIV, EPI_MUL = 9, 10
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32

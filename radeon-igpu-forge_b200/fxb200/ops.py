@@ -10,7 +10,8 @@ import torch
 
 from . import _lib
 from ._lib import (EPI_STORE, EPI_RESIDUAL, EPI_GELU, EPI_DGELU, EPI_BIAS,  # noqa: F401
-                   EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_ACCUM_F32, EPI_DSILU)
+                   EPI_BIAS_GELU, EPI_BIAS_SILU, EPI_ACCUM_F32, EPI_DSILU,
+                   EPI_GELU_DERIV, EPI_MUL)
 
 _TC_DTYPES = (torch.bfloat16, torch.float16)
 

@@ -69,23 +69,26 @@ class _MLPBlock(torch.autograd.Function):
         x2 = x.reshape(B * T, D)
         h, rstd = rmsnorm_fwd(x2, ln_w, eps)
         F = W1.shape[0]
-        z = torch.empty(B * T, F, device=x.device, dtype=x.dtype)
+        # gz = gelu'(z) is saved instead of the pre-activation z: the forward
+        # epilogue gets it from the same tanh as gelu(z), and the backward's
+        # dz = (dy W2) * gz becomes a plain multiply in its epilogue
+        gz = torch.empty(B * T, F, device=x.device, dtype=x.dtype)
         a = torch.empty(B * T, F, device=x.device, dtype=x.dtype)
-        ops.gemm(h, W1, a, epilogue=ops.EPI_GELU, Z=z)
+        ops.gemm(h, W1, a, epilogue=ops.EPI_GELU_DERIV, Z=gz)
         y = ops.linear_fwd(a, W2, residual=x2)
-        ctx.save_for_backward(x2, ln_w, rstd, h, z, a, W1, W2)
+        ctx.save_for_backward(x2, ln_w, rstd, h, gz, a, W1, W2)
         ctx.shape = (B, T, D)
         return y.view(B, T, D)
 
     @staticmethod
     def backward(ctx, dy):
-        x2, ln_w, rstd, h, z, a, W1, W2 = ctx.saved_tensors
+        x2, ln_w, rstd, h, gz, a, W1, W2 = ctx.saved_tensors
         B, T, D = ctx.shape
         d2 = dy.reshape(B * T, D)
         if not d2.is_contiguous():
             d2 = d2.contiguous()
-        dz = torch.empty_like(z)
-        ops.gemm(d2, W2, dz, b_trans=True, epilogue=ops.EPI_DGELU, R=z)   # (dy W2) * gelu'(z)
+        dz = torch.empty_like(gz)
+        ops.gemm(d2, W2, dz, b_trans=True, epilogue=ops.EPI_MUL, R=gz)   # (dy W2) * gelu'(z)
         gW2 = ops.weight_grad(d2, a, W2) if ctx.needs_input_grad[3] else None
         dh = ops.linear_dx(dz, W1)
         gW1 = ops.weight_grad(dz, h, W1) if ctx.needs_input_grad[2] else None

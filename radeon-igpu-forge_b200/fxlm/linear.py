@@ -73,9 +73,9 @@ class _MLP(torch.autograd.Function):
         if not h2.is_contiguous():
             h2 = h2.contiguous()
         M = h2.shape[0]
-        z = torch.empty(M, F, device=h.device, dtype=h.dtype)
+        gz = torch.empty(M, F, device=h.device, dtype=h.dtype)  # gelu'(z), for backward
         a = torch.empty(M, F, device=h.device, dtype=h.dtype)
-        ops.gemm(h2, W1, a, epilogue=ops.EPI_GELU, Z=z)
+        ops.gemm(h2, W1, a, epilogue=ops.EPI_GELU_DERIV, Z=gz)
         out = torch.empty(M, D, device=h.device, dtype=h.dtype)
         if residual is not None:
             res2 = residual.reshape(-1, D)
@@ -84,20 +84,20 @@ class _MLP(torch.autograd.Function):
             ops.gemm(a, W2, out, epilogue=ops.EPI_RESIDUAL, R=res2)
         else:
             ops.gemm(a, W2, out)
-        ctx.save_for_backward(h2, z, a, W1, W2)
+        ctx.save_for_backward(h2, gz, a, W1, W2)
         ctx.has_res = residual is not None
         ctx.hshape = h.shape
         return out.view(h.shape)
 
     @staticmethod
     def backward(ctx, dout):
-        h2, z, a, W1, W2 = ctx.saved_tensors
+        h2, gz, a, W1, W2 = ctx.saved_tensors
         D = W1.shape[1]
         d2 = dout.reshape(-1, D)
         if not d2.is_contiguous():
             d2 = d2.contiguous()
-        dz = torch.empty_like(z)
-        ops.gemm(d2, W2, dz, b_trans=True, epilogue=ops.EPI_DGELU, R=z)   # dz = (dout W2) * gelu'(z)
+        dz = torch.empty_like(gz)
+        ops.gemm(d2, W2, dz, b_trans=True, epilogue=ops.EPI_MUL, R=gz)   # dz = (dout W2) * gelu'(z)
         gW2 = ops.weight_grad(d2, a, W2) if ctx.needs_input_grad[2] else None
         dh = ops.linear_dx(dz, W1).view(ctx.hshape) if ctx.needs_input_grad[0] else None
         gW1 = ops.weight_grad(dz, h2, W1) if ctx.needs_input_grad[1] else None

@@ -248,6 +248,19 @@ def test_gemm_epilogues(dev, gemm_mode, dtype, M, N, K):
     assert (C.float() - F.silu(Z.float())).abs().max().item() < 2e-2
     ops.gemm(A, B, C, epilogue=ops.EPI_BIAS, bias=bias)
     assert (C.float() - (acc + bias.float())).abs().max().item() < tol + 2e-2
+    # gelu + its derivative (both from the rounded pre-activation), then the
+    # backward as a multiply by that derivative
+    G = torch.empty(M, N, device=dev, dtype=dtype)
+    ops.gemm(A, B, C, epilogue=ops.EPI_GELU_DERIV, Z=G)
+    zq = acc.to(dtype).float().requires_grad_()
+    gref = F.gelu(zq, approximate="tanh")
+    gref.backward(torch.ones_like(gref))
+    # (the kernel rounds its own fp32 accumulator: a pre-activation may land
+    # one 16-bit ulp away from torch's, hence the magnitude-relative bound)
+    assert (C.float() - gref.detach()).abs().max().item() < 1e-2 * gref.abs().max().item() + 2e-2
+    assert (G.float() - zq.grad).abs().max().item() < 2e-2
+    ops.gemm(A, B, C, epilogue=ops.EPI_MUL, R=G, alpha=0.5)
+    assert (C.float() - 0.5 * acc * G.float()).abs().max().item() < 2e-2 * (acc * G.float()).abs().max().item() + 1e-2
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
