@@ -274,9 +274,9 @@ def run_micro(args):
         shapes = [  # name, M, N, K, a_trans, b_trans, epilogue
             ("fwd qkv", T_, 3 * D, D, False, False, ops.EPI_STORE),
             ("fwd proj+res", T_, D, D, False, False, ops.EPI_RESIDUAL),
-            ("fwd fc+gelu", T_, F_, D, False, False, ops.EPI_GELU),
+            ("fwd fc+gelu(+gelu')", T_, F_, D, False, False, ops.EPI_GELU_DERIV),
             ("fwd fc2+res", T_, D, F_, False, False, ops.EPI_RESIDUAL),
-            ("bwd dz=dout.W2 (dgelu)", T_, F_, D, False, True, ops.EPI_DGELU),
+            ("bwd dz=dout.W2*gelu'", T_, F_, D, False, True, ops.EPI_MUL),
             ("bwd dh=dz.W1", T_, D, F_, False, True, ops.EPI_STORE),
             ("bwd dy=dx.Wproj", T_, D, D, False, True, ops.EPI_STORE),
             ("bwd dh=dqkv.Wqkv", T_, D, 3 * D, False, True, ops.EPI_STORE),
@@ -294,8 +294,8 @@ def run_micro(args):
             B = ((torch.randn(K, N, device=dev) if bt else torch.randn(N, K, device=dev)) / math.sqrt(K)).to(bf)
             acc = epi == ops.EPI_ACCUM_F32
             C = torch.zeros(M, N, device=dev, dtype=torch.float32 if acc else bf)
-            R = torch.randn(M, N, device=dev).to(bf) if epi in (ops.EPI_RESIDUAL, ops.EPI_DGELU) else None
-            Z = torch.empty(M, N, device=dev, dtype=bf) if epi == ops.EPI_GELU else None
+            R = torch.randn(M, N, device=dev).to(bf) if epi in (ops.EPI_RESIDUAL, ops.EPI_MUL) else None
+            Z = torch.empty(M, N, device=dev, dtype=bf) if epi == ops.EPI_GELU_DERIV else None
             ms = _time_ms(lambda: ops.gemm(A, B, C, a_trans=at, b_trans=bt, epilogue=epi, R=R, Z=Z), it)
             Ar = A.t() if at else A
             Br = B if bt else B.t()
