@@ -552,8 +552,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x;
-  const int bh = blockIdx.y;
+  // one CTA per (key tile, batch*head), numbered key tile major: with a causal
+  // mask key tile kt meets nqt - kt query tiles, so the CTAs are launched
+  // heaviest first and the last ones to start are the shortest
+  const int BH = p.B * p.H;
+  const int kt = (int)(blockIdx.x / BH);
+  const int bh = (int)(blockIdx.x - kt * BH);
   const int b = bh / p.H, h = bh - b * p.H;
   const int kv0 = kt * TILE;
   const int i0 = p.causal ? kt : 0;
@@ -976,7 +980,7 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
     if ((r = set_smem(k, bwd_smem()))) return r;
     once[dev & 63] = true;
   }
-  dim3 grid(p.nkt, a->B * a->H);
+  dim3 grid((unsigned)(p.nkt * a->B * a->H));
   fxb::pdl_launch(k, grid, kBwdThreads, bwd_smem(), st, mq, mk, mv, mdo, mdq, p);
   if ((r = fxb::check_launch("attn_bwd"))) return r;
   const int64_t n = rows * (DH / 8);
