@@ -676,6 +676,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int kk = 0; kk < TILE / 16; ++kk)
           umma_f16(tDK, desc_add(dsd, kmajor_off(kk)), desc_add(qm, mnmajor_off(kk)), I_KV,
                    (it > 0 || kk > 0));
+        // Q / dO of this tile have no readers after dK (dQ reads dS and K): the
+        // producer may load the tile after next into the stage now
+        umma_commit(qdo_empty(st));
         if (!mbar_wait(dq_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
         const uint64_t dsm = mnmajor_desc0(ds_s), km = mnmajor_desc0(sK);
@@ -683,7 +686,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int kk = 0; kk < TILE / 16; ++kk)
           umma_f16(tDQ, desc_add(dsm, mnmajor_off(kk)), desc_add(km, mnmajor_off(kk)), I_Q, kk > 0);
         umma_commit(dq_full);
-        umma_commit(qdo_empty(st));
       }
       umma_commit(acc_full);
       mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT);
