@@ -29,7 +29,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int TILE = 128;
 constexpr int kFwdThreads = 576;  // forward: warps 0-15 softmax, 16 MMA, 17 TMA
-constexpr int kBwdThreads = 320;  // backward: warps 0-7 softmax / dS, 8 MMA, 9 TMA
+constexpr int kBwdThreads = 576;  // backward: warps 0-15 softmax / dS, 16 MMA, 17 TMA
+constexpr int kBwdWarpMma = 16, kBwdWarpTma = 17;
 constexpr int kFwdWarpMma = 16, kFwdWarpTma = 17;
 // Forward pipeline depths: K/V ring stages and Q buffers (shared memory:
 // (QN + 2 KS) DH-wide tiles + exchange) and P buffers (tensor memory)
@@ -570,15 +571,15 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(qdo_empty(s), 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 256);
-    mbar_init(ds_full, 256);
+    mbar_init(s_empty, 512);  // every softmax thread
+    mbar_init(ds_full, 512);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 256);
+    mbar_init(dq_empty, 512);
     mbar_init(acc_full, 1);
     mbar_init(pt_free, 1);
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == kBwdWarpMma) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -591,7 +592,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
   const uint32_t tPT = tmem + 448;  // P^T, 16-bit pairs (128 queries in 64 columns)
 
-  if (warp == 9) {
+  if (warp == kBwdWarpTma) {
     // ------------------------------------------------ producer: TMA (lane 0)
     // plus the query tile's LSE (log2 units) and delta, four queries per lane,
     // into the same double buffer as Q / dO
@@ -630,7 +631,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         mbar_wait(qdo_full(it & 1), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
     }
     __syncwarp();
-  } else if (warp == 8) {
+  } else if (warp == kBwdWarpMma) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t I_SS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);  // S^T, dP^T
@@ -692,45 +693,44 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------ softmax / dS warps 0..7
+    // ------------------------------------------------ softmax / dS warps 0..15
     // warp w: TMEM lane quarter w & 3 (32 key rows for S^T / dP^T, 32 query
-    // rows for the dQ partial), column half w >> 2 (64 of the 128 queries of
-    // S^T / dP^T, 32 of the 64 head dims of dQ / dK / dV)
-    const int quarter = warp & 3, half = warp >> 2;
+    // rows for the dQ partial), column part w >> 2 (32 of the 128 queries of
+    // S^T / dP^T, 16 of the 64 head dims of dQ / dK / dV): four warps per
+    // sub-partition keep its pipes busy through the tensor-memory and
+    // barrier latencies of the chain
+    const int quarter = warp & 3, part = warp >> 2;
     const int r = quarter * 32 + lane;
     const int kv = kv0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int qc0 = half * 64;
+    const int qc0 = part * 32;
     bool ok = true;
     // dQ partial of query tile it (row r is query row quarter*32 + lane of the
-    // tile, head dims half*32..+32): tensor memory -> registers -> this warp's
-    // 128B-swizzled staging tile -> asynchronous fp32 TMA add-reduction into
-    // the dQ accumulator (rows past T are clipped by the tensor map). Waiting
-    // for dq_full also means the tile's dV / dK / dQ MMAs no longer read P^T /
-    // dS^T in shared memory.
+    // tile, head dims part*16..+16): tensor memory -> registers -> this warp's
+    // 64B-swizzled staging tile (32 rows x 64 bytes) -> asynchronous fp32 TMA
+    // add-reduction into the dQ accumulator (rows past T are clipped by the
+    // tensor map). Waiting for dq_full also means the tile's dV / dK / dQ MMAs
+    // no longer read P^T / dS^T in shared memory.
     auto flush_dq = [&](int it) -> bool {
       if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) return false;
       tc_fence_after();
-      const uint32_t stg = sDQ + (uint32_t)warp * 4096u;
+      const uint32_t stg = sDQ + (uint32_t)warp * 2048u;
       if (lane == 0) bulk_wait_read0();  // the previous reduction has read the staging tile
       __syncwarp();
-      const uint32_t row = stg + (uint32_t)lane * 128u;
+      const uint32_t row = stg + (uint32_t)lane * 64u;
+      uint32_t rr[16];
+      tmem_ld16(tDQ + lane_off + part * 16, rr);
+      tmem_wait_ld();
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {  // 16 columns at a time (register pressure)
-        uint32_t rr[16];
-        tmem_ld16(tDQ + lane_off + half * 32 + hh * 16, rr);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          st_shared_v4(row + (uint32_t)(((4 * hh + c) ^ (lane & 7)) << 4),
-                       make_uint4(rr[4 * c], rr[4 * c + 1], rr[4 * c + 2], rr[4 * c + 3]));
-      }
+      for (int c = 0; c < 4; ++c)
+        st_shared_v4(row + (uint32_t)((c ^ ((lane >> 1) & 3)) << 4),
+                     make_uint4(rr[4 * c], rr[4 * c + 1], rr[4 * c + 2], rr[4 * c + 3]));
       tc_fence_before();
       mbar_arrive(dq_empty);  // the dQ partial has left tensor memory
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_reduce_add_3d(&tmDQ, stg, half * 32, (i0 + it) * TILE + quarter * 32, bh);
+        tma_reduce_add_3d(&tmDQ, stg, part * 16, (i0 + it) * TILE + quarter * 32, bh);
         bulk_commit();
       }
       return true;
@@ -751,31 +751,31 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           !__all_sync(0xffffffffu, mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
       tc_fence_after();
       const bool diag = p.causal && (q0 < kv0 + TILE);
-      uint32_t pw[32], dw[32];  // P^T and dS^T of this thread's 64 queries, 16-bit pairs
+      uint32_t pw[16], dw[16];  // P^T and dS^T of this thread's 32 queries, 16-bit pairs
 #pragma unroll
-      for (int hq = 0; hq < 2; ++hq) {  // 32 queries at a time (register pressure)
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tST + lane_off + qc0 + hq * 32, sr);
-        tmem_ld32(tDPT + lane_off + qc0 + hq * 32, dr);
+      for (int hq = 0; hq < 2; ++hq) {  // 16 queries at a time (register pressure)
+        uint32_t sr[16], dr[16];
+        tmem_ld16(tST + lane_off + qc0 + hq * 16, sr);
+        tmem_ld16(tDPT + lane_off + qc0 + hq * 16, dr);
         tmem_wait_ld();
         if (hq == 1) {
           tc_fence_before();
           mbar_arrive(s_empty);  // S^T / dP^T are in registers: the next tile's may overwrite them
         }
-        const float* ls = lse_s + sb * 128 + qc0 + hq * 32;
-        const float* dl = del_s + sb * 128 + qc0 + hq * 32;
+        const float* ls = lse_s + sb * 128 + qc0 + hq * 16;
+        const float* dl = del_s + sb * 128 + qc0 + hq * 16;
 #pragma unroll
-        for (int qc = 0; qc < 32; qc += 2) {
+        for (int qc = 0; qc < 16; qc += 2) {
           float pp[2], dd[2];
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             float e = ex2_ftz(fmaf(__uint_as_float(sr[qc + i]), p.scale_log2, -ls[qc + i]));
-            if (kv >= p.T || (diag && q0 + qc0 + hq * 32 + qc + i < kv)) e = 0.f;
+            if (kv >= p.T || (diag && q0 + qc0 + hq * 16 + qc + i < kv)) e = 0.f;
             pp[i] = e;
             dd[i] = e * (__uint_as_float(dr[qc + i]) - dl[qc + i]);
           }
-          pw[hq * 16 + (qc >> 1)] = pack2<T16>(pp[0], pp[1]);
-          dw[hq * 16 + (qc >> 1)] = pack2<T16>(dd[0], dd[1]);
+          pw[hq * 8 + (qc >> 1)] = pack2<T16>(pp[0], pp[1]);
+          dw[hq * 8 + (qc >> 1)] = pack2<T16>(dd[0], dd[1]);
         }
       }
       // P^T -> tensor memory once dV of the previous tile has read it; dS^T ->
@@ -786,11 +786,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         continue;
       }
       tc_fence_after();
-      tmem_st32(tPT + lane_off + half * 32, pw);
-      uint8_t* ds = gbase + (sDS - base) + sb * 32768;
+      tmem_st16(tPT + lane_off + part * 16, pw);
+      uint8_t* ds = gbase + (sDS - base) + (it & 1) * 32768;
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        *reinterpret_cast<uint4*>(ds + sw128_offset(r, half * 8 + u)) =
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(ds + sw128_offset(r, part * 4 + u)) =
             make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
       tmem_wait_st();
       fence_proxy_async_smem();
@@ -802,18 +802,18 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     if (ok && n_it > 0 && !flush_dq(n_it - 1)) ok = false;
     if (lane == 0) bulk_wait_all0();  // dQ reductions complete before the kernel ends
     __syncwarp();
-    // final dK (scaled) and dV for key row kv, head dims half*32..+32
+    // final dK (scaled) and dV for key row kv, head dims part*16..+16
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT))) {
       tc_fence_after();
-      uint32_t rk[32], rv[32];
-      tmem_ld32(tDK + lane_off + half * 32, rk);
-      tmem_ld32(tDV + lane_off + half * 32, rv);
+      uint32_t rk[16], rv[16];
+      tmem_ld16(tDK + lane_off + part * 16, rk);
+      tmem_ld16(tDV + lane_off + part * 16, rv);
       tmem_wait_ld();
       if (kv < p.T) {
-        T16* krow = static_cast<T16*>(p.dk) + b * p.dk_sb + (int64_t)kv * p.dk_st + h * p.dk_sh + half * 32;
-        T16* vrow = static_cast<T16*>(p.dv) + b * p.dv_sb + (int64_t)kv * p.dv_st + h * p.dv_sh + half * 32;
+        T16* krow = static_cast<T16*>(p.dk) + b * p.dk_sb + (int64_t)kv * p.dk_st + h * p.dk_sh + part * 16;
+        T16* vrow = static_cast<T16*>(p.dv) + b * p.dv_sb + (int64_t)kv * p.dv_st + h * p.dv_sh + part * 16;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 2; ++u) {
           float fk[8], fv[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -829,7 +829,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kBwdWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -860,13 +860,13 @@ int make_map4(CUtensorMap* map, int dtype, const void* ptr, int D, int T, int H,
 }
 
 // fp32 dQ accumulator (B*H, T, D) for the backward's TMA add-reductions:
-// boxes of 32 rows x 32 columns (128 bytes, 128B swizzle)
+// boxes of 32 rows x 16 columns (64 bytes, 64B swizzle)
 int make_map_dq(CUtensorMap* map, float* dq_acc, int D, int T, int BH) {
   uint64_t dims[3] = {(uint64_t)D, (uint64_t)T, (uint64_t)BH};
   uint64_t strides[2] = {(uint64_t)D * 4, (uint64_t)T * D * 4};
-  uint32_t box[3] = {32, 32, 1};
+  uint32_t box[3] = {16, 32, 1};
   return fxb::encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_acc, dims, strides, box,
-                           CU_TENSOR_MAP_SWIZZLE_128B);
+                           CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 bool strides_ok(int64_t sb, int64_t st, int64_t sh) {
