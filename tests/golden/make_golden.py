@@ -10,13 +10,18 @@ exact same values to the bf16 kernels.
 
     python tests/golden/make_golden.py --ref /path/to/reference [--skip-curve] [--skip-d768]
 
-Outputs (committed): ops.npz, gpt_tiny.npz, curve_tiny.json, gpt_d768.json.
+Outputs (committed): ops.npz, gpt_tiny.npz, curve_tiny.json, gpt_d768.json,
+prepare_bytes.json (the reference's ml/fxlm/prepare_bytes.py run as a script on
+the tree of prepare_bytes_tree.py: meta and SHA-256 of the token files).
 """
 import argparse
+import hashlib
 import json
 import math
 import os
+import subprocess
 import sys
+import tempfile
 import time
 import types
 import zlib
@@ -254,13 +259,39 @@ def make_d768(ref_model):
     print("gpt_d768:", res)
 
 
+def make_prepare_bytes(ref_root):
+    sys.path.insert(0, HERE)
+    from prepare_bytes_tree import build_tree, CASES
+    script = os.path.join(ref_root, "ml", "fxlm", "prepare_bytes.py")
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        root = os.path.join(tmp, "tree")
+        build_tree(root)
+        for name, inputs, opts in CASES:
+            prefix = os.path.join(tmp, "out", name)
+            subprocess.run([sys.executable, script, *[os.path.join(root, i) for i in inputs],
+                            "--out", prefix, *opts], check=True, capture_output=True)
+            rec = {"meta": json.load(open(prefix + ".json", encoding="utf-8"))}
+            for part in ("train", "val"):
+                with open(f"{prefix}_{part}.bin", "rb") as f:
+                    rec["sha256_" + part] = hashlib.sha256(f.read()).hexdigest()
+            out[name] = rec
+    with open(os.path.join(HERE, "prepare_bytes.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    print("prepare_bytes.json:", {k: v["meta"] for k, v in out.items()})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="root of the reference repository")
     ap.add_argument("--skip-curve", action="store_true")
     ap.add_argument("--skip-d768", action="store_true")
+    ap.add_argument("--only-prepare-bytes", action="store_true")
     ap.add_argument("--steps", type=int, default=200)
     args = ap.parse_args()
+    make_prepare_bytes(args.ref)
+    if args.only_prepare_bytes:
+        return
     torch.set_num_threads(os.cpu_count())
     ref_model, ref_fxgpu_model, ref_selftest = _import_reference(args.ref)
     make_ops(ref_model, ref_fxgpu_model, ref_selftest)

@@ -353,3 +353,55 @@ def test_graphed_step_matches_eager(dev):
         assert abs(a - b) <= 1e-3 * abs(b), (graphed, eager[1:])
     r = rel(og_.master, oe.master)
     assert r < 1e-2, f"master rel diff {r:.3e}"
+
+
+def test_prepare_train_resume_sample(dev, tmp_path):
+    """The reference's workflow end to end (ml/fxlm/prepare_bytes.py ->
+    train_lm.py -> sample.py): byte tokens of this package's sources, a small
+    run with eval and checkpoint, a resumed run, and generation from the
+    checkpoint. The fused bf16 model's last-position logits at several
+    prompt lengths track the fp32 model within twice the error of the same
+    weights on the bf16 torch path."""
+    from fxlm import prepare_bytes, train_lm, sample
+    from fxlm.model import GPT, GPTConfig
+    pkg = os.path.join(os.path.dirname(GOLD), "..", "radeon-igpu-forge_b200", "fxlm")
+    data = str(tmp_path / "data" / "src")
+    meta = prepare_bytes.main([os.path.join(pkg, "*.py"), "--out", data])
+    assert meta["vocab_size"] == 256 and meta["n_val"] > 200
+    out = str(tmp_path / "run")
+    common = ["--data", data + "_train.bin", "--out", out, "--seq-len", "64", "--layers", "2",
+              "--heads", "2", "--dim", "128", "--batch", "8", "--warmup", "5",
+              "--eval-every", "30", "--eval-batches", "2", "--log-every", "10"]
+    train_lm.main(common + ["--steps", "30"])
+    ckpt = os.path.join(out, "ckpt_last.pt")
+    sd = torch.load(ckpt, map_location="cpu", weights_only=False)
+    assert sd["step"] == 30 and sd["meta"]["tokenizer"] == "bytes"
+    with pytest.raises(SystemExit, match="exists"):
+        train_lm.main(common + ["--steps", "31"])
+    train_lm.main(common + ["--steps", "40", "--resume", ckpt])
+    sd2 = torch.load(ckpt, map_location="cpu", weights_only=False)
+    assert sd2["step"] == 40
+    assert any(not torch.equal(sd["model"][k], sd2["model"][k]) for k in sd["model"])
+
+    mf, meta, missing = sample.load_checkpoint(ckpt, dev)
+    assert not missing and mf.tok_emb.weight.dtype == torch.bfloat16
+    torch_cfg = dict(sd2["config"], attn_impl="sdpa", norm_impl="torch", ce_impl="torch",
+                     linear_impl="torch")
+    mt = GPT(GPTConfig(**torch_cfg)).to(dev)
+    mt.load_state_dict({k: v for k, v in sd2["model"].items()})
+    mr = GPT(GPTConfig(**torch_cfg)).to(dev).eval()
+    mr.load_state_dict(mt.state_dict())
+    mt = mt.bfloat16().eval()
+    g = torch.Generator().manual_seed(5)
+    with torch.inference_mode():
+        for T in (1, 4, 37, 64):
+            idx = torch.randint(0, 256, (1, T), generator=g).to(dev)
+            lf = mf(idx)[:, -1].float()
+            lt = mt(idx)[:, -1].float()
+            lr_ = mr(idx)[:, -1]
+            e_our, e_t = (lf - lr_).abs().max().item(), (lt - lr_).abs().max().item()
+            assert e_our <= 2 * e_t + 2e-2, (T, e_our, e_t)
+
+    args = ["--ckpt", ckpt, "--prompt", "def ", "--max-new", "48", "--seed", "3"]
+    a, b = sample.main(args), sample.main(args)
+    assert isinstance(a, str) and a == b and len(a.encode("utf-8", "replace")) >= 1
