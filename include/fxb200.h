@@ -45,7 +45,8 @@ int fxb_version(void);
 const char* fxb_last_error(void);
 
 /* Reads (and with clear != 0 resets) the device error word that kernels set
- * when a bounded wait expires (bit 1 GEMM, 2 attention, 4 gather). Synchronises
+ * when a bounded wait expires (bit 1 GEMM, 2 attention, 4 gather, 8 cross-
+ * entropy). Synchronises
  * the current device. No reference counterpart (the reference has no bounded
  * waits). */
 int fxb_device_error(int32_t* code, int32_t clear);
