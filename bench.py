@@ -8,9 +8,11 @@ architecture (V32768, L12, D768, H12, T1024) on a per-GPU micro-batch of 8
 sequences of Zipf(1.1) tokens (seed 3 + rank), bf16 compute with fp32 master
 weights. The step is captured once in a CUDA graph (fxlm.GraphedStep, after
 the warm-up steps) and replayed; `--no-graph` runs it eagerly. For N > 1 the
-driver launches this under torchrun (one rank per GPU, NCCL); gradients are
-all-reduced in buckets that overlap backward, and those NCCL calls are part
-of the captured graph.
+driver launches this under torchrun (one rank per GPU, NCCL); gradient
+buckets are reduced to the rank owning each shard of FlatAdamW while backward
+runs, each rank updates its shard and the bf16 parameters are all-gathered
+(fxb200.zero; `--no-zero`: all-reduce and a full update on every rank), and
+those NCCL calls are part of the captured graph.
 
 Printed (rank 0, one JSON line): `value` = tokens/s of the whole job with the
 token batch already in HBM, timed on the device with CUDA events (max over
@@ -428,7 +430,10 @@ def run_ours(args, rank, world, local_rank):
     model = GPT(GPTConfig(**CFG4, eps=1e-6)).to(dev)
     opt = FlatAdamW(model, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
                     max_grad_norm=1.0, init_scale=1.0, param_dtype=torch.bfloat16)
-    if world > 1:
+    if world > 1 and args.zero:
+        from fxb200.zero import ShardedDataParallel
+        ShardedDataParallel(model, opt)
+    elif world > 1:
         from fxb200.ddp import DataParallel
         DataParallel(model, opt)
     x_cpu, y_cpu = zipf_tokens(CFG4["vocab_size"], MB, SEQ, seed=3 + rank)
@@ -574,7 +579,8 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic Zipf(1.1) tokens, seed 3 + rank; reference init (seed 3)",
             "config": {"workload": WORKLOAD, "global_batch": MB * world, "seq_len": SEQ,
-                       "parallelism": f"dp{world}", "model": "GPT d768x12L tied, V32768",
+                       "parallelism": f"dp{world}" + ("-zero1" if args.zero and world > 1 else ""),
+                       "model": "GPT d768x12L tied, V32768",
                        "step": "CUDA graph replay" if graphed is not None else "eager",
                        "l2": "no flush: one step moves several GB (> 126 MB L2)"},
             "e2e": e2e,
@@ -612,6 +618,9 @@ def main():
     ap.add_argument("--no-attn", action="store_true", help="skip the attention microbench")
     ap.add_argument("--no-graph", action="store_true",
                     help="run the step eagerly instead of replaying a captured CUDA graph")
+    ap.add_argument("--no-zero", dest="zero", action="store_false",
+                    help="N > 1: plain data parallelism (all-reduce, every rank updates every "
+                         "parameter) instead of the sharded update (fxb200.zero, the default)")
     ap.add_argument("--micro", default=None,
                     help="per-kernel microbenchmarks instead of the step: all or a comma list "
                          "of gemm,attn,rmsnorm,ce,adamw")

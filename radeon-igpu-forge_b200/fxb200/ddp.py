@@ -82,23 +82,24 @@ class DataParallel:
         return pre_hook
 
     def _reduce_range(self, start, end):
-        """Enqueue the mean all-reduce of grad[start:end]; returns (work, view, needs_div)."""
+        """Enqueue the mean all-reduce of grad[start:end]; returns a list of
+        (work, view, needs_div)."""
         view = self.opt.grad[start:end]
         if self.stream is None:
             # CPU / gloo (tests): gloo has no AVG, so SUM then divide after wait
-            return dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.pg, async_op=True), view, True
+            return [(dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.pg, async_op=True), view, True)]
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(view.device))
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(ev)
-            return dist.all_reduce(view, op=dist.ReduceOp.AVG, group=self.pg, async_op=True), view, False
+            return [(dist.all_reduce(view, op=dist.ReduceOp.AVG, group=self.pg, async_op=True), view, False)]
 
     def _launch(self, bidx):
         if bidx in self._done:
             return
         self._done.add(bidx)
         _n, s, e = self.buckets[bidx]
-        self._pending.append(self._reduce_range(s, e))
+        self._pending.extend(self._reduce_range(s, e))
 
     def _finish(self, _opt):
         # buckets whose hook did not fire (e.g. no grad path) are reduced here,
@@ -107,7 +108,7 @@ class DataParallel:
             if b not in self._done:
                 self._launch(b)
         for s, e in self._rest:
-            self._pending.append(self._reduce_range(s, e))
+            self._pending.extend(self._reduce_range(s, e))
         for w, view, needs_div in self._pending:
             w.wait()
             if needs_div:

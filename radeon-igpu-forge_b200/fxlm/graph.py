@@ -13,9 +13,10 @@ work without changing a single kernel or its arguments.
 Conditions (checked where cheap): fixed batch shape; the optimizer is a
 FlatAdamW whose gradient buffer is consumed by its update (so no zeroing op
 is needed between replays); the learning rate is read from `opt.lr_dev`, a
-device scalar written before each replay; optimizer pre-step hooks only if
-their owner declares `graph_capturable` (fxb200.ddp.DataParallel does: its
-bucket all-reduces are NCCL calls on a side stream forked from the capturing
+device scalar written before each replay; optimizer hooks (pre-step, norm,
+post-step) only if their owner declares `graph_capturable`
+(fxb200.ddp.DataParallel and fxb200.zero.ShardedDataParallel do: their
+collectives are NCCL calls on a side stream forked from the capturing
 stream, so they are recorded into the graph and replayed with it). The
 warm-up steps before capture are real training steps (they also trigger every
 lazy initialisation: library load, tensor-map encoders, shared-memory
@@ -29,10 +30,11 @@ from fxb200 import _lib
 
 class GraphedStep:
     def __init__(self, model, opt, x_example, y_example, warmup=3):
-        for h in getattr(opt, "pre_step_hooks", None) or ():
-            if not getattr(getattr(h, "__self__", None), "graph_capturable", False):
-                raise ValueError("GraphedStep: optimizer has a pre-step hook that cannot be "
-                                 "captured; run the step eagerly")
+        for kind in ("pre_step_hooks", "norm_hooks", "post_step_hooks"):
+            for h in getattr(opt, kind, None) or ():
+                if not getattr(getattr(h, "__self__", None), "graph_capturable", False):
+                    raise ValueError(f"GraphedStep: optimizer has a {kind[:-1].replace('_', '-')} "
+                                     "that cannot be captured; run the step eagerly")
         if warmup < 1:
             raise ValueError("GraphedStep: warmup >= 1 (lazy initialisation must happen "
                              "before capture)")

@@ -27,6 +27,21 @@ def _align8(n):
     return (n + 7) & ~7
 
 
+def shard_segments(ends, wds, lo, hi):
+    """Weight-decay segments of flat[lo:hi): `ends` are the parameters'
+    exclusive aligned end offsets (ascending), `wds` their flags. Returns
+    (ends relative to lo, flags) of the segments that overlap the range, the
+    last end clipped to hi - lo."""
+    rel_end, rel_wd = [], []
+    start = 0
+    for e, wd in zip(ends, wds):
+        if e > lo and start < hi:
+            rel_end.append(min(e, hi) - lo)
+            rel_wd.append(int(wd))
+        start = e
+    return rel_end, rel_wd
+
+
 class FlatAdamW:
     """fp32 master + low-precision params + dynamic loss scale + global clip.
 
@@ -104,6 +119,13 @@ class FlatAdamW:
         # hooks run after the gradient is complete and before the update
         # (data-parallel reduction of self.grad registers one here)
         self.pre_step_hooks = []
+        # optimizer sharding (fxb200.zero): the sum of squares and the update
+        # cover only [lo, hi) of the flat buffers; norm hooks run between the
+        # sum of squares and finalize (cross-rank sum of the partial norms),
+        # post-step hooks after the update (gather of the updated parameters)
+        self.shard = None
+        self.norm_hooks = []
+        self.post_step_hooks = []
 
     # -- helpers -----------------------------------------------------------
 
@@ -119,6 +141,27 @@ class FlatAdamW:
             p.grad = None
             self._grad_dirty = True
 
+    def set_shard(self, lo, hi):
+        """Restrict the sum of squares and the update to flat[lo:hi) (lo, hi
+        multiples of 8, 0 <= lo <= hi <= numel); set_shard(None, None)
+        restores the whole buffer. The caller owns the rest: reducing the norm across shards
+        (norm_hooks), refreshing the other parameters and zeroing the
+        gradient outside the shard (post_step_hooks)."""
+        if lo is None:
+            self.shard = None
+            return
+        lo, hi = int(lo), int(hi)
+        if lo % 8 or hi % 8 or not 0 <= lo <= hi <= self.numel:
+            raise ValueError(f"bad shard [{lo}, {hi}) of {self.numel}")
+        ends = [off + _align8(n) for _nm, _p, off, n, _w in self._info]
+        wds = [wd for _nm, _p, _o, _n, wd in self._info]
+        rel_end, rel_wd = shard_segments(ends, wds, lo, hi)
+        dev = self.grad.device
+        self.shard = (lo, hi)
+        self._shard_end = torch.tensor(rel_end or [0], device=dev, dtype=torch.int64)
+        self._shard_wd = torch.tensor(rel_wd or [0], device=dev, dtype=torch.int32)
+        self._shard_nseg = len(rel_end)
+
     # -- API -----------------------------------------------------------------
 
     def backward(self, loss):
@@ -132,21 +175,35 @@ class FlatAdamW:
             hook(self)
         st = _lib.stream_ptr(self.grad.device)
         P = _lib.ptr
-        _lib.call("fxb_adamw_sumsq_det", 0, P(self.grad), self.numel, P(self.scratch),
-                  P(self._flags), P(self._sumsq_ws), st)
+        if self.shard is None:
+            lo, n = 0, self.numel
+            seg_end, seg_wd, nseg = self._seg_end, self._seg_wd, len(self._info)
+        else:
+            lo, n = self.shard[0], self.shard[1] - self.shard[0]
+            seg_end, seg_wd, nseg = self._shard_end, self._shard_wd, self._shard_nseg
+        if n:
+            _lib.call("fxb_adamw_sumsq_det", 0, P(self.grad[lo:]), n, P(self.scratch),
+                      P(self._flags), P(self._sumsq_ws), st)
+        for hook in self.norm_hooks:
+            hook(self)
         _lib.call("fxb_adamw_final", P(self.scratch), P(self._flags), P(self._step_ctr),
                   P(self._found_inf), P(self._norm), P(self.scale),
                   float(self.max_grad_norm), st)
-        _lib.call("fxb_adamw_update", 0, _lib.dtype_code(self.param_dtype), P(self.grad),
-                  P(self.master), P(self.m), P(self.v), P(self.flat16), self.numel,
-                  P(self._seg_end), P(self._seg_wd), len(self._info), P(self.scratch),
-                  P(self._found_inf), P(self.scale), P(self._step_ctr), lr_v,
-                  P(self.lr_dev) if self.lr_dev is not None else None,
-                  float(self.betas[0]), float(self.betas[1]), float(self.eps),
-                  float(self.weight_decay), st)
+        if n:
+            _lib.call("fxb_adamw_update", 0, _lib.dtype_code(self.param_dtype), P(self.grad[lo:]),
+                      P(self.master[lo:]), P(self.m[lo:]), P(self.v[lo:]), P(self.flat16[lo:]), n,
+                      P(seg_end), P(seg_wd), nseg, P(self.scratch),
+                      P(self._found_inf), P(self.scale), P(self._step_ctr), lr_v,
+                      P(self.lr_dev) if self.lr_dev is not None else None,
+                      float(self.betas[0]), float(self.betas[1]), float(self.eps),
+                      float(self.weight_decay), st)
         torch._amp_update_scale_(self.scale, self._growth, self._found_inf, 2.0, 0.5,
                                  self.growth_interval)
-        self._grad_dirty = False  # the update consumed (zeroed) the flat gradient
+        for hook in self.post_step_hooks:
+            hook(self)
+        # the update consumed (zeroed) the flat gradient; with a shard, a
+        # post-step hook zeroes the rest
+        self._grad_dirty = False
         return {"grad_norm": self._norm, "found_inf": self._found_inf, "scale": self.scale}
 
     def zero_grad(self):

@@ -9,7 +9,8 @@ weights by parameter name, the FlatAdamW state, config, step, meta and args
 (:162-174), `--resume` (:134-139) and refusal to overwrite an existing run
 (:140-142). Additions: `--synthetic V` trains on Zipf(1.1) tokens instead of
 a file; under torchrun the batch is data-parallel over the ranks (NCCL,
-bucketed all-reduce) and only rank 0 logs and writes checkpoints.
+bucketed all-reduce; `--zero` shards the optimizer update instead) and only
+rank 0 logs and writes checkpoints.
 
     python -m fxlm.train_lm --data data/demo_train.bin --out runs/demo
     torchrun --nproc-per-node 8 -m fxlm.train_lm --synthetic 32768 --out runs/dp8 ...
@@ -51,6 +52,8 @@ def _parse(argv=None):
     ap.add_argument("--ce", choices=["fused", "torch"], default="fused")
     ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--zero", action="store_true",
+                    help="under torchrun: shard FlatAdamW's update over the ranks (ZeRO-1)")
     return ap.parse_args(argv)
 
 
@@ -112,7 +115,11 @@ def main(argv=None):
     pdt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
     opt = FlatAdamW(model, lr=args.lr, weight_decay=args.wd, max_grad_norm=args.clip,
                     init_scale=args.init_scale, param_dtype=pdt)
-    if world > 1:
+    sharded = None
+    if world > 1 and args.zero:
+        from fxb200.zero import ShardedDataParallel
+        sharded = ShardedDataParallel(model, opt)
+    elif world > 1:
         from fxb200.ddp import DataParallel
         DataParallel(model, opt)
     if rank == 0:
@@ -140,6 +147,8 @@ def main(argv=None):
         return seq[:, :-1], seq[:, 1:]
 
     def save_ckpt(step, tag="last"):
+        if sharded is not None:
+            sharded.consolidate()  # collective: every rank, before rank 0 writes
         if rank != 0:
             return
         sd = {"model": {k: v.detach().to("cpu", torch.float32) for k, v in opt.master_state_dict().items()},
