@@ -41,7 +41,9 @@ def _parse(argv=None):
     ap.add_argument("--warmup", type=int, default=100)
     ap.add_argument("--wd", type=float, default=0.1)
     ap.add_argument("--clip", type=float, default=1.0)
-    ap.add_argument("--init-scale", type=float, default=1.0)
+    ap.add_argument("--init-scale", type=float, default=None,
+                    help="initial loss scale (default: 2^16 for fp16 as in the reference, "
+                         "1 for bf16)")
     ap.add_argument("--eval-every", type=int, default=200)
     ap.add_argument("--eval-batches", type=int, default=20)
     ap.add_argument("--log-every", type=int, default=20)
@@ -51,10 +53,15 @@ def _parse(argv=None):
     ap.add_argument("--norm", choices=["fused", "torch"], default="fused")
     ap.add_argument("--ce", choices=["fused", "torch"], default="fused")
     ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
+    ap.add_argument("--tunable", action="store_true",
+                    help="accepted for command-line compatibility (no runtime tuning here)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--zero", action="store_true",
                     help="under torchrun: shard FlatAdamW's update over the ranks (ZeRO-1)")
-    return ap.parse_args(argv)
+    args = ap.parse_args(argv)
+    if args.init_scale is None:
+        args.init_scale = 2.0 ** 16 if args.dtype == "fp16" else 1.0
+    return args
 
 
 def lr_at(step, args):

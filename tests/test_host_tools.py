@@ -196,3 +196,31 @@ def test_prepare_bytes_matches_reference_outputs(tmp_path):
         for part in ("train", "val"):
             with open(f"{prefix}_{part}.bin", "rb") as f:
                 assert hashlib.sha256(f.read()).hexdigest() == gold[name]["sha256_" + part], (name, part)
+
+
+# ------------------------------------------------------------------ train_lm
+def test_train_lm_cli_defaults_and_lr_schedule():
+    """Defaults of the reference's command line (ml/fxlm/train_lm.py:26-51)
+    and its warmup + cosine schedule (:154-160), restated here."""
+    import math
+    from fxlm import train_lm
+    a = train_lm._parse(["--data", "x_train.bin", "--out", "o", "--tunable"])
+    assert (a.seq_len, a.layers, a.heads, a.dim, a.batch, a.accum, a.steps) == (256, 8, 8, 512, 16, 1, 2000)
+    assert (a.lr, a.min_lr_frac, a.warmup, a.wd, a.clip) == (6e-4, 0.1, 100, 0.1, 1.0)
+    assert (a.eval_every, a.eval_batches, a.log_every, a.seed) == (200, 20, 20, 0)
+    assert a.init_scale == 1.0 and a.dtype == "bf16"
+    assert train_lm._parse(["--out", "o", "--dtype", "fp16"]).init_scale == 2.0 ** 16
+    assert train_lm._parse(["--out", "o", "--init-scale", "8"]).init_scale == 8.0
+
+    def ref(step, lr, warm, steps, mf):
+        if step < warm:
+            return lr * (step + 1) / warm
+        t = (step - warm) / max(1, steps - warm)
+        return lr * (mf + (1.0 - mf) * 0.5 * (1.0 + math.cos(math.pi * min(1.0, t))))
+    for steps, warm in ((2000, 100), (10, 0), (5, 5), (1, 1)):
+        a = train_lm._parse(["--out", "o", "--steps", str(steps), "--warmup", str(warm)])
+        for s in list(range(0, steps + 3)):
+            assert train_lm.lr_at(s, a) == pytest.approx(ref(s, a.lr, warm, steps, a.min_lr_frac), rel=1e-12)
+    a = train_lm._parse(["--out", "o"])
+    assert train_lm.lr_at(99, a) == pytest.approx(6e-4) and train_lm.lr_at(100, a) == pytest.approx(6e-4)
+    assert train_lm.lr_at(2000, a) == pytest.approx(6e-5) and train_lm.lr_at(5000, a) == pytest.approx(6e-5)
