@@ -408,6 +408,53 @@ def run_micro(args):
         out.append({"kernel": "adamw_sumsq + adamw_final + adamw_update", "case": f"{n} params fp32 grad",
                     "ms": ms, "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm,
                     "bytes_per_param": 38})
+    if "wmlp" in which or "all" in which:
+        # the fxgpu window MLP training step (gather-linear
+        # 1024 -> 512 + bias + GELU, 512 -> 256 + GELU, 256 -> 1, MSE, FlatAdamW)
+        from fxgpu import WindowMLP
+        from fxlm.optim import FlatAdamW
+        R, Fe, Wn, Bsz = 500_000, 16, 64, 32768
+        g = torch.Generator(device=dev).manual_seed(4)
+        X16 = torch.randn(R, Fe, device=dev, generator=g).half()
+        idx32 = torch.randint(0, R - Wn + 1, (Bsz,), device=dev, generator=g, dtype=torch.int32)
+        tgt = torch.randn(Bsz, 1, device=dev, generator=g)
+        torch.manual_seed(4)
+        m = WindowMLP(Fe, Wn, hidden=512, hidden2=256, master=True, act="gelu",
+                      dtype=torch.float16).to(dev)
+        opt = FlatAdamW(m, lr=1e-3, init_scale=1024.0, param_dtype=torch.float16)
+
+        def step():
+            loss = ((m(X16, idx32).float() - tgt) ** 2).mean()
+            opt.backward(loss)
+            opt.step()
+            opt.zero_grad()
+        ms = _time_ms(step, it)
+        flop = 94.6e9  # L1 fwd + dW, L2 and L3 fwd + dX + dW (no dX for L1)
+        case = f"config 5: R={R} F={Fe} window={Wn} B={Bsz} 1024-512-256-1 GELU fp16"
+        out.append({"kernel": "WindowMLP train step (gather, 3 GEMMs fwd, 5 bwd, FlatAdamW)",
+                    "case": case + ", eager", "ms": ms, "tflops": flop / ms / 1e9,
+                    "frac_of_measured_burst": flop / ms / 1e9 / tc, "samples_per_s": Bsz / ms * 1e3})
+        # the same step captured once in a CUDA graph and replayed (the eager
+        # loop is bound by host launch overhead at this size)
+        try:
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    step()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                step()
+            ms_g = _time_ms(graph.replay, it)
+            out.append({"kernel": "WindowMLP train step (gather, 3 GEMMs fwd, 5 bwd, FlatAdamW)",
+                        "case": case + ", CUDA graph replay", "ms": ms_g, "tflops": flop / ms_g / 1e9,
+                        "frac_of_measured_burst": flop / ms_g / 1e9 / tc, "samples_per_s": Bsz / ms_g * 1e3})
+            graph.reset()
+        except Exception as e:  # report the eager number regardless
+            out.append({"kernel": "WindowMLP train step, CUDA graph replay", "case": case,
+                        "error": repr(e)[:300]})
     for o in out:
         print(json.dumps(o), flush=True)
 
@@ -623,7 +670,7 @@ def main():
                          "parameter) instead of the sharded update (fxb200.zero, the default)")
     ap.add_argument("--micro", default=None,
                     help="per-kernel microbenchmarks instead of the step: all or a comma list "
-                         "of gemm,attn,rmsnorm,ce,adamw")
+                         "of gemm,attn,rmsnorm,ce,adamw,wmlp")
     ap.add_argument("--iters", type=int, default=20, help="iterations per microbenchmark")
     ap.add_argument("--only", default=None,
                     help="gemm_layer: comma-separated substrings selecting shapes (profiling)")

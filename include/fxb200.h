@@ -310,7 +310,8 @@ int fxb_axpy(int32_t ddtype, void* dst, int32_t sdtype, const void* src, const f
 int fxb_gather_windows(int32_t dtype, const void* X, int64_t R, int32_t F, const int32_t* idx,
                        int32_t B, int32_t window, void* Xg, void* stream);
 
-/* out[c] (fp32) = (accumulate ? out[c] : 0) + sum_r g[r, c]; g (rows, cols) row-major.
+/* out[c] (fp32) = (accumulate ? out[c] : 0) + sum_r g[r, c]; g (rows, cols) row-major
+ * (may be NULL when rows == 0). Deterministic (fixed summation order, no atomics).
  * The bias gradient db = g.sum(0) of ml/fxgpu/fused_linear.py:95. */
 int fxb_colsum(int32_t dtype, const void* g, int64_t rows, int32_t cols, float* out,
                int32_t accumulate, void* stream);

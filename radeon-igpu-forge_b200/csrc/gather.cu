@@ -53,6 +53,110 @@ __global__ void colsum_kernel(const T* __restrict__ g, int64_t rows, int cols,
   }
 }
 
+// Same sum when a row is a whole number of 16-byte vectors: block b owns the
+// E = 16 / sizeof(T) columns of vector b and all rows, so the sum needs no
+// cross-block step (deterministic, no workspace). Thread t reads rows t,
+// t + blockDim.x, ... with four 16-byte loads in flight, then the block adds
+// its threads' sums in a fixed tree order (warp shuffles, then the warps'
+// partials in warp order).
+template <typename T>
+__global__ void __launch_bounds__(1024, 1)
+colsum_vec_kernel(const T* __restrict__ g, int64_t rows, int cols, float* __restrict__ out,
+                  int accumulate) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  constexpr int E = 16 / sizeof(T);
+  __shared__ float part[32][E];
+  const int64_t vecs_per_row = cols / E;
+  const uint4* src = reinterpret_cast<const uint4*>(g) + blockIdx.x;
+  float s[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) s[j] = 0.f;
+  const int64_t step = blockDim.x;
+  int64_t r = threadIdx.x;
+  for (; r + 3 * step < rows; r += 4 * step) {
+    uint4 u[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) u[k] = src[(r + k * step) * vecs_per_row];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const T* h = reinterpret_cast<const T*>(&u[k]);
+#pragma unroll
+      for (int j = 0; j < E; ++j) s[j] += to_f<T>(h[j]);
+    }
+  }
+  for (; r < rows; r += step) {
+    const uint4 u = src[r * vecs_per_row];
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < E; ++j) s[j] += to_f<T>(h[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < E; ++j) s[j] = warp_sum(s[j]);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < E; ++j) part[wid][j] = s[j];
+  }
+  __syncthreads();
+  if (threadIdx.x < E) {
+    const int nw = (blockDim.x + 31) >> 5;
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) t += part[w][threadIdx.x];
+    const int64_t c = (int64_t)blockIdx.x * E + threadIdx.x;
+    out[c] = accumulate ? out[c] + t : t;
+  }
+}
+
+// Narrow outputs (fewer columns than one 16-byte vector, e.g. the single
+// output of a regression head): block c sums column c over all rows with
+// eight loads in flight per thread, then the same fixed-order block sum.
+template <typename T>
+__global__ void __launch_bounds__(1024, 1)
+colsum_col_kernel(const T* __restrict__ g, int64_t rows, int cols, float* __restrict__ out,
+                  int accumulate) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  __shared__ float part[32];
+  const int c = blockIdx.x;
+  const int64_t step = blockDim.x;
+  float s = 0.f;
+  int64_t r = threadIdx.x;
+  for (; r + 7 * step < rows; r += 8 * step) {
+    T v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = g[(r + k * step) * cols + c];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += to_f<T>(v[k]);
+  }
+  for (; r < rows; r += step) s += to_f<T>(g[r * cols + c]);
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) t += part[w];
+    out[c] = accumulate ? out[c] + t : t;
+  }
+}
+
+template <typename T>
+void launch_colsum(const T* g, int64_t rows, int cols, float* out, int accumulate, cudaStream_t st) {
+  constexpr int E = 16 / sizeof(T);
+  const int threads = rows >= 1024 ? 1024 : (int)((rows + 31) / 32) * 32;
+  if (cols % E == 0 && fxb::aligned16(g) && rows > 0) {
+    fxb::pdl_launch(colsum_vec_kernel<T>, cols / E, threads, 0, st, g, rows, cols, out, accumulate);
+    return;
+  }
+  if (cols < E && rows > 0) {
+    fxb::pdl_launch(colsum_col_kernel<T>, cols, threads, 0, st, g, rows, cols, out, accumulate);
+    return;
+  }
+  dim3 block(32, 8), grid((cols + 31) / 32);
+  fxb::pdl_launch(colsum_kernel<T>, grid, block, 0, st, g, rows, cols, out, accumulate);
+}
+
 }  // namespace
 
 extern "C" {
@@ -83,19 +187,22 @@ int fxb_gather_windows(int32_t dtype, const void* X, int64_t R, int32_t F, const
 
 int fxb_colsum(int32_t dtype, const void* g, int64_t rows, int32_t cols, float* out,
                int32_t accumulate, void* stream) {
-  if (fxb::dtype_size(dtype) == 0 || rows < 0 || cols <= 0 || !g || !out)
+  if (fxb::dtype_size(dtype) == 0 || rows < 0 || cols <= 0 || !out || (rows > 0 && !g))
     return fxb::set_error(FXB_EINVAL, "colsum: bad arguments");
-  dim3 block(32, 8), grid((cols + 31) / 32);
   cudaStream_t st = fxb::as_stream(stream);
+  if (rows == 0) {  // empty sum: out = 0 (or unchanged when accumulating)
+    if (accumulate) return FXB_OK;
+    return fxb::check_cuda(cudaMemsetAsync(out, 0, (size_t)cols * sizeof(float), st), "colsum memset");
+  }
   switch (dtype) {
     case FXB_DTYPE_F16:
-      fxb::pdl_launch(colsum_kernel<__half>, grid, block, 0, st, static_cast<const __half*>(g), rows, cols, out, accumulate);
+      launch_colsum(static_cast<const __half*>(g), rows, cols, out, accumulate, st);
       break;
     case FXB_DTYPE_BF16:
-      fxb::pdl_launch(colsum_kernel<__nv_bfloat16>, grid, block, 0, st, static_cast<const __nv_bfloat16*>(g), rows, cols, out, accumulate);
+      launch_colsum(static_cast<const __nv_bfloat16*>(g), rows, cols, out, accumulate, st);
       break;
     default:
-      fxb::pdl_launch(colsum_kernel<float>, grid, block, 0, st, static_cast<const float*>(g), rows, cols, out, accumulate);
+      launch_colsum(static_cast<const float*>(g), rows, cols, out, accumulate, st);
   }
   return fxb::check_launch("colsum");
 }

@@ -1,0 +1,212 @@
+"""GPU parity of the fxgpu path: FusedGatherLinear and WindowMLP on sm_100a.
+
+Cases follow the reference's ml/fxgpu/selftest.py: the gather-linear against
+the unfold + Fn.linear reference (R=100000, F=40, window 30, 256 outputs,
+B=8192; :27-57), its gradients (:50-56), the rejection of F % 8 != 0
+(:59-71), WindowMLP fused vs forward_dense with master weights on and off
+(:73-82) and under inference_mode (:84-108). Added: the golden vectors made
+from the reference's own WindowMLP (tests/golden/ops.npz, wmlp_*), bf16 and
+the GELU variant of BASELINE config 5, gradient parity against fp32
+autograd, out-of-range windows (zero-filled, no read outside X) and a short
+FlatAdamW training run. Tolerance: the reference's 0.05 absolute on outputs;
+gradients within twice the error of the same computation in torch's 16-bit
+path, measured against fp32.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as Fn
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda")
+
+
+@pytest.fixture(autouse=True)
+def _no_expired_waits(dev):
+    yield
+    from fxb200 import _lib
+    assert _lib.device_error(clear=True) == 0
+
+
+def _unfold(X, idx, W):
+    B = idx.numel()
+    return X.unfold(0, W, 1)[idx.long()].transpose(1, 2).reshape(B, W * X.shape[1])
+
+
+def _err(a, b):
+    return (a.double() - b.double()).abs().max().item()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_fused_gather_linear_selftest_case(dev, dtype):
+    from fxgpu import fused_gather_linear
+    torch.manual_seed(0)
+    R, F, W, HID, B = 100_000, 40, 30, 256, 8192
+    K = W * F
+    X16 = torch.randn(R, F, device=dev).to(dtype)
+    weight = (torch.randn(HID, K, device=dev) * 0.03).to(dtype)
+    bias = (torch.randn(HID, device=dev) * 0.01).to(dtype)
+    idx32 = torch.randint(0, R - W + 1, (B,), device=dev, dtype=torch.int32)
+    xb = _unfold(X16, idx32, W)
+    # fp32 reference and torch's own 16-bit path
+    w32, b32 = weight.float().requires_grad_(), bias.float().requires_grad_()
+    out32 = Fn.linear(xb.float(), w32, b32)
+    wl, bl = weight.clone().requires_grad_(), bias.clone().requires_grad_()
+    outl = Fn.linear(xb, wl, bl)
+    wf, bf = weight.clone().requires_grad_(), bias.clone().requires_grad_()
+    outf = fused_gather_linear(X16, idx32, wf, bf)
+    assert outf.dtype == dtype and outf.shape == (B, HID)
+    assert _err(outf, out32) < 0.05
+    g = torch.randn(B, HID, device=dev).to(dtype)
+    out32.backward(g.float())
+    outl.backward(g)
+    outf.backward(g)
+    for ours, lp, ref, nm in ((wf.grad, wl.grad, w32.grad, "dW"), (bf.grad, bl.grad, b32.grad, "db")):
+        assert ours.dtype == dtype
+        e_o, e_l = _err(ours, ref), _err(lp, ref)
+        assert e_o <= 2 * e_l + 1e-3 * ref.abs().max().item(), f"{nm}: {e_o:.3e} vs torch {e_l:.3e}"
+
+
+def test_fused_gather_linear_rejects_and_zero_fills(dev):
+    from fxgpu import FusedGatherLinear, fused_gather_linear
+    W = 4
+    bad = torch.randn(1000, 37, device=dev, dtype=torch.float16)
+    w37 = torch.randn(16, 37 * W, device=dev, dtype=torch.float16)
+    b16 = torch.zeros(16, device=dev, dtype=torch.float16)
+    idx = torch.zeros(8, device=dev, dtype=torch.int32)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        FusedGatherLinear.apply(bad, idx, w37, b16)
+    with pytest.raises(TypeError):
+        fused_gather_linear(bad[:, :32].contiguous(), idx.long(), w37[:, :128].contiguous(), b16)
+    # windows that would leave X read as zeros: out = bias there
+    X = torch.randn(100, 16, device=dev, dtype=torch.float16)
+    w = torch.randn(16, 16 * W, device=dev, dtype=torch.float16)
+    b = torch.randn(16, device=dev, dtype=torch.float16)
+    idx = torch.tensor([0, 96, 97, -1, 5000], device=dev, dtype=torch.int32)
+    out = fused_gather_linear(X, idx, w, b)
+    ref = Fn.linear(_unfold(X, idx[:2], W).float(), w.float(), b.float())
+    assert _err(out[:2], ref) < 0.05
+    assert torch.equal(out[2:], b.expand(3, -1))
+
+
+@pytest.mark.parametrize("master", [True, False])
+@pytest.mark.parametrize("act,dtype", [("silu", torch.float16), ("gelu", torch.bfloat16)])
+def test_window_mlp_fused_vs_dense(dev, master, act, dtype):
+    from fxgpu import WindowMLP
+    torch.manual_seed(1)
+    R, F, W, B = 100_000, 40, 30, 8192
+    X16 = torch.randn(R, F, device=dev).to(dtype)
+    idx32 = torch.randint(0, R - W + 1, (B,), device=dev, dtype=torch.int32)
+    m = WindowMLP(F, W, master=master, act=act, dtype=dtype).to(dev)
+    o1 = m(X16, idx32)
+    o2 = m.forward_dense(_unfold(X16, idx32, W))
+    assert o1.shape == (B, 1) and o1.dtype == dtype
+    assert _err(o1, o2) < 0.05
+    m.eval()
+    with torch.inference_mode():
+        o3 = m(X16, idx32)
+    assert _err(o3, o2) < 0.05
+
+
+def test_window_mlp_golden(dev):
+    """Output of the reference's WindowMLP (fp32, SiLU) on bf16-exact inputs."""
+    from fxgpu import WindowMLP, fused_gather_linear
+    g = np.load(os.path.join(GOLD, "ops.npz"))
+    X = torch.from_numpy(g["wmlp_X"]).to(dev, torch.bfloat16)
+    idx = torch.from_numpy(g["wmlp_idx"]).to(dev, torch.int32)
+    m = WindowMLP(16, 4, hidden=32, hidden2=16, master=True, act="silu", dtype=torch.bfloat16).to(dev)
+    with torch.no_grad():
+        for nm in ("W1", "b1", "W2", "b2", "W3", "b3"):
+            getattr(m, nm).copy_(torch.from_numpy(g[f"wmlp_{nm}"]))
+    h1 = fused_gather_linear(X, idx, m.W1.detach().bfloat16(), m.b1.detach().bfloat16())
+    ref_h1 = torch.from_numpy(g["wmlp_h1"]).to(dev)
+    assert (h1.float() - ref_h1).norm() / ref_h1.norm() < 2e-2
+    y = m(X, idx)
+    ref_y = torch.from_numpy(g["wmlp_y"]).to(dev)
+    assert (y.float() - ref_y).norm() / ref_y.norm() < 2e-2
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu"])
+def test_window_mlp_gradients(dev, act):
+    """Weight and bias gradients of the fused step (fp16) against fp32
+    autograd of forward_dense, bounded by torch's own fp16 autograd error."""
+    from fxgpu import WindowMLP
+    torch.manual_seed(3)
+    R, F, W, B = 20_000, 16, 64, 4096
+    X16 = torch.randn(R, F, device=dev).half()
+    idx32 = torch.randint(0, R - W + 1, (B,), device=dev, dtype=torch.int32)
+    tgt = torch.randn(B, 1, device=dev)
+    mf = WindowMLP(F, W, hidden=512, hidden2=256, master=True, act=act, dtype=torch.float16).to(dev)
+    ml = WindowMLP(F, W, hidden=512, hidden2=256, master=True, act=act, dtype=torch.float16).to(dev)
+    mr = WindowMLP(F, W, hidden=512, hidden2=256, master=True, act=act, dtype=torch.float32).to(dev)
+    ml.load_state_dict(mf.state_dict())
+    mr.load_state_dict(mf.state_dict())
+    xb = _unfold(X16, idx32, W)
+    ((mf(X16, idx32).float() - tgt) ** 2).mean().backward()
+    ((ml.forward_dense(xb).float() - tgt) ** 2).mean().backward()
+    ((mr.forward_dense(xb.float()) - tgt) ** 2).mean().backward()
+    pl, pr = dict(ml.named_parameters()), dict(mr.named_parameters())
+    for nm, p in mf.named_parameters():
+        ref = pr[nm].grad
+        e_o, e_l = _err(p.grad, ref), _err(pl[nm].grad, ref)
+        assert e_o <= 2 * e_l + 1e-3 * ref.abs().max().item(), f"{nm}: {e_o:.3e} vs torch-fp16 {e_l:.3e}"
+
+
+def test_window_mlp_trains_with_flat_adamw(dev):
+    """Config-5 shapes at a smaller batch: the MSE falls under FlatAdamW with
+    the weight / bias gradients written straight into its flat buffer."""
+    from fxgpu import WindowMLP
+    from fxlm.optim import FlatAdamW
+    torch.manual_seed(4)
+    R, F, W, B = 50_000, 16, 64, 4096
+    X16 = torch.randn(R, F, device=dev).half()
+    idx32 = torch.randint(0, R - W + 1, (B,), device=dev, dtype=torch.int32)
+    # a learnable target: a fixed random linear read-out of the window
+    probe = torch.randn(W * F, device=dev) / (W * F) ** 0.5
+    tgt = (_unfold(X16, idx32, W).float() @ probe)[:, None]
+    m = WindowMLP(F, W, hidden=512, hidden2=256, master=True, act="gelu", dtype=torch.float16).to(dev)
+    opt = FlatAdamW(m, lr=1e-3, init_scale=1024.0, param_dtype=torch.float16)
+    losses = []
+    for _ in range(60):
+        loss = ((m(X16, idx32).float() - tgt) ** 2).mean()
+        opt.backward(loss)
+        st = opt.step()
+        opt.zero_grad()
+        losses.append(loss.item())
+        assert not bool(st["found_inf"])
+    assert all(np.isfinite(losses))
+    assert losses[-1] < 0.5 * losses[0], losses[::10]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_colsum_kernel(dev, dtype):
+    """fxb_colsum (the bias gradient, sum over rows) on each of its three
+    paths, write and accumulate, bitwise repeatable."""
+    from fxb200 import _lib
+    st = _lib.stream_ptr(dev)
+    code = _lib.dtype_code(dtype)
+    # vector path (cols % (16 / itemsize) == 0), per-column path (narrower),
+    # general path (other widths), empty
+    for rows, cols in [(1, 8), (37, 16), (1000, 24), (4096, 512), (32768, 512), (5, 3), (70_000, 8),
+                       (3000, 1), (32768, 1), (100, 13), (2000, 37), (0, 16)]:
+        g = torch.randn(rows, cols, device=dev).to(dtype)
+        out = torch.full((cols,), 7.0, device=dev)
+        _lib.call("fxb_colsum", code, _lib.ptr(g), rows, cols, _lib.ptr(out), 0, st)
+        ref = g.double().sum(0)
+        tol = 1e-5 * g.double().abs().sum(0) + 1e-6
+        assert ((out.double() - ref).abs() <= tol).all(), (rows, cols)
+        again = torch.zeros(cols, device=dev)
+        _lib.call("fxb_colsum", code, _lib.ptr(g), rows, cols, _lib.ptr(again), 0, st)
+        assert torch.equal(again, out), (rows, cols)
+        acc = torch.ones(cols, device=dev)
+        _lib.call("fxb_colsum", code, _lib.ptr(g), rows, cols, _lib.ptr(acc), 1, st)
+        assert torch.equal(acc, out + 1.0) or ((acc.double() - out.double() - 1).abs() <= 1e-6).all()
