@@ -21,6 +21,7 @@ __all__ = [
     "GPT",
     "GPTConfig",
     "GraphedStep",
+    "GraphedFunction",
 ]
 
 
@@ -43,9 +44,9 @@ def __getattr__(name):
     if name == "FlatAdamW":
         from .optim import FlatAdamW
         return FlatAdamW
-    if name == "GraphedStep":
-        from .graph import GraphedStep
-        return GraphedStep
+    if name in ("GraphedStep", "GraphedFunction"):
+        from . import graph as _m
+        return getattr(_m, name)
     if name in ("GPT", "GPTConfig"):
         from . import model as _m
         return getattr(_m, name)

@@ -86,3 +86,66 @@ class GraphedStep:
             torch.cuda.synchronize()
             self.graph.reset()
             self.graph = None
+
+
+class GraphedFunction:
+    """Any training step as a replayed CUDA graph: `fn(*static_args)` is run
+    `warmup` times on a side stream (real steps: lazy initialisation happens
+    there), then captured once; each call copies its arguments into the
+    static device buffers (None keeps the previous contents), replays, and
+    returns the captured output (device tensors, overwritten by the next
+    call).
+
+        def train_step(idx, tgt):
+            loss = ((model(X16, idx).float() - tgt) ** 2).mean()
+            opt.backward(loss); opt.step(); opt.zero_grad()
+            return loss.detach()
+        step = GraphedFunction(train_step, idx_example, tgt_example)
+        loss = step(idx, tgt)
+
+    The same conditions as GraphedStep hold for what `fn` does: fixed shapes,
+    no host synchronisation, and a FlatAdamW learning rate that changes
+    between replays read from `opt.lr_dev` (set it before constructing).
+    Tensors the closure reads but that are not arguments are captured by
+    address: update them in place.
+    """
+
+    def __init__(self, fn, *example_args, warmup=3):
+        if warmup < 1:
+            raise ValueError("GraphedFunction: warmup >= 1 (lazy initialisation must happen "
+                             "before capture)")
+        if not example_args or not all(isinstance(a, torch.Tensor) and a.is_cuda
+                                       for a in example_args):
+            raise TypeError("GraphedFunction: example arguments must be cuda tensors")
+        self.fn = fn
+        dev = example_args[0].device
+        self.args = [a.detach().clone() for a in example_args]
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                fn(*self.args)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = _lib.launch_count()
+        with torch.cuda.graph(self.graph):
+            self.out = fn(*self.args)
+        self.launches_per_call = _lib.launch_count() - n0
+
+    def __call__(self, *args):
+        if len(args) > len(self.args):
+            raise TypeError(f"GraphedFunction: {len(args)} arguments, captured with {len(self.args)}")
+        for dst, src in zip(self.args, args):
+            if src is not None:
+                dst.copy_(src, non_blocking=True)
+        self.graph.replay()
+        return self.out
+
+    def release(self):
+        """Free the captured graph (before destroy_process_group when the
+        step holds NCCL collectives)."""
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None
