@@ -224,3 +224,14 @@ def test_train_lm_cli_defaults_and_lr_schedule():
     a = train_lm._parse(["--out", "o"])
     assert train_lm.lr_at(99, a) == pytest.approx(6e-4) and train_lm.lr_at(100, a) == pytest.approx(6e-4)
     assert train_lm.lr_at(2000, a) == pytest.approx(6e-5) and train_lm.lr_at(5000, a) == pytest.approx(6e-5)
+
+
+def test_graphed_function_argument_checks():
+    """Host-side checks of fxlm.GraphedFunction (capture itself needs a GPU)."""
+    from fxlm import GraphedFunction
+    with pytest.raises(TypeError, match="cuda tensors"):
+        GraphedFunction(lambda a: a, torch.zeros(4))
+    with pytest.raises(TypeError, match="cuda tensors"):
+        GraphedFunction(lambda: None)
+    with pytest.raises(ValueError, match="warmup"):
+        GraphedFunction(lambda a: a, torch.zeros(4), warmup=0)
