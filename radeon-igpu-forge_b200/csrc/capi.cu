@@ -39,20 +39,42 @@ int check_cuda(cudaError_t e, const char* what) {
   return set_error(FXB_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }
 
+uintptr_t context_token() {
+  typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  CUcontext c = nullptr;
+  if (!fn || fn(&c) != CUDA_SUCCESS) return 0;
+  return reinterpret_cast<uintptr_t>(c);
+}
+
 int* dev_error_ptr() {
+  static std::mutex mu;
   static int* cached[64] = {nullptr};
+  static uintptr_t cached_ctx[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     set_error(FXB_ECUDA, "dev_error_ptr: no current device");
     return nullptr;
   }
-  if (!cached[dev]) {
+  // cudaGetDevice does not create the context; the symbol lookup below does
+  // (first call on the device), so the token is read after it on a miss
+  std::lock_guard<std::mutex> lock(mu);
+  const uintptr_t ctx = context_token();
+  if (!cached[dev] || ctx == 0 || cached_ctx[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_fxb_dev_error) != cudaSuccess) {
       set_error(FXB_ECUDA, "dev_error_ptr: cudaGetSymbolAddress failed");
       return nullptr;
     }
     cached[dev] = static_cast<int*>(p);
+    cached_ctx[dev] = context_token();
   }
   return cached[dev];
 }

@@ -69,6 +69,12 @@ inline int dtype_size(int32_t dt) {
 // into it when a bounded wait expires); nullptr + error set on failure.
 int* dev_error_ptr();
 
+// Identity of the calling thread's current CUDA context (0 if none). Caches
+// of device addresses are keyed on it as well as on the device ordinal: a
+// cudaDeviceReset() ends the primary context, the next call creates a new one
+// and addresses looked up in the old one are stale.
+uintptr_t context_token();
+
 // Cached SM count of the current device.
 int num_sms();
 

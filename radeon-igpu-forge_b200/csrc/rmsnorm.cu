@@ -2,9 +2,10 @@
 //
 // Math follows the reference kernels ml/fxlm/kernels/norm.hip:33-59 (fwd),
 // :64-95 (dx) and :102-127 (dw partials), which compute in fp32 over 16-bit
-// inputs. Layout differs: one warp owns a row, the row lives in registers as
-// 16-byte vectors (one HBM read of x, one write of y), and the dw reduction is
-// a per-block partial followed by a fixed-order column sum (deterministic).
+// inputs. Layout differs: one warp owns a row (one block, for long rows), the
+// row lives in registers as 16-byte vectors (one HBM read of x, one write of
+// y), and the dw reduction is a per-block partial followed by a fixed-order
+// column sum (deterministic).
 #include <mutex>
 
 #include "common.cuh"
@@ -199,6 +200,151 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
   }
 }
 
+// ---------------------------------------------------------------- long rows
+// Rows longer than one warp's registers hold (the forward: more than 8
+// vectors per lane, D > 2048 in 16-bit, D > 1024 in fp32; the backward, which
+// keeps two rows of x, dy and dres per warp in flight: more than 4, D > 1024 /
+// D > 512; up to the ABI's D <= 8192): one block
+// of kRowThreads threads owns a row, each thread VPT 16-byte vectors at
+// stride kRowThreads (coalesced). The row sums go through warp shuffles and a
+// kWarps-slot shared array that alternates between two copies by row parity,
+// so one barrier per row suffices: a warp can only overwrite a copy after
+// every warp has passed the barrier of the row in between, i.e. after all of
+// them finished reading it.
+constexpr int kRowThreads = kWarps * 32;
+
+FXB_DEV float block_row_sum(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < kWarps; ++k) s += red[k];  // same order in every thread
+  return s;
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kRowThreads)
+rmsnorm_fwd_row_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                       float* __restrict__ rstd, int64_t rows, int D, float eps) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  constexpr int E = Vec<T>::N;
+  __shared__ float red[2][kWarps];
+  const int nvec = D / E;
+  float wv[VPT][E];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = i * kRowThreads + threadIdx.x;
+    if (v < nvec) load_vec<T>(w + (int64_t)v * E, wv[i]);
+  }
+  int par = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, par ^= 1) {
+    const T* xr = x + r * D;
+    float xv[VPT][E];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int v = i * kRowThreads + threadIdx.x;
+      if (v < nvec) {
+        load_vec<T>(xr + (int64_t)v * E, xv[i]);
+#pragma unroll
+        for (int j = 0; j < E; ++j) ss += xv[i][j] * xv[i][j];
+      }
+    }
+    ss = block_row_sum(ss, red[par]);
+    const float rs = rsqrtf(ss / (float)D + eps);
+    if (threadIdx.x == 0) rstd[r] = rs;
+    T* yr = y + r * D;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int v = i * kRowThreads + threadIdx.x;
+      if (v < nvec) {
+        float o[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) o[j] = xv[i][j] * rs * wv[i][j];
+        store_vec<T>(yr + (int64_t)v * E, o);
+      }
+    }
+  }
+}
+
+// dx per row, as rmsnorm_bwd_kernel, and the block's dw partial kept in
+// registers (each thread owns fixed columns), written once at the end.
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kRowThreads)
+rmsnorm_bwd_row_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                       const float* __restrict__ rstd, const T* __restrict__ dy,
+                       const T* __restrict__ dres, T* __restrict__ dx,
+                       float* __restrict__ part, int64_t rows, int D) {
+  pdl_trigger();
+  pdl_wait();  // inputs come from the previous kernel on the stream
+  constexpr int E = Vec<T>::N;
+  __shared__ float red[2][kWarps];
+  const int nvec = D / E;
+  float wv[VPT][E], acc[VPT][E];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = i * kRowThreads + threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < E; ++j) acc[i][j] = wv[i][j] = 0.f;
+    if (v < nvec) load_vec<T>(w + (int64_t)v * E, wv[i]);
+  }
+  const float invD = 1.f / (float)D;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  int par = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, par ^= 1) {
+    uint4 xp[VPT], gp[VPT], dp[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int v = i * kRowThreads + threadIdx.x;
+      const bool ok = v < nvec;
+      const int64_t off = r * D + (int64_t)v * E;
+      xp[i] = ok ? *reinterpret_cast<const uint4*>(x + off) : zero;
+      gp[i] = ok ? *reinterpret_cast<const uint4*>(dy + off) : zero;
+      dp[i] = (ok && dres) ? *reinterpret_cast<const uint4*>(dres + off) : zero;
+    }
+    const float rs = rstd[r];
+    float tt = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      float xv[E], gv[E];
+      unpack_vec<T>(xp[i], xv);
+      unpack_vec<T>(gp[i], gv);
+#pragma unroll
+      for (int j = 0; j < E; ++j) tt += xv[j] * wv[i][j] * gv[j];
+    }
+    const float t = block_row_sum(tt, red[par]);
+    const float corr = rs * rs * rs * t * invD;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int v = i * kRowThreads + threadIdx.x;
+      if (v < nvec) {
+        float xv[E], gv[E], dv[E], o[E];
+        unpack_vec<T>(xp[i], xv);
+        unpack_vec<T>(gp[i], gv);
+        unpack_vec<T>(dp[i], dv);  // zero without a residual gradient
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          o[j] = rs * wv[i][j] * gv[j] - xv[j] * corr + dv[j];
+          acc[i][j] += xv[j] * rs * gv[j];
+        }
+        store_vec<T>(dx + r * D + (int64_t)v * E, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = i * kRowThreads + threadIdx.x;
+    if (v < nvec) {
+      float4* p = reinterpret_cast<float4*>(part + (int64_t)blockIdx.x * D + (int64_t)v * E);
+#pragma unroll
+      for (int j = 0; j < E / 4; ++j)
+        p[j] = make_float4(acc[i][4 * j], acc[i][4 * j + 1], acc[i][4 * j + 2], acc[i][4 * j + 3]);
+    }
+  }
+}
+
 // dw[d] = (acc ? dw[d] : 0) + sum_b part[b, d]   (fixed order over b)
 template <typename T>
 __global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ part, int nparts, int D,
@@ -246,16 +392,39 @@ int launch_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows,
   case V:                                                                         \
     fxb::pdl_launch(rmsnorm_fwd_kernel<T, V>, blocks, kWarps * 32, 0, st, X, W, Y, rstd, rows, D, eps); \
     break;
+  if (vpl > 8) {  // long rows: a block per row
+    const int nvec = D / E;
+    const int64_t cap = (int64_t)fxb::num_sms() * 4;
+    const int rb = (int)(rows < cap ? rows : cap);
+    if (nvec <= 2 * kRowThreads)
+      fxb::pdl_launch(rmsnorm_fwd_row_kernel<T, 2>, rb, kRowThreads, 0, st, X, W, Y, rstd, rows, D, eps);
+    else if (nvec <= 4 * kRowThreads)
+      fxb::pdl_launch(rmsnorm_fwd_row_kernel<T, 4>, rb, kRowThreads, 0, st, X, W, Y, rstd, rows, D, eps);
+    else if (nvec <= 8 * kRowThreads)
+      fxb::pdl_launch(rmsnorm_fwd_row_kernel<T, 8>, rb, kRowThreads, 0, st, X, W, Y, rstd, rows, D, eps);
+    else
+      return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm: D=%d too large", D);
+    return fxb::check_launch("rmsnorm_fwd_row");
+  }
   switch (vpl) {
     FXB_RMS_FWD(1) FXB_RMS_FWD(2) FXB_RMS_FWD(3) FXB_RMS_FWD(4) FXB_RMS_FWD(5) FXB_RMS_FWD(6)
     FXB_RMS_FWD(7) FXB_RMS_FWD(8)
     default:
-      if (vpl <= 16) { fxb::pdl_launch(rmsnorm_fwd_kernel<T, 16>, blocks, kWarps * 32, 0, st, X, W, Y, rstd, rows, D, eps); }
-      else if (vpl <= 32) { fxb::pdl_launch(rmsnorm_fwd_kernel<T, 32>, blocks, kWarps * 32, 0, st, X, W, Y, rstd, rows, D, eps); }
-      else return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm: D=%d too large", D);
+      return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm: D=%d too large", D);
   }
 #undef FXB_RMS_FWD
   return fxb::check_launch("rmsnorm_fwd");
+}
+
+// rows of at most 4 vectors per lane take the warp-per-row kernels (beyond
+// that their two rows in flight per warp spill registers)
+template <typename T> constexpr int kWarpRowMaxD = 4 * 32 * Vec<T>::N;
+
+// long-row backward: two blocks per SM, one row per block at a time
+int row_blocks(int64_t rows) {
+  const int64_t cap = (int64_t)fxb::num_sms() * 2;
+  const int64_t b = rows < cap ? rows : cap;
+  return b < 1 ? 1 : (int)b;
 }
 
 int bwd_blocks(int64_t rows) {
@@ -273,7 +442,8 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
                int dw_dtype, int acc, float* ws, int64_t rows, int D, cudaStream_t st) {
   constexpr int E = Vec<T>::N;
   const int vpl = (D / E + 31) / 32;
-  const int blocks = bwd_blocks(rows);
+  const bool long_rows = D > kWarpRowMaxD<T>;
+  const int blocks = long_rows ? row_blocks(rows) : bwd_blocks(rows);
   const size_t smem = (size_t)kWarps * D * sizeof(float);
   auto X = static_cast<const T*>(x);
   auto W = static_cast<const T*>(w);
@@ -287,11 +457,25 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
     fxb::pdl_launch(k, blocks, kWarps * 32, smem, st, X, W, rstd, G, static_cast<const T*>(dres), DX, ws, rows, D); \
     break;                                                                               \
   }
-  switch (vpl) {
-    FXB_RMS_BWD(1) FXB_RMS_BWD(2) FXB_RMS_BWD(3) FXB_RMS_BWD(4) FXB_RMS_BWD(5) FXB_RMS_BWD(6)
-    FXB_RMS_BWD(7) FXB_RMS_BWD(8)
-    default:
-      return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm bwd: D=%d > %d not supported", D, 8 * 32 * E);
+  if (long_rows) {
+    const int nvec = D / E;
+    auto DR = static_cast<const T*>(dres);
+    if (nvec <= kRowThreads)
+      fxb::pdl_launch(rmsnorm_bwd_row_kernel<T, 1>, blocks, kRowThreads, 0, st, X, W, rstd, G, DR, DX, ws, rows, D);
+    else if (nvec <= 2 * kRowThreads)
+      fxb::pdl_launch(rmsnorm_bwd_row_kernel<T, 2>, blocks, kRowThreads, 0, st, X, W, rstd, G, DR, DX, ws, rows, D);
+    else if (nvec <= 4 * kRowThreads)
+      fxb::pdl_launch(rmsnorm_bwd_row_kernel<T, 4>, blocks, kRowThreads, 0, st, X, W, rstd, G, DR, DX, ws, rows, D);
+    else if (nvec <= 8 * kRowThreads)
+      fxb::pdl_launch(rmsnorm_bwd_row_kernel<T, 8>, blocks, kRowThreads, 0, st, X, W, rstd, G, DR, DX, ws, rows, D);
+    else
+      return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm bwd: D=%d too large", D);
+  } else {
+    switch (vpl) {
+      FXB_RMS_BWD(1) FXB_RMS_BWD(2) FXB_RMS_BWD(3) FXB_RMS_BWD(4)
+      default:
+        return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm bwd: D=%d not supported", D);
+    }
   }
 #undef FXB_RMS_BWD
   int r = fxb::check_launch("rmsnorm_bwd");
@@ -320,9 +504,11 @@ __device__ __align__(256) float g_rms_scratch[kStaticScratchBytes / sizeof(float
 
 std::mutex g_scratch_mu;
 float* g_scratch_ptr[64] = {nullptr};
+uintptr_t g_scratch_ctx[64] = {0};
 
-// Address of g_rms_scratch on the current device; looked up once per device
-// (the first call there), never allocated.
+// Address of g_rms_scratch on the current device; looked up on the first call
+// on a device (and again if that device's context was replaced, e.g. after a
+// cudaDeviceReset), never allocated.
 int static_scratch(float** out) {
   int dev = 0;
   int r = fxb::check_cuda(cudaGetDevice(&dev), "rmsnorm bwd static: cudaGetDevice");
@@ -330,12 +516,14 @@ int static_scratch(float** out) {
   if (dev < 0 || dev >= 64)
     return fxb::set_error(FXB_EUNSUPPORTED, "rmsnorm bwd static: device ordinal %d >= 64", dev);
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  const uintptr_t ctx = fxb::context_token();
+  if (!g_scratch_ptr[dev] || ctx == 0 || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
     r = fxb::check_cuda(cudaGetSymbolAddress(&p, g_rms_scratch),
                         "rmsnorm bwd static: cudaGetSymbolAddress(scratch)");
     if (r) return r;
     g_scratch_ptr[dev] = static_cast<float*>(p);
+    g_scratch_ctx[dev] = fxb::context_token();
   }
   *out = g_scratch_ptr[dev];
   return FXB_OK;
@@ -370,7 +558,10 @@ int fxb_rmsnorm_fwd(int32_t dtype, const void* x, const void* w, void* y, float*
 }
 
 size_t fxb_rmsnorm_bwd_workspace(int64_t rows, int32_t D) {
-  return (size_t)bwd_blocks(rows) * (size_t)(D > 0 ? D : 0) * sizeof(float);
+  // the dtype is not an argument: rows longer than fp32's warp-row limit may
+  // take either kernel, so size for the larger (long-row) grid
+  const int blocks = D > kWarpRowMaxD<float> ? row_blocks(rows) : bwd_blocks(rows);
+  return (size_t)blocks * (size_t)(D > 0 ? D : 0) * sizeof(float);
 }
 
 int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rstd,
