@@ -490,6 +490,7 @@ __global__ void attn_bwd_prep_kernel(const T16* __restrict__ o, int64_t o_sb, in
   for (int off = LPR / 2; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (!ok) return;
   if (sub == 0) delta[row] = s;
+  if (!dq_acc) return;  // head dim 128: the transposed accumulator is cleared separately
   float4* z = reinterpret_cast<float4*>(dq_acc + row * DH + sub * 8);
   z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
   z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -835,6 +836,349 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   }
 }
 
+// ============================================================ backward, head dim 128
+// Same schedule as attn_bwd_kernel (one CTA per key tile of 128 keys and
+// batch*head, walking the query tiles that see it, the next tile's scores
+// computed while the current tile's dV / dK / dQ MMAs run), with the query
+// tile halved to 64 rows so that every accumulator fits the 512 tensor-memory
+// columns at head dim 128:
+//   S^T, dP^T  [128 keys][64 queries]       fp32   64 + 64 columns
+//   dV, dK     [128 keys][128 head dims]    fp32  128 + 128 columns
+//   dQ^T       [128 head dims][64 queries]  fp32   64 columns
+//   P^T        [128 keys][64 queries]       16-bit pairs, 32 columns
+// dQ is produced transposed (dQ^T = K^T dS^T, M = head dims): its rows are
+// head dims, so the partial for a query tile leaves as fp32 TMA
+// add-reductions into a transposed accumulator (B*H, 128, Tp), Tp = T
+// rounded up to 64, which the post kernel reads back in the caller's layout.
+// Shared memory: K, V (32 KB each), Q and dO double-buffered (16 KB tiles),
+// dS^T double-buffered (16 KB), dQ staging (16 warps x 2 KB), LSE / delta.
+// Warp roles as in the head-dim-64 kernel: warps 0-15 softmax / dS (warp w:
+// key rows (w & 3)*32.., query columns (w >> 2)*16..; for dQ^T head-dim rows
+// (w & 3)*32.. and the same query columns; for the final dK / dV head dims
+// (w >> 2)*32..), warp 16 MMA issuer, warp 17 TMA producer.
+constexpr int QT128 = 64;  // query rows per tile at head dim 128
+constexpr int kB128Tile = TILE * 128 * 2;   // K / V tile bytes (32 KB)
+constexpr int kB128QTile = QT128 * 128 * 2; // Q / dO tile bytes (16 KB)
+__host__ __device__ constexpr int t_pad128(int T) { return (T + QT128 - 1) / QT128 * QT128; }
+
+template <int FMT>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+attn_bwd128_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                   const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
+  constexpr int DH = 128;
+  using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sK = base;                     // [128 keys][128] as two 16 KB column blocks
+  const uint32_t sV = sK + kB128Tile;
+  const uint32_t sQ = sV + kB128Tile;           // 2 stages of [64][128] (two 8 KB blocks)
+  const uint32_t sDO = sQ + 2 * kB128QTile;     // 2 stages
+  const uint32_t sDS = sDO + 2 * kB128QTile;    // 2 buffers of dS^T [128 keys][64 q] (16 KB)
+  const uint32_t sDQ = sDS + 2 * 16384;         // dQ^T staging: 16 warps x [32 rows][16 fp32]
+  const uint32_t sStat = sDQ + 32768;           // lse2[2][64], delta[2][64] fp32
+  float* lse_s = reinterpret_cast<float*>(gbase + (sStat - base));
+  float* del_s = lse_s + 2 * QT128;
+  const uint32_t bars = sStat + 1024;
+  const uint32_t kv_full = bars;
+  auto qdo_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto qdo_empty = [&](int s) { return bars + 8u * (3 + s); };
+  const uint32_t s_full = bars + 8u * 5;
+  const uint32_t s_empty = bars + 8u * 6;
+  const uint32_t ds_full = bars + 8u * 7;
+  const uint32_t dq_full = bars + 8u * 8;
+  const uint32_t dq_empty = bars + 8u * 9;
+  const uint32_t acc_full = bars + 8u * 10;
+  const uint32_t pt_free = bars + 8u * 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = p.B * p.H;
+  const int kt = (int)(blockIdx.x / BH);
+  const int bh = (int)(blockIdx.x - kt * BH);
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int kv0 = kt * TILE;
+  const int nq64 = (p.T + QT128 - 1) / QT128;
+  const int i0 = p.causal ? kt * (TILE / QT128) : 0;  // first query tile that sees this key tile
+  const int n_it = nq64 - i0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(qdo_full(s), 1 + 32);  // TMA bytes + the producer warp's LSE / delta stores
+      mbar_init(qdo_empty(s), 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 512);
+    mbar_init(ds_full, 512);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 512);
+    mbar_init(acc_full, 1);
+    mbar_init(pt_free, 1);
+    fence_mbar_init();
+  }
+  if (warp == kBwdWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // q / k / v (and dO, lse, delta) come from earlier kernels on the stream
+  const uint32_t tST = tmem, tDPT = tmem + 64, tDV = tmem + 128, tDK = tmem + 256;
+  const uint32_t tDQ = tmem + 384, tPT = tmem + 448;
+
+  if (warp == kBwdWarpTma) {
+    // ------------------------------------------------ producer (lane 0 issues TMA)
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV); tma_prefetch_desc(&tmDO);
+      mbar_expect_tx(kv_full, 2 * kB128Tile);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tma_load_4d(sK + c * 16384, &tmK, kv_full, 64 * c, kv0, h, b);
+        tma_load_4d(sV + c * 16384, &tmV, kv_full, 64 * c, kv0, h, b);
+      }
+    }
+    __syncwarp();
+    int armed = 0;
+    for (int it = 0; it < n_it; ++it) {
+      const int st = it & 1;
+      const int qq0 = (i0 + it) * QT128;
+      if (!mbar_wait_warp(qdo_empty(st), ((it >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
+      if (lane == 0) {
+        mbar_expect_tx(qdo_full(st), 2 * kB128QTile);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tma_load_4d(sQ + st * kB128QTile + c * 8192, &tmQ, qdo_full(st), 64 * c, qq0, h, b);
+          tma_load_4d(sDO + st * kB128QTile + c * 8192, &tmDO, qdo_full(st), 64 * c, qq0, h, b);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int qi = lane * 2 + i;
+        const int q = qq0 + qi;
+        const bool v = q < p.T;
+        lse_s[st * QT128 + qi] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
+        del_s[st * QT128 + qi] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
+      }
+      mbar_arrive(qdo_full(st));
+      armed = it + 1;
+    }
+    if (lane == 0) {
+      mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+      for (int it = (armed > 2 ? armed - 2 : 0); it < armed; ++it)
+        mbar_wait(qdo_full(it & 1), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+    }
+    __syncwarp();
+  } else if (warp == kBwdWarpMma) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t I_SS = umma_idesc_f16(FMT, 0, 0, TILE, QT128);  // S^T, dP^T
+      constexpr uint32_t I_KV = umma_idesc_f16(FMT, 0, 1, TILE, DH);     // dV, dK
+      constexpr uint32_t I_QT = umma_idesc_f16(FMT, 1, 1, DH, QT128);    // dQ^T
+      bool ok = mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+      const uint64_t kd = kmajor_desc0(sK), vd = kmajor_desc0(sV);
+      const uint64_t km = mnmajor_desc0(sK);  // K^T: head dims (M) contiguous
+      auto issue_s = [&](int it) -> bool {
+        const int st = it & 1;
+        const uint32_t q_s = sQ + st * kB128QTile, do_s = sDO + st * kB128QTile;
+        if (!mbar_wait(qdo_full(st), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        tc_fence_after();
+        const uint64_t qd = umma_desc_sw128(q_s, 16, 1024), dod = umma_desc_sw128(do_s, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {  // K slices of 16 head dims; 64-row B tiles: 8 KB blocks
+          const uint32_t offb = (kk >> 2) * 8192 + (kk & 3) * 32;
+          umma_f16(tST, desc_add(kd, kmajor_off(kk)), desc_add(qd, offb), I_SS, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {
+          const uint32_t offb = (kk >> 2) * 8192 + (kk & 3) * 32;
+          umma_f16(tDPT, desc_add(vd, kmajor_off(kk)), desc_add(dod, offb), I_SS, kk > 0);
+        }
+        umma_commit(s_full);
+        return true;
+      };
+      if (ok && n_it > 0) ok = issue_s(0);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
+        const int st = it & 1;
+        const uint32_t q_s = sQ + st * kB128QTile, do_s = sDO + st * kB128QTile;
+        if (!mbar_wait(ds_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ds_s = sDS + (uint32_t)st * 16384u;
+        const uint64_t dsk = kmajor_desc0(ds_s);         // dS^T as A (K = queries, one block)
+        const uint64_t dsm = mnmajor_desc0(ds_s);        // dS^T as B (N = queries, MN-major)
+        const uint64_t dom = umma_desc_sw128(do_s, 8192, 1024);  // dO as B: N = head dims
+        const uint64_t qm = umma_desc_sw128(q_s, 8192, 1024);
+#pragma unroll
+        for (int kk = 0; kk < QT128 / 16; ++kk)  // dV += P^T dO, A = P^T from tensor memory
+          umma_f16_ta(tDV, tPT + kk * 8, desc_add(dom, mnmajor_off(kk)), I_KV, (it > 0 || kk > 0));
+        umma_commit(pt_free);
+#pragma unroll
+        for (int kk = 0; kk < QT128 / 16; ++kk)  // dK += dS^T Q
+          umma_f16(tDK, desc_add(dsk, kmajor_off(kk)), desc_add(qm, mnmajor_off(kk)), I_KV,
+                   (it > 0 || kk > 0));
+        umma_commit(qdo_empty(st));
+        if (!mbar_wait(dq_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TILE / 16; ++kk)  // dQ^T = K^T dS^T over the 128 keys
+          umma_f16(tDQ, desc_add(km, mnmajor_off(kk)), desc_add(dsm, mnmajor_off(kk)), I_QT, kk > 0);
+        umma_commit(dq_full);
+      }
+      umma_commit(acc_full);
+      mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ softmax / dS warps 0..15
+    const int quarter = warp & 3, part = warp >> 2;
+    const int r = quarter * 32 + lane;  // key row (S^T, dP^T, dK, dV) / head-dim row (dQ^T)
+    const int kv = kv0 + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int qc0 = part * 16;          // this thread's 16 query columns
+    bool ok = true;
+    auto flush_dq = [&](int it) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) return false;
+      tc_fence_after();
+      const uint32_t stg = sDQ + (uint32_t)warp * 2048u;
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
+      const uint32_t row = stg + (uint32_t)lane * 64u;
+      uint32_t rr[16];
+      tmem_ld16(tDQ + lane_off + qc0, rr);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        st_shared_v4(row + (uint32_t)((c ^ ((lane >> 1) & 3)) << 4),
+                     make_uint4(rr[4 * c], rr[4 * c + 1], rr[4 * c + 2], rr[4 * c + 3]));
+      tc_fence_before();
+      mbar_arrive(dq_empty);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_3d(&tmDQ, stg, (i0 + it) * QT128 + qc0, quarter * 32, bh);
+        bulk_commit();
+      }
+      return true;
+    };
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = (i0 + it) * QT128;
+      const int sb = it & 1;
+      if (!ok) continue;
+      if (!__all_sync(0xffffffffu, mbar_wait(qdo_full(sb), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) ||
+          !__all_sync(0xffffffffu, mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
+      tc_fence_after();
+      const bool diag = p.causal && (q0 < kv0 + TILE);
+      uint32_t pw[8], dw[8];
+      {
+        uint32_t sr[16], dr[16];
+        tmem_ld16(tST + lane_off + qc0, sr);
+        tmem_ld16(tDPT + lane_off + qc0, dr);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(s_empty);
+        const float* ls = lse_s + sb * QT128 + qc0;
+        const float* dl = del_s + sb * QT128 + qc0;
+#pragma unroll
+        for (int qc = 0; qc < 16; qc += 2) {
+          float pp[2], dd[2];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            float e = ex2_ftz(fmaf(__uint_as_float(sr[qc + i]), p.scale_log2, -ls[qc + i]));
+            if (kv >= p.T || (diag && q0 + qc0 + qc + i < kv)) e = 0.f;
+            pp[i] = e;
+            dd[i] = e * (__uint_as_float(dr[qc + i]) - dl[qc + i]);
+          }
+          pw[qc >> 1] = pack2<T16>(pp[0], pp[1]);
+          dw[qc >> 1] = pack2<T16>(dd[0], dd[1]);
+        }
+      }
+      if (it > 0 && !__all_sync(0xffffffffu, mbar_wait(pt_free, (it - 1) & 1, p.err, FXB_DERR_ATTN_WAIT))) {
+        ok = false;
+        continue;
+      }
+      tc_fence_after();
+      tmem_st8(tPT + lane_off + part * 8, pw);
+      uint8_t* ds = gbase + (sDS - base) + (it & 1) * 16384;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int chunk = part * 2 + u;
+        *reinterpret_cast<uint4*>(ds + r * 128 + ((chunk ^ (r & 7)) << 4)) =
+            make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+      if (it > 0 && !flush_dq(it - 1)) { ok = false; continue; }
+    }
+    if (ok && n_it > 0 && !flush_dq(n_it - 1)) ok = false;
+    if (lane == 0) bulk_wait_all0();
+    __syncwarp();
+    // final dK (scaled) and dV of key row kv, head dims part*32..+32
+    if (__all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT))) {
+      tc_fence_after();
+      uint32_t rk[32], rv[32];
+      tmem_ld32(tDK + lane_off + part * 32, rk);
+      tmem_ld32(tDV + lane_off + part * 32, rv);
+      tmem_wait_ld();
+      if (kv < p.T) {
+        T16* krow = static_cast<T16*>(p.dk) + b * p.dk_sb + (int64_t)kv * p.dk_st + h * p.dk_sh + part * 32;
+        T16* vrow = static_cast<T16*>(p.dv) + b * p.dv_sb + (int64_t)kv * p.dv_st + h * p.dv_sh + part * 32;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float fk[8], fv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            fk[i] = __uint_as_float(rk[8 * u + i]) * p.scale;
+            fv[i] = __uint_as_float(rv[8 * u + i]);
+          }
+          *reinterpret_cast<uint4*>(krow + 8 * u) = pack8<T16>(fk);
+          *reinterpret_cast<uint4*>(vrow + 8 * u) = pack8<T16>(fv);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kBwdWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dq = dq_acc^T * scale in the caller's layout (head dim 128): thread per
+// (batch*head, 8-wide head-dim chunk, query), queries fastest so that each of
+// the eight strided reads is coalesced across the warp
+template <typename T16>
+__global__ void attn_bwd128_post_kernel(const float* __restrict__ dqt, T16* __restrict__ dq,
+                                        int64_t dq_sb, int64_t dq_st, int64_t dq_sh, float scale,
+                                        int B, int T, int H, int Tp) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t n = (int64_t)B * H * 16 * T;
+  if (idx >= n) return;
+  const int t = (int)(idx % T);
+  const int64_t rest = idx / T;
+  const int dc = (int)(rest % 16);
+  const int bh = (int)(rest / 16);
+  const int b = bh / H, h = bh - b * H;
+  const float* src = dqt + ((int64_t)bh * 128 + dc * 8) * Tp + t;
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = src[(int64_t)j * Tp] * scale;
+  *reinterpret_cast<uint4*>(dq + b * dq_sb + (int64_t)t * dq_st + h * dq_sh + dc * 8) = pack8<T16>(f);
+}
+
 // ============================================================ host side
 // Each CTA allocates all 512 TMEM columns, so at most one CTA may be resident
 // per SM: the dynamic shared memory request is padded above half of the SM's
@@ -848,12 +1192,15 @@ template <int DH> constexpr int fwd_smem() {
 }
 static_assert(fwd_smem<64>() <= 232448 && fwd_smem<128>() <= 232448, "forward shared memory");
 constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 3 * 32768 + 2048 + 1024 + 256; }  // dS^T x2 + dQ staging
+// K, V, Q x2, dO x2, dS^T x2, dQ^T staging, LSE / delta, barriers, alignment
+constexpr int bwd128_smem() { return 2 * kB128Tile + 4 * kB128QTile + 2 * 16384 + 32768 + 1024 + 256 + 1024; }
+static_assert(bwd128_smem() <= 232448 && bwd128_smem() > kOneCtaPerSm, "head-dim-128 backward shared memory");
 
 int make_map4(CUtensorMap* map, int dtype, const void* ptr, int D, int T, int H, int B,
-              int64_t sb, int64_t st, int64_t sh) {
+              int64_t sb, int64_t st, int64_t sh, int box_rows = TILE) {
   uint64_t dims[4] = {(uint64_t)D, (uint64_t)T, (uint64_t)H, (uint64_t)B};
   uint64_t strides[3] = {(uint64_t)st * 2, (uint64_t)sh * 2, (uint64_t)sb * 2};
-  uint32_t box[4] = {64, (uint32_t)TILE, 1, 1};
+  uint32_t box[4] = {64, (uint32_t)box_rows, 1, 1};
   CUtensorMapDataType dt =
       dtype == FXB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   return fxb::encode_tiled(map, dt, 4, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -869,6 +1216,16 @@ int make_map_dq(CUtensorMap* map, float* dq_acc, int D, int T, int BH) {
                            CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
+// transposed fp32 dQ accumulator (B*H, 128, Tp) of the head-dim-128
+// backward: boxes of 16 queries x 32 head dims (64 bytes, 64B swizzle)
+int make_map_dqt(CUtensorMap* map, float* dqt, int Tp, int BH) {
+  uint64_t dims[3] = {(uint64_t)Tp, 128, (uint64_t)BH};
+  uint64_t strides[2] = {(uint64_t)Tp * 4, (uint64_t)128 * Tp * 4};
+  uint32_t box[3] = {16, 32, 1};
+  return fxb::encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dqt, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 bool strides_ok(int64_t sb, int64_t st, int64_t sh) {
   return sb % 8 == 0 && st % 8 == 0 && sh % 8 == 0 && sb > 0 && st > 0 && sh > 0;
 }
@@ -876,13 +1233,14 @@ bool strides_ok(int64_t sb, int64_t st, int64_t sh) {
 int check_args(const fxb_attn_args* a, bool bwd) {
   if (!a) return fxb::set_error(FXB_EINVAL, "attn: args is NULL");
   if (a->dtype != FXB_DTYPE_BF16 && a->dtype != FXB_DTYPE_F16)
-    return fxb::set_error(FXB_EUNSUPPORTED, "attn: dtype %d (bf16 or f16)", a->dtype);
+    return fxb::set_error(FXB_EINVAL, "attn: dtype %d (bf16, f16 or f32)", a->dtype);
   if (a->D != 64 && a->D != 128)
     return fxb::set_error(FXB_EINVAL, "attn: head_dim %d not supported (64 or 128)", a->D);
   if (a->B < 1 || a->T < 1 || a->H < 1)
     return fxb::set_error(FXB_EINVAL, "attn: bad shape B=%d T=%d H=%d", a->B, a->T, a->H);
-  if ((int64_t)a->B * a->H > 65535)
-    return fxb::set_error(FXB_EINVAL, "attn: B*H=%lld > 65535", (long long)a->B * a->H);
+  // 1-D grids (the backward launches one CTA per key tile and batch*head)
+  if ((int64_t)a->B * a->H * ((a->T + TILE - 1) / TILE) >= (int64_t(1) << 31))
+    return fxb::set_error(FXB_EINVAL, "attn: B*H*ceil(T/128) >= 2^31");
   const void* ptrs[4] = {a->q, a->k, a->v, a->o};
   for (const void* q : ptrs)
     if (!q || !fxb::aligned16(q)) return fxb::set_error(FXB_EINVAL, "attn: q/k/v/o must be 16-byte aligned");
@@ -891,8 +1249,6 @@ int check_args(const fxb_attn_args* a, bool bwd) {
     return fxb::set_error(FXB_EINVAL, "attn: strides must be positive multiples of 8 elements");
   if (!a->lse) return fxb::set_error(FXB_EINVAL, "attn: lse is NULL");
   if (bwd) {
-    if (a->D != 64)
-      return fxb::set_error(FXB_EUNSUPPORTED, "attn bwd: head_dim %d (this build: 64)", a->D);
     const void* g[4] = {a->dout, a->dq, a->dk, a->dv};
     for (const void* q : g)
       if (!q || !fxb::aligned16(q)) return fxb::set_error(FXB_EINVAL, "attn bwd: dout/dq/dk/dv alignment");
@@ -939,6 +1295,59 @@ int launch_fwd(const fxb_attn_args* a, cudaStream_t st) {
   const int grid = (int)(items < fxb::num_sms() ? items : fxb::num_sms());
   fxb::pdl_launch(k, grid, kFwdThreads, fwd_smem<DH>(), st, mq, mk, mv, p);
   return fxb::check_launch("attn_fwd");
+}
+
+template <int FMT>
+int launch_bwd128(const fxb_attn_args* a, cudaStream_t st) {
+  using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
+  constexpr int DH = 128;
+  const int64_t rows = (int64_t)a->B * a->H * a->T;
+  const int Tp = t_pad128(a->T);
+  float* delta = a->workspace;
+  float* dqt = a->workspace + ((rows + 3) / 4) * 4;
+  int r = fxb::check_cuda(cudaMemsetAsync(dqt, 0, (size_t)a->B * a->H * DH * Tp * sizeof(float), st),
+                          "attn bwd: clear dQ accumulator");
+  if (r) return r;
+  fxb::pdl_launch(attn_bwd_prep_kernel<T16, DH>, (unsigned)((rows * (DH / 8) + 255) / 256), 256, 0, st,
+      static_cast<const T16*>(a->o), a->o_sb, a->o_st, a->o_sh, static_cast<const T16*>(a->dout),
+      a->do_sb, a->do_st, a->do_sh, delta, static_cast<float*>(nullptr), a->B, a->T, a->H);
+  if ((r = fxb::check_launch("attn_bwd_prep"))) return r;
+  CUtensorMap mq, mk, mv, mdo, mdq;
+  if ((r = make_map4(&mq, a->dtype, a->q, DH, a->T, a->H, a->B, a->q_sb, a->q_st, a->q_sh, QT128))) return r;
+  if ((r = make_map4(&mk, a->dtype, a->k, DH, a->T, a->H, a->B, a->k_sb, a->k_st, a->k_sh))) return r;
+  if ((r = make_map4(&mv, a->dtype, a->v, DH, a->T, a->H, a->B, a->v_sb, a->v_st, a->v_sh))) return r;
+  if ((r = make_map4(&mdo, a->dtype, a->dout, DH, a->T, a->H, a->B, a->do_sb, a->do_st, a->do_sh, QT128)))
+    return r;
+  if ((r = make_map_dqt(&mdq, dqt, Tp, a->B * a->H))) return r;
+  BwdParams p;
+  p.B = a->B; p.T = a->T; p.H = a->H;
+  p.nqt = (a->T + TILE - 1) / TILE;
+  p.nkt = p.nqt;
+  p.causal = a->causal ? 1 : 0;
+  p.scale_log2 = a->scale * kLog2e;
+  p.scale = a->scale;
+  p.lse = a->lse;
+  p.delta = delta;
+  p.dq_acc = dqt;
+  p.dk = a->dk; p.dk_sb = a->dk_sb; p.dk_st = a->dk_st; p.dk_sh = a->dk_sh;
+  p.dv = a->dv; p.dv_sb = a->dv_sb; p.dv_st = a->dv_st; p.dv_sh = a->dv_sh;
+  p.err = fxb::dev_error_ptr();
+  if (!p.err) return FXB_ECUDA;
+  auto k = attn_bwd128_kernel<FMT>;
+  static bool once[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!once[dev & 63]) {
+    if ((r = set_smem(k, bwd128_smem()))) return r;
+    once[dev & 63] = true;
+  }
+  fxb::pdl_launch(k, dim3((unsigned)(p.nkt * a->B * a->H)), kBwdThreads, bwd128_smem(), st, mq, mk, mv,
+                  mdo, mdq, p);
+  if ((r = fxb::check_launch("attn_bwd128"))) return r;
+  const int64_t n = (int64_t)a->B * a->H * 16 * a->T;
+  fxb::pdl_launch(attn_bwd128_post_kernel<T16>, (unsigned)((n + 255) / 256), 256, 0, st, dqt,
+                  static_cast<T16*>(a->dq), a->dq_sb, a->dq_st, a->dq_sh, a->scale, a->B, a->T, a->H, Tp);
+  return fxb::check_launch("attn_bwd128_post");
 }
 
 template <int FMT>
@@ -993,9 +1402,15 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
 
 }  // namespace
 
+namespace fxb {
+int attn_fwd_f32(const fxb_attn_args* a, cudaStream_t st);  // csrc/attn_f32.cu
+int attn_bwd_f32(const fxb_attn_args* a, cudaStream_t st);
+}
+
 extern "C" {
 
 int fxb_attn_fwd(const fxb_attn_args* a, void* stream) {
+  if (a && a->dtype == FXB_DTYPE_F32) return fxb::attn_fwd_f32(a, fxb::as_stream(stream));
   int r = check_args(a, false);
   if (r) return r;
   cudaStream_t st = fxb::as_stream(stream);
@@ -1007,13 +1422,18 @@ int fxb_attn_fwd(const fxb_attn_args* a, void* stream) {
 size_t fxb_attn_bwd_workspace(int32_t B, int32_t T, int32_t H, int32_t D) {
   if (B < 1 || T < 1 || H < 1 || D < 1) return 0;
   const int64_t rows = (int64_t)B * H * T;
-  return (size_t)(((rows + 3) / 4) * 4 + rows * D) * sizeof(float);
+  // delta, then the fp32 dQ accumulator: (B*H, T, D), or at head dim 128 the
+  // transposed (B*H, 128, T rounded up to 64)
+  const int64_t acc = D == 128 ? (int64_t)B * H * 128 * t_pad128(T) : rows * D;
+  return (size_t)(((rows + 3) / 4) * 4 + acc) * sizeof(float);
 }
 
 int fxb_attn_bwd(const fxb_attn_args* a, void* stream) {
+  if (a && a->dtype == FXB_DTYPE_F32) return fxb::attn_bwd_f32(a, fxb::as_stream(stream));
   int r = check_args(a, true);
   if (r) return r;
   cudaStream_t st = fxb::as_stream(stream);
+  if (a->D == 128) return a->dtype == FXB_DTYPE_BF16 ? launch_bwd128<1>(a, st) : launch_bwd128<0>(a, st);
   return a->dtype == FXB_DTYPE_BF16 ? launch_bwd<1>(a, st) : launch_bwd<0>(a, st);
 }
 

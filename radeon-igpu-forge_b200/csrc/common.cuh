@@ -47,6 +47,11 @@ template <typename T> FXB_DEV void unpack8(const uint4& u, float* f) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) f[i] = to_f<T>(h[i]);
 }
+// 8 consecutive elements (16-bit: one 16-byte vector; fp32: two) <-> 8 floats;
+// the address must be 16-byte aligned
+template <typename T> FXB_DEV void load8(const T* p, float* f);
+template <typename T> FXB_DEV void store8(T* p, const float* f);
+
 // two floats -> two 16-bit values in one word (a in the low half), one paired
 // round-to-nearest conversion instruction
 template <typename T> FXB_DEV uint32_t pack2(float a, float b);
@@ -61,6 +66,23 @@ template <> FXB_DEV uint32_t pack2<__half>(float a, float b) {
 template <typename T> FXB_DEV uint4 pack8(const float* f) {
   return make_uint4(pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]), pack2<T>(f[4], f[5]),
                     pack2<T>(f[6], f[7]));
+}
+
+template <typename T> FXB_DEV void load8(const T* p, float* f) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    unpack8<T>(*reinterpret_cast<const uint4*>(p), f);
+  }
+}
+template <typename T> FXB_DEV void store8(T* p, const float* f) {
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  } else {
+    *reinterpret_cast<uint4*>(p) = pack8<T>(f);
+  }
 }
 
 // two 16-bit values in one 32-bit word (element 0 in the low half)
@@ -383,6 +405,13 @@ FXB_DEV void tmem_st16(uint32_t taddr, const uint32_t* r) {
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
+      : "memory");
+}
+FXB_DEV void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
       : "memory");
 }
 FXB_DEV void tmem_ld16(uint32_t taddr, uint32_t* r) {
