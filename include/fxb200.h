@@ -77,9 +77,10 @@ size_t fxb_rmsnorm_bwd_workspace(int64_t rows, int32_t D);
  * gradient reaching x through a residual connection, summed in the same pass);
  * dw = sum_rows x*rstd*dy.
  * dw (dtype dw_dtype, e.g. an fp32 flat-gradient slot) is written
- * (dw_accumulate == 0) or added to (dw_accumulate != 0). D <= 2048 for 16-bit
- * dtypes (1024 for fp32). Deterministic: per-block partials, then a
- * fixed-order sum.
+ * (dw_accumulate == 0) or added to (dw_accumulate != 0). Any D the forward
+ * takes (D % 8 == 0, D <= 8192): rows of up to 2048 16-bit (1024 fp32)
+ * elements are handled a warp per row, longer rows a block per row.
+ * Deterministic: per-block partials, then a fixed-order sum.
  * Replaces rms_norm_bwd_dx + rms_norm_bwd_dw + part.sum(0)
  * (ml/fxlm/kernels/norm.hip:64,102; ml/fxlm/norm.py:62-84). */
 int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rstd,
@@ -88,8 +89,7 @@ int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rs
                     void* stream);
 
 /* fxb_rmsnorm_bwd without a workspace argument: the call allocates nothing.
- * No counterpart in the reference (its rms_norm backward allocates the dw
- * partials with torch, ml/fxlm/norm.py:75-84); this entry exists for callers
+ * It has no counterpart in the reference; this entry exists for callers
  * that cannot allocate device memory on the call path, e.g. a host runtime
  * with a fixed memory budget that owns no allocator, or code that must not
  * call cudaMalloc / cudaFree (which synchronise the device).
@@ -97,7 +97,8 @@ int fxb_rmsnorm_bwd(int32_t dtype, const void* x, const void* w, const float* rs
  * so identical dw). The dw partials live in a file-scope device array of
  * fxb_rmsnorm_bwd_static_max_bytes() bytes (4 MiB), one per device:
  *  - the first call on a device looks up that array's address
- *    (cudaGetSymbolAddress) and caches it; make that first call before any
+ *    (cudaGetSymbolAddress) and caches it (again after the device's context
+ *    was replaced, e.g. by cudaDeviceReset); make that first call before any
  *    stream capture;
  *  - a call whose partials need more than the array holds
  *    (fxb_rmsnorm_bwd_workspace(rows, D) > the maximum) returns FXB_EINVAL;
@@ -194,7 +195,8 @@ int fxb_adamw_update(int32_t gdtype, int32_t pdtype, const void* grad, float* ma
                                GELU backward without recomputing the activation) */
 
 typedef struct fxb_gemm_args {
-  int32_t dtype;     /* A/B dtype: FXB_DTYPE_BF16 or FXB_DTYPE_F16 */
+  int32_t dtype;     /* A/B dtype: FXB_DTYPE_BF16 / FXB_DTYPE_F16 (tensor cores) or
+                        FXB_DTYPE_F32 (fp32 parity mode: C, R, Z, bias fp32 too) */
   int32_t M, N, K;
   const void* A;     /* a_trans == 0: (M,K) row stride lda; 1: (K,M) row stride lda */
   int64_t lda;
@@ -224,6 +226,9 @@ typedef struct fxb_gemm_args {
 /* tcgen05 / TMEM GEMM with TMA-fed operands. Requires K % 8 == 0 for K-major
  * operands and M (resp. N) % 8 == 0 for transposed ones (16-byte TMA rows),
  * 16-byte aligned bases, N % 8 == 0 for C.
+ * dtype FXB_DTYPE_F32 runs an fp32 SIMT kernel instead (every epilogue, exact
+ * tanh / exp, no shape or alignment constraints beyond positive leading
+ * dimensions): the 1e-5 fp32 parity mode, not a fast path.
  * Replaces the rocBLAS matmuls on the hot path: nn.Linear qkv/proj/fc/fc2
  * (ml/fxlm/model.py:48-51,61,69-71), the linear-CE chunk mm's
  * (ml/fxlm/cross_entropy.py:131-135,180) and the fxgpu dW mm
@@ -265,7 +270,10 @@ typedef struct fxb_attn_args {
 } fxb_attn_args;
 
 /* Causal / non-causal flash-attention forward: o = softmax(q k^T * scale) v,
- * lse = logsumexp of the scaled scores (natural log).
+ * lse = logsumexp of the scaled scores (natural log). dtype bf16 / f16 run
+ * the tcgen05 kernel (strides multiples of 8 elements, 16-byte aligned
+ * bases); dtype f32 runs an fp32 SIMT kernel (the 1e-5 parity mode; any
+ * positive strides). Head dim 64 or 128.
  * Replaces attn_fwd (ml/fxlm/kernels/attention.hip:104) as launched by _fwd
  * (ml/fxlm/attention.py:87-104). */
 int fxb_attn_fwd(const fxb_attn_args* args, void* stream);
@@ -273,7 +281,8 @@ int fxb_attn_fwd(const fxb_attn_args* args, void* stream);
 /* Workspace bytes for fxb_attn_bwd (delta = rowsum(dO*O), fp32 dQ staging). */
 size_t fxb_attn_bwd_workspace(int32_t B, int32_t T, int32_t H, int32_t D);
 
-/* Flash-attention backward: dq, dk, dv from q, k, v, o, lse, dout.
+/* Flash-attention backward: dq, dk, dv from q, k, v, o, lse, dout (head dim
+ * 64 or 128; bf16 / f16 on tensor cores, f32 as the forward).
  * Replaces attn_bwd_prep + attn_bwd_dkv + attn_bwd_dq
  * (ml/fxlm/kernels/attention.hip:229,256,411) as launched by _bwd
  * (ml/fxlm/attention.py:107-134). */
@@ -282,7 +291,7 @@ int fxb_attn_bwd(const fxb_attn_args* args, void* stream);
 /* ------------------------------------------------------------------ embedding / glue */
 
 /* out[b,t,:] = tok[idx[b,t],:] + pos[t,:]. idx int64 (B*T). Rows of out are D
- * contiguous. Replaces tok_emb(idx) + pos_emb[:T] (ml/fxlm/model.py:118). */
+ * contiguous; dtype bf16, f16 or f32; D % 8 == 0, 16-byte aligned buffers. Replaces tok_emb(idx) + pos_emb[:T] (ml/fxlm/model.py:118). */
 int fxb_embedding_fwd(int32_t dtype, const int64_t* idx, const void* tok, const void* pos,
                       void* out, int64_t B, int64_t T, int32_t D, int64_t V, void* stream);
 
@@ -302,7 +311,8 @@ int fxb_axpy(int32_t ddtype, void* dst, int32_t sdtype, const void* src, const f
 /* ------------------------------------------------------------------ fxgpu window model */
 
 /* Xg[b, :] = X[idx[b] : idx[b] + window, :] flattened window-major (K = window*F),
- * i.e. Xg[b, w*F + f] = X[idx[b] + w, f]. X (R, F) 16-bit row-major, F % 8 == 0,
+ * i.e. Xg[b, w*F + f] = X[idx[b] + w, f]. X (R, F) row-major (bf16, f16 or
+ * f32), F % 8 == 0,
  * idx int32; windows that leave [0, R) are written as zeros.
  * Replaces the A-operand gather and the Xg write-out of gather_gemm
  * (ml/fxgpu/gather_gemm.hip:17-180, launched by ml/fxgpu/fused_linear.py:76-85);

@@ -35,11 +35,11 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const T* _
     T* o = out + r * D;
     for (int d = lane * 8; d < D; d += 256) {
       float fa[8], fb[8];
-      unpack8<T>(*reinterpret_cast<const uint4*>(a + d), fa);
-      unpack8<T>(*reinterpret_cast<const uint4*>(b + d), fb);
+      load8<T>(a + d, fa);
+      load8<T>(b + d, fb);
 #pragma unroll
       for (int j = 0; j < 8; ++j) fa[j] += fb[j];
-      *reinterpret_cast<uint4*>(o + d) = pack8<T>(fa);
+      store8<T>(o + d, fa);
     }
   }
 }
@@ -60,7 +60,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const T* _
     const T* g = dout + r * D;
     for (int d = lane * 8; d < D; d += 256) {
       float f[8];
-      unpack8<T>(*reinterpret_cast<const uint4*>(g + d), f);
+      load8<T>(g + d, f);
       if (ok && dtok) {
         red_add4(dtok + id * D + d, f);
         red_add4(dtok + id * D + d + 4, f + 4);
@@ -121,8 +121,8 @@ extern "C" {
 
 int fxb_embedding_fwd(int32_t dtype, const int64_t* idx, const void* tok, const void* pos,
                       void* out, int64_t B, int64_t T, int32_t D, int64_t V, void* stream) {
-  if (dtype != FXB_DTYPE_BF16 && dtype != FXB_DTYPE_F16)
-    return fxb::set_error(FXB_EUNSUPPORTED, "embedding_fwd: dtype %d (16-bit only)", dtype);
+  if (fxb::dtype_size(dtype) == 0)
+    return fxb::set_error(FXB_EINVAL, "embedding_fwd: bad dtype %d", dtype);
   if (D <= 0 || D % 8 || B < 0 || T <= 0 || V <= 0)
     return fxb::set_error(FXB_EINVAL, "embedding_fwd: bad shape");
   if (!fxb::aligned16(tok) || !fxb::aligned16(pos) || !fxb::aligned16(out))
@@ -134,17 +134,21 @@ int fxb_embedding_fwd(int32_t dtype, const int64_t* idx, const void* tok, const 
     fxb::pdl_launch(embedding_fwd_kernel<__nv_bfloat16>, emb_blocks(rows), 256, 0, st, 
         idx, static_cast<const __nv_bfloat16*>(tok), static_cast<const __nv_bfloat16*>(pos),
         static_cast<__nv_bfloat16*>(out), rows, T, D, V);
-  else
+  else if (dtype == FXB_DTYPE_F16)
     fxb::pdl_launch(embedding_fwd_kernel<__half>, emb_blocks(rows), 256, 0, st, 
         idx, static_cast<const __half*>(tok), static_cast<const __half*>(pos),
         static_cast<__half*>(out), rows, T, D, V);
+  else
+    fxb::pdl_launch(embedding_fwd_kernel<float>, emb_blocks(rows), 256, 0, st,
+        idx, static_cast<const float*>(tok), static_cast<const float*>(pos),
+        static_cast<float*>(out), rows, T, D, V);
   return fxb::check_launch("embedding_fwd");
 }
 
 int fxb_embedding_bwd(int32_t dtype, const int64_t* idx, const void* dout, float* dtok_ws,
                       float* dpos_ws, int64_t B, int64_t T, int32_t D, int64_t V, void* stream) {
-  if (dtype != FXB_DTYPE_BF16 && dtype != FXB_DTYPE_F16)
-    return fxb::set_error(FXB_EUNSUPPORTED, "embedding_bwd: dtype %d (16-bit only)", dtype);
+  if (fxb::dtype_size(dtype) == 0)
+    return fxb::set_error(FXB_EINVAL, "embedding_bwd: bad dtype %d", dtype);
   if (D <= 0 || D % 8 || B < 0 || T <= 0 || V <= 0)
     return fxb::set_error(FXB_EINVAL, "embedding_bwd: bad shape");
   if (!fxb::aligned16(dout) || (dtok_ws && !fxb::aligned16(dtok_ws)) ||
@@ -156,9 +160,12 @@ int fxb_embedding_bwd(int32_t dtype, const int64_t* idx, const void* dout, float
   if (dtype == FXB_DTYPE_BF16)
     fxb::pdl_launch(embedding_bwd_kernel<__nv_bfloat16>, emb_blocks(rows), 256, 0, st, 
         idx, static_cast<const __nv_bfloat16*>(dout), dtok_ws, dpos_ws, rows, T, D, V);
-  else
+  else if (dtype == FXB_DTYPE_F16)
     fxb::pdl_launch(embedding_bwd_kernel<__half>, emb_blocks(rows), 256, 0, st, 
         idx, static_cast<const __half*>(dout), dtok_ws, dpos_ws, rows, T, D, V);
+  else
+    fxb::pdl_launch(embedding_bwd_kernel<float>, emb_blocks(rows), 256, 0, st,
+        idx, static_cast<const float*>(dout), dtok_ws, dpos_ws, rows, T, D, V);
   return fxb::check_launch("embedding_bwd");
 }
 

@@ -11,7 +11,8 @@
 
 namespace {
 
-// one warp per output row, 16-byte vectors (F % 8 == 0 => row starts aligned)
+// one warp per output row, 16-byte vectors (F % 8 == 0 => row starts aligned,
+// for 16-bit and fp32 elements alike)
 template <typename T>
 __global__ void gather_windows_kernel(const T* __restrict__ X, int64_t R, int F,
                                       const int* __restrict__ idx, int B, int window,
@@ -20,7 +21,7 @@ __global__ void gather_windows_kernel(const T* __restrict__ X, int64_t R, int F,
   pdl_wait();  // inputs come from the previous kernel on the stream
   const int lane = threadIdx.x & 31;
   const int64_t K = (int64_t)window * F;
-  const int64_t nvec = K / 8;
+  const int64_t nvec = K * (int64_t)sizeof(T) / 16;  // 16-byte vectors per window
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t b = warp; b < B; b += nw) {
@@ -163,8 +164,8 @@ extern "C" {
 
 int fxb_gather_windows(int32_t dtype, const void* X, int64_t R, int32_t F, const int32_t* idx,
                        int32_t B, int32_t window, void* Xg, void* stream) {
-  if (dtype != FXB_DTYPE_F16 && dtype != FXB_DTYPE_BF16)
-    return fxb::set_error(FXB_EUNSUPPORTED, "gather_windows: dtype %d (16-bit only)", dtype);
+  if (fxb::dtype_size(dtype) == 0)
+    return fxb::set_error(FXB_EINVAL, "gather_windows: bad dtype %d", dtype);
   if (F <= 0 || F % 8 != 0)
     return fxb::set_error(FXB_EINVAL, "gather_windows: F=%d must be a positive multiple of 8", F);
   if (R < 0 || B < 0 || window <= 0 || !idx || !X || !Xg)
@@ -179,9 +180,12 @@ int fxb_gather_windows(int32_t dtype, const void* X, int64_t R, int32_t F, const
   if (dtype == FXB_DTYPE_F16)
     fxb::pdl_launch(gather_windows_kernel<__half>, blocks, 256, 0, st, static_cast<const __half*>(X), R, F, idx, B,
                                                           window, static_cast<__half*>(Xg));
-  else
+  else if (dtype == FXB_DTYPE_BF16)
     fxb::pdl_launch(gather_windows_kernel<__nv_bfloat16>, blocks, 256, 0, st, 
         static_cast<const __nv_bfloat16*>(X), R, F, idx, B, window, static_cast<__nv_bfloat16*>(Xg));
+  else
+    fxb::pdl_launch(gather_windows_kernel<float>, blocks, 256, 0, st,
+        static_cast<const float*>(X), R, F, idx, B, window, static_cast<float*>(Xg));
   return fxb::check_launch("gather_windows");
 }
 

@@ -266,8 +266,35 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
 }
 }  // namespace fxb
 
+namespace fxb {
+int gemm_f32(const fxb_gemm_args* a, cudaStream_t st);  // csrc/gemm_f32.cu
+}
+
+// fp32 operands (the parity mode): validated here, computed by the SIMT kernel
+static int gemm_f32_entry(const fxb_gemm_args* a, cudaStream_t st) {
+  using namespace fxb;
+  const int M = a->M, N = a->N, K = a->K, epi = a->epilogue;
+  if (M < 0 || N < 0 || K < 0) return set_error(FXB_EINVAL, "gemm: negative size");
+  if (!a->A || !a->B || !a->C) return set_error(FXB_EINVAL, "gemm: NULL operand");
+  if (epi < 0 || epi > FXB_EPI_MUL) return set_error(FXB_EINVAL, "gemm: bad epilogue %d", epi);
+  if (a->lda < (a->a_trans ? M : K) || a->ldb < (a->b_trans ? N : K) || a->ldc < N)
+    return set_error(FXB_EINVAL, "gemm: leading dimension shorter than a row");
+  const bool needs_r = (epi == FXB_EPI_RESIDUAL || epi == FXB_EPI_DGELU || epi == FXB_EPI_DSILU ||
+                        epi == FXB_EPI_MUL);
+  if (needs_r && (!a->R || a->ldr < N)) return set_error(FXB_EINVAL, "gemm: epilogue needs R");
+  const bool needs_z = (epi == FXB_EPI_GELU || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU ||
+                        epi == FXB_EPI_GELU_DERIV);
+  if (needs_z && (!a->Z || a->ldz < N)) return set_error(FXB_EINVAL, "gemm: epilogue needs Z");
+  const bool has_bias = (epi == FXB_EPI_BIAS || epi == FXB_EPI_BIAS_GELU || epi == FXB_EPI_BIAS_SILU);
+  if (has_bias && !a->bias) return set_error(FXB_EINVAL, "gemm: epilogue needs bias");
+  if (M == 0 || N == 0) return FXB_OK;
+  if (K == 0) return set_error(FXB_EUNSUPPORTED, "gemm: K == 0");
+  return gemm_f32(a, st);
+}
+
 extern "C" int fxb_gemm(const fxb_gemm_args* args, void* stream) {
   if (!args) return fxb::set_error(FXB_EINVAL, "gemm: args is NULL");
+  if (args->dtype == FXB_DTYPE_F32) return gemm_f32_entry(args, fxb::as_stream(stream));
   return fxb::gemm_launch(args, args->epilogue, 0, fxb::as_stream(stream));
 }
 

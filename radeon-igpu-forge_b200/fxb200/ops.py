@@ -14,6 +14,7 @@ from ._lib import (EPI_STORE, EPI_RESIDUAL, EPI_GELU, EPI_DGELU, EPI_BIAS,  # no
                    EPI_GELU_DERIV, EPI_MUL)
 
 _TC_DTYPES = (torch.bfloat16, torch.float16)
+_GEMM_DTYPES = _TC_DTYPES + (torch.float32,)  # fp32: the library's fp32 parity-mode GEMM
 
 # Optional per-launch timing of the GEMM (bench.py's live roofline): when a
 # list is installed here, every gemm() appends (flops, start, end) with CUDA
@@ -27,22 +28,60 @@ def set_gemm_timing(records):
     _GEMM_TIMING = records
 
 
-# GEMM workspace (tail split, see fxb_gemm_args.workspace): one zero-filled
-# buffer per (device, stream), allocated on first use and kept, so that
-# captured CUDA graphs keep pointing at it.
+# GEMM workspace (tail split, see fxb_gemm_args.workspace): one buffer per
+# (device, stream) for eager launches, allocated on first use and kept. A
+# captured CUDA graph gets workspaces of its own (see `graph_workspaces`), so
+# two graphs, or a graph and eager launches, never share arrival counters.
+# The first 4096 bytes are arrival counters that must be zero before a GEMM
+# starts; GEMMs reset them themselves, except after an expired wait (device
+# error word bit 1), when `_reset_workspaces` zeroes them.
 _GEMM_WS = {}
+_CAPTURE_WS = None  # dict of the graph being captured, or None
 
 
 def _gemm_workspace(device):
     st = torch.cuda.current_stream(device)
     key = (device.index, st.cuda_stream)
-    ws = _GEMM_WS.get(key)
+    table = _CAPTURE_WS if _CAPTURE_WS is not None else _GEMM_WS
+    ws = table.get(key)
     if ws is None:
         n = int(_lib.load().fxb_gemm_workspace_size())
         ws = torch.empty(n, device=device, dtype=torch.uint8)
-        ws[:4096].zero_()  # the arrival counters; the partial tiles need no init
-        _GEMM_WS[key] = ws
+        ws[:4096].zero_()  # the arrival counters (inside a capture: a memset node of the graph)
+        table[key] = ws
     return ws
+
+
+class graph_workspaces:
+    """Context manager used around a CUDA-graph capture: GEMMs captured inside
+    it use workspaces stored in `table` (owned by the graph object, alive as
+    long as the graph), whose counters are zeroed by a memset node at the
+    start of every replay's first GEMM on that stream."""
+
+    def __init__(self, table):
+        self.table = table
+
+    def __enter__(self):
+        global _CAPTURE_WS
+        self.prev, _CAPTURE_WS = _CAPTURE_WS, self.table
+        return self.table
+
+    def __exit__(self, *exc):
+        global _CAPTURE_WS
+        _CAPTURE_WS = self.prev
+        return False
+
+
+def _reset_workspaces(code):
+    """After an expired GEMM wait the owner of a tail tile may have left its
+    counter non-zero: zero the counters of every eager workspace (graph
+    workspaces are zeroed at the start of each replay)."""
+    if code & _lib.DERR_GEMM_WAIT:
+        for ws in _GEMM_WS.values():
+            ws[:4096].zero_()
+
+
+_lib._ON_DEVICE_ERROR.append(_reset_workspaces)
 
 
 def _rowmajor(t, name):
@@ -56,11 +95,13 @@ def gemm(A, B, out, *, a_trans=False, b_trans=False, epilogue=EPI_STORE, alpha=1
     """out[M,N] = epilogue(opA(A) @ opB(B)^T) on tcgen05 tensor cores.
 
     opA(A) = A (M,K) or, with a_trans, A stored (K,M); opB(B) = B (N,K) or,
-    with b_trans, B stored (K,N). A and B share one 16-bit dtype; `out`, R, Z
-    and bias share out's dtype (fp32 out is required for EPI_ACCUM_F32).
+    with b_trans, B stored (K,N). A and B share one dtype (bf16 / fp16 on the
+    tensor cores, or fp32: the fp32 parity-mode kernel, then every other
+    tensor is fp32 too); `out`, R, Z and bias share out's dtype (fp32 out is
+    required for EPI_ACCUM_F32).
     """
-    if A.dtype not in _TC_DTYPES or B.dtype != A.dtype:
-        raise TypeError(f"gemm operands must both be bf16 or fp16 ({A.dtype}, {B.dtype})")
+    if A.dtype not in _GEMM_DTYPES or B.dtype != A.dtype:
+        raise TypeError(f"gemm operands must share bf16, fp16 or fp32 ({A.dtype}, {B.dtype})")
     if not (A.is_cuda and B.is_cuda and out.is_cuda):
         raise TypeError("gemm operands must be cuda tensors")
     lda = _rowmajor(A, "A")

@@ -3,9 +3,9 @@
 Same surface as the reference (ml/fxlm/attention.py): q, k, v are (B,T,H,Dh)
 views with unit stride on Dh and free other strides (so the fused qkv buffer
 is used without copies); o is returned (B,T,H,Dh) contiguous and lse (B,H,T)
-fp32 is saved for backward. Dh in {64, 128} for the forward; the tcgen05
-backward of this build covers Dh = 64 (Dh = 128 raises RuntimeError from the
-library). dtype: bf16 or fp16 (the reference is fp16 only).
+fp32 is saved for backward. Dh in {64, 128}, forward and backward. dtype:
+bf16 or fp16 on the tcgen05 kernels (the reference is fp16 only), or fp32 on
+the library's fp32 kernels (the 1e-5 parity mode).
 """
 import ctypes
 import math
@@ -16,7 +16,7 @@ from fxb200 import _lib
 
 
 def _check_qkv(q, k, v):
-    """Validation of ml/fxlm/attention.py:57-79 (dtype widened to bf16/fp16)."""
+    """Validation of ml/fxlm/attention.py:57-79 (dtype widened to bf16/fp16/fp32)."""
     if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
         raise ValueError(f"q, k, v must share one 4-D shape: {tuple(q.shape)} "
                          f"{tuple(k.shape)} {tuple(v.shape)}")
@@ -26,16 +26,14 @@ def _check_qkv(q, k, v):
     if T < 1 or B < 1 or H < 1:
         raise ValueError(f"invalid shape: {tuple(q.shape)}")
     for nm, t in (("q", q), ("k", k), ("v", v)):
-        if t.dtype not in (torch.float16, torch.bfloat16) or t.dtype != q.dtype:
-            raise TypeError(f"{nm} must be bf16 or fp16 (and match q), got {t.dtype}")
+        if t.dtype not in (torch.float16, torch.bfloat16, torch.float32) or t.dtype != q.dtype:
+            raise TypeError(f"{nm} must be bf16, fp16 or fp32 (and match q), got {t.dtype}")
         if not t.is_cuda:
             raise TypeError(f"{nm} must be a cuda tensor")
         if t.stride(-1) != 1:
             raise ValueError(f"{nm} last axis must be contiguous (stride(-1)={t.stride(-1)})")
     if q.numel() >= 2 ** 31:
         raise ValueError("tensor too large (2^31 element limit)")
-    if B * H > 65535:
-        raise ValueError(f"B*H={B * H} > 65535 (grid.y limit)")
     return B, T, H, Dh
 
 

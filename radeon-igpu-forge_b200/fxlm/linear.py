@@ -9,17 +9,19 @@ The MLP keeps the pre-activation Z from the fc epilogue and folds gelu'(Z)
 into the epilogue of fc2's dX GEMM. Weight gradients are produced by a split-K
 GEMM that accumulates fp32 directly into the FlatAdamW flat-gradient slot when
 the weight is managed by FlatAdamW (else they are returned to autograd).
+fp32 tensors take the library's fp32 GEMM (the 1e-5 parity mode) through the
+same calls and epilogues.
 """
 import torch
 
 from fxb200 import ops
 
-_DTYPES = (torch.float16, torch.bfloat16)
+_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
 
 
 def _check(x, W):
     if x.dtype not in _DTYPES or W.dtype != x.dtype:
-        raise TypeError(f"x and weight must share bf16 or fp16 ({x.dtype}, {W.dtype})")
+        raise TypeError(f"x and weight must share bf16, fp16 or fp32 ({x.dtype}, {W.dtype})")
     if not (x.is_cuda and W.is_cuda):
         raise TypeError("x and weight must be cuda tensors")
     if W.dim() != 2 or x.shape[-1] != W.shape[1]:

@@ -115,8 +115,7 @@ class Block(nn.Module):
     def forward(self, x):
         B, T, D = x.shape
         fused = self.linear_impl == "fused"
-        if (fused and self.attn_impl == "flash" and self.norm_impl == "fused"
-                and self.head_dim == 64 and x.dtype != torch.float32):
+        if fused and self.attn_impl == "flash" and self.norm_impl == "fused":
             # both halves of the block as single Functions (residual-path
             # gradients summed inside the RMSNorm backward kernel)
             x = attn_block(x, self.ln1_w, self.qkv.weight, self.proj.weight, self.eps, self.n_head)
@@ -181,7 +180,7 @@ class GPT(nn.Module):
         B, T = idx.shape
         if T > self.cfg.seq_len:
             raise ValueError(f"T={T} > seq_len={self.cfg.seq_len}")
-        if self.cfg.linear_impl == "fused" and self.tok_emb.weight.dtype != torch.float32:
+        if self.cfg.linear_impl == "fused":
             x = _Embedding.apply(idx.contiguous(), self.tok_emb.weight, self.pos_emb)
         else:
             x = self.tok_emb(idx) + self.pos_emb[:T]
