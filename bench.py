@@ -29,6 +29,7 @@ the timed region; `gpu_launches` = kernels of libfxb200 in the timed region
 """
 import argparse
 import datetime
+import gc
 import json
 import os
 import re
@@ -57,13 +58,32 @@ def _metric():
         return "GPT d768x12L train tokens/s"
 
 
-def _peaks():
+def _peaks(clocks=None):
+    """bf16 tensor peak for the roofline. The burst figure applies unless the
+    clock record of the timed region shows the SM clock held below its
+    maximum (power capping over a long run), when the sustained one does."""
+    capped = False
+    if clocks and clocks.get("sm_mhz") and clocks.get("sm_max_mhz"):
+        capped = clocks["sm_mhz"] < 0.97 * clocks["sm_max_mhz"]
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
-        return float(d["bf16_tflops_sustained"]), "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
+        if capped:
+            return float(d["bf16_tflops_sustained"]), \
+                "MEASURED_PEAKS.json bf16_tflops_sustained (of measured; SM clock below max in the timed region)"
+        return float(d["bf16_tflops"]), \
+            "MEASURED_PEAKS.json bf16_tflops burst (of measured; SM clock at max in the timed region)"
     except Exception:
-        return 1400.0, "fallback 1.4 PFLOP/s sustained (of fallback)"
+        return (1400.0, "fallback 1.4 PFLOP/s sustained (of fallback)") if capped else \
+            (1590.0, "fallback 1.59 PFLOP/s burst (of fallback)")
+
+
+def _hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s (of fallback)"
 
 
 def _gemm_traffic():
@@ -408,6 +428,23 @@ def run_micro(args):
         out.append({"kernel": "adamw_sumsq + adamw_final + adamw_update", "case": f"{n} params fp32 grad",
                     "ms": ms, "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm,
                     "bytes_per_param": 38})
+    if "head" in which:
+        # the config-4 LM head: linear_cross_entropy over 8192 rows (D 768,
+        # V 32768) forward + backward, at several logits-chunk sizes
+        from fxlm.cross_entropy import linear_cross_entropy
+        Nr, D, V = 8192, 768, 32768
+        g = torch.Generator(device=dev).manual_seed(3)
+        x = torch.randn(Nr, D, device=dev, generator=g).to(bf).requires_grad_()
+        W = (torch.randn(V, D, device=dev, generator=g) * 0.02).to(bf).requires_grad_()
+        tg = torch.randint(0, V, (Nr,), device=dev, generator=g)
+        for ch in (8192, 4096, 2048, 1024, 768):
+            def f():
+                loss = linear_cross_entropy(x, W, tg, chunk_rows=ch)
+                loss.backward()
+            ms = _time_ms(f, it)
+            out.append({"kernel": "linear_cross_entropy fwd+bwd (3 GEMMs + CE per chunk)",
+                        "case": f"N{Nr} D{D} V{V} chunk_rows {ch} (logits chunk {ch * V * 2 / 1e6:.0f} MB)",
+                        "ms": ms, "tflops": 3 * 2.0 * Nr * D * V / ms / 1e9})
     if "wmlp" in which or "all" in which:
         # the fxgpu window MLP training step (gather-linear
         # 1024 -> 512 + bias + GELU, 512 -> 256 + GELU, 256 -> 1, MSE, FlatAdamW)
@@ -458,6 +495,130 @@ def run_micro(args):
                         "error": repr(e)[:300]})
     for o in out:
         print(json.dumps(o), flush=True)
+
+
+# ---------------------------------------------------------------- loss-curve and data-parallel checks
+def _gpt_and_opt(dev):
+    """Config-4 model from the reference init (seed 3) and its FlatAdamW."""
+    import torch
+    from fxlm import GPT, GPTConfig, FlatAdamW
+    torch.manual_seed(3)
+    model = GPT(GPTConfig(**CFG4, eps=1e-6)).to(dev)
+    opt = FlatAdamW(model, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                    max_grad_norm=1.0, init_scale=1.0, param_dtype=torch.bfloat16)
+    return model, opt
+
+
+def _golden_curve(acc):
+    try:
+        with open(os.path.join(ROOT, "tests", "golden", "curve_d768.json")) as f:
+            return json.load(f).get(f"acc{acc}")
+    except Exception:
+        return None
+
+
+def curve_check(args, rank, world, local_rank, dev):
+    """Config-4 loss curve of `steps` training steps from the reference init on
+    the bench's fixed micro-batches (rank r: Zipf seed 3 + r), outside the
+    timed region.
+
+    N = 1: every step's loss against the reference's own fp32 CPU curve
+    (tests/golden/curve_d768.json, produced by tests/golden/make_golden.py
+    from ml/fxlm/model.py), within 2%.
+    N > 1: the data-parallel run (the bench's collectives: ZeRO-1 or
+    all-reduce) against a single-process gradient accumulation of the same N
+    micro-batches on rank 0 (loss / N per micro-batch, the reference's
+    accumulation path, ml/fxlm/train_lm.py:199-205), which is what data
+    parallelism must equal; also the reference's CPU curve when one was
+    generated for that accumulation count. Every rank's parameters must end
+    bitwise equal."""
+    import torch
+    import torch.distributed as dist
+    from fxb200.data import zipf_tokens
+    steps = args.curve_steps if args.curve_steps is not None else (200 if world == 1 else 100)
+    if steps <= 0:
+        return None
+    gold = _golden_curve(world)
+    model, opt = _gpt_and_opt(dev)
+    if world > 1 and args.zero:
+        from fxb200.zero import ShardedDataParallel
+        ShardedDataParallel(model, opt)
+    elif world > 1:
+        from fxb200.ddp import DataParallel
+        DataParallel(model, opt)
+    x, y = (t.to(dev) for t in zipf_tokens(CFG4["vocab_size"], MB, SEQ, seed=3 + rank))
+    losses = torch.zeros(steps, device=dev)
+    norms = torch.zeros(steps, device=dev)
+    for s in range(steps):
+        loss = model(x, y, grad_scale=opt.scale)
+        opt.backward(loss)
+        st = opt.step(6e-4)
+        opt.zero_grad()
+        losses[s] = loss.detach()
+        norms[s] = st["grad_norm"]
+    torch.cuda.synchronize()
+    out = {"steps": steps, "data": "fixed micro-batch per rank (Zipf seed 3 + rank), reference init (seed 3)"}
+    if world > 1:
+        dist.all_reduce(losses, op=dist.ReduceOp.SUM)
+        losses /= world
+        # bitwise identity of the replicas: a position-weighted checksum of the
+        # bf16 parameters, gathered from every rank
+        bits = opt.flat16.view(torch.int16).to(torch.int64)
+        w = torch.arange(bits.numel(), device=dev, dtype=torch.int64) % 65521 + 1
+        h = torch.stack([(bits * w).sum(), bits.sum()])
+        hs = [torch.zeros_like(h) for _ in range(world)]
+        dist.all_gather(hs, h)
+        out["ranks_bitwise_equal"] = all(torch.equal(hs[0], t) for t in hs)
+    ours = losses.cpu().tolist()
+    our_norms = norms.cpu().tolist()
+    del model, opt
+    gc.collect()
+    torch.cuda.empty_cache()
+    ref, kind = None, None
+    if world == 1:
+        if gold:
+            ref, kind = gold["losses"], "reference fp32 CPU curve (tests/golden/curve_d768.json acc1)"
+    elif rank == 0:
+        # single-process accumulation of the N micro-batches (rank 0 alone)
+        m1, o1 = _gpt_and_opt(dev)
+        batches = [tuple(t.to(dev) for t in zipf_tokens(CFG4["vocab_size"], MB, SEQ, seed=3 + r))
+                   for r in range(world)]
+        acc_l = torch.zeros(steps, device=dev)
+        acc_n = torch.zeros(steps, device=dev)
+        for s in range(steps):
+            tot = torch.zeros((), device=dev)
+            for xb, yb in batches:
+                lb = m1(xb, yb, grad_scale=o1.scale)
+                o1.backward(lb / world)
+                tot += lb.detach() / world
+            st = o1.step(6e-4)
+            o1.zero_grad()
+            acc_l[s] = tot
+            acc_n[s] = st["grad_norm"]
+        torch.cuda.synchronize()
+        ref = acc_l.cpu().tolist()
+        kind = f"single-process accumulation of the {world} micro-batches (rank 0, same kernels)"
+        nref = acc_n.cpu().tolist()
+        out["grad_norm_step1"] = {"dp": our_norms[0], "accumulation": nref[0],
+                                  "rel": abs(our_norms[0] - nref[0]) / max(abs(nref[0]), 1e-30)}
+        del m1, o1
+        torch.cuda.empty_cache()
+        if gold:
+            g = gold["losses"][:steps]
+            out["vs_reference_cpu"] = {"steps": len(g), "max_rel_dev": max(
+                abs(a - b) / abs(b) for a, b in zip(ours, g))}
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    if ref is not None:
+        n = min(len(ref), len(ours))
+        dev_rel = [abs(a - b) / abs(b) for a, b in zip(ours[:n], ref[:n])]
+        out.update({"against": kind, "steps_compared": n, "max_rel_dev": max(dev_rel),
+                    "at_step": int(max(range(n), key=lambda i: dev_rel[i])),
+                    "first_loss": ours[0], "ref_first_loss": ref[0], "final_loss": ours[n - 1],
+                    "ref_final_loss": ref[n - 1], "tolerance": 0.02, "within_tolerance": max(dev_rel) < 0.02})
+    elif rank == 0:
+        out["against"] = "none (no golden curve for this accumulation count)"
+    return out
 
 
 # ---------------------------------------------------------------- our arm
@@ -618,8 +779,19 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     derr = _lib.device_error(clear=True)
 
+    # ---- loss curve (N = 1: against the reference; N > 1: against gradient
+    # accumulation) and replica identity, on a fresh model after the timed work
+    if graphed is not None:
+        graphed.release()
+        graphed = None
+    del model, opt
+    gc.collect()
+    torch.cuda.empty_cache()
+    curve = curve_check(args, rank, world, local_rank, dev)
+    derr |= _lib.device_error(clear=True)
+
     if rank == 0:
-        peak, peak_src = _peaks()
+        peak, peak_src = _peaks(clocks)
         traffic = _gemm_traffic()
         line = {
             "metric": _metric(), "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -646,6 +818,8 @@ def run_ours(args, rank, world, local_rank):
         }
         if attn is not None:
             line["attn"] = attn
+        if curve is not None:
+            line["curve_check"] = curve
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
@@ -673,6 +847,9 @@ def main():
                     help="per-kernel microbenchmarks instead of the step: all or a comma list "
                          "of gemm,attn,rmsnorm,ce,adamw,wmlp")
     ap.add_argument("--iters", type=int, default=20, help="iterations per microbenchmark")
+    ap.add_argument("--curve-steps", type=int, default=None,
+                    help="loss-curve check length after the timed run (default 200 at N = 1, "
+                         "100 at N > 1; 0 skips it)")
     ap.add_argument("--only", default=None,
                     help="gemm_layer: comma-separated substrings selecting shapes (profiling)")
     args = ap.parse_args()

@@ -173,3 +173,27 @@ def device_error(clear=True):
     v = _i32(0)
     check(load().fxb_device_error(ctypes.byref(v), 1 if clear else 0), "fxb_device_error")
     return v.value
+
+
+# bits of the device error word (csrc/common.cuh)
+DERR_NAMES = {1: "gemm (tensor-core pipeline or tail-split wait)", 2: "attention pipeline",
+              4: "gather pipeline", 8: "cross-entropy row copy"}
+DERR_GEMM_WAIT = 1
+
+# called with the word when a check finds it non-zero, before raising
+# (fxb200.ops registers the reset of its GEMM workspaces' arrival counters)
+_ON_DEVICE_ERROR = []
+
+
+def raise_on_device_error(where=""):
+    """Read (and clear) the device error word; raise RuntimeError if a kernel's
+    bounded wait expired since the last check. A training loop calls this at
+    its existing host synchronisation points: results computed after an
+    expired wait are not trustworthy (the kernel gave up and returned)."""
+    code = device_error(clear=True)
+    if code:
+        for fn in _ON_DEVICE_ERROR:
+            fn(code)
+        what = ", ".join(n for b, n in DERR_NAMES.items() if code & b) or "unknown"
+        raise RuntimeError(f"libfxb200: a kernel's bounded wait expired{' ' + where if where else ''} "
+                           f"(device error word {code}: {what}); the step's results are invalid")

@@ -24,18 +24,41 @@ _EPI_ACT = {"silu": ops.EPI_BIAS_SILU, "gelu": ops.EPI_BIAS_GELU}
 _EPI_DACT = {"silu": ops.EPI_DSILU, "gelu": ops.EPI_DGELU}
 
 
-def _pad_rows(W, b, rows=8):
-    """Last layer has N = 1 output; the GEMM wants N % 8 == 0: zero-pad."""
-    Wp = torch.zeros(rows, W.shape[1], device=W.device, dtype=W.dtype)
-    bp = torch.zeros(rows, device=b.device, dtype=b.dtype)
-    Wp[:W.shape[0]] = W
-    bp[:b.shape[0]] = b
-    return Wp, bp
+class _PadCache:
+    """Persistent zero-padded copies for the 1-output head: the GEMM wants
+    N % 8 == 0, so W3 / b3 are written into row 0 of 8-row buffers and dy into
+    column 0 of a (B, 8) buffer; rows / columns 1..7 stay zero. The buffers
+    are allocated once per shape and refreshed in place each call (no
+    per-step allocation or zero fill, and stable addresses under CUDA-graph
+    capture)."""
+
+    def __init__(self):
+        self.bufs = {}
+
+    def get(self, name, shape, like):
+        key = (name, tuple(shape), like.dtype, like.device)
+        t = self.bufs.get(key)
+        if t is None:
+            t = torch.zeros(shape, device=like.device, dtype=like.dtype)
+            self.bufs[key] = t
+        return t
+
+    def pad_rows(self, W, b, rows=8):
+        Wp = self.get("W", (rows, W.shape[1]), W)
+        bp = self.get("b", (rows,), b)
+        Wp[:W.shape[0]].copy_(W)
+        bp[:b.shape[0]].copy_(b)
+        return Wp, bp
+
+    def pad_cols(self, dy, dtype, cols=8):
+        d8 = self.get("dy", (dy.shape[0], cols), torch.empty((), device=dy.device, dtype=dtype))
+        d8[:, :dy.shape[1]].copy_(dy)
+        return d8
 
 
 class _WindowMLPFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, X16, idx32, W1, b1, W2, b2, W3, b3, act, window):
+    def forward(ctx, X16, idx32, W1, b1, W2, b2, W3, b3, act, window, pads):
         B = idx32.numel()
         dev, dt = X16.device, X16.dtype
         Xg = gather_windows(X16, idx32, window)
@@ -46,32 +69,32 @@ class _WindowMLPFn(torch.autograd.Function):
         z2 = torch.empty(B, H2, device=dev, dtype=dt)
         a2 = torch.empty(B, H2, device=dev, dtype=dt)
         ops.gemm(a1, W2, a2, epilogue=_EPI_ACT[act], Z=z2, bias=b2)
-        W3p, b3p = _pad_rows(W3, b3)
+        W3p, b3p = pads.pad_rows(W3, b3)
         y8 = torch.empty(B, W3p.shape[0], device=dev, dtype=dt)
         ops.gemm(a2, W3p, y8, epilogue=ops.EPI_BIAS, bias=b3p)
         ctx.save_for_backward(Xg, z1, a1, z2, a2, W1, b1, W2, b2, W3, b3, W3p)
         ctx.act = act
+        ctx.pads = pads
         return y8[:, :W3.shape[0]].contiguous()
 
     @staticmethod
     def backward(ctx, dy):
         Xg, z1, a1, z2, a2, W1, b1, W2, b2, W3, b3, W3p = ctx.saved_tensors
         act = ctx.act
-        B = dy.shape[0]
-        dy8 = torch.zeros(B, W3p.shape[0], device=dy.device, dtype=z1.dtype)
-        dy8[:, :dy.shape[1]] = dy
+        dy8 = ctx.pads.pad_cols(dy, z1.dtype, W3p.shape[0])
         # layer 3
         dz2 = torch.empty_like(z2)
         ops.gemm(dy8, W3p, dz2, b_trans=True, epilogue=_EPI_DACT[act], R=z2)
         sink3 = ops.param_grad_sink(W3)
         if sink3 is not None:
-            dW3p = torch.zeros(W3p.shape, device=dy.device, dtype=torch.float32)
+            dW3p = ctx.pads.get("dW3", W3p.shape, torch.empty((), device=dy.device, dtype=torch.float32))
+            dW3p.zero_()
             ops.linear_dw_into(dy8, a2, dW3p)
             sink3.add_(dW3p[:W3.shape[0]])
             gW3 = None
         else:
             gW3 = ops.weight_grad(dy8, a2, W3p)[:W3.shape[0]].contiguous()
-        gb3 = bias_grad(dy.contiguous().to(z1.dtype), b3)
+        gb3 = bias_grad(dy.contiguous().to(z1.dtype), b3)  # (B, 1): no copy in the usual case
         # layer 2
         dz1 = torch.empty_like(z1)
         ops.gemm(dz2, W2, dz1, b_trans=True, epilogue=_EPI_DACT[act], R=z1)
@@ -80,7 +103,8 @@ class _WindowMLPFn(torch.autograd.Function):
         # layer 1 (input layer: no gradient for X)
         gW1 = ops.weight_grad(dz1, Xg, W1)
         gb1 = bias_grad(dz1, b1)
-        return None, None, gW1, gb1, gW2, gb2, gW3, gb3, None, None
+        ctx.pads = None
+        return None, None, gW1, gb1, gW2, gb2, gW3, gb3, None, None, None
 
 
 class WindowMLP(nn.Module):
@@ -103,6 +127,7 @@ class WindowMLP(nn.Module):
         self.b2 = nn.Parameter(torch.zeros(hidden2, dtype=pdtype))
         self.W3 = nn.Parameter(torch.randn(1, hidden2, dtype=pdtype) * 0.1)
         self.b3 = nn.Parameter(torch.zeros(1, dtype=pdtype))
+        self._pads = _PadCache()
 
     def _half_params(self):
         ps = (self.W1, self.b1, self.W2, self.b2, self.W3, self.b3)
@@ -124,7 +149,8 @@ class WindowMLP(nn.Module):
         if self.dropout > 0 and self.training:
             h1 = FusedGatherLinear.apply(X16, idx32, W1, b1)
             return self._trunk(h1, W2, b2, W3, b3)
-        return _WindowMLPFn.apply(X16, idx32, W1, b1, W2, b2, W3, b3, self.act, self.window)
+        return _WindowMLPFn.apply(X16, idx32, W1, b1, W2, b2, W3, b3, self.act, self.window,
+                                  self._pads)
 
     def forward_dense(self, xb16):
         """Same computation from a pre-gathered (B,K) batch (parity twin)."""

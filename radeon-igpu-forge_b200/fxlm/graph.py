@@ -25,7 +25,7 @@ released (`release()`) before the process group is destroyed.
 """
 import torch
 
-from fxb200 import _lib
+from fxb200 import _lib, ops
 
 
 class GraphedStep:
@@ -53,9 +53,11 @@ class GraphedStep:
                 self._step()
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
+        _lib.raise_on_device_error("during GraphedStep warm-up")
         self.graph = torch.cuda.CUDAGraph()
+        self._ws = {}  # GEMM workspaces of this graph
         n0 = _lib.launch_count()
-        with torch.cuda.graph(self.graph):
+        with ops.graph_workspaces(self._ws), torch.cuda.graph(self.graph):
             self.loss = self._step()
         # kernels of this library inside one replay
         self.launches_per_step = _lib.launch_count() - n0
@@ -70,14 +72,23 @@ class GraphedStep:
     def __call__(self, x=None, y=None, lr=None):
         """Copy (x, y) into the static inputs (when given), set the learning
         rate (when given) and replay; returns the step's loss (device)."""
-        if x is not None:
-            self.x.copy_(x, non_blocking=True)
-        if y is not None:
-            self.y.copy_(y, non_blocking=True)
+        for name, dst, src in (("x", self.x, x), ("y", self.y, y)):
+            if src is None:
+                continue
+            if tuple(src.shape) != tuple(dst.shape) or src.dtype != dst.dtype:
+                raise ValueError(f"GraphedStep: {name} is {tuple(src.shape)} {src.dtype}, "
+                                 f"captured with {tuple(dst.shape)} {dst.dtype}")
+            dst.copy_(src, non_blocking=True)
         if lr is not None:
             self.opt.lr_dev.fill_(float(lr))
         self.graph.replay()
         return self.loss
+
+    def check(self):
+        """Synchronise and raise RuntimeError if a kernel's bounded wait expired
+        in a replay since the last check (call it where the loop reads the
+        loss anyway, e.g. at log steps)."""
+        _lib.raise_on_device_error("in a GraphedStep replay")
 
     def release(self):
         """Free the captured graph (required before destroy_process_group when
@@ -127,20 +138,35 @@ class GraphedFunction:
                 fn(*self.args)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
+        _lib.raise_on_device_error("during GraphedFunction warm-up")
         self.graph = torch.cuda.CUDAGraph()
+        self._ws = {}  # GEMM workspaces of this graph
         n0 = _lib.launch_count()
-        with torch.cuda.graph(self.graph):
+        with ops.graph_workspaces(self._ws), torch.cuda.graph(self.graph):
             self.out = fn(*self.args)
         self.launches_per_call = _lib.launch_count() - n0
 
     def __call__(self, *args):
         if len(args) > len(self.args):
             raise TypeError(f"GraphedFunction: {len(args)} arguments, captured with {len(self.args)}")
-        for dst, src in zip(self.args, args):
-            if src is not None:
-                dst.copy_(src, non_blocking=True)
+        for i, (dst, src) in enumerate(zip(self.args, args)):
+            if src is None:
+                continue
+            # copy_ would broadcast or cast silently: a wrong shape or dtype is an error here
+            if tuple(src.shape) != tuple(dst.shape):
+                raise ValueError(f"GraphedFunction: argument {i} has shape {tuple(src.shape)}, "
+                                 f"captured with {tuple(dst.shape)}")
+            if src.dtype != dst.dtype:
+                raise TypeError(f"GraphedFunction: argument {i} has dtype {src.dtype}, "
+                                f"captured with {dst.dtype}")
+            dst.copy_(src, non_blocking=True)
         self.graph.replay()
         return self.out
+
+    def check(self):
+        """Synchronise and raise RuntimeError if a kernel's bounded wait expired
+        in a replay since the last check."""
+        _lib.raise_on_device_error("in a GraphedFunction replay")
 
     def release(self):
         """Free the captured graph (before destroy_process_group when the

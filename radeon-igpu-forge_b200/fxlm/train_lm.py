@@ -83,6 +83,7 @@ def main(argv=None):
     import numpy as np
     import torch
     import torch.distributed as dist
+    from fxb200 import _lib
     from fxlm.model import GPT, GPTConfig
     from fxlm.optim import FlatAdamW
 
@@ -195,6 +196,9 @@ def main(argv=None):
                 loss_acc /= world
             torch.cuda.synchronize()
             dt = time.perf_counter() - t0
+            # a kernel whose bounded wait expired returned early: stop before
+            # its results reach the weights of another step or a checkpoint
+            _lib.raise_on_device_error(f"before step {gstep}")
             if rank == 0:
                 print(f"step {gstep:5d} | loss {float(loss_acc) / nb:.4f} | lr {lr:.2e} | "
                       f"{nb * B * T * world / dt:,.0f} tok/s | gnorm {float(stats['grad_norm']):.3f} | "

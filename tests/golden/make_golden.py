@@ -9,9 +9,10 @@ these paths). Inputs are rounded through bf16 so the GPU tests can feed the
 exact same values to the bf16 kernels.
 
     python tests/golden/make_golden.py --ref /path/to/reference [--skip-curve] [--skip-d768]
+    python tests/golden/make_golden.py --ref /path/to/reference --d768-curve ACC --steps 200
 
 Outputs (committed): ops.npz, gpt_tiny.npz, curve_tiny.json, gpt_d768.json,
-prepare_bytes.json (the reference's ml/fxlm/prepare_bytes.py run as a script on
+curve_d768.json (config-4 loss curve, --d768-curve), prepare_bytes.json (the reference's ml/fxlm/prepare_bytes.py run as a script on
 the tree of prepare_bytes_tree.py: meta and SHA-256 of the token files).
 """
 import argparse
@@ -259,6 +260,49 @@ def make_d768(ref_model):
     print("gpt_d768:", res)
 
 
+def make_curve_d768(ref_model, steps, acc, path):
+    """Config 4 loss curve: the reference model (torch path, fp32) trained for
+    `steps` steps on fixed Zipf batches, the selftest's FlatAdamW oracle
+    (torch AdamW lr 6e-4, betas (0.9, 0.95), wd 0.1 on ndim >= 2, clip 1.0).
+    acc micro-batches of 8 x 1024 per step (seeds 3 .. 3 + acc - 1, each loss
+    divided by acc, as ml/fxlm/train_lm.py:199-205 accumulates) are what
+    acc data-parallel ranks of bench.py train on (rank r: seed 3 + r). The
+    file is rewritten every 5 steps so a partial run is usable."""
+    cfg = dict(vocab_size=32768, seq_len=1024, n_layer=12, n_head=12, d_model=768)
+    torch.manual_seed(3)
+    m = _ref_gpt(ref_model, cfg, 1e-6)
+    opt = torch.optim.AdamW([{"params": [p for p in m.parameters() if p.dim() >= 2], "weight_decay": 0.1},
+                             {"params": [p for p in m.parameters() if p.dim() < 2], "weight_decay": 0.0}],
+                            lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    batches = [zipf(32768, 8, 1024, seed=3 + r) for r in range(acc)]
+    rec = json.load(open(path)) if os.path.exists(path) else {}
+    key = f"acc{acc}"
+    losses, norms = [], []
+    t0 = time.time()
+    for s in range(steps):
+        opt.zero_grad(set_to_none=True)
+        tot = 0.0
+        for x, y in batches:
+            loss = m(x, y)
+            (loss / acc).backward()
+            tot += float(loss.detach()) / acc
+        gn = torch.nn.utils.clip_grad_norm_(list(m.parameters()), 1.0)
+        opt.step()
+        losses.append(tot)
+        norms.append(float(gn))
+        if s % 5 == 4 or s == steps - 1:
+            rec[key] = {"config": "V32768 L12 D768 H12 eps1e-6, init seed 3, micro-batches 8x1024 "
+                                  f"zipf seeds 3..{2 + acc} fixed every step, loss/acc, AdamW lr6e-4 "
+                                  "b(0.9,0.95) wd0.1 (ndim>=2) clip1.0, fp32 CPU",
+                        "losses": losses, "grad_norms": norms, "steps_done": len(losses),
+                        "cpu_seconds": time.time() - t0, "threads": torch.get_num_threads()}
+            with open(path + ".tmp", "w") as f:
+                json.dump(rec, f)
+            os.replace(path + ".tmp", path)
+            print(f"  d768 acc{acc} step {s} loss {tot:.4f} norm {norms[-1]:.3f} "
+                  f"({time.time() - t0:.0f}s)", flush=True)
+
+
 def make_prepare_bytes(ref_root):
     sys.path.insert(0, HERE)
     from prepare_bytes_tree import build_tree, CASES
@@ -288,11 +332,18 @@ def main():
     ap.add_argument("--skip-d768", action="store_true")
     ap.add_argument("--only-prepare-bytes", action="store_true")
     ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--d768-curve", type=int, default=0, metavar="ACC",
+                    help="only the config-4 loss curve with ACC micro-batches per step")
+    ap.add_argument("--threads", type=int, default=os.cpu_count())
     args = ap.parse_args()
+    torch.set_num_threads(args.threads)
+    if args.d768_curve:
+        ref_model, _, _ = _import_reference(args.ref)
+        make_curve_d768(ref_model, args.steps, args.d768_curve, os.path.join(HERE, "curve_d768.json"))
+        return
     make_prepare_bytes(args.ref)
     if args.only_prepare_bytes:
         return
-    torch.set_num_threads(os.cpu_count())
     ref_model, ref_fxgpu_model, ref_selftest = _import_reference(args.ref)
     make_ops(ref_model, ref_fxgpu_model, ref_selftest)
     make_gpt_tiny(ref_model)
