@@ -178,6 +178,20 @@ def cpu_baseline(steps=3, warmup=1):
 def run_reference(args, rank, world):
     if rank != 0:
         return
+    if args.workload == "wmlp":
+        base = cpu_baseline_wmlp(steps=max(1, args.steps), warmup=max(1, args.warmup))
+        line = {"metric": "fxgpu window MLP train samples/s (BASELINE config 5)", "value": base["value"],
+                "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 4096 / base["value"] * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) (seed 4)",
+                "impl": "reference",
+                "config": {"workload": WMLP_WORKLOAD, "global_batch": 4096, "parallelism": "cpu",
+                           "sample": base["sample"]},
+                "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "samples/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     base = cpu_baseline(steps=max(1, args.steps), warmup=max(1, args.warmup))
     line = {"metric": _metric(), "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": SEQ / base["value"] * 1e3,
@@ -242,14 +256,22 @@ def _time_ms(fn, iters, warmup=3):
 
 
 def run_micro(args):
-    """One JSON line per kernel: BASELINE configs 2 and 3 shapes, the block
+    """One JSON line per kernel (see micro_results)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    for o in micro_results(args.micro, args.iters, args.only):
+        print(json.dumps(o), flush=True)
+
+
+def micro_results(micro, iters, only=None):
+    """Per-kernel measurements: BASELINE configs 2 and 3 shapes, the block
     GEMMs of config 4 and the AdamW pass over config 4's parameters. Inputs
-    are larger than L2 (126 MB) except where noted."""
+    are larger than L2 (126 MB) except where noted. Returns a list of dicts."""
     import math
     import torch
     from fxb200 import _lib, ops
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    dev = torch.device("cuda", torch.cuda.current_device())
     _lib.load()
     hbm = None
     try:
@@ -259,8 +281,8 @@ def run_micro(args):
     except Exception:
         hbm, tc = 6650.0, 1590.0
     out = []
-    which = args.micro.split(",")
-    it = args.iters
+    which = micro.split(",")
+    it = iters
     bf = torch.bfloat16
     if "gemm" in which or "gemm_fc" in which or "all" in which:
         cases = [(8192, 3072, 768, ops.EPI_GELU, "fc+gelu"), (8192, 2304, 768, ops.EPI_STORE, "qkv"),
@@ -308,8 +330,8 @@ def run_micro(args):
             ("bwd dWproj", D, D, T_, True, True, ops.EPI_ACCUM_F32),
             ("bwd dWqkv", 3 * D, D, T_, True, True, ops.EPI_ACCUM_F32),
         ]
-        if args.only:
-            keep = args.only.split(",")
+        if only:
+            keep = only.split(",")
             shapes = [s for s in shapes if any(k in s[0] for k in keep)]
         tot_f, tot_ms = 0.0, 0.0
         for nm, M, N, K, at, bt, epi in shapes:
@@ -388,7 +410,24 @@ def run_micro(args):
         byt = 4 * Ns * D * 2 + Ns * 4
         out.append({"kernel": "rmsnorm_bwd (+dres, + dw reduce)", "case": f"config 4 step [{Ns},{D}] bf16",
                     "ms": ms, "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm})
-    if "ce" in which or "all" in which:
+    if "ce4" in which:
+        # the config-4 step's cross entropy: 8192 rows of V 32768 (537 MB of
+        # logits, in place as in the linear-CE chunk), small enough to profile
+        Nr, V = 8192, 32768
+        g = torch.Generator(device=dev).manual_seed(3)
+        lg = torch.randn(Nr, V, device=dev, generator=g, dtype=bf)
+        tg = torch.randint(0, V, (Nr,), device=dev, generator=g)
+        loss = torch.zeros(Nr, device=dev)
+        mul = torch.full((), 1.0 / Nr, device=dev)
+        st = _lib.stream_ptr(dev)
+        f = lambda: _lib.call("fxb_ce_fwd_grad", 2, _lib.ptr(lg), V, _lib.ptr(tg), _lib.ptr(lg),  # noqa: E731
+                              _lib.ptr(loss), _lib.ptr(mul), Nr, V, -100, st)
+        ms = _time_ms(f, it)
+        byt = 2 * Nr * V * 2
+        out.append({"kernel": "ce_fwd_grad", "case": f"config 4 step [{Nr},{V}] bf16, gradient in place",
+                    "ms": ms, "gbs": byt / ms / 1e6, "frac_of_measured_hbm": byt / ms / 1e6 / hbm})
+        del lg
+    if ("ce" in which and "ce4" not in which) or "all" in which:
         Nr, V = 65536, 32768
         g = torch.Generator(device=dev).manual_seed(2)
         lg = torch.randn(Nr, V, device=dev, generator=g, dtype=bf)
@@ -493,8 +532,32 @@ def run_micro(args):
         except Exception as e:  # report the eager number regardless
             out.append({"kernel": "WindowMLP train step, CUDA graph replay", "case": case,
                         "error": repr(e)[:300]})
-    for o in out:
-        print(json.dumps(o), flush=True)
+    return out
+
+
+def kernel_rooflines(iters=10):
+    """Roofline entries for the non-GEMM kernels of the north star, event-timed
+    in this run (1 GPU): attention forward and forward + backward at config 2
+    against the bf16 tensor peak; RMSNorm forward / backward (config 3 and the
+    step's shape), cross entropy (config 3) and the FlatAdamW pass (config 4's
+    parameters) against the measured HBM copy bandwidth."""
+    hbm, hbm_src = _hbm_peak()
+    tc, tc_src = _peaks({"sm_mhz": 1.0, "sm_max_mhz": 1.0})  # kernels timed alone: burst
+    res = []
+    for o in micro_results("attn,rmsnorm,ce,adamw", iters):
+        k = o.get("kernel", "")
+        if k.startswith("attn"):
+            for what, key, ms in (("attn_fwd_kernel", "fwd_tflops", o["fwd_ms"]),
+                                  ("attn_fwd_kernel + attn_bwd_kernel (+ prep, post)", "fwd_bwd_tflops",
+                                   o["fwd_ms"] + o["bwd_ms"])):
+                a = o[key]
+                res.append({"kernel": what, "case": "BASELINE config 2: " + o["shape"], "bound": "tensor",
+                            "achieved": a, "peak": tc, "unit": "TFLOP/s", "frac": a / tc, "ms": ms,
+                            "peak_source": tc_src})
+        elif "gbs" in o:
+            res.append({"kernel": k, "case": o["case"], "bound": "hbm", "achieved": o["gbs"], "peak": hbm,
+                        "unit": "GB/s", "frac": o["gbs"] / hbm, "ms": o["ms"], "peak_source": hbm_src})
+    return res
 
 
 # ---------------------------------------------------------------- loss-curve and data-parallel checks
@@ -512,26 +575,32 @@ def _gpt_and_opt(dev):
 def _golden_curve(acc):
     try:
         with open(os.path.join(ROOT, "tests", "golden", "curve_d768.json")) as f:
-            return json.load(f).get(f"acc{acc}")
+            return json.load(f).get(f"acc{acc}_stream")
     except Exception:
         return None
 
 
 def curve_check(args, rank, world, local_rank, dev):
-    """Config-4 loss curve of `steps` training steps from the reference init on
-    the bench's fixed micro-batches (rank r: Zipf seed 3 + r), outside the
-    timed region.
+    """Config-4 loss curve of `steps` training steps from the reference init,
+    outside the timed region, on a fresh Zipf batch every step (micro-batch r
+    of step s: seed 1000 * (s + 1) + r; rank r trains micro-batch r).
 
-    N = 1: every step's loss against the reference's own fp32 CPU curve
-    (tests/golden/curve_d768.json, produced by tests/golden/make_golden.py
-    from ml/fxlm/model.py), within 2%.
+    N = 1: every step's loss against the reference's own fp32 CPU curve on the
+    same batches (tests/golden/curve_d768.json "acc1_stream", produced by
+    tests/golden/make_golden.py from ml/fxlm/model.py), within 2%.
     N > 1: the data-parallel run (the bench's collectives: ZeRO-1 or
     all-reduce) against a single-process gradient accumulation of the same N
     micro-batches on rank 0 (loss / N per micro-batch, the reference's
     accumulation path, ml/fxlm/train_lm.py:199-205), which is what data
-    parallelism must equal; also the reference's CPU curve when one was
+    parallelism must equal, and against the reference's CPU curve when one was
     generated for that accumulation count. Every rank's parameters must end
-    bitwise equal."""
+    bitwise equal.
+
+    A fixed-batch curve is not used as the criterion: at this learning rate
+    the memorisation run spikes at step 3, and past the spike the trajectory
+    depends on the order of fp32 summation (the reference's own PyTorch path
+    in fp32 on the GPU and on the CPU part there), so no implementation tracks
+    the CPU curve within 2% beyond it."""
     import torch
     import torch.distributed as dist
     from fxb200.data import zipf_tokens
@@ -539,6 +608,12 @@ def curve_check(args, rank, world, local_rank, dev):
     if steps <= 0:
         return None
     gold = _golden_curve(world)
+    V = CFG4["vocab_size"]
+
+    def batch(s, r):
+        x, y = zipf_tokens(V, MB, SEQ, seed=1000 * (s + 1) + r)
+        return x.pin_memory(), y.pin_memory()
+
     model, opt = _gpt_and_opt(dev)
     if world > 1 and args.zero:
         from fxb200.zero import ShardedDataParallel
@@ -546,10 +621,11 @@ def curve_check(args, rank, world, local_rank, dev):
     elif world > 1:
         from fxb200.ddp import DataParallel
         DataParallel(model, opt)
-    x, y = (t.to(dev) for t in zipf_tokens(CFG4["vocab_size"], MB, SEQ, seed=3 + rank))
     losses = torch.zeros(steps, device=dev)
     norms = torch.zeros(steps, device=dev)
     for s in range(steps):
+        xh, yh = batch(s, rank)
+        x, y = xh.to(dev, non_blocking=True), yh.to(dev, non_blocking=True)
         loss = model(x, y, grad_scale=opt.scale)
         opt.backward(loss)
         st = opt.step(6e-4)
@@ -557,7 +633,8 @@ def curve_check(args, rank, world, local_rank, dev):
         losses[s] = loss.detach()
         norms[s] = st["grad_norm"]
     torch.cuda.synchronize()
-    out = {"steps": steps, "data": "fixed micro-batch per rank (Zipf seed 3 + rank), reference init (seed 3)"}
+    out = {"steps": steps, "data": "a fresh Zipf batch every step (seed 1000*(step+1) + rank), "
+                                   "reference init (seed 3)"}
     if world > 1:
         dist.all_reduce(losses, op=dist.ReduceOp.SUM)
         losses /= world
@@ -577,18 +654,17 @@ def curve_check(args, rank, world, local_rank, dev):
     ref, kind = None, None
     if world == 1:
         if gold:
-            ref, kind = gold["losses"], "reference fp32 CPU curve (tests/golden/curve_d768.json acc1)"
+            ref, kind = gold["losses"], "reference fp32 CPU curve (tests/golden/curve_d768.json acc1_stream)"
     elif rank == 0:
         # single-process accumulation of the N micro-batches (rank 0 alone)
         m1, o1 = _gpt_and_opt(dev)
-        batches = [tuple(t.to(dev) for t in zipf_tokens(CFG4["vocab_size"], MB, SEQ, seed=3 + r))
-                   for r in range(world)]
         acc_l = torch.zeros(steps, device=dev)
         acc_n = torch.zeros(steps, device=dev)
         for s in range(steps):
             tot = torch.zeros((), device=dev)
-            for xb, yb in batches:
-                lb = m1(xb, yb, grad_scale=o1.scale)
+            for r in range(world):
+                xh, yh = batch(s, r)
+                lb = m1(xh.to(dev, non_blocking=True), yh.to(dev, non_blocking=True), grad_scale=o1.scale)
                 o1.backward(lb / world)
                 tot += lb.detach() / world
             st = o1.step(6e-4)
@@ -602,6 +678,7 @@ def curve_check(args, rank, world, local_rank, dev):
         out["grad_norm_step1"] = {"dp": our_norms[0], "accumulation": nref[0],
                                   "rel": abs(our_norms[0] - nref[0]) / max(abs(nref[0]), 1e-30)}
         del m1, o1
+        gc.collect()
         torch.cuda.empty_cache()
         if gold:
             g = gold["losses"][:steps]
@@ -619,6 +696,159 @@ def curve_check(args, rank, world, local_rank, dev):
     elif rank == 0:
         out["against"] = "none (no golden curve for this accumulation count)"
     return out
+
+
+# ---------------------------------------------------------------- config 5: window MLP
+WMLP = dict(R=500_000, F=16, window=64, B=32768, hidden=512, hidden2=256)
+WMLP_WORKLOAD = ("fxgpu window MLP (BASELINE config 5): per-GPU batch 32768, window 64 x 16 features -> "
+                 "1024 -> 512 (+bias, GELU) -> 256 (GELU) -> 1, MSE, fp16 + fp32-master FlatAdamW lr 1e-3")
+WMLP_FLOP = 94.6e9  # per 32768-sample step: L1 fwd + dW, L2 / L3 fwd + dX + dW
+
+
+def cpu_baseline_wmlp(steps=3, warmup=1, rows=4096):
+    """The reference window model's dense path (forward_dense, fp32) with
+    autograd and an AdamW step on the host cores, on `rows` samples per step."""
+    import torch
+    from fxgpu.model import WindowMLP
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(4)
+    xb = torch.randn(rows, WMLP["window"] * WMLP["F"], generator=g)
+    tgt = torch.randn(rows, 1, generator=g)
+    torch.manual_seed(4)
+    m = WindowMLP(WMLP["F"], WMLP["window"], hidden=WMLP["hidden"], hidden2=WMLP["hidden2"],
+                  master=True, act="gelu", dtype=torch.float32)
+    opt = torch.optim.AdamW(m.parameters(), lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        opt.zero_grad(set_to_none=True)
+        loss = ((m.forward_dense(xb) - tgt) ** 2).mean()
+        loss.backward()
+        opt.step()
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    v = rows / statistics.mean(times)
+    return {"value": v, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} samples per step, {steps} timed steps after {warmup} warm-up (fp32 dense "
+                      f"trunk of the reference WindowMLP, ml/fxgpu/model.py forward_dense, + torch AdamW)"}
+
+
+def run_wmlp(args, rank, world, local_rank):
+    """Config 5 at N GPUs: each rank trains on its own 32768-sample batch
+    (index seed 4 + rank) of one shared 500K x 16 fp16 series; the flat fp32
+    gradient is reduced by fxb200.ddp.DataParallel (the model has no blocks:
+    one reduction from the optimizer's pre-step hook) or ZeRO-1; the whole step
+    (gather, 3 GEMMs forward, 5 backward, reduction, FlatAdamW) is one
+    replayed CUDA graph."""
+    import torch
+    import torch.distributed as dist
+    from fxb200 import _lib
+    from fxgpu import WindowMLP
+    from fxlm import FlatAdamW, GraphedFunction
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.load()
+    R, Fe, Wn, Bsz = WMLP["R"], WMLP["F"], WMLP["window"], WMLP["B"]
+    g = torch.Generator(device=dev).manual_seed(4)
+    X16 = torch.randn(R, Fe, device=dev, generator=g).half()
+    gi = torch.Generator().manual_seed(4 + rank)
+    idx_host = torch.randint(0, R - Wn + 1, (Bsz,), generator=gi, dtype=torch.int32).pin_memory()
+    tgt_host = torch.randn(Bsz, 1, generator=gi).pin_memory()
+    idx, tgt = idx_host.to(dev), tgt_host.to(dev)
+    torch.manual_seed(4)
+    m = WindowMLP(Fe, Wn, hidden=WMLP["hidden"], hidden2=WMLP["hidden2"], master=True, act="gelu",
+                  dtype=torch.float16).to(dev)
+    opt = FlatAdamW(m, lr=1e-3, init_scale=1024.0, param_dtype=torch.float16)
+    opt.lr_dev = torch.full((), 1e-3, device=dev)
+    if world > 1 and args.zero:
+        from fxb200.zero import ShardedDataParallel
+        ShardedDataParallel(m, opt)
+    elif world > 1:
+        from fxb200.ddp import DataParallel
+        DataParallel(m, opt)
+
+    def train_step(ix, t):
+        loss = ((m(X16, ix).float() - t) ** 2).mean()
+        opt.backward(loss)
+        opt.step()
+        opt.zero_grad()
+        return loss.detach()
+
+    graphed = GraphedFunction(train_step, idx, tgt, warmup=max(3, args.warmup))
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    torch.cuda.synchronize()
+    barrier()
+    clk = ClockSampler(local_rank)
+    clk.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss = graphed(None, None)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    barrier()
+    t_ms = max_over_ranks(e0.elapsed_time(e1))
+    samples = world * Bsz * args.steps
+    value = samples / (t_ms / 1e3)
+    # end to end: the batch (indices, targets) from pinned host memory every
+    # step, the loss read back every step (synchronously: a 4-byte copy)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    last = None
+    for _ in range(args.steps):
+        loss = graphed(idx_host.to(dev, non_blocking=True), tgt_host.to(dev, non_blocking=True))
+        last = float(loss)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    graphed.check()
+    launches = graphed.launches_per_call * args.steps
+    graphed.release()
+    if rank == 0:
+        peak, peak_src = _peaks(clocks)
+        achieved = WMLP_FLOP * world * args.steps / (t_ms / 1e3) / 1e12 / world
+        line = {"metric": "fxgpu window MLP train samples/s (BASELINE config 5)", "value": value,
+                "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "fp16", "data": "synthetic N(0,1) series and targets (seed 4)",
+                "config": {"workload": WMLP_WORKLOAD, "global_batch": Bsz * world,
+                           "parallelism": f"dp{world}" + ("-zero1" if args.zero and world > 1 else ""),
+                           "step": "CUDA graph replay (fxlm.GraphedFunction)",
+                           "l2": "no flush: a step moves ~1 GB (> 126 MB L2)"},
+                "e2e": {"value": samples / (e2e_ms / 1e3), "unit": "samples/s",
+                        "h2d_bytes_per_step": Bsz * 4 + Bsz * 4, "d2h_bytes_per_step": 4,
+                        "last_loss": last},
+                "gpu_launches": launches,
+                "roofline": {"bound": "tensor", "kernel": "whole step (3 GEMMs fwd, 5 bwd, gather, FlatAdamW)",
+                             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                             "traffic": None, "peak_source": peak_src,
+                             "flops_per_step": WMLP_FLOP},
+                "clocks": clocks, "final_loss": last}
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_baseline_wmlp()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------- our arm
@@ -820,6 +1050,8 @@ def run_ours(args, rank, world, local_rank):
             line["attn"] = attn
         if curve is not None:
             line["curve_check"] = curve
+        if world == 1 and not args.no_kernels:
+            line["kernels"] = kernel_rooflines()
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
@@ -836,8 +1068,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["gpt", "wmlp"], default="gpt",
+                    help="gpt: BASELINE config 4 (default); wmlp: config 5, the window MLP")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-attn", action="store_true", help="skip the attention microbench")
+    ap.add_argument("--no-kernels", action="store_true",
+                    help="skip the per-kernel roofline entries (N = 1)")
     ap.add_argument("--no-graph", action="store_true",
                     help="run the step eagerly instead of replaying a captured CUDA graph")
     ap.add_argument("--no-zero", dest="zero", action="store_false",
@@ -860,6 +1096,8 @@ def main():
         return run_micro(args)
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload == "wmlp":
+        return run_wmlp(args, rank, world, local_rank)
     return run_ours(args, rank, world, local_rank)
 
 

@@ -260,7 +260,7 @@ def make_d768(ref_model):
     print("gpt_d768:", res)
 
 
-def make_curve_d768(ref_model, steps, acc, path):
+def make_curve_d768(ref_model, steps, acc, path, stream=False):
     """Config 4 loss curve: the reference model (torch path, fp32) trained for
     `steps` steps on fixed Zipf batches, the selftest's FlatAdamW oracle
     (torch AdamW lr 6e-4, betas (0.9, 0.95), wd 0.1 on ndim >= 2, clip 1.0).
@@ -276,12 +276,14 @@ def make_curve_d768(ref_model, steps, acc, path):
                             lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
     batches = [zipf(32768, 8, 1024, seed=3 + r) for r in range(acc)]
     rec = json.load(open(path)) if os.path.exists(path) else {}
-    key = f"acc{acc}"
+    key = f"acc{acc}" + ("_stream" if stream else "")
     losses, norms = [], []
     t0 = time.time()
     for s in range(steps):
         opt.zero_grad(set_to_none=True)
         tot = 0.0
+        if stream:  # a fresh batch every step: micro-batch r of step s has seed 1000 * (s + 1) + r
+            batches = [zipf(32768, 8, 1024, seed=1000 * (s + 1) + r) for r in range(acc)]
         for x, y in batches:
             loss = m(x, y)
             (loss / acc).backward()
@@ -291,8 +293,10 @@ def make_curve_d768(ref_model, steps, acc, path):
         losses.append(tot)
         norms.append(float(gn))
         if s % 5 == 4 or s == steps - 1:
+            data = (f"zipf seeds 1000*(s+1)+r, r < {acc}, a fresh batch every step" if stream else
+                    f"zipf seeds 3..{2 + acc} fixed every step")
             rec[key] = {"config": "V32768 L12 D768 H12 eps1e-6, init seed 3, micro-batches 8x1024 "
-                                  f"zipf seeds 3..{2 + acc} fixed every step, loss/acc, AdamW lr6e-4 "
+                                  f"{data}, loss/acc, AdamW lr6e-4 "
                                   "b(0.9,0.95) wd0.1 (ndim>=2) clip1.0, fp32 CPU",
                         "losses": losses, "grad_norms": norms, "steps_done": len(losses),
                         "cpu_seconds": time.time() - t0, "threads": torch.get_num_threads()}
@@ -334,12 +338,15 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--d768-curve", type=int, default=0, metavar="ACC",
                     help="only the config-4 loss curve with ACC micro-batches per step")
+    ap.add_argument("--stream", action="store_true",
+                    help="--d768-curve: a fresh batch every step instead of fixed micro-batches")
     ap.add_argument("--threads", type=int, default=os.cpu_count())
     args = ap.parse_args()
     torch.set_num_threads(args.threads)
     if args.d768_curve:
         ref_model, _, _ = _import_reference(args.ref)
-        make_curve_d768(ref_model, args.steps, args.d768_curve, os.path.join(HERE, "curve_d768.json"))
+        make_curve_d768(ref_model, args.steps, args.d768_curve, os.path.join(HERE, "curve_d768.json"),
+                        stream=args.stream)
         return
     make_prepare_bytes(args.ref)
     if args.only_prepare_bytes:

@@ -162,3 +162,87 @@ def test_dp_rank_failure_surfaces_as_error():
     assert res[1][0] == "error" and "simulated" in res[1][1]
     status, msg = res[0]
     assert status == "error", "survivor should see a collective error, not hang"
+
+
+# ------------------------------------------------------------------ config 5 (window MLP)
+class _WindowMLPLike(nn.Module):
+    """The window model's parameter layout (W1, b1, W2, b2, W3, b3) and
+    gradient contract: weight gradients written into the flat buffer inside
+    backward, bias gradients arriving in p.grad (folded at step). It has no
+    `blocks`, so data parallelism reduces the whole flat gradient from the
+    optimizer's pre-step hook."""
+
+    def __init__(self, K=24, H1=16, H2=8):
+        super().__init__()
+        self.W1 = nn.Parameter(torch.randn(H1, K) * 0.1)
+        self.b1 = nn.Parameter(torch.randn(H1) * 0.1)
+        self.W2 = nn.Parameter(torch.randn(H2, H1) * 0.1)
+        self.b2 = nn.Parameter(torch.randn(H2) * 0.1)
+        self.W3 = nn.Parameter(torch.randn(1, H2) * 0.1)
+        self.b3 = nn.Parameter(torch.zeros(1))
+
+    def forward(self, xb, tgt):
+        h = torch.nn.functional.gelu(_FlatLinearFn.apply(xb, self.W1) + self.b1, approximate="tanh")
+        h = torch.nn.functional.gelu(_FlatLinearFn.apply(h, self.W2) + self.b2, approximate="tanh")
+        y = _FlatLinearFn.apply(h, self.W3) + self.b3
+        return ((y - tgt) ** 2).mean()
+
+
+def _wmlp_worker(rank, world, port, batches, out_q, zero):
+    import sys
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(here, "radeon-igpu-forge_b200"))
+    from fxb200.ddp import DataParallel
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    try:
+        torch.manual_seed(0)
+        m = _WindowMLPLike()
+        opt = _FlatOpt(m)
+        dp = DataParallel(m, opt)
+        assert not dp.buckets and dp._rest == [(0, opt.numel)]  # one pre-step range
+        m(*batches[rank]).backward()
+        opt.step()
+        out_q.put((rank, "ok", opt.grad.clone()))
+    except Exception as e:
+        out_q.put((rank, "error", repr(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_window_mlp_dp_equals_accumulation():
+    """Config 5 data parallelism: two gloo ranks with different batches of the
+    window model end with the mean gradient, i.e. the single-process
+    accumulation over both batches."""
+    world = 2
+    torch.manual_seed(5)
+    batches = [(torch.randn(32, 24), torch.randn(32, 1)) for _ in range(world)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_wmlp_worker, args=(r, world, port, batches, q, False))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, status, payload = q.get(timeout=120)
+        res[r] = (status, payload)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    torch.manual_seed(0)
+    m = _WindowMLPLike()
+    opt = _FlatOpt(m)
+    for xb, tb in batches:
+        (m(xb, tb) / world).backward()
+    opt.fold()
+    for r in range(world):
+        status, g = res[r]
+        assert status == "ok", g
+        assert torch.allclose(g, opt.grad, atol=1e-6, rtol=1e-5), (g - opt.grad).abs().max()

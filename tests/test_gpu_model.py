@@ -319,6 +319,76 @@ def test_gpt_d768_first_step_loss(dev):
     assert abs(gn - ref["grad_norm"]) <= 2e-2 * ref["grad_norm"], (gn, ref["grad_norm"])
 
 
+def _cfg4_losses(dev, steps, batch_of_step, param_dtype, torch_path=False):
+    """Losses and gradient norms of `steps` config-4 training steps from the
+    reference init (seed 3) with FlatAdamW (lr 6e-4, betas (0.9, 0.95), wd 0.1,
+    clip 1.0); torch_path runs the reference's own PyTorch path of the model
+    (sdpa, torch RMSNorm / CE / linears) instead of the fused kernels."""
+    from fxlm import GPT, GPTConfig, FlatAdamW
+    cfg = dict(vocab_size=32768, seq_len=1024, n_layer=12, n_head=12, d_model=768, eps=1e-6)
+    if torch_path:
+        cfg.update(attn_impl="sdpa", norm_impl="torch", ce_impl="torch", linear_impl="torch")
+    torch.manual_seed(3)
+    m = GPT(GPTConfig(**cfg)).to(dev)
+    opt = FlatAdamW(m, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_grad_norm=1.0,
+                    init_scale=1.0, param_dtype=param_dtype)
+    L, N = torch.zeros(steps, device=dev), torch.zeros(steps, device=dev)
+    for s in range(steps):
+        x, y = batch_of_step(s)
+        loss = m(x.to(dev), y.to(dev), grad_scale=opt.scale)
+        opt.backward(loss)
+        st = opt.step(6e-4)
+        opt.zero_grad()
+        L[s], N[s] = loss.detach(), st["grad_norm"]
+    out = L.cpu().tolist(), N.cpu().tolist()
+    del m, opt
+    torch.cuda.empty_cache()
+    return out
+
+
+def test_config4_spike_fp32_matches_torch_path(dev):
+    """Config 4 on its fixed batch spikes at step 3 (loss 14.0); past the
+    spike the trajectory depends on fp32 summation order, so the reference's
+    CPU curve cannot be tracked there by any implementation (the reference's
+    own PyTorch path in fp32 on this GPU lands at 13.57 at step 4, the CPU run
+    at 8.11). Through the spike, the fused kernels in fp32 mode follow that
+    PyTorch path on the same device: losses within 1e-4 and gradient norms
+    within 1e-3 for the first 5 steps, and the first 4 losses within 1e-4 of
+    the reference's CPU curve."""
+    from fxb200.data import zipf_tokens
+    torch.backends.cuda.matmul.allow_tf32 = False
+    x, y = zipf_tokens(32768, 8, 1024, seed=3)
+    fixed = lambda s: (x, y)  # noqa: E731
+    lf, nf = _cfg4_losses(dev, 5, fixed, torch.float32)
+    lt, nt = _cfg4_losses(dev, 5, fixed, torch.float32, torch_path=True)
+    for s in range(5):
+        assert abs(lf[s] - lt[s]) <= 1e-4 * lt[s], (s, lf, lt)
+        assert abs(nf[s] - nt[s]) <= 1e-3 * nt[s], (s, nf, nt)
+    with open(os.path.join(GOLD, "curve_d768.json")) as f:
+        ref = json.load(f)["acc1"]["losses"]
+    for s in range(4):
+        assert abs(lf[s] - ref[s]) <= 1e-4 * ref[s], (s, lf[:4], ref[:4])
+
+
+def test_config4_curve_200_steps(dev):
+    """Config 4 (d768 x 12L, V32768, bf16 + fp32-master FlatAdamW), 200 steps
+    on a fresh Zipf batch every step: every step's loss within 2% of the
+    reference's own fp32 CPU curve on the same batches (golden
+    curve_d768.json "acc1_stream", from tests/golden/make_golden.py)."""
+    from fxb200.data import zipf_tokens
+    with open(os.path.join(GOLD, "curve_d768.json")) as f:
+        gold = json.load(f).get("acc1_stream")
+    if not gold:
+        pytest.skip("no acc1_stream curve in tests/golden/curve_d768.json")
+    ref = gold["losses"]
+    ours, _ = _cfg4_losses(dev, len(ref), lambda s: zipf_tokens(32768, 8, 1024, seed=1000 * (s + 1)),
+                           torch.bfloat16)
+    dev_rel = [abs(a - b) / abs(b) for a, b in zip(ours, ref)]
+    print(f"\nconfig-4 curve: {len(ref)} steps, max rel dev {max(dev_rel):.4f} "
+          f"(step {int(np.argmax(dev_rel))}), final {ours[-1]:.4f} vs {ref[-1]:.4f}")
+    assert max(dev_rel) < 0.02, f"max rel deviation {max(dev_rel):.4f} at step {int(np.argmax(dev_rel))}"
+
+
 def test_graphed_step_matches_eager(dev):
     """fxlm.GraphedStep (one captured training step, replayed) follows the
     eager step: same losses over a fresh batch per step and the same master
