@@ -20,6 +20,8 @@
 // is bounded (FXB_DERR_ATTN_WAIT); after an expired wait a thread keeps
 // stepping through its loop without work so that named barriers are always
 // met by every participant.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -453,6 +455,364 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   tc_fence_before();
   __syncthreads();
   if (warp == kFwdWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================ forward, head dim 64: two query tiles per CTA
+// One work item is a pair of query tiles (256 query rows) of one batch*head;
+// persistent CTAs walk the items heaviest first (causal: the last pairs see
+// the most key tiles). Both tiles share one K/V stream (each K/V tile is
+// loaded once for 256 rows).
+//
+// Warp roles (352 threads): warps 0-3 softmax group 0 (query tile 2i),
+// warps 4-7 softmax group 1 (query tile 2i+1), warps 8 and 9 the MMA issuers
+// of groups 0 and 1 (one issuing thread per group, so that neither group's
+// products wait for the other group's softmax), warp 10 TMA.
+// A softmax thread owns one query row: TMEM lane quarter (warp & 3) gives it
+// row quarter*32 + lane of its group's S, so the row maximum and sum need no
+// exchange between threads. Tensor memory (512 columns):
+//   S0 [0,128)  S1 [128,256)   fp32 scores of the current key tile
+//   P0 [256,320) P1 [320,384)  probabilities, 16-bit pairs (A operand of P.V)
+//   O0 [384,448) O1 [448,512)  fp32 output accumulators
+// A softmax thread loads its whole row of S from tensor memory once (four
+// 32-column loads, one wait); with S and P in separate columns the group's
+// next S = Q K^T is issued as soon as the row is in registers, while the
+// exponentials run, the P columns are written and P.V runs. The MMA issue order per key tile j is S0(j+1), P0 V(j),
+// S1(j+1), P1 V(j): the two groups drift half a tile apart and keep the
+// tensor core and the exponential units busy in turn. O uses the same lazy
+// rescaling as attn_fwd_kernel (only when a row maximum grows by more than
+// 2^8), done by the owning thread after the group's previous P.V completed.
+constexpr int kFwd2Threads = 352;
+constexpr int kFwd2WarpMma = 8, kFwd2WarpTma = 10;  // warps 8, 9: MMA issuers of groups 0, 1
+constexpr int kFwd2KS = 4;                // K/V ring stages
+constexpr int kFwd2Tile = TILE * 64 * 2;  // one [128][64] 16-bit tile (16 KB)
+
+template <int FMT>
+__global__ void __launch_bounds__(kFwd2Threads, 1)
+attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                 const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using T16 = typename std::conditional<FMT == 1, __nv_bfloat16, __half>::type;
+  constexpr int KS = kFwd2KS;
+  constexpr int QB = kFwd2Tile;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base;            // [group][buffer] Q tiles
+  const uint32_t sK = sQ + 4 * QB;     // KS stages
+  const uint32_t sV = sK + KS * QB;    // KS stages
+  const uint32_t bars = sV + KS * QB;
+  auto q_full = [&](int g, int b) { return bars + 8u * (g * 2 + b); };
+  auto q_empty = [&](int g, int b) { return bars + 8u * (4 + g * 2 + b); };
+  auto k_full = [&](int s) { return bars + 8u * (8 + s); };
+  auto v_full = [&](int s) { return bars + 8u * (8 + KS + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (8 + 2 * KS + s); };
+  auto s_full = [&](int g) { return bars + 8u * (8 + 3 * KS + g); };
+  auto s_empty = [&](int g) { return bars + 8u * (10 + 3 * KS + g); };
+  auto p_full = [&](int g) { return bars + 8u * (12 + 3 * KS + g); };
+  auto p_empty = [&](int g) { return bars + 8u * (14 + 3 * KS + g); };  // = that group's P.V done
+  const uint32_t final_bar = bars + 8u * (16 + 3 * KS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (17 + 3 * KS));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = p.B * p.H;
+  const int npairs = (p.nqt + 1) / 2;
+  const int n_items = npairs * BH;
+  // item -> (pair, batch*head) and the key-tile counts of its two query tiles
+  // (0 for a tile past the end of the sequence)
+  auto item_coords = [&](int w, int& pi, int& bh, int* n_kv) {
+    const int t = w / BH;
+    bh = w - t * BH;
+    pi = p.causal ? (npairs - 1 - t) : t;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int qt = 2 * pi + g;
+      n_kv[g] = qt >= p.nqt ? 0 : (p.causal ? min(qt + 1, p.nkt) : p.nkt);
+    }
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(bars + 8u * i, 1);        // q_full
+      mbar_init(bars + 8u * (4 + i), 1);  // q_empty
+    }
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(kv_empty(s), 2);  // both groups' issuers
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full(g), 1);
+      mbar_init(s_empty(g), 128);  // the group's softmax threads
+      mbar_init(p_full(g), 128);
+      mbar_init(p_empty(g), 1);
+    }
+    mbar_init(final_bar, 2);
+    fence_mbar_init();
+  }
+  if (warp == kFwd2WarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // q / k / v come from earlier kernels on the stream
+
+  if (warp == kFwd2WarpTma) {
+    // ------------------------------------------------ TMA producer (lane 0)
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      bool ok = true;
+      int t = 0;               // K/V tiles issued (all items)
+      int cq[2] = {0, 0};      // Q tiles loaded per group
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+        int pi, bh, n_kv[2];
+        item_coords(w, pi, bh, n_kv);
+        const int b = bh / p.H, h = bh - b * p.H;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          if (!n_kv[g]) continue;
+          const int qb = cq[g] & 1;
+          if (!mbar_wait(q_empty(g, qb), ((cq[g] >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          mbar_expect_tx(q_full(g, qb), QB);
+          tma_load_4d(sQ + (g * 2 + qb) * QB, &tmQ, q_full(g, qb), 0, (2 * pi + g) * TILE, h, b);
+          ++cq[g];
+        }
+        const int nk = max(n_kv[0], n_kv[1]);
+        for (int j = 0; j < nk && ok; ++j, ++t) {
+          const int st = t % KS;
+          if (!mbar_wait(kv_empty(st), ((t / KS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          mbar_expect_tx(k_full(st), QB);
+          tma_load_4d(sK + st * QB, &tmK, k_full(st), 0, j * TILE, h, b);
+          mbar_expect_tx(v_full(st), QB);
+          tma_load_4d(sV + st * QB, &tmV, v_full(st), 0, j * TILE, h, b);
+        }
+      }
+      // drain: every copy issued has landed before shared memory goes away
+      for (int g = 0; g < 2; ++g)
+        for (int i = (cq[g] > 2 ? cq[g] - 2 : 0); i < cq[g]; ++i)
+          mbar_wait(q_full(g, i & 1), (i >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      for (int u = (t > KS ? t - KS : 0); u < t; ++u) {
+        mbar_wait(k_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+        mbar_wait(v_full(u % KS), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kFwd2WarpMma || warp == kFwd2WarpMma + 1) {
+    // ------------------------------------------------ MMA issuer of group g (lane 0)
+    if (lane == 0) {
+      const int g = warp - kFwd2WarpMma;
+      constexpr uint32_t IS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);
+      constexpr uint32_t IPV = umma_idesc_f16(FMT, 0, 1, TILE, 64);
+      const uint32_t tSg = tmem + g * 128, tPg = tmem + 256 + g * 64, tOg = tmem + 384 + g * 64;
+      bool ok = true;
+      int t = 0;                    // K/V tiles of the stream (all items)
+      int cq = 0, cs = 0, cp = 0;   // this group's Q tiles, S products, P.V products
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+        int pi, bh, n_kv[2];
+        item_coords(w, pi, bh, n_kv);
+        const int nk = max(n_kv[0], n_kv[1]);
+        const int ng = n_kv[g];
+        const int qb = cq & 1;
+        if (ng && !mbar_wait(q_full(g, qb), (cq >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        const int t0 = t;
+        const uint64_t qd = kmajor_desc0(sQ + (g * 2 + qb) * QB);
+        // S = Q K_j^T into the group's S columns
+        auto issue_s = [&](int j) -> bool {
+          const int u = t0 + j, st = u % KS;
+          if (!mbar_wait(k_full(st), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+          if (!mbar_wait(s_empty(g), (cs & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+          tc_fence_after();
+          const uint64_t kd = kmajor_desc0(sK + st * QB);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tSg, desc_add(qd, kmajor_off(kk)), desc_add(kd, kmajor_off(kk)), IS, kk > 0);
+          umma_commit(s_full(g));
+          if (j + 1 == ng) umma_commit(q_empty(g, qb));  // the group's last S has read Q
+          ++cs;
+          return true;
+        };
+        // O (+)= P V_j, A = P from tensor memory (16 keys = 8 columns per MMA)
+        auto issue_pv = [&](int j) -> bool {
+          const int u = t0 + j, st = u % KS;
+          if (!mbar_wait(p_full(g), cp & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+          if (!mbar_wait(v_full(st), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+          tc_fence_after();
+          const uint64_t vd = mnmajor_desc0(sV + st * QB);
+#pragma unroll
+          for (int kk = 0; kk < TILE / 16; ++kk)
+            umma_f16_ta(tOg, tPg + kk * 8, desc_add(vd, mnmajor_off(kk)), IPV, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(p_empty(g));
+          ++cp;
+          return true;
+        };
+        if (ng && !issue_s(0)) { ok = false; break; }
+        for (int j = 0; j < nk && ok; ++j) {
+          if (j + 1 < ng && !issue_s(j + 1)) { ok = false; break; }
+          if (j < ng && !issue_pv(j)) { ok = false; break; }
+          // this group is done with K/V tile j. A group that does not use the
+          // tile first waits for it to land: the stage's previous release has
+          // then completed, so the arrival counts toward this use of the stage
+          const int u = t0 + j, st = u % KS;
+          if (j < ng) {
+            umma_commit(kv_empty(st));
+          } else {
+            if (!mbar_wait(k_full(st), (u / KS) & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+            mbar_arrive(kv_empty(st));
+          }
+        }
+        t += nk;
+        if (ng) ++cq;
+      }
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, p.err, FXB_DERR_ATTN_WAIT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ softmax: warps 0-3 group 0, 4-7 group 1
+    const int g = warp >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the group's tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + g * 128 + lane_off;
+    const uint32_t tP = tmem + 256 + g * 64 + lane_off;
+    const uint32_t tO = tmem + 384 + g * 64 + lane_off;
+    bool ok = true;
+    int cs = 0;  // tiles this group consumed (all items)
+    auto uwait = [&](uint32_t bar, uint32_t parity) -> bool {
+      const bool rr = mbar_wait(bar, parity, p.err, FXB_DERR_ATTN_WAIT);
+      return __all_sync(0xffffffffu, rr);
+    };
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+      int pi, bh, n_kv[2];
+      item_coords(w, pi, bh, n_kv);
+      const int nkv = n_kv[g];
+      if (!nkv || !ok) { cs += ok ? nkv : 0; continue; }
+      const int q0 = (2 * pi + g) * TILE;
+      const int q = q0 + r;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < nkv; ++j, ++cs) {
+        if (!uwait(s_full(g), cs & 1)) { ok = false; break; }
+        tc_fence_after();
+        const int kv0 = j * TILE;
+        const bool need_mask = (kv0 + TILE > p.T) || (p.causal && kv0 + TILE > q0 + 1);  // warp-uniform
+        // valid keys of this row in the tile: columns < lim (key < T, key <= q when causal)
+        const int lim = min(p.T, p.causal ? q + 1 : p.T) - kv0;
+        // masked scores read as -inf (64 columns from column c0)
+        auto mask64 = [&](uint32_t* v, int c0) {
+          if (need_mask) {
+            const int l64 = lim - c0;
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              if (i >= l64) v[i] = __float_as_uint(-INFINITY);
+          }
+        };
+        // the whole row of S in registers (one round trip to tensor memory)
+        uint32_t v[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, v + 32 * c);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(s_empty(g));  // S is in registers: the next S may overwrite it
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i >= lim) v[i] = __float_as_uint(-INFINITY);
+        }
+        float mv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mv[i] = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) mv[i & 7] = fmaxf(mv[i & 7], __uint_as_float(v[i]));
+        const float mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])),
+                               fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
+        const float m_new = fmaxf(m_ref, mx * p.scale_log2);
+        bool resc = false;
+        float alpha = 1.f;
+        if (j == 0) {
+          m_ref = m_new;  // O is overwritten by this item's first P.V
+        } else {
+          const bool need = m_new > m_ref + kRescaleLog2;
+          if (__any_sync(0xffffffffu, need)) {
+            resc = true;
+            if (need) {
+              alpha = ex2_ftz(m_ref - m_new);
+              m_ref = m_new;
+            }
+          }
+        }
+        const float m_off = (m_ref == -INFINITY) ? 0.f : m_ref;
+        // probabilities, packed in place (word i: keys 2i, 2i+1)
+        float rs[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rs[i] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float e0 = ex2_ftz(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, -m_off));
+          const float e1 = ex2_ftz(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, -m_off));
+          rs[(2 * i) & 7] += e0;
+          rs[(2 * i + 1) & 7] += e1;
+          v[i] = pack2<T16>(e0, e1);
+        }
+        // the group's previous P.V has completed: its P columns are free and O
+        // is stable for a rescale
+        if (j > 0 && !uwait(p_empty(g), (cs - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_st16(tP + c * 16, v + 16 * c);
+        if (resc) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t orr[16];
+            tmem_ld16(tO + c * 16, orr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 16; ++d) orr[d] = __float_as_uint(__uint_as_float(orr[d]) * alpha);
+            tmem_st16(tO + c * 16, orr);
+          }
+          l *= alpha;
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full(g));
+        l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+      }
+      if (!ok) continue;
+      // the item's last P.V has completed: O is final
+      if (!uwait(p_empty(g), (cs - 1) & 1)) { ok = false; continue; }
+      tc_fence_after();
+      const int b = bh / p.H, h = bh - b * p.H;
+      const float inv = 1.f / l;
+      T16* orow = static_cast<T16*>(p.o) + b * p.o_sb + (int64_t)q * p.o_st + h * p.o_sh;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t orr[16];
+        tmem_ld16(tO + c * 16, orr);  // warp-collective: every lane loads
+        tmem_wait_ld();
+        if (q < p.T) {
+#pragma unroll
+          for (int d = 0; d < 16; d += 8) {
+            float f[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(orr[d + i]) * inv;
+            *reinterpret_cast<uint4*>(orow + c * 16 + d) = pack8<T16>(f);
+          }
+        }
+      }
+      if (q < p.T) p.lse[(int64_t)bh * p.T + q] = (m_ref + log2f(l)) * kLn2;
+      tc_fence_before();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kFwd2WarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -1261,10 +1621,22 @@ int check_args(const fxb_attn_args* a, bool bwd) {
   return FXB_OK;
 }
 
+// FXB_ATTN_FWD=1 selects the one-tile forward at head dim 64 (A/B tests)
+bool fwd_one_tile() {
+  static const bool v = [] {
+    const char* e = getenv("FXB_ATTN_FWD");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 template <typename K> int set_smem(K k, int bytes) {
   return fxb::check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                          "attn smem attribute");
 }
+
+constexpr int fwd2_smem() { return (4 + 2 * kFwd2KS) * kFwd2Tile + 1024 + 512; }
+static_assert(fwd2_smem() <= 232448 && fwd2_smem() > kOneCtaPerSm, "two-tile forward shared memory");
 
 template <int DH, int FMT>
 int launch_fwd(const fxb_attn_args* a, cudaStream_t st) {
@@ -1283,10 +1655,23 @@ int launch_fwd(const fxb_attn_args* a, cudaStream_t st) {
   p.lse = a->lse;
   p.err = fxb::dev_error_ptr();
   if (!p.err) return FXB_ECUDA;
-  auto k = attn_fwd_kernel<DH, FMT>;
-  static bool once[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
+  if (DH == 64 && !fwd_one_tile()) {
+    // two query tiles per CTA (attn_fwd2_kernel)
+    auto k2 = attn_fwd2_kernel<FMT>;
+    static bool once2[64] = {false};
+    if (!once2[dev & 63]) {
+      if ((r = set_smem(k2, fwd2_smem()))) return r;
+      once2[dev & 63] = true;
+    }
+    const int64_t items = (int64_t)((p.nqt + 1) / 2) * a->B * a->H;
+    const int grid = (int)(items < fxb::num_sms() ? items : fxb::num_sms());
+    fxb::pdl_launch(k2, grid, kFwd2Threads, fwd2_smem(), st, mq, mk, mv, p);
+    return fxb::check_launch("attn_fwd2");
+  }
+  auto k = attn_fwd_kernel<DH, FMT>;
+  static bool once[64] = {false};
   if (!once[dev & 63]) {
     if ((r = set_smem(k, fwd_smem<DH>()))) return r;
     once[dev & 63] = true;

@@ -351,18 +351,21 @@ __global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ part, int npa
                                          T* __restrict__ dw, int accumulate) {
   pdl_trigger();
   pdl_wait();  // inputs come from the previous kernel on the stream
-  // block (32 columns) x (8 row groups); each row group sums a fixed stride of
-  // partials, then the 8 group sums are added in a fixed order (deterministic)
-  __shared__ float grp[8][33];
+  // block (32 columns) x (32 row groups); row group y sums partials y, y + 32,
+  // ... (four loads in flight), then the 32 group sums are added in a fixed
+  // order (deterministic). 32 row groups keep the chain short: the reduction
+  // is latency-bound (a few hundred partials of a few KB).
+  constexpr int RG = 32;
+  __shared__ float grp[RG][33];
   const int d = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
   if (d < D) {
     float s4[4] = {0.f, 0.f, 0.f, 0.f};  // four loads in flight, fixed assignment
     int b = threadIdx.y;
-    for (; b + 24 < nparts; b += 32)
+    for (; b + 3 * RG < nparts; b += 4 * RG)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) s4[u] += part[(int64_t)(b + 8 * u) * D + d];
-    for (; b < nparts; b += 8) s4[0] += part[(int64_t)b * D + d];
+      for (int u = 0; u < 4; ++u) s4[u] += part[(int64_t)(b + RG * u) * D + d];
+    for (; b < nparts; b += RG) s4[0] += part[(int64_t)b * D + d];
     s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
   }
   grp[threadIdx.y][threadIdx.x] = s;
@@ -370,7 +373,7 @@ __global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ part, int npa
   if (threadIdx.y == 0 && d < D) {
     float t = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) t += grp[k][threadIdx.x];
+    for (int k = 0; k < RG; ++k) t += grp[k][threadIdx.x];
     if (accumulate) t += to_f<T>(dw[d]);
     dw[d] = from_f<T>(t);
   }
@@ -480,7 +483,7 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
 #undef FXB_RMS_BWD
   int r = fxb::check_launch("rmsnorm_bwd");
   if (r) return r;
-  const dim3 g((D + 31) / 32), blk(32, 8);
+  const dim3 g((D + 31) / 32), blk(32, 32);
   switch (dw_dtype) {
     case FXB_DTYPE_BF16:
       fxb::pdl_launch(rmsnorm_dw_reduce_kernel<__nv_bfloat16>, g, blk, 0, st, ws, blocks, D, static_cast<__nv_bfloat16*>(dw), acc);
