@@ -484,6 +484,26 @@ def micro_results(micro, iters, only=None):
             out.append({"kernel": "linear_cross_entropy fwd+bwd (3 GEMMs + CE per chunk)",
                         "case": f"N{Nr} D{D} V{V} chunk_rows {ch} (logits chunk {ch * V * 2 / 1e6:.0f} MB)",
                         "ms": ms, "tflops": 3 * 2.0 * Nr * D * V / ms / 1e9})
+        # loss only: logits reduced on chip (fxb_linear_ce_loss) against the
+        # logits GEMM + CE kernel over a materialised logits buffer
+        from fxlm.cross_entropy import _ce_rows, _inv_nvalid
+        xd, Wd = x.detach(), W.detach()
+
+        def fused():
+            with torch.no_grad():
+                return linear_cross_entropy(xd, Wd, tg)
+        lg_buf = torch.empty(Nr, V, device=dev, dtype=bf)
+        rl = torch.empty(Nr, device=dev)
+
+        def unfused():
+            ops.gemm(xd, Wd, lg_buf)
+            _ce_rows(lg_buf, tg, None, rl, _inv_nvalid(tg, -100), -100)
+            return rl.sum()
+        for nm, fn in (("loss only, logits kept on chip (fxb_linear_ce_loss)", fused),
+                       ("loss only, logits GEMM + CE kernel over 537 MB of logits", unfused)):
+            ms = _time_ms(fn, it)
+            out.append({"kernel": "linear cross entropy " + nm, "case": f"N{Nr} D{D} V{V} bf16",
+                        "ms": ms, "tflops": 2.0 * Nr * D * V / ms / 1e9})
     if "wmlp" in which or "all" in which:
         # the fxgpu window MLP training step (gather-linear
         # 1024 -> 512 + bias + GELU, 512 -> 256 + GELU, 256 -> 1, MSE, FlatAdamW)

@@ -249,6 +249,24 @@ size_t fxb_gemm_workspace_size(void);
 int fxb_gemm_plan(int32_t M, int32_t N, int32_t K, int32_t epilogue, int32_t* pair,
                   int32_t* bn, int32_t* splits);
 
+/* Loss-only linear cross entropy with the logits kept on chip:
+ *   row_loss[r] = logsumexp_v(x_r . w_v) - x_r . w_{target[r]}
+ * (0 for rows whose target is ignore_index or outside [0, V)). The tcgen05
+ * GEMM of x (N, D) by w (V, D)^T reduces each accumulator tile in tensor
+ * memory to per-row (max, sum of exp) pairs and the target column's value
+ * (fp32, before any rounding), so no (N, V) logits are written; a second
+ * kernel merges the pairs per row. x, w bf16 or f16, 16-byte aligned, D and
+ * V multiples of 8; workspace of fxb_linear_ce_loss_workspace(N, V) bytes,
+ * 16-byte aligned. The caller sums row_loss (fixed order) and divides by the
+ * number of valid rows.
+ * Replaces the loss-only chunk loop of _linear_ce_loss_only
+ * (ml/fxlm/cross_entropy.py:170-183: mm to a logits chunk, then ce_fwd_grad
+ * without gradient, ml/fxlm/kernels/ce.hip:32). */
+size_t fxb_linear_ce_loss_workspace(int64_t N, int32_t V);
+int fxb_linear_ce_loss(int32_t dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                       const int64_t* target, float* row_loss, void* workspace, int64_t N,
+                       int32_t D, int32_t V, int64_t ignore_index, void* stream);
+
 /* ------------------------------------------------------------------ attention */
 
 typedef struct fxb_attn_args {

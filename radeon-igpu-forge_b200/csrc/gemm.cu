@@ -35,6 +35,8 @@ extern template int gemm_dispatch<EK_DACT16>(bool, int, int, bool, bool, const M
                                              const GemmParams&, int, cudaStream_t);
 extern template int gemm_dispatch<EK_F32>(bool, int, int, bool, bool, const Maps&,
                                           const GemmParams&, int, cudaStream_t);
+extern template int gemm_dispatch<EK_CESTAT>(bool, int, int, bool, bool, const Maps&,
+                                             const GemmParams&, int, cudaStream_t);
 }  // namespace gk
 }  // namespace fxb
 
@@ -268,6 +270,119 @@ int gemm_launch(const fxb_gemm_args* a, int epi, int force_splits, cudaStream_t 
 
 namespace fxb {
 int gemm_f32(const fxb_gemm_args* a, cudaStream_t st);  // csrc/gemm_f32.cu
+}
+
+// ---------------------------------------------------------------- loss-only linear CE
+namespace {
+// statistics pairs per row: two per tile of the narrowest tile width (128)
+int64_t ce_nstat(int V) { return 2 * (((int64_t)V + 127) / 128); }
+
+// row_loss[r] = logsumexp over the row's (max, sum) pairs - target logit, or
+// 0 for an ignored / out-of-range target. One warp per row; the pairs are
+// merged around the row maximum (fixed order: deterministic).
+__global__ void ce_stats_merge_kernel(const float2* __restrict__ stats, int nstat,
+                                      const float* __restrict__ tlogit,
+                                      const int64_t* __restrict__ target, float* __restrict__ row_loss,
+                                      int64_t rows, int V, int64_t ignore_index) {
+  pdl_trigger();
+  pdl_wait();  // statistics come from the GEMM before it on the stream
+  const int lane = threadIdx.x & 31;
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (r >= rows) return;
+  const float2* sr = stats + r * nstat;
+  float mx = -INFINITY;  // over the pairs that hold columns (sum > 0)
+  for (int i = lane; i < nstat; i += 32)
+    if (sr[i].y > 0.f) mx = fmaxf(mx, sr[i].x);
+  mx = warp_max(mx);
+  float s = 0.f;
+  for (int i = lane; i < nstat; i += 32) {
+    const float2 v = sr[i];
+    if (v.y > 0.f) s += v.y * expf(v.x - mx);
+  }
+  s = warp_sum(s);
+  if (lane == 0) {
+    const int64_t t = target[r];
+    const bool valid = t != ignore_index && t >= 0 && t < V;
+    row_loss[r] = valid ? (mx + logf(s)) - tlogit[r] : 0.f;
+  }
+}
+}  // namespace
+
+extern "C" size_t fxb_linear_ce_loss_workspace(int64_t N, int32_t V) {
+  if (N < 0 || V < 1) return 0;
+  return (size_t)(N * ce_nstat(V) * sizeof(float2) + ((N + 3) / 4) * 4 * sizeof(float));
+}
+
+extern "C" int fxb_linear_ce_loss(int32_t dtype, const void* x, int64_t ldx, const void* w,
+                                  int64_t ldw, const int64_t* target, float* row_loss,
+                                  void* workspace, int64_t N, int32_t D, int32_t V,
+                                  int64_t ignore_index, void* stream) {
+  using namespace fxb;
+  using namespace fxb::gk;
+  if (dtype != FXB_DTYPE_BF16 && dtype != FXB_DTYPE_F16)
+    return set_error(FXB_EUNSUPPORTED, "linear_ce_loss: dtype %d (bf16 or f16)", dtype);
+  if (N < 0 || D <= 0 || V <= 0 || D % 8 || V % 8 || N > INT32_MAX)
+    return set_error(FXB_EINVAL, "linear_ce_loss: bad shape N=%lld D=%d V=%d (D, V multiples of 8)",
+                     (long long)N, D, V);
+  if (!x || !w || !target || !row_loss || !workspace)
+    return set_error(FXB_EINVAL, "linear_ce_loss: NULL argument");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(workspace) || ldx < D || ldw < D || ldx % 8 || ldw % 8)
+    return set_error(FXB_EINVAL, "linear_ce_loss: x / w / workspace alignment or leading dimensions");
+  if (N == 0) return FXB_OK;
+  cudaStream_t st = as_stream(stream);
+  int* err = dev_error_ptr();
+  if (!err) return FXB_ECUDA;
+  const int sms = num_sms();
+  const int M = (int)N, NN = V, K = D;
+  Plan pl = plan(M, NN, K, FXB_EPI_STORE, false, sms, force_mode());
+  const int BN = pl.BN;
+  const int rows = pl.pair ? 256 : 128;
+  const int nstat = (int)ce_nstat(V);
+  float2* stats = static_cast<float2*>(workspace);
+  float* tlogit = reinterpret_cast<float*>(stats + (int64_t)N * nstat);
+  Maps mp;
+  int r = make_map(&mp.a, dtype, x, (uint64_t)K, (uint64_t)M, ldx, 64, 128);
+  if (r) return r;
+  r = make_map(&mp.b, dtype, w, (uint64_t)K, (uint64_t)NN, ldw, 64, (uint32_t)(pl.pair ? BN / 2 : BN));
+  if (r) return r;
+  // no output is stored; the descriptor slots point at the statistics buffer
+  r = make_out_map(&mp.c, FXB_DTYPE_F32, stats, 16, (uint64_t)N, 16);
+  if (r) return r;
+  mp.z = mp.c;
+  GemmParams p{};
+  p.M = M; p.N = NN; p.K = K;
+  p.tiles_m = (M + rows - 1) / rows;
+  p.tiles_n = (NN + BN - 1) / BN;
+  p.num_kb = (K + BK - 1) / BK;
+  p.splits = 1;
+  p.kb_per_split = p.num_kb;
+  p.tail_splits = 1;
+  p.tail_kb = p.num_kb;
+  p.full_units = p.tiles_m * p.tiles_n;
+  p.total_units = p.full_units;
+  p.epi = FXB_EPI_STORE;
+  p.c_dtype = FXB_DTYPE_F32;
+  p.alpha = 1.f;
+  p.err = err;
+  p.ce_stats = stats;
+  p.ce_nstat = nstat;
+  p.ce_target = target;
+  p.ce_tlogit = tlogit;
+  // pairs of tiles past the vocabulary end (nstat counts 128-column tiles)
+  // and rows whose target is not in range are never written by the GEMM
+  r = check_cuda(cudaMemsetAsync(stats, 0, (size_t)N * nstat * sizeof(float2), st), "linear_ce_loss: clear");
+  if (r) return r;
+  const long slots = pl.pair ? sms / 2 : sms;
+  const long used = p.total_units < slots ? p.total_units : slots;
+  const int grid = (int)(pl.pair ? 2 * used : used);
+  const int fmt = dtype == FXB_DTYPE_BF16 ? 1 : 0;
+  r = gemm_dispatch<EK_CESTAT>(pl.pair, BN, fmt, false, false, mp, p, grid, st);
+  if (r) return r;
+  const int64_t threads = N * 32;
+  pdl_launch(ce_stats_merge_kernel, (unsigned)((threads + 255) / 256), 256, 0, st,
+             static_cast<const float2*>(stats), nstat, static_cast<const float*>(tlogit), target,
+             row_loss, (int64_t)N, V, ignore_index);
+  return check_launch("ce_stats_merge");
 }
 
 // fp32 operands (the parity mode): validated here, computed by the SIMT kernel

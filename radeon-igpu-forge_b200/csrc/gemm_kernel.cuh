@@ -50,6 +50,7 @@ constexpr int EK_LIN16 = 0;   // 16-bit C: store / residual / bias / multiply
 constexpr int EK_ACT16 = 1;   // 16-bit C: GELU / bias+GELU / bias+SiLU / GELU+derivative (+ Z)
 constexpr int EK_DACT16 = 2;  // 16-bit C: dGELU / dSiLU (reads R)
 constexpr int EK_F32 = 3;     // fp32 C: store / residual / bias / accumulate
+constexpr int EK_CESTAT = 4;  // no C: per-row softmax statistics of the tile (loss-only linear-CE)
 
 // C element type of a kernel: fp32 for EK_F32, else the operand type
 template <int EK, int AB_FMT> struct CType { using T = __nv_bfloat16; };
@@ -57,6 +58,7 @@ template <> struct CType<EK_LIN16, 0> { using T = __half; };
 template <> struct CType<EK_ACT16, 0> { using T = __half; };
 template <> struct CType<EK_DACT16, 0> { using T = __half; };
 template <int AB_FMT> struct CType<EK_F32, AB_FMT> { using T = float; };
+template <int AB_FMT> struct CType<EK_CESTAT, AB_FMT> { using T = float; };
 
 struct GemmParams {
   int M, N, K;
@@ -77,6 +79,13 @@ struct GemmParams {
   int64_t ldz;
   const void* bias;
   int* err;
+  // EK_CESTAT: per (row, 64- or 128-column half tile) the pair (max, sum of
+  // exp(acc - max)) in ce_stats[row * ce_nstat + tile_n * 2 + half], and the
+  // accumulator at column ce_target[row] in ce_tlogit[row]
+  float2* ce_stats;
+  int ce_nstat;
+  const int64_t* ce_target;
+  float* ce_tlogit;
 };
 
 template <int BN> struct Cfg {
@@ -513,9 +522,53 @@ struct EpiWarp {
 
   // m_next / ntile0_next: this warp's row and first column in its next tile
   // (has_next false when there is none)
+  // EK_CESTAT: the warp's columns of the tile reduced to (max, sum of exp) per
+  // row with an online merge across its 32-column chunks, plus the target
+  // column's value when it falls in them; no C is written
+  FXB_DEV void run_stats(const GemmParams& p, int m, int ntile0, int half, uint32_t tbase) {
+    constexpr float kL2e = 1.4426950408889634f;
+    const int64_t tgt = (m < p.M) ? p.ce_target[m] : -1;
+    float rm = -INFINITY, rsum = 0.f;
+#pragma unroll 1
+    for (int cc = 0; cc < NCH; ++cc) {
+      const int c = half * NCH + cc;
+      const int n0 = ntile0 + c * 32;
+      if (n0 >= p.N) break;  // warp-uniform
+      uint32_t acc[32];
+      tmem_ld32(tbase + c * 32, acc);
+      tmem_wait_ld();
+      const int nv = min(32, p.N - n0);
+      float cm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nv) cm = fmaxf(cm, __uint_as_float(acc[i]));
+      const float nm = fmaxf(rm, cm);
+      const float nml = nm * kL2e;
+      float cs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nv) cs[i & 3] += exp2f(fmaf(__uint_as_float(acc[i]), kL2e, -nml));
+      rsum = rsum * exp2f((rm - nm) * kL2e) + ((cs[0] + cs[1]) + (cs[2] + cs[3]));
+      rm = nm;
+      if (tgt >= n0 && tgt < n0 + nv) {
+        float tv = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (tgt - n0 == i) tv = __uint_as_float(acc[i]);
+        p.ce_tlogit[m] = tv;
+      }
+    }
+    if (m < p.M)
+      p.ce_stats[(int64_t)m * p.ce_nstat + (ntile0 / BN) * 2 + half] = make_float2(rm, rsum);
+  }
+
   FXB_DEV void run(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmZ, int m,
                    int m0, int ntile0, int half, uint32_t tbase, uint32_t sbuf, int lane,
                    uint32_t& cnt, bool has_next, int m_next, int ntile0_next) {
+    if constexpr (EK == EK_CESTAT) {
+      run_stats(p, m, ntile0, half, tbase);
+      return;
+    }
     // unrolled by the prefetch ring's period (two chunks) only: the chunk
     // body is large, and the instruction cache is shared with the MMA warp
 #pragma unroll 1

@@ -92,6 +92,9 @@ SIGNATURES = {
     "fxb_gemm_workspace_size": (ctypes.c_size_t, []),
     "fxb_gemm_plan": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.POINTER(_i32),
                                      ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
+    "fxb_linear_ce_loss_workspace": (ctypes.c_size_t, [_i64, _i32]),
+    "fxb_linear_ce_loss": (ctypes.c_int, [_i32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i32, _i32,
+                                          _i64, _vp]),
     "fxb_attn_fwd": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
     "fxb_attn_bwd_workspace": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "fxb_attn_bwd": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),

@@ -159,13 +159,26 @@ class _LinearCE(torch.autograd.Function):
 
 
 def _linear_ce_loss_only(x, weight, target, ignore_index, chunk_rows):
-    """Grad-disabled path: no dx/dW/dlogits buffers (ml/fxlm/cross_entropy.py:170-183)."""
+    """Grad-disabled path: no dx/dW/dlogits buffers (ml/fxlm/cross_entropy.py:170-183).
+
+    16-bit inputs take fxb_linear_ce_loss: the logits never leave the chip
+    (the GEMM epilogue reduces each tile to per-row softmax statistics in
+    tensor memory and registers; chunk_rows does not apply). fp32 inputs keep
+    the chunk loop on the fp32 kernels."""
     N, D, V = _check_lin(x, weight, target)
     dev = x.device
-    if chunk_rows is None:
-        chunk_rows = _auto_chunk(N, D, V)
     inv_n = _inv_nvalid(target, ignore_index)
     row_loss = torch.empty(N, device=dev, dtype=torch.float32)
+    if x.dtype != torch.float32 and D % 8 == 0 and V % 8 == 0:
+        lib = _lib.load()
+        ws = torch.empty(max(16, int(lib.fxb_linear_ce_loss_workspace(N, V))), device=dev,
+                         dtype=torch.uint8)
+        _lib.call("fxb_linear_ce_loss", _lib.dtype_code(x.dtype), _lib.ptr(x), x.stride(0),
+                  _lib.ptr(weight), weight.stride(0), _lib.ptr(target), _lib.ptr(row_loss),
+                  _lib.ptr(ws), N, D, V, int(ignore_index), _lib.stream_ptr(dev))
+        return row_loss.sum() * inv_n
+    if chunk_rows is None:
+        chunk_rows = _auto_chunk(N, D, V)
     buf = torch.empty(min(chunk_rows, N), V, device=dev, dtype=x.dtype)
     for r0 in range(0, N, chunk_rows):
         r1 = min(r0 + chunk_rows, N)
