@@ -1096,9 +1096,13 @@ def main():
                     help="skip the per-kernel roofline entries (N = 1)")
     ap.add_argument("--no-graph", action="store_true",
                     help="run the step eagerly instead of replaying a captured CUDA graph")
-    ap.add_argument("--no-zero", dest="zero", action="store_false",
+    ap.add_argument("--no-zero", dest="zero", action="store_false", default=None,
                     help="N > 1: plain data parallelism (all-reduce, every rank updates every "
-                         "parameter) instead of the sharded update (fxb200.zero, the default)")
+                         "parameter) instead of the sharded update (fxb200.zero, the default "
+                         "for the gpt workload)")
+    ap.add_argument("--zero", dest="zero", action="store_true",
+                    help="N > 1: the sharded update (default for gpt; the window MLP's 0.66 M "
+                         "parameters are cheaper to all-reduce than to shard)")
     ap.add_argument("--micro", default=None,
                     help="per-kernel microbenchmarks instead of the step: all or a comma list "
                          "of gemm,attn,rmsnorm,ce,adamw,wmlp")
@@ -1109,6 +1113,8 @@ def main():
     ap.add_argument("--only", default=None,
                     help="gemm_layer: comma-separated substrings selecting shapes (profiling)")
     args = ap.parse_args()
+    if args.zero is None:
+        args.zero = args.workload == "gpt"
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
