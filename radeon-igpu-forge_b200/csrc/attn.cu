@@ -966,6 +966,21 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     __syncwarp();
     int armed = 0;
+    // LSE / delta of a query tile are read from global memory one tile ahead
+    // into registers, so that their latency passes while the producer waits
+    // for the stage to be freed instead of after it
+    float nl[4], nd[4];
+    auto prefetch = [&](int it) {
+      const int qq0 = (i0 + it) * TILE;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int q = qq0 + lane * 4 + i;
+        const bool v = q < p.T;
+        nl[i] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
+        nd[i] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
+      }
+    };
+    if (n_it > 0) prefetch(0);
     for (int it = 0; it < n_it; ++it) {
       const int st = it & 1;
       const int qq0 = (i0 + it) * TILE;
@@ -977,14 +992,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int qi = lane * 4 + i;
-        const int q = qq0 + qi;
-        const bool v = q < p.T;
-        lse_s[st * 128 + qi] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
-        del_s[st * 128 + qi] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
+        lse_s[st * 128 + lane * 4 + i] = nl[i];
+        del_s[st * 128 + lane * 4 + i] = nd[i];
       }
       mbar_arrive(qdo_full(st));
       armed = it + 1;
+      if (it + 1 < n_it) prefetch(it + 1);
     }
     if (lane == 0) {
       mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
