@@ -580,6 +580,20 @@ def kernel_rooflines(iters=10):
     return res
 
 
+def attach_dp(args, world, model, opt):
+    """N > 1: the data-parallel gradient exchange the run uses (ZeRO-1 or
+    all-reduce; fp32 or bf16 on the wire)."""
+    import torch
+    if world <= 1:
+        return None
+    cd = torch.bfloat16 if args.grad_bf16 else None
+    if args.zero:
+        from fxb200.zero import ShardedDataParallel
+        return ShardedDataParallel(model, opt, comm_dtype=cd)
+    from fxb200.ddp import DataParallel
+    return DataParallel(model, opt, comm_dtype=cd)
+
+
 # ---------------------------------------------------------------- loss-curve and data-parallel checks
 def _gpt_and_opt(dev):
     """Config-4 model from the reference init (seed 3) and its FlatAdamW."""
@@ -635,12 +649,7 @@ def curve_check(args, rank, world, local_rank, dev):
         return x.pin_memory(), y.pin_memory()
 
     model, opt = _gpt_and_opt(dev)
-    if world > 1 and args.zero:
-        from fxb200.zero import ShardedDataParallel
-        ShardedDataParallel(model, opt)
-    elif world > 1:
-        from fxb200.ddp import DataParallel
-        DataParallel(model, opt)
+    attach_dp(args, world, model, opt)
     losses = torch.zeros(steps, device=dev)
     norms = torch.zeros(steps, device=dev)
     for s in range(steps):
@@ -784,12 +793,7 @@ def run_wmlp(args, rank, world, local_rank):
                   dtype=torch.float16).to(dev)
     opt = FlatAdamW(m, lr=1e-3, init_scale=1024.0, param_dtype=torch.float16)
     opt.lr_dev = torch.full((), 1e-3, device=dev)
-    if world > 1 and args.zero:
-        from fxb200.zero import ShardedDataParallel
-        ShardedDataParallel(m, opt)
-    elif world > 1:
-        from fxb200.ddp import DataParallel
-        DataParallel(m, opt)
+    attach_dp(args, world, m, opt)
 
     def train_step(ix, t):
         loss = ((m(X16, ix).float() - t) ** 2).mean()
@@ -889,12 +893,7 @@ def run_ours(args, rank, world, local_rank):
     model = GPT(GPTConfig(**CFG4, eps=1e-6)).to(dev)
     opt = FlatAdamW(model, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
                     max_grad_norm=1.0, init_scale=1.0, param_dtype=torch.bfloat16)
-    if world > 1 and args.zero:
-        from fxb200.zero import ShardedDataParallel
-        ShardedDataParallel(model, opt)
-    elif world > 1:
-        from fxb200.ddp import DataParallel
-        DataParallel(model, opt)
+    attach_dp(args, world, model, opt)
     x_cpu, y_cpu = zipf_tokens(CFG4["vocab_size"], MB, SEQ, seed=3 + rank)
     x_host, y_host = x_cpu.pin_memory(), y_cpu.pin_memory()
     x_dev, y_dev = x_cpu.to(dev), y_cpu.to(dev)
@@ -1049,7 +1048,8 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic Zipf(1.1) tokens, seed 3 + rank; reference init (seed 3)",
             "config": {"workload": WORKLOAD, "global_batch": MB * world, "seq_len": SEQ,
-                       "parallelism": f"dp{world}" + ("-zero1" if args.zero and world > 1 else ""),
+                       "parallelism": f"dp{world}" + ("-zero1" if args.zero and world > 1 else "")
+                                      + ("-bf16grad" if args.grad_bf16 and world > 1 else ""),
                        "model": "GPT d768x12L tied, V32768",
                        "step": "CUDA graph replay" if graphed is not None else "eager",
                        "l2": "no flush: one step moves several GB (> 126 MB L2)"},
@@ -1100,6 +1100,8 @@ def main():
                     help="N > 1: plain data parallelism (all-reduce, every rank updates every "
                          "parameter) instead of the sharded update (fxb200.zero, the default "
                          "for the gpt workload)")
+    ap.add_argument("--grad-bf16", action="store_true",
+                    help="N > 1: gradient buckets cross NVLink as bf16 (half the bytes) instead of fp32")
     ap.add_argument("--zero", dest="zero", action="store_true",
                     help="N > 1: the sharded update (default for gpt; the window MLP's 0.66 M "
                          "parameters are cheaper to all-reduce than to shard)")

@@ -30,13 +30,22 @@ class DataParallel:
     loss = model(x, y, grad_scale=opt.scale); opt.backward(loss); opt.step(lr)
     """
 
-    def __init__(self, model, opt, process_group=None, block_attr="blocks", bucket_mb=None):
+    def __init__(self, model, opt, process_group=None, block_attr="blocks", bucket_mb=None,
+                 comm_dtype=None):
         if not dist.is_available() or not dist.is_initialized():
             raise RuntimeError("torch.distributed must be initialised before DataParallel")
         self.model, self.opt = model, opt
         self.pg = process_group
         self.world = dist.get_world_size(process_group)
         dev = opt.grad.device
+        # comm_dtype=torch.bfloat16: buckets cross NVLink as bf16 (half the bytes
+        # of the fp32 gradient; NCCL sums in bf16) and are widened back to fp32
+        # after the reduction; None keeps the fp32 gradient on the wire
+        if comm_dtype not in (None, torch.float32, torch.bfloat16):
+            raise ValueError(f"comm_dtype must be None, float32 or bfloat16, got {comm_dtype}")
+        self.comm_dtype = None if comm_dtype in (None, torch.float32) else comm_dtype
+        self._wire = (torch.empty(opt.grad.numel(), device=dev, dtype=self.comm_dtype)
+                      if self.comm_dtype is not None else None)
         self.stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
         # the hooks only enqueue work (events, NCCL on a side stream, stream
         # waits) and never read results on the host, so a step that runs
@@ -87,11 +96,23 @@ class DataParallel:
         view = self.opt.grad[start:end]
         if self.stream is None:
             # CPU / gloo (tests): gloo has no AVG, so SUM then divide after wait
+            if self._wire is not None:
+                wire = self._wire[start:end]
+                wire.copy_(view)
+                w = dist.all_reduce(wire, op=dist.ReduceOp.SUM, group=self.pg, async_op=True)
+                return [(w, view, True, wire)]
             return [(dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.pg, async_op=True), view, True)]
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(view.device))
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(ev)
+            if self._wire is not None:
+                wire = self._wire[start:end]
+                wire.copy_(view)
+                w = dist.all_reduce(wire, op=dist.ReduceOp.AVG, group=self.pg, async_op=True)
+                w.wait()          # the side stream waits for NCCL's stream (no host sync)
+                view.copy_(wire)  # then widens the reduced bucket back to fp32
+                return [(w, view, False)]
             return [(dist.all_reduce(view, op=dist.ReduceOp.AVG, group=self.pg, async_op=True), view, False)]
 
     def _launch(self, bidx):
@@ -109,8 +130,11 @@ class DataParallel:
                 self._launch(b)
         for s, e in self._rest:
             self._pending.extend(self._reduce_range(s, e))
-        for w, view, needs_div in self._pending:
+        for item in self._pending:
+            w, view, needs_div = item[:3]
             w.wait()
+            if len(item) > 3:  # CPU path with a narrower wire dtype
+                view.copy_(item[3])
             if needs_div:
                 view.div_(self.world)
         if self.stream is not None:

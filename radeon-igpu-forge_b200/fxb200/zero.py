@@ -62,8 +62,9 @@ class ShardedDataParallel(DataParallel):
     sdp.consolidate(); torch.save(opt.state_dict(), ...)
     """
 
-    def __init__(self, model, opt, process_group=None, block_attr="blocks"):
-        super().__init__(model, opt, process_group=process_group, block_attr=block_attr)
+    def __init__(self, model, opt, process_group=None, block_attr="blocks", comm_dtype=None):
+        super().__init__(model, opt, process_group=process_group, block_attr=block_attr,
+                         comm_dtype=comm_dtype)
         self.rank = dist.get_rank(process_group)
         self.shards, self.shard_size = shard_ranges(opt.numel, self.world)
         self._global = [dist.get_global_rank(process_group, r) if process_group is not None else r
@@ -90,10 +91,18 @@ class ShardedDataParallel(DataParallel):
         grad = self.opt.grad
         pieces = split_by_shard(start, end, self.shards)
         out = []
+        wire_all = self._wire
         if self.stream is None:
             # CPU / gloo (tests): SUM, then the owner divides after the wait
             for r, a, b in pieces:
                 view = grad[a:b]
+                if wire_all is not None:
+                    wire = wire_all[a:b]
+                    wire.copy_(view)
+                    w = dist.reduce(wire, dst=self._global[r], op=dist.ReduceOp.SUM, group=self.pg,
+                                    async_op=True)
+                    out.append((w, view, r == self.rank, wire) if r == self.rank else (w, view, False))
+                    continue
                 w = dist.reduce(view, dst=self._global[r], op=dist.ReduceOp.SUM, group=self.pg,
                                 async_op=True)
                 out.append((w, view, r == self.rank))
@@ -104,6 +113,18 @@ class ShardedDataParallel(DataParallel):
             self.stream.wait_event(ev)
             for r, a, b in pieces:
                 view = grad[a:b]
+                if wire_all is not None:
+                    # the bucket crosses NVLink as bf16; the owner widens its
+                    # reduced piece back into the fp32 gradient (stream-ordered)
+                    wire = wire_all[a:b]
+                    wire.copy_(view)
+                    w = dist.reduce(wire, dst=self._global[r], op=dist.ReduceOp.AVG, group=self.pg,
+                                    async_op=True)
+                    if r == self.rank:
+                        w.wait()  # the side stream waits for NCCL's stream (no host sync)
+                        view.copy_(wire)
+                    out.append((w, view, False))
+                    continue
                 w = dist.reduce(view, dst=self._global[r], op=dist.ReduceOp.AVG, group=self.pg,
                                 async_op=True)
                 out.append((w, view, False))

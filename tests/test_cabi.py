@@ -72,21 +72,30 @@ def test_einval_paths_without_gpu(lib):
     rc = lib.fxb_gemm(ctypes.byref(a), None)
     assert rc == -1 and "N=12" in _lib.last_error()
     # GEMM: unsupported operand dtype
-    a.dtype, a.N = 0, 16
+    a.dtype, a.N = 7, 16
     assert lib.fxb_gemm(ctypes.byref(a), None) == -2
+    # GEMM: fp32 (the parity-mode kernel) still needs its operands
+    a.dtype = 0
+    assert lib.fxb_gemm(ctypes.byref(a), None) == -1 and "NULL" in _lib.last_error()
     # attention: head_dim 96
     at = _lib.AttnArgs()
     at.dtype, at.B, at.T, at.H, at.D = 2, 1, 8, 1, 96
     assert lib.fxb_attn_fwd(ctypes.byref(at), None) == -1
     assert "head_dim 96" in _lib.last_error()
-    # attention backward: head_dim 128 not in this build
+    # attention backward at head_dim 128: checked like head_dim 64 (dout missing here)
     at.D = 128
     at.q = at.k = at.v = at.o = 256
     at.q_sb = at.q_st = at.q_sh = at.k_sb = at.k_st = at.k_sh = 8
     at.v_sb = at.v_st = at.v_sh = at.o_sb = at.o_st = at.o_sh = 8
     at.lse = 256
-    assert lib.fxb_attn_bwd(ctypes.byref(at), None) == -2
+    assert lib.fxb_attn_bwd(ctypes.byref(at), None) == -1
+    assert "dout" in _lib.last_error()
     assert lib.fxb_attn_bwd_workspace(2, 10, 3, 64) == (60 + 60 * 64) * 4
+    # head_dim 128: delta, then the transposed dQ accumulator (B*H, 128, T rounded up to 64)
+    assert lib.fxb_attn_bwd_workspace(2, 10, 3, 128) == (60 + 6 * 128 * 64) * 4
+    # loss-only linear cross entropy: D / V must be multiples of 8
+    rc = lib.fxb_linear_ce_loss(2, None, 16, None, 16, None, None, None, 4, 12, 64, -100, None)
+    assert rc == -1 and "D=12" in _lib.last_error()
 
 
 def test_wrapper_validation_is_host_side():
@@ -110,8 +119,12 @@ def test_wrapper_validation_is_host_side():
     x = torch.zeros(4, 8, dtype=torch.bfloat16, requires_grad=True)
     with pytest.raises(TypeError, match="cuda"):
         linear_cross_entropy(x, torch.zeros(16, 8, dtype=torch.bfloat16), torch.zeros(4, dtype=torch.int64))
-    with pytest.raises(TypeError, match="bf16 or fp16"):
-        linear_cross_entropy(x.float(), torch.zeros(16, 8), torch.zeros(4, dtype=torch.int64))
+    with pytest.raises(TypeError, match="share"):  # x and weight of different dtypes
+        linear_cross_entropy(x.float(), torch.zeros(16, 8, dtype=torch.bfloat16),
+                             torch.zeros(4, dtype=torch.int64))
+    with pytest.raises(TypeError, match="bf16, fp16 or fp32"):
+        linear_cross_entropy(x.double(), torch.zeros(16, 8, dtype=torch.float64),
+                             torch.zeros(4, dtype=torch.int64))
 
 
 def test_auto_chunk_bounds_logits_buffer():
