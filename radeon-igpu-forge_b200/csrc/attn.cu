@@ -33,6 +33,12 @@ constexpr int TILE = 128;
 constexpr int kFwdThreads = 576;  // forward: warps 0-15 softmax, 16 MMA, 17 TMA
 constexpr int kBwdThreads = 576;  // backward: warps 0-15 softmax / dS, 16 MMA, 17 TMA
 constexpr int kBwdWarpMma = 16, kBwdWarpTma = 17;
+// head-dim-64 backward: warps 0-15 softmax / dS (four per TMEM lane quarter),
+// 16-19 dQ flush (one per quarter), 20 MMA, 21 TMA; the register cap comes
+// from 768 threads (6 warps x 80 registers per sub-partition)
+constexpr int kBwd64Threads = 704;
+constexpr int kBwd64WarpFlush = 16, kBwd64WarpMma = 20, kBwd64WarpTma = 21;
+constexpr int kBwdQS = 3;  // head-dim-64 backward: Q / dO ring stages
 constexpr int kFwdWarpMma = 16, kFwdWarpTma = 17;
 // Forward pipeline depths: K/V ring stages and Q buffers (shared memory:
 // (QN + 2 KS) DH-wide tiles + exchange) and P buffers (tensor memory)
@@ -880,7 +886,7 @@ __global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, T16* __re
 
 
 template <int FMT>
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(768, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                 const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
@@ -891,27 +897,28 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
+  constexpr int QS = kBwdQS;         // Q / dO / LSE / delta ring stages
   const uint32_t sK = base;
   const uint32_t sV = sK + QB;
-  const uint32_t sQ = sV + QB;        // 2 stages
-  const uint32_t sDO = sQ + 2 * QB;   // 2 stages
-  const uint32_t sDS = sDO + 2 * QB;  // 2 buffers of dS^T [128 kv][128 q] 16-bit
-  const uint32_t sDQ = sDS + 65536;   // dQ staging: 8 warps x [32 rows][32 fp32], 128B-swizzled
-  const uint32_t sStat = sDQ + 32768; // lse2[2][128], delta[2][128] fp32
+  const uint32_t sQ = sV + QB;        // QS stages
+  const uint32_t sDO = sQ + QS * QB;  // QS stages
+  const uint32_t sDS = sDO + QS * QB; // 2 buffers of dS^T [128 kv][128 q] 16-bit
+  const uint32_t sDQ = sDS + 65536;   // dQ staging: 4 flush warps x 2 x [32 rows][16 fp32], 64B-swizzled
+  const uint32_t sStat = sDQ + 16384; // lse2[QS][128], delta[QS][128] fp32
   float* lse_s = reinterpret_cast<float*>(gbase + (sStat - base));
-  float* del_s = lse_s + 256;
-  const uint32_t bars = sStat + 2048;
+  float* del_s = lse_s + QS * 128;
+  const uint32_t bars = sStat + QS * 1024;
   const uint32_t kv_full = bars;
   auto qdo_full = [&](int s) { return bars + 8u * (1 + s); };
-  auto qdo_empty = [&](int s) { return bars + 8u * (3 + s); };
-  const uint32_t s_full = bars + 8u * 5;
-  const uint32_t s_empty = bars + 8u * 6;
-  const uint32_t ds_full = bars + 8u * 7;
-  const uint32_t dq_full = bars + 8u * 8;
-  const uint32_t dq_empty = bars + 8u * 9;
-  const uint32_t acc_full = bars + 8u * 10;
-  const uint32_t pt_free = bars + 8u * 11;  // dV of the tile has read P^T from tensor memory
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * 12);
+  auto qdo_empty = [&](int s) { return bars + 8u * (1 + QS + s); };
+  const uint32_t s_full = bars + 8u * (1 + 2 * QS);
+  const uint32_t s_empty = s_full + 8u;
+  const uint32_t ds_full = s_full + 16u;
+  const uint32_t dq_full = s_full + 24u;
+  const uint32_t dq_empty = s_full + 32u;
+  const uint32_t acc_full = s_full + 40u;
+  const uint32_t pt_free = s_full + 48u;  // dV of the tile has read P^T from tensor memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (pt_free + 8u - base));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // one CTA per (key tile, batch*head), numbered key tile major: with a causal
@@ -927,7 +934,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < QS; ++s) {
       mbar_init(qdo_full(s), 1 + 32);  // TMA bytes + the producer warp's LSE / delta stores
       mbar_init(qdo_empty(s), 1);
     }
@@ -935,12 +942,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     mbar_init(s_empty, 512);  // every softmax thread
     mbar_init(ds_full, 512);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 512);
+    mbar_init(dq_empty, 128);  // every dQ flush thread
     mbar_init(acc_full, 1);
     mbar_init(pt_free, 1);
     fence_mbar_init();
   }
-  if (warp == kBwdWarpMma) {
+  if (warp == kBwd64WarpMma) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -953,7 +960,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
   const uint32_t tPT = tmem + 448;  // P^T, 16-bit pairs (128 queries in 64 columns)
 
-  if (warp == kBwdWarpTma) {
+  if (warp == kBwd64WarpTma) {
     // ------------------------------------------------ producer: TMA (lane 0)
     // plus the query tile's LSE (log2 units) and delta, four queries per lane,
     // into the same double buffer as Q / dO
@@ -982,9 +989,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     };
     if (n_it > 0) prefetch(0);
     for (int it = 0; it < n_it; ++it) {
-      const int st = it & 1;
+      const int st = it % QS;
       const int qq0 = (i0 + it) * TILE;
-      if (!mbar_wait_warp(qdo_empty(st), ((it >> 1) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
+      if (!mbar_wait_warp(qdo_empty(st), ((it / QS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
       if (lane == 0) {
         mbar_expect_tx(qdo_full(st), 2 * QB);
         tma_load_4d(sQ + st * QB, &tmQ, qdo_full(st), 0, qq0, h, b);
@@ -1001,11 +1008,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     if (lane == 0) {
       mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
-      for (int it = (armed > 2 ? armed - 2 : 0); it < armed; ++it)
-        mbar_wait(qdo_full(it & 1), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      for (int it = (armed > QS ? armed - QS : 0); it < armed; ++it)
+        mbar_wait(qdo_full(it % QS), (it / QS) & 1, p.err, FXB_DERR_ATTN_WAIT);
     }
     __syncwarp();
-  } else if (warp == kBwdWarpMma) {
+  } else if (warp == kBwd64WarpMma) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t I_SS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);  // S^T, dP^T
@@ -1015,9 +1022,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       // S^T and dP^T of query tile `it` (once its Q / dO have landed and the
       // previous S^T / dP^T have been read out of tensor memory)
       auto issue_s = [&](int it) -> bool {
-        const int st = it & 1;
+        const int st = it % QS;
         const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
-        if (!mbar_wait(qdo_full(st), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(qdo_full(st), (it / QS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         tc_fence_after();
         const uint64_t kd = kmajor_desc0(sK), qd = kmajor_desc0(q_s);
@@ -1036,23 +1043,25 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         // the next tile's scores run on the tensor core while the softmax
         // warps turn this tile's scores into P^T and dS^T
         if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
-        const int st = it & 1;
+        const int st = it % QS;
         const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
         if (!mbar_wait(ds_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ds_s = sDS + (uint32_t)st * 32768u;
+        const uint32_t ds_s = sDS + (uint32_t)(it & 1) * 32768u;
         const uint64_t dsd = kmajor_desc0(ds_s);
         const uint64_t dom = mnmajor_desc0(do_s), qm = mnmajor_desc0(q_s);
 #pragma unroll
         for (int kk = 0; kk < TILE / 16; ++kk)  // A = P^T from tensor memory, 16 queries = 8 columns
           umma_f16_ta(tDV, tPT + kk * 8, desc_add(dom, mnmajor_off(kk)), I_KV, (it > 0 || kk > 0));
+        // completes when dV has read P^T and every earlier MMA (the previous
+        // tile's dQ, the last reader of the other dS^T buffer) is done
         umma_commit(pt_free);
 #pragma unroll
         for (int kk = 0; kk < TILE / 16; ++kk)
           umma_f16(tDK, desc_add(dsd, kmajor_off(kk)), desc_add(qm, mnmajor_off(kk)), I_KV,
                    (it > 0 || kk > 0));
         // Q / dO of this tile have no readers after dK (dQ reads dS and K): the
-        // producer may load the tile after next into the stage now
+        // producer may load tile it + QS into the stage now
         umma_commit(qdo_empty(st));
         if (!mbar_wait(dq_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
         tc_fence_after();
@@ -1066,68 +1075,91 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT);
     }
     __syncwarp();
+  } else if (warp >= kBwd64WarpFlush) {
+    // ------------------------------------------------ dQ flush warps 16..19
+    // warp w: TMEM lane quarter w & 3 = query rows quarter*32.. of the tile's
+    // dQ partial, all 64 head dims in two rounds of 32: tensor memory ->
+    // registers -> this warp's 4 KB staging (two 64B-swizzled [32 rows][16
+    // fp32] boxes) -> fp32 TMA add-reductions into the dQ accumulator (rows
+    // past T are clipped by the tensor map). The accumulator is released for
+    // the next tile's dQ MMA once both rounds have left tensor memory. The
+    // softmax warps never wait on this path.
+    const int quarter = warp & 3;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t stg = sDQ + (uint32_t)quarter * 4096u;
+    const int sw = (lane >> 1) & 3;
+    for (int it = 0; it < n_it; ++it) {
+      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int rd = 0; rd < 2; ++rd) {
+        uint32_t rr[32];
+        tmem_ld16(tDQ + lane_off + rd * 32, rr);
+        tmem_ld16(tDQ + lane_off + rd * 32 + 16, rr + 16);
+        tmem_wait_ld();
+        if (rd == 1) {
+          tc_fence_before();
+          mbar_arrive(dq_empty);  // the dQ partial has left tensor memory
+        }
+        if (lane == 0) bulk_wait_read0();  // the previous round's reductions have read the staging
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t row = stg + (uint32_t)c * 2048u + (uint32_t)lane * 64u;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            st_shared_v4(row + (uint32_t)((j ^ sw) << 4),
+                         make_uint4(rr[16 * c + 4 * j], rr[16 * c + 4 * j + 1], rr[16 * c + 4 * j + 2],
+                                    rr[16 * c + 4 * j + 3]));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            tma_reduce_add_3d(&tmDQ, stg + (uint32_t)c * 2048u, rd * 32 + c * 16,
+                              (i0 + it) * TILE + quarter * 32, bh);
+          bulk_commit();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all0();  // dQ reductions complete before the kernel ends
+    __syncwarp();
   } else {
     // ------------------------------------------------ softmax / dS warps 0..15
-    // warp w: TMEM lane quarter w & 3 (32 key rows for S^T / dP^T, 32 query
-    // rows for the dQ partial), column part w >> 2 (32 of the 128 queries of
-    // S^T / dP^T, 16 of the 64 head dims of dQ / dK / dV): four warps per
-    // sub-partition keep its pipes busy through the tensor-memory and
-    // barrier latencies of the chain
+    // warp w: TMEM lane quarter w & 3 (32 key rows of S^T / dP^T / dK / dV),
+    // column part w >> 2 (32 of the 128 queries of S^T / dP^T, 16 of the 64
+    // head dims of dK / dV): four warps per sub-partition keep its pipes busy
+    // through the tensor-memory and barrier latencies of the chain
     const int quarter = warp & 3, part = warp >> 2;
     const int r = quarter * 32 + lane;
     const int kv = kv0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int qc0 = part * 32;
     bool ok = true;
-    // dQ partial of query tile it (row r is query row quarter*32 + lane of the
-    // tile, head dims part*16..+16): tensor memory -> registers -> this warp's
-    // 64B-swizzled staging tile (32 rows x 64 bytes) -> asynchronous fp32 TMA
-    // add-reduction into the dQ accumulator (rows past T are clipped by the
-    // tensor map). Waiting for dq_full also means the tile's dV / dK / dQ MMAs
-    // no longer read P^T / dS^T in shared memory.
-    auto flush_dq = [&](int it) -> bool {
-      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) return false;
-      tc_fence_after();
-      const uint32_t stg = sDQ + (uint32_t)warp * 2048u;
-      if (lane == 0) bulk_wait_read0();  // the previous reduction has read the staging tile
-      __syncwarp();
-      const uint32_t row = stg + (uint32_t)lane * 64u;
-      uint32_t rr[16];
-      tmem_ld16(tDQ + lane_off + part * 16, rr);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        st_shared_v4(row + (uint32_t)((c ^ ((lane >> 1) & 3)) << 4),
-                     make_uint4(rr[4 * c], rr[4 * c + 1], rr[4 * c + 2], rr[4 * c + 3]));
-      tc_fence_before();
-      mbar_arrive(dq_empty);  // the dQ partial has left tensor memory
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_reduce_add_3d(&tmDQ, stg, part * 16, (i0 + it) * TILE + quarter * 32, bh);
-        bulk_commit();
-      }
-      return true;
-    };
-    // Software-pipelined: P^T / dS^T of tile it are computed in registers while
-    // the dV / dK / dQ MMAs of tile it-1 run; tile it's are stored (P^T to
-    // tensor memory, dS^T to a double-buffered shared tile), and tile it-1's
-    // dQ is flushed while tile it's dV / dK run.
-    // The query tile's LSE / delta were written to the double buffer by the
+    // P^T / dS^T of tile it are computed while the dV / dK / dQ MMAs of tile
+    // it-1 run, 16 queries at a time, each half stored as soon as it is done
+    // (P^T to tensor memory, dS^T to shared buffer it & 1) once the previous
+    // tile's dV has read P^T (pt_free, which also covers the dQ of tile it-2,
+    // the last reader of this dS^T buffer).
+    // The query tile's LSE / delta were written to the ring stage by the
     // producer warp before it arrived on qdo_full; waiting on that barrier here
     // makes them visible.
     for (int it = 0; it < n_it; ++it) {
       const int q0 = (i0 + it) * TILE;
-      const int sb = it & 1;
+      const int sb = it % QS;
       if (!ok) continue;
       // waits are made warp-uniform: the tensor-memory loads that follow are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(qdo_full(sb), (it >> 1) & 1, p.err, FXB_DERR_ATTN_WAIT)) ||
+      if (!__all_sync(0xffffffffu, mbar_wait(qdo_full(sb), (it / QS) & 1, p.err, FXB_DERR_ATTN_WAIT)) ||
           !__all_sync(0xffffffffu, mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
       tc_fence_after();
       const bool diag = p.causal && (q0 < kv0 + TILE);
-      uint32_t pw[16], dw[16];  // P^T and dS^T of this thread's 32 queries, 16-bit pairs
+      // tile-uniform: every (key, query) pair of the tile is kept (queries past
+      // T carry LSE = +inf, so their P and dS are zero without a mask)
+      const bool full = !diag && kv0 + TILE <= p.T;
+      uint8_t* ds = gbase + (sDS - base) + (it & 1) * 32768;
 #pragma unroll
-      for (int hq = 0; hq < 2; ++hq) {  // 16 queries at a time (register pressure)
+      for (int hq = 0; hq < 2; ++hq) {
         uint32_t sr[16], dr[16];
         tmem_ld16(tST + lane_off + qc0 + hq * 16, sr);
         tmem_ld16(tDPT + lane_off + qc0 + hq * 16, dr);
@@ -1136,46 +1168,59 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           tc_fence_before();
           mbar_arrive(s_empty);  // S^T / dP^T are in registers: the next tile's may overwrite them
         }
-        const float* ls = lse_s + sb * 128 + qc0 + hq * 16;
-        const float* dl = del_s + sb * 128 + qc0 + hq * 16;
+        // the 16 queries' LSE (log2 units) and delta: 16-byte shared loads
+        float ls[16], dl[16];
 #pragma unroll
-        for (int qc = 0; qc < 16; qc += 2) {
-          float pp[2], dd[2];
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            float e = ex2_ftz(fmaf(__uint_as_float(sr[qc + i]), p.scale_log2, -ls[qc + i]));
-            if (kv >= p.T || (diag && q0 + qc0 + hq * 16 + qc + i < kv)) e = 0.f;
-            pp[i] = e;
-            dd[i] = e * (__uint_as_float(dr[qc + i]) - dl[qc + i]);
-          }
-          pw[hq * 8 + (qc >> 1)] = pack2<T16>(pp[0], pp[1]);
-          dw[hq * 8 + (qc >> 1)] = pack2<T16>(dd[0], dd[1]);
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const float4 a = *reinterpret_cast<const float4*>(lse_s + sb * 128 + qc0 + hq * 16 + 4 * v4);
+          const float4 c = *reinterpret_cast<const float4*>(del_s + sb * 128 + qc0 + hq * 16 + 4 * v4);
+          ls[4 * v4] = a.x; ls[4 * v4 + 1] = a.y; ls[4 * v4 + 2] = a.z; ls[4 * v4 + 3] = a.w;
+          dl[4 * v4] = c.x; dl[4 * v4 + 1] = c.y; dl[4 * v4 + 2] = c.z; dl[4 * v4 + 3] = c.w;
         }
-      }
-      // P^T -> tensor memory once dV of the previous tile has read it; dS^T ->
-      // shared buffer it & 1 (its previous user, tile it-2, finished with its
-      // dQ, which the flush of the previous iteration waited for)
-      if (it > 0 && !__all_sync(0xffffffffu, mbar_wait(pt_free, (it - 1) & 1, p.err, FXB_DERR_ATTN_WAIT))) {
-        ok = false;
-        continue;
-      }
-      tc_fence_after();
-      tmem_st16(tPT + lane_off + part * 16, pw);
-      uint8_t* ds = gbase + (sDS - base) + (it & 1) * 32768;
+        uint32_t pw[8], dw[8];  // P^T and dS^T of 16 queries, 16-bit pairs
+        if (full) {
+          // no causal or key-row mask in this tile: exp2, subtract, multiply, pack
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        *reinterpret_cast<uint4*>(ds + sw128_offset(r, part * 4 + u)) =
-            make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+          for (int qc = 0; qc < 16; qc += 2) {
+            const float e0 = ex2_ftz(fmaf(__uint_as_float(sr[qc]), p.scale_log2, -ls[qc]));
+            const float e1 = ex2_ftz(fmaf(__uint_as_float(sr[qc + 1]), p.scale_log2, -ls[qc + 1]));
+            pw[qc >> 1] = pack2<T16>(e0, e1);
+            dw[qc >> 1] = pack2<T16>(e0 * (__uint_as_float(dr[qc]) - dl[qc]),
+                                     e1 * (__uint_as_float(dr[qc + 1]) - dl[qc + 1]));
+          }
+        } else {
+#pragma unroll
+          for (int qc = 0; qc < 16; qc += 2) {
+            float pp[2], dd[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              float e = ex2_ftz(fmaf(__uint_as_float(sr[qc + i]), p.scale_log2, -ls[qc + i]));
+              if (kv >= p.T || (diag && q0 + qc0 + hq * 16 + qc + i < kv)) e = 0.f;
+              pp[i] = e;
+              dd[i] = e * (__uint_as_float(dr[qc + i]) - dl[qc + i]);
+            }
+            pw[qc >> 1] = pack2<T16>(pp[0], pp[1]);
+            dw[qc >> 1] = pack2<T16>(dd[0], dd[1]);
+          }
+        }
+        if (hq == 0 && it > 0 &&
+            !__all_sync(0xffffffffu, mbar_wait(pt_free, (it - 1) & 1, p.err, FXB_DERR_ATTN_WAIT))) {
+          ok = false;
+          break;
+        }
+        if (hq == 0) tc_fence_after();
+        tmem_st8(tPT + lane_off + part * 16 + hq * 8, pw);
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          *reinterpret_cast<uint4*>(ds + sw128_offset(r, part * 4 + hq * 2 + u)) =
+              make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+      }
+      if (!ok) continue;
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
-      // the previous tile's dQ is flushed while this tile's dV / dK run
-      if (it > 0 && !flush_dq(it - 1)) { ok = false; continue; }
     }
-    if (ok && n_it > 0 && !flush_dq(n_it - 1)) ok = false;
-    if (lane == 0) bulk_wait_all0();  // dQ reductions complete before the kernel ends
-    __syncwarp();
     // final dK (scaled) and dV for key row kv, head dims part*16..+16
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT))) {
       tc_fence_after();
@@ -1203,7 +1248,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kBwdWarpMma) {
+  if (warp == kBwd64WarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -1225,7 +1270,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 // rounded up to 64, which the post kernel reads back in the caller's layout.
 // Shared memory: K, V (32 KB each), Q and dO double-buffered (16 KB tiles),
 // dS^T double-buffered (16 KB), dQ staging (16 warps x 2 KB), LSE / delta.
-// Warp roles as in the head-dim-64 kernel: warps 0-15 softmax / dS (warp w:
+// Warp roles: warps 0-15 softmax / dS (warp w:
 // key rows (w & 3)*32.., query columns (w >> 2)*16..; for dQ^T head-dim rows
 // (w & 3)*32.. and the same query columns; for the final dK / dV head dims
 // (w >> 2)*32..), warp 16 MMA issuer, warp 17 TMA producer.
@@ -1564,7 +1609,9 @@ template <int DH> constexpr int fwd_smem() {
   return fwd_smem_raw<DH>() > kOneCtaPerSm ? fwd_smem_raw<DH>() : kOneCtaPerSm;
 }
 static_assert(fwd_smem<64>() <= 232448 && fwd_smem<128>() <= 232448, "forward shared memory");
-constexpr int bwd_smem() { return 6 * TILE * 64 * 2 + 3 * 32768 + 2048 + 1024 + 256; }  // dS^T x2 + dQ staging
+// K, V, QS stages of Q and dO, 2 x dS^T, dQ staging, LSE / delta, align, barriers
+constexpr int bwd_smem() { return (2 + 2 * kBwdQS) * TILE * 64 * 2 + 2 * 32768 + 16384 + kBwdQS * 1024 + 1024 + 256; }
+static_assert(bwd_smem() <= 232448, "head-dim-64 backward shared memory");
 // K, V, Q x2, dO x2, dS^T x2, dQ^T staging, LSE / delta, barriers, alignment
 constexpr int bwd128_smem() { return 2 * kB128Tile + 4 * kB128QTile + 2 * 16384 + 32768 + 1024 + 256 + 1024; }
 static_assert(bwd128_smem() <= 232448 && bwd128_smem() > kOneCtaPerSm, "head-dim-128 backward shared memory");
@@ -1790,7 +1837,7 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
     once[dev & 63] = true;
   }
   dim3 grid((unsigned)(p.nkt * a->B * a->H));
-  fxb::pdl_launch(k, grid, kBwdThreads, bwd_smem(), st, mq, mk, mv, mdo, mdq, p);
+  fxb::pdl_launch(k, grid, kBwd64Threads, bwd_smem(), st, mq, mk, mv, mdo, mdq, p);
   if ((r = fxb::check_launch("attn_bwd"))) return r;
   const int64_t n = rows * (DH / 8);
   fxb::pdl_launch(attn_bwd_post_kernel<T16, DH>, (unsigned)((n + 255) / 256), 256, 0, st, 
