@@ -567,8 +567,8 @@ def kernel_rooflines(iters=10):
     for o in micro_results("attn,rmsnorm,ce,adamw", iters):
         k = o.get("kernel", "")
         if k.startswith("attn"):
-            for what, key, ms in (("attn_fwd_kernel", "fwd_tflops", o["fwd_ms"]),
-                                  ("attn_fwd_kernel + attn_bwd_kernel (+ prep, post)", "fwd_bwd_tflops",
+            for what, key, ms in (("attn_fwd2_kernel", "fwd_tflops", o["fwd_ms"]),
+                                  ("attn_fwd2_kernel + attn_bwd_kernel (+ prep, post)", "fwd_bwd_tflops",
                                    o["fwd_ms"] + o["bwd_ms"])):
                 a = o[key]
                 res.append({"kernel": what, "case": "BASELINE config 2: " + o["shape"], "bound": "tensor",

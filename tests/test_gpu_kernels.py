@@ -444,3 +444,103 @@ def test_device_error_word_clear(dev):
     from fxb200 import _lib
     torch.cuda.synchronize()
     assert _lib.device_error(clear=True) == 0
+
+
+# ------------------------------------------------------------------ config 3 at full size
+# RMSNorm over [65536, 768], the LM-head GEMM
+# [65536, 768] x [32768, 768]^T and cross-entropy over [65536, 32768] logits,
+# bf16, each with the plan the library picks for that shape (GEMM tile, split
+# and tail split; CE row path). Checked against fp32 torch on every row where
+# that is cheap and on seeded row samples where the fp32 reference would be
+# tens of GB.
+C3_N, C3_D, C3_V = 65536, 768, 32768
+
+
+def test_config3_rms_norm_full_shape(dev):
+    from fxlm.norm import rms_norm
+    torch.manual_seed(31)
+    x = (torch.randn(C3_N, C3_D, device=dev) * 3).to(torch.bfloat16)
+    w = (torch.randn(C3_D, device=dev) * 0.5 + 1).to(torch.bfloat16)
+    g = torch.randn(C3_N, C3_D, device=dev).to(torch.bfloat16)
+    xq, wq = x.clone().requires_grad_(), w.clone().requires_grad_()
+    xr, wr = x.float().requires_grad_(), w.float().requires_grad_()
+    xt, wt = x.clone().requires_grad_(), w.clone().requires_grad_()
+    y = rms_norm(xq, wq, 1e-6)
+    yr = F.rms_norm(xr, (C3_D,), wr, 1e-6)
+    yt = F.rms_norm(xt, (C3_D,), wt, 1e-6)
+    y.backward(g); yr.backward(g.float()); yt.backward(g)
+    for ours, ref, lp, nm in ((y, yr, yt, "y"), (xq.grad, xr.grad, xt.grad, "dx"),
+                              (wq.grad, wr.grad, wt.grad, "dw")):
+        ok, e, b = rule(ours, ref.detach(), lp)
+        assert ok, f"{nm}: err {e:.3e} vs torch-lowp {b:.3e}"
+
+
+def test_config3_head_gemms_full_shape(dev):
+    """logits = x W^T, dx = dlogits W and dW += dlogits^T x at the config-3
+    shapes through the head's own calls (fxb200.ops.linear_fwd / linear_dx /
+    linear_dw_into); 512 sampled logits rows and dx rows, 256 sampled dW rows
+    against fp32 matmuls of the same bf16 inputs."""
+    import ctypes
+    from fxb200 import _lib, ops
+    plans = []
+    for M, N, K, epi in ((C3_N, C3_V, C3_D, ops.EPI_STORE), (C3_N, C3_D, C3_V, ops.EPI_STORE),
+                         (C3_V, C3_D, C3_N, ops.EPI_ACCUM_F32)):
+        pair, bn, sp = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        _lib.call("fxb_gemm_plan", M, N, K, epi, ctypes.byref(pair), ctypes.byref(bn), ctypes.byref(sp))
+        plans.append((pair.value, bn.value, sp.value))
+    torch.manual_seed(32)
+    x = (torch.randn(C3_N, C3_D, device=dev)).to(torch.bfloat16)
+    W = (torch.randn(C3_V, C3_D, device=dev) * 0.02).to(torch.bfloat16)
+    logits = ops.linear_fwd(x, W)
+    rows = torch.randint(0, C3_N, (512,), device=dev, generator=torch.Generator(dev).manual_seed(7))
+    ref = x[rows].float() @ W.float().t()
+    err = (logits[rows].float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, f"logits rel err {err:.3e} (plan {plans[0]})"
+    del logits, ref
+    dl = (torch.randn(C3_N, C3_V, device=dev) * 1e-3).to(torch.bfloat16)
+    dx = ops.linear_dx(dl, W)
+    ref = dl[rows].float() @ W.float()
+    err = (dx[rows].float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, f"dx rel err {err:.3e} (plan {plans[1]})"
+    del dx, ref
+    dw = torch.zeros(C3_V, C3_D, device=dev, dtype=torch.float32)
+    ops.linear_dw_into(dl, x, dw)
+    vrows = torch.randint(0, C3_V, (256,), device=dev, generator=torch.Generator(dev).manual_seed(8))
+    ref = dl[:, vrows].float().t() @ x.float()
+    err = (dw[vrows] - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-3, f"dW rel err {err:.3e} (plan {plans[2]})"
+
+
+def test_config3_cross_entropy_full_shape(dev):
+    """Per-row losses of all 65536 rows against fp32 torch (in 4096-row
+    chunks), and the in-place gradient (softmax - onehot) / N on 256 sampled
+    rows, with ignored targets."""
+    from fxb200 import _lib
+    torch.manual_seed(33)
+    N, V = C3_N, C3_V
+    lg = (torch.randn(N, V, device=dev) * 4).to(torch.bfloat16)
+    tg = torch.randint(0, V, (N,), device=dev)
+    tg[::11] = -100
+    valid = tg >= 0
+    st = _lib.stream_ptr(dev)
+    mul = torch.full((), 1.0 / N, device=dev)
+    loss = torch.empty(N, device=dev)
+    buf = lg.clone()
+    _lib.call("fxb_ce_fwd_grad", _lib.dtype_code(torch.bfloat16), _lib.ptr(buf), V, _lib.ptr(tg),
+              _lib.ptr(buf), _lib.ptr(loss), _lib.ptr(mul), N, V, -100, st)
+    torch.cuda.synchronize()
+    worst = 0.0
+    for r0 in range(0, N, 4096):
+        sl = slice(r0, r0 + 4096)
+        ref = F.cross_entropy(lg[sl].float(), tg[sl].clamp(min=0), reduction="none")
+        ref = torch.where(valid[sl], ref, torch.zeros((), device=dev))
+        worst = max(worst, (loss[sl] - ref).abs().max().item())
+    assert worst <= 1e-4 * 20, f"per-row loss err {worst}"
+    rows = torch.randint(0, N, (256,), device=dev, generator=torch.Generator(dev).manual_seed(9))
+    p = torch.softmax(lg[rows].float(), dim=1)
+    vr = valid[rows]
+    p[vr.nonzero().squeeze(1), tg[rows][vr]] -= 1.0
+    gref = p * (vr.float() / N)[:, None]
+    err = (buf[rows].float() - gref).abs().max().item()
+    assert err <= 2e-2 * gref.abs().max().item(), err
+    assert not torch.isnan(buf[rows].float()).any()
