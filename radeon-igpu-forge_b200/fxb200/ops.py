@@ -5,6 +5,7 @@ Every function launches on torch's current stream, allocates outputs with
 torch (the library never allocates) and raises RuntimeError on failure.
 """
 import ctypes
+import os
 
 import torch
 
@@ -172,12 +173,50 @@ def param_grad_sink(p):
     return g
 
 
-def weight_grad(dy, x, W):
+# Weight-gradient GEMMs on a side stream. A block's backward has dX GEMMs on
+# its critical path and dW GEMMs that nothing in the block waits for; each
+# persistent GEMM leaves SMs idle in its first and last waves. Forking the
+# dW GEMMs onto a per-device side stream (when their inputs are ready) and
+# joining it at the end of the block's backward lets them fill those SMs.
+# The join happens while every input is still referenced, so the caching
+# allocator never reuses memory a side-stream GEMM still reads; the gradient
+# hooks of data parallelism and the optimizer run after the join. Inside a
+# CUDA-graph capture the fork and join become graph edges.
+# FXB_DW_STREAM=0 keeps everything on the current stream.
+_DW_STREAMS = {}
+
+
+def dw_side_stream(device):
+    """The side stream for weight-gradient GEMMs on `device`, made to wait
+    for all work queued so far on the current stream; None when disabled."""
+    if os.environ.get("FXB_DW_STREAM", "1") == "0" or device.type != "cuda":
+        return None
+    side = _DW_STREAMS.get(device.index)
+    if side is None:
+        side = torch.cuda.Stream(device=device)
+        _DW_STREAMS[device.index] = side
+    side.wait_stream(torch.cuda.current_stream(device))
+    return side
+
+
+def dw_join(side, device):
+    """The current stream waits for everything queued on `side`."""
+    if side is not None:
+        torch.cuda.current_stream(device).wait_stream(side)
+
+
+def weight_grad(dy, x, W, side=None):
     """dW for y = x W^T: accumulated into W's flat fp32 slot when W belongs to
-    a FlatAdamW (returns None), else returned as a tensor of W's dtype."""
+    a FlatAdamW (returns None), else returned as a tensor of W's dtype. With
+    `side` (from dw_side_stream), the accumulation is queued on that stream;
+    the caller joins it (dw_join) before the inputs can be freed."""
     sink = param_grad_sink(W)
     if sink is not None:
-        linear_dw_into(dy, x, sink.view(W.shape[0], W.shape[1]))
+        if side is not None:
+            with torch.cuda.stream(side):
+                linear_dw_into(dy, x, sink.view(W.shape[0], W.shape[1]))
+        else:
+            linear_dw_into(dy, x, sink.view(W.shape[0], W.shape[1]))
         return None
     tmp = torch.zeros(W.shape[0], W.shape[1], device=W.device, dtype=torch.float32)
     linear_dw_into(dy, x, tmp)

@@ -46,16 +46,24 @@ class _AttnBlock(torch.autograd.Function):
         dx1 = dx1.reshape(B * T, D)
         if not dx1.is_contiguous():
             dx1 = dx1.contiguous()
+        dev = dx1.device
+        # the weight gradients run on a side stream beside the dX chain: the
+        # fork is taken where their inputs are ready, and each dX GEMM is
+        # queued before its dW partner so that the critical path gets the SMs
+        side = ops.dw_side_stream(dev)                     # dx1, o ready
         do = ops.linear_dx(dx1, Wproj)                     # d(attn out)
-        gWproj = ops.weight_grad(dx1, o.view(B * T, D), Wproj) if ctx.needs_input_grad[3] else None
+        gWproj = ops.weight_grad(dx1, o.view(B * T, D), Wproj, side) if ctx.needs_input_grad[3] else None
         qkv5 = qkv.view(B, T, 3, H, D // H)
         dqkv = torch.empty_like(qkv)
         d5 = dqkv.view(B, T, 3, H, D // H)
         _attn_bwd(qkv5[:, :, 0], qkv5[:, :, 1], qkv5[:, :, 2], o, lse, do.view(B, T, H, D // H),
                   True, scale, d5[:, :, 0], d5[:, :, 1], d5[:, :, 2])
+        if side is not None:
+            side = ops.dw_side_stream(dev)                 # dqkv ready
         dh = ops.linear_dx(dqkv, Wqkv)
-        gWqkv = ops.weight_grad(dqkv, h, Wqkv) if ctx.needs_input_grad[2] else None
+        gWqkv = ops.weight_grad(dqkv, h, Wqkv, side) if ctx.needs_input_grad[2] else None
         dx, gln = rmsnorm_bwd(x2, ln_w, rstd, dh, dres=dx1, need_dw=ctx.needs_input_grad[1])
+        ops.dw_join(side, dev)
         return dx.view(B, T, D), gln, gWqkv, gWproj, None, None
 
 
@@ -87,12 +95,19 @@ class _MLPBlock(torch.autograd.Function):
         d2 = dy.reshape(B * T, D)
         if not d2.is_contiguous():
             d2 = d2.contiguous()
+        dev = d2.device
+        # the weight gradients run on a side stream beside the dX chain (see
+        # _AttnBlock.backward)
+        side = ops.dw_side_stream(dev)                     # d2, a ready
         dz = torch.empty_like(gz)
         ops.gemm(d2, W2, dz, b_trans=True, epilogue=ops.EPI_MUL, R=gz)   # (dy W2) * gelu'(z)
-        gW2 = ops.weight_grad(d2, a, W2) if ctx.needs_input_grad[3] else None
+        gW2 = ops.weight_grad(d2, a, W2, side) if ctx.needs_input_grad[3] else None
+        if side is not None:
+            side = ops.dw_side_stream(dev)                 # dz ready
         dh = ops.linear_dx(dz, W1)
-        gW1 = ops.weight_grad(dz, h, W1) if ctx.needs_input_grad[2] else None
+        gW1 = ops.weight_grad(dz, h, W1, side) if ctx.needs_input_grad[2] else None
         dx, gln = rmsnorm_bwd(x2, ln_w, rstd, dh, dres=d2, need_dw=ctx.needs_input_grad[1])
+        ops.dw_join(side, dev)
         return dx.view(B, T, D), gln, gW1, gW2, None
 
 

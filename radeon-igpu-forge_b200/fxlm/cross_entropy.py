@@ -130,8 +130,16 @@ class _LinearCE(torch.autograd.Function):
             dl = dl_buf[:r1 - r0]
             ops.gemm(xc, weight, dl)                          # logits chunk
             _ce_rows(dl, target[r0:r1], dl, row_loss[r0:r1], mul, ignore_index)  # in place
+            # dx and dW only read dl: dW runs on the weight-gradient side
+            # stream beside dx, joined before the next chunk overwrites dl
+            side = ops.dw_side_stream(dev)
             ops.gemm(dl, weight, dx[r0:r1], b_trans=True)     # dx chunk
-            ops.linear_dw_into(dl, xc, dW)                    # dW += dl^T x (fp32)
+            if side is not None:
+                with torch.cuda.stream(side):
+                    ops.linear_dw_into(dl, xc, dW)            # dW += dl^T x (fp32)
+                ops.dw_join(side, dev)
+            else:
+                ops.linear_dw_into(dl, xc, dW)
         ctx.save_for_backward(dx, dW)
         ctx.grad_scale = grad_scale
         ctx.weight = weight
