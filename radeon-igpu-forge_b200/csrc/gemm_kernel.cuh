@@ -37,11 +37,12 @@ namespace gk {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = 128 bytes = one swizzle row
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-// Per-epilogue-warp output staging: two 2 KB buffers after the operand ring;
-// the warp's lane 0 issues the TMA stores (or fp32 add-reductions) and owns
-// their bulk groups.
-constexpr int kEpiWarpBytes = 4096;
-constexpr int kEpiBytes = 8 * kEpiWarpBytes;
+// Per-epilogue-warp output staging after the operand ring: two 2 KB
+// buffers, or for the epilogue kind that writes C and Z (EK_ACT16) two pairs
+// of them, so that a chunk's stores of C and Z drain while the next chunk is
+// computed; the warp's lane 0 issues the TMA stores (or fp32 add-reductions)
+// and owns their bulk groups.
+constexpr int kSmemBudget = 232448;
 
 // Epilogue kinds: each kernel instantiation carries one, so that its
 // epilogue holds only the arithmetic of that kind (a runtime switch over every
@@ -88,13 +89,19 @@ struct GemmParams {
   float* ce_tlogit;
 };
 
-template <int BN> struct Cfg {
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+template <int EK> struct Epi {
+  static constexpr int WARP_BYTES = (EK == EK_ACT16) ? 8192 : 4096;
+  static constexpr int BYTES = 8 * WARP_BYTES;
+};
+
+template <int BN, int EK> struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int RING_MAX = (kSmemBudget - Epi<EK>::BYTES - 1024 - 256) / STAGE_BYTES;
+  static constexpr int STAGES = RING_MAX > 6 ? 6 : RING_MAX;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + kEpiBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + Epi<EK>::BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 FXB_DEV void tile_coords(int unit, const GemmParams& p, int& tm, int& tn, int& split) {
@@ -427,10 +434,10 @@ struct EpiWarp {
     return n8;
   }
 
-  // Staging: an epilogue that writes only C alternates between the warp's two
-  // 2 KB buffers (one bulk group per piece, so a piece waits only for the
-  // group before last to have been read); one that also writes Z uses both
-  // buffers for every piece and waits for the previous group.
+  // Staging: each 32-column chunk is one bulk group (C, plus Z in the next
+  // 2 KB for the epilogues that write it), and consecutive chunks alternate
+  // between two buffer sets, so a chunk waits only for the group before last
+  // to have been read.
   FXB_DEV void chunk(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmZ, int m,
                      int m0, int n0, uint32_t taddr, int cc, uint32_t sbuf, int lane,
                      uint32_t& cnt) {
@@ -440,13 +447,15 @@ struct EpiWarp {
     tmem_ld32(taddr, acc);
     tmem_wait_ld();
     if constexpr (sizeof(CT) == 2) {
-      const uint32_t b = wz ? sbuf : sbuf + (cnt & 1u) * 2048u;
-      stage_begin(lane, wz);
+      // C (and Z, in the next 2 KB) alternate between two buffer sets: the
+      // group before last has been read once the newest is the only one left
+      const uint32_t b = sbuf + (cnt & 1u) * (EK == EK_ACT16 ? 4096u : 2048u);
+      stage_begin(lane, false);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         piece(p, m, n0 + 16 * h, acc + 16 * h, cc & 1, &pre[cc & 1][2 * h], v, z);
         stage_piece<CT>(b, lane, h, v);
-        if (wz) stage_piece<CT>(sbuf + 2048, lane, h, z);
+        if (wz) stage_piece<CT>(b + 2048, lane, h, z);
       }
       stage_issue(tmC, n0, wz ? tmZ : nullptr, n0, m0, false, b, lane);
       ++cnt;
@@ -594,13 +603,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmZ,
                const GemmParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, EK>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // 1024B aligned for 128B swizzle
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t epi0 = base + C::STAGES * C::STAGE_BYTES;  // output staging
-  const uint32_t bar0 = epi0 + kEpiBytes;
+  const uint32_t bar0 = epi0 + Epi<EK>::BYTES;
   // barrier layout: full[S], empty[S], tfull[2], tempty[2], final, then tmem slot
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
@@ -724,7 +733,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
-    const uint32_t sbuf = epi0 + (uint32_t)(warp - 2) * kEpiWarpBytes;
+    const uint32_t sbuf = epi0 + (uint32_t)(warp - 2) * Epi<EK>::WARP_BYTES;
     uint32_t ecnt = 0;  // staging pieces issued by this warp (buffer alternation)
     int abuf = 0;
     uint32_t aphase = 0;
@@ -786,13 +795,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // barriers of both CTAs (tcgen05.commit multicast). Shared-memory operand
 // traffic per SM is half of the 1-SM kernel's for the same tile width, which
 // is what lets the tensor pipe run at full rate.
-template <int BN> struct Cfg2 {
+template <int BN, int EK> struct Cfg2 {
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = (BN / 2) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+  static constexpr int RING_MAX = (kSmemBudget - Epi<EK>::BYTES - 1024 - 256) / STAGE_BYTES;
+  static constexpr int STAGES = RING_MAX > 8 ? 8 : RING_MAX;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + kEpiBytes + 1024 + 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + Epi<EK>::BYTES + 1024 + 256;
 };
 
 template <int BN, bool A_MN, bool B_MN, int AB_FMT, int EK>
@@ -800,13 +810,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmZ,
                 const GemmParams p) {
-  using C = Cfg2<BN>;
+  using C = Cfg2<BN, EK>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t epi0 = base + C::STAGES * C::STAGE_BYTES;  // output staging
-  const uint32_t bar0 = epi0 + kEpiBytes;
+  const uint32_t bar0 = epi0 + Epi<EK>::BYTES;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
   auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * C::STAGES + b); };
@@ -940,7 +950,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = (int)rank * 128 + quarter * 32 + lane;
-    const uint32_t sbuf = epi0 + (uint32_t)(warp - 2) * kEpiWarpBytes;
+    const uint32_t sbuf = epi0 + (uint32_t)(warp - 2) * Epi<EK>::WARP_BYTES;
     uint32_t ecnt = 0;  // staging pieces issued by this warp (buffer alternation)
     int abuf = 0;
     uint32_t aphase = 0;
@@ -1006,7 +1016,7 @@ int launch_one(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
   void (*k)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
             const GemmParams) =
       PAIR ? gemm_tc2_kernel<BN, A_MN, B_MN, AB_FMT, EK> : gemm_tc_kernel<BN, A_MN, B_MN, AB_FMT, EK>;
-  constexpr int smem = PAIR ? Cfg2<BN>::SMEM : Cfg<BN>::SMEM;
+  constexpr int smem = PAIR ? Cfg2<BN, EK>::SMEM : Cfg<BN, EK>::SMEM;
   static_assert(smem <= 232448, "shared memory budget");
   static bool attr_set[64] = {false};
   int dev = 0;
