@@ -649,7 +649,7 @@ def curve_check(args, rank, world, local_rank, dev):
         return x.pin_memory(), y.pin_memory()
 
     model, opt = _gpt_and_opt(dev)
-    attach_dp(args, world, model, opt)
+    dp = attach_dp(args, world, model, opt)
     losses = torch.zeros(steps, device=dev)
     norms = torch.zeros(steps, device=dev)
     for s in range(steps):
@@ -667,6 +667,8 @@ def curve_check(args, rank, world, local_rank, dev):
     if world > 1:
         dist.all_reduce(losses, op=dist.ReduceOp.SUM)
         losses /= world
+        if hasattr(dp, "finish_gather"):
+            dp.finish_gather()  # ZeRO-1 gathers the last update's parameters lazily
         # bitwise identity of the replicas: a position-weighted checksum of the
         # bf16 parameters, gathered from every rank
         bits = opt.flat16.view(torch.int16).to(torch.int64)

@@ -155,6 +155,7 @@ def _zero_worker(rank, port, out_q):
         mz, oz = _fresh(dev)
         sz = ShardedDataParallel(mz, oz)
         zr = run(mz, oz)
+        sz.finish_gather()  # the last update's parameters (gathered lazily otherwise)
         flat_z = oz.flat16.detach().float().cpu()
         sz.consolidate()
         mg, og2 = _fresh(dev)

@@ -60,6 +60,11 @@ class _Model(torch.nn.Module):
         self.emb = torch.nn.Parameter(torch.zeros(10, 3))
         self.extra = torch.nn.Parameter(torch.zeros(5))
 
+    def forward(self):
+        # touches every block, so that forward pre-hooks run as in a GPT
+        self.blocks[0](torch.zeros(1, 5, dtype=torch.bfloat16))
+        self.blocks[1](torch.zeros(1, 7, dtype=torch.bfloat16))
+
 
 class _FlatStandIn:
     """The buffers and hook lists of FlatAdamW that the sharding touches."""
@@ -84,7 +89,7 @@ class _FlatStandIn:
         self.shard = (lo, hi)
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, defer=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
@@ -92,7 +97,7 @@ def _worker(rank, world, port, q):
         from fxb200.zero import ShardedDataParallel
         model = _Model()
         opt = _FlatStandIn(model)
-        sdp = ShardedDataParallel(model, opt)
+        sdp = ShardedDataParallel(model, opt, defer_gather=defer)
         lo, hi = opt.shard
         n = opt.numel
         base = torch.arange(n, dtype=torch.float32) + 1
@@ -111,6 +116,11 @@ def _worker(rank, world, port, q):
         opt.grad[lo:hi].zero_()                   # what the shard update leaves
         for h in opt.post_step_hooks:
             h(opt)
+        if defer:
+            # the gather waits for the next forward: only this rank's shard is new
+            res["flat16_before"] = opt.flat16.float().clone()
+            model()
+            sdp.finish_gather()                   # nothing left to do
         res["flat16"] = opt.flat16.float().clone()
         res["grad_after"] = opt.grad.clone()
         for t, k in ((opt.master, 1.0), (opt.m, 2.0), (opt.v, 3.0)):
@@ -134,12 +144,16 @@ def _free_port():
     return p
 
 
-def test_sharded_hooks_three_gloo_ranks():
+@pytest.mark.parametrize("defer", [False, True])
+def test_sharded_hooks_three_gloo_ranks(defer):
+    """defer=True: the parameter gather runs in the next forward's pre-hook
+    (per-range broadcasts from the owners, the GPU path's order) instead of
+    right after the update."""
     world = 3
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, defer)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -167,6 +181,11 @@ def test_sharded_hooks_three_gloo_ranks():
         assert torch.equal(o[r]["grad_shard"], mean[lo:hi]), r
         assert o[r]["norm"] == (6.0, 1)
         assert torch.equal(o[r]["flat16"], expect_flat)
+        if defer:
+            lo, hi = o[r]["shard"]
+            before = o[r]["flat16_before"]
+            assert torch.equal(before[lo:hi], expect_flat[lo:hi])
+            assert torch.count_nonzero(torch.cat([before[:lo], before[hi:]])) == 0
         assert torch.count_nonzero(o[r]["grad_after"]) == 0
         assert o[r]["param_is_view"]
         assert torch.equal(o[r]["state"], o[0]["state"])
