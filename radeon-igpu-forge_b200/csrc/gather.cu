@@ -54,59 +54,84 @@ __global__ void colsum_kernel(const T* __restrict__ g, int64_t rows, int cols,
   }
 }
 
-// Same sum when a row is a whole number of 16-byte vectors: block b owns the
-// E = 16 / sizeof(T) columns of vector b and all rows, so the sum needs no
-// cross-block step (deterministic, no workspace). Thread t reads rows t,
-// t + blockDim.x, ... with four 16-byte loads in flight, then the block adds
-// its threads' sums in a fixed tree order (warp shuffles, then the warps'
-// partials in warp order).
+// Same sum when a row is a whole number of 16-byte vectors. A cluster of
+// kColsumCluster CTAs owns a group of cv consecutive vectors (cv * E columns);
+// its CTAs split the rows into equal ranges. Within a CTA, thread t reads
+// vector t % cv of rows t / cv, t / cv + 256 / cv, ... (a warp reads whole
+// cv * 16-byte row segments, four loads in flight), and the CTA adds its
+// threads' sums over the row offsets in a fixed order into a shared partial.
+// After a cluster barrier CTA 0 adds the CTAs' partials, read through
+// distributed shared memory, in rank order, and writes the columns: the sum
+// needs no workspace and no atomics, so it is the same on every run. cv is
+// chosen so that the clusters cover the SMs with row segments of >= 32 bytes.
+constexpr int kColsumCluster = 8;
+constexpr int kColsumThreads = 256;
+
 template <typename T>
-__global__ void __launch_bounds__(1024, 1)
-colsum_vec_kernel(const T* __restrict__ g, int64_t rows, int cols, float* __restrict__ out,
-                  int accumulate) {
+__global__ void __cluster_dims__(kColsumCluster, 1, 1) __launch_bounds__(kColsumThreads)
+colsum_cluster_kernel(const T* __restrict__ g, int64_t rows, int cols, int cv,
+                      float* __restrict__ out, int accumulate) {
   pdl_trigger();
   pdl_wait();  // inputs come from the previous kernel on the stream
   constexpr int E = 16 / sizeof(T);
-  __shared__ float part[32][E];
-  const int64_t vecs_per_row = cols / E;
-  const uint4* src = reinterpret_cast<const uint4*>(g) + blockIdx.x;
+  __shared__ float part[kColsumThreads * E];  // [row offset][vector][element]
+  __shared__ float cta_sum[32 * E];            // cv <= 32 vectors of E columns
+  const int nvec = cols / E;
+  const int rank = (int)cluster_ctarank();
+  const int grp = (int)(blockIdx.x / kColsumCluster);
+  const int tid = threadIdx.x;
+  const int tv = tid % cv, tr = tid / cv, rstep = kColsumThreads / cv;
+  const int vec = grp * cv + tv;
+  const int64_t per = (rows + kColsumCluster - 1) / kColsumCluster;
+  const int64_t r0 = (int64_t)rank * per;
+  const int64_t r1 = r0 + per < rows ? r0 + per : rows;
   float s[E];
 #pragma unroll
   for (int j = 0; j < E; ++j) s[j] = 0.f;
-  const int64_t step = blockDim.x;
-  int64_t r = threadIdx.x;
-  for (; r + 3 * step < rows; r += 4 * step) {
-    uint4 u[4];
+  if (vec < nvec) {
+    const uint4* src = reinterpret_cast<const uint4*>(g) + vec;
+    int64_t r = r0 + tr;
+    for (; r + 3 * rstep < r1; r += 4 * rstep) {
+      uint4 u[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) u[k] = src[(r + k * step) * vecs_per_row];
+      for (int k = 0; k < 4; ++k) u[k] = src[(r + (int64_t)k * rstep) * nvec];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const T* h = reinterpret_cast<const T*>(&u[k]);
+      for (int k = 0; k < 4; ++k) {
+        const T* h = reinterpret_cast<const T*>(&u[k]);
+#pragma unroll
+        for (int j = 0; j < E; ++j) s[j] += to_f<T>(h[j]);
+      }
+    }
+    for (; r < r1; r += rstep) {
+      const uint4 u = src[r * nvec];
+      const T* h = reinterpret_cast<const T*>(&u);
 #pragma unroll
       for (int j = 0; j < E; ++j) s[j] += to_f<T>(h[j]);
     }
   }
-  for (; r < rows; r += step) {
-    const uint4 u = src[r * vecs_per_row];
-    const T* h = reinterpret_cast<const T*>(&u);
 #pragma unroll
-    for (int j = 0; j < E; ++j) s[j] += to_f<T>(h[j]);
-  }
-#pragma unroll
-  for (int j = 0; j < E; ++j) s[j] = warp_sum(s[j]);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (lane == 0) {
-#pragma unroll
-    for (int j = 0; j < E; ++j) part[wid][j] = s[j];
-  }
+  for (int j = 0; j < E; ++j) part[(tr * cv + tv) * E + j] = s[j];
   __syncthreads();
-  if (threadIdx.x < E) {
-    const int nw = (blockDim.x + 31) >> 5;
+  // this CTA's sum of (vector tv, element j) over its row offsets, in order
+  const int ncol = cv * E;
+  if (tid < ncol) {
     float t = 0.f;
-    for (int w = 0; w < nw; ++w) t += part[w][threadIdx.x];
-    const int64_t c = (int64_t)blockIdx.x * E + threadIdx.x;
-    out[c] = accumulate ? out[c] + t : t;
+    for (int k = 0; k < rstep; ++k) t += part[k * ncol + tid];
+    cta_sum[tid] = t;
   }
+  cluster_sync();  // every CTA's cta_sum is written and visible to the cluster
+  if (rank == 0 && tid < ncol) {
+    const int c = grp * ncol + tid;
+    float t = 0.f;
+    const uint32_t a = smem_u32(&cta_sum[tid]);
+    for (int q = 0; q < kColsumCluster; ++q) {
+      float v;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(mapa_shared(a, (uint32_t)q)) : "memory");
+      t += v;
+    }
+    if (c < cols) out[c] = accumulate ? out[c] + t : t;
+  }
+  cluster_sync();  // the partials stay in place until CTA 0 has read them
 }
 
 // Narrow outputs (fewer columns than one 16-byte vector, e.g. the single
@@ -147,7 +172,14 @@ void launch_colsum(const T* g, int64_t rows, int cols, float* out, int accumulat
   constexpr int E = 16 / sizeof(T);
   const int threads = rows >= 1024 ? 1024 : (int)((rows + 31) / 32) * 32;
   if (cols % E == 0 && fxb::aligned16(g) && rows > 0) {
-    fxb::pdl_launch(colsum_vec_kernel<T>, cols / E, threads, 0, st, g, rows, cols, out, accumulate);
+    // vectors per cluster: >= 2 (32-byte row segments), growing with the
+    // width so that about 16 clusters (128 CTAs) share the columns
+    const int nvec = cols / E;
+    int cv = 2;
+    while (cv < 32 && (nvec + cv - 1) / cv > 16) cv *= 2;
+    const int clusters = (nvec + cv - 1) / cv;
+    fxb::pdl_launch(colsum_cluster_kernel<T>, clusters * kColsumCluster, kColsumThreads, 0, st, g, rows,
+                    cols, cv, out, accumulate);
     return;
   }
   if (cols < E && rows > 0) {

@@ -197,7 +197,8 @@ def test_colsum_kernel(dev, dtype):
     # vector path (cols % (16 / itemsize) == 0), per-column path (narrower),
     # general path (other widths), empty
     for rows, cols in [(1, 8), (37, 16), (1000, 24), (4096, 512), (32768, 512), (5, 3), (70_000, 8),
-                       (3000, 1), (32768, 1), (100, 13), (2000, 37), (0, 16)]:
+                       (3000, 1), (32768, 1), (100, 13), (2000, 37), (0, 16),
+                       (3000, 2048), (513, 4096), (9, 1032), (65536, 256)]:
         g = torch.randn(rows, cols, device=dev).to(dtype)
         out = torch.full((cols,), 7.0, device=dev)
         _lib.call("fxb_colsum", code, _lib.ptr(g), rows, cols, _lib.ptr(out), 0, st)
