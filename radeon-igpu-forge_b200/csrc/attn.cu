@@ -95,9 +95,10 @@ FXB_DEV float ex2_ftz(float x) {
   return y;
 }
 
-// Persistent kernel: each CTA walks work items (query tile, batch*head) from
-// blockIdx.x in steps of gridDim.x; items are numbered heaviest first for
-// causal attention (the last query tiles see the most key tiles). Tensor
+// Persistent kernel: each CTA walks work items (query tile, batch*head) in
+// rounds of gridDim.x items (CTA order in even rounds, reverse order in odd
+// ones); items are numbered heaviest first for causal attention (the last
+// query tiles see the most key tiles). Tensor
 // memory, barriers and tensor maps are set up once per CTA, Q is
 // double-buffered (Dh 64) and the K/V ring, S buffers and P buffers run on
 // counters that continue across items, so the next item's loads and first
@@ -164,6 +165,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     qt = p.causal ? (p.nqt - 1 - t) : t;
     n_kv = p.causal ? min(qt + 1, p.nkt) : p.nkt;
   };
+  // the k-th item of this CTA: rounds of gridDim.x items, taken in CTA order
+  // in even rounds and in reverse order in odd ones, so that with items
+  // numbered heaviest first the CTAs' totals even out (once an index passes
+  // the end, every later round's does too)
+  auto item_of = [&](int k) {
+    const int r = k * (int)gridDim.x;
+    return (k & 1) ? r + (int)gridDim.x - 1 - (int)blockIdx.x : r + (int)blockIdx.x;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -208,7 +217,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       int t = 0;   // K/V tiles issued (all items)
       int it = 0;  // items of this CTA
       int q_armed = 0;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+      for (int k = 0, w = item_of(0); w < n_items && ok; w = item_of(++k), ++it) {
         int qt, bh, n_kv;
         item_coords(w, qt, bh, n_kv);
         const int b = bh / p.H, h = bh - b * p.H;
@@ -271,7 +280,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         ++ts;
         return true;
       };
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++it) {
+      for (int k = 0, w = item_of(0); w < n_items && ok; w = item_of(++k), ++it) {
         int qt, bh, n_kv;
         item_coords(w, qt, bh, n_kv);
         const int qb = it % QN;
@@ -334,7 +343,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     // After a failed (timed-out) wait a thread keeps stepping through the
     // tiles without waiting or computing, so that the four warps of a row
     // quarter always meet at the same named barriers.
-    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+    for (int k = 0, w = item_of(0); w < n_items; w = item_of(++k)) {
       int qt, bh, n_kv;
       item_coords(w, qt, bh, n_kv);
       const int q0 = qt * TILE;
@@ -538,6 +547,14 @@ attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       n_kv[g] = qt >= p.nqt ? 0 : (p.causal ? min(qt + 1, p.nkt) : p.nkt);
     }
   };
+  // the k-th item of this CTA: rounds of gridDim.x items, taken in CTA order
+  // in even rounds and in reverse order in odd ones, so that with items
+  // numbered heaviest first the CTAs' totals even out (once an index passes
+  // the end, every later round's does too)
+  auto item_of = [&](int k) {
+    const int r = k * (int)gridDim.x;
+    return (k & 1) ? r + (int)gridDim.x - 1 - (int)blockIdx.x : r + (int)blockIdx.x;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 4; ++i) {
@@ -578,7 +595,7 @@ attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       bool ok = true;
       int t = 0;               // K/V tiles issued (all items)
       int cq[2] = {0, 0};      // Q tiles loaded per group
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      for (int k = 0, w = item_of(0); w < n_items && ok; w = item_of(++k)) {
         int pi, bh, n_kv[2];
         item_coords(w, pi, bh, n_kv);
         const int b = bh / p.H, h = bh - b * p.H;
@@ -621,7 +638,7 @@ attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       bool ok = true;
       int t = 0;                    // K/V tiles of the stream (all items)
       int cq = 0, cs = 0, cp = 0;   // this group's Q tiles, S products, P.V products
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      for (int k = 0, w = item_of(0); w < n_items && ok; w = item_of(++k)) {
         int pi, bh, n_kv[2];
         item_coords(w, pi, bh, n_kv);
         const int nk = max(n_kv[0], n_kv[1]);
@@ -695,7 +712,7 @@ attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       const bool rr = mbar_wait(bar, parity, p.err, FXB_DERR_ATTN_WAIT);
       return __all_sync(0xffffffffu, rr);
     };
-    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+    for (int k = 0, w = item_of(0); w < n_items; w = item_of(++k)) {
       int pi, bh, n_kv[2];
       item_coords(w, pi, bh, n_kv);
       const int nkv = n_kv[g];
