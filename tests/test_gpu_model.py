@@ -234,8 +234,15 @@ def _our_gpt(cfg, eps, seed, dev):
 
 
 def test_gpt_tiny_vs_oracle(dev):
-    """Config 1: loss within 1e-3 rel and every gradient within 2e-2 rel of
-    the fp32 oracle (pinned to the reference by tests/test_oracle.py)."""
+    """Config 1 on the bf16 path: loss within 1e-3 rel and every gradient
+    within 2e-2 rel of the fp32 oracle (pinned to the reference by
+    tests/test_oracle.py); then one FlatAdamW step. From the same gradients
+    the fp32 master update matches the oracle optimizer to 1e-5 per
+    parameter, and the bf16 parameters are the masters rounded. From each
+    side's own gradients the updated parameters agree within 1e-2 over the
+    flat vector: a first AdamW step moves each element by about lr * sign(g),
+    so the elements whose bf16 gradient lies near zero may move the other
+    way. (fp32 mode holds the whole step to 1e-5: tests/test_gpu_fp32.py.)"""
     from fxlm import FlatAdamW
     from oracle import gpt as og
     cfg = CFG1
@@ -248,10 +255,29 @@ def test_gpt_tiny_vs_oracle(dev):
     loss = m(x.to(dev), y.to(dev), grad_scale=opt.scale)
     opt.backward(loss)
     assert abs(loss.item() - ref_loss.item()) <= 1e-3 * abs(ref_loss.item())
+    our_grads = {}
     for name, p, off, n, _w in opt._info:
         ours = opt.grad[off:off + n].view(p.shape)
         r = rel(ours, ref_grads[name])
         assert r < 2e-2, f"{name}: grad rel err {r:.3e}"
+        our_grads[name] = ours.detach().cpu().clone()
+    ref_opt = og.OracleFlatAdamW(list(state.items()), lr=3e-4, init_scale=1.0)
+    ref_opt.step(ref_grads)
+    same_g = og.OracleFlatAdamW(list(state.items()), lr=3e-4, init_scale=1.0)
+    same_g.step(our_grads)
+    opt.step()
+    torch.cuda.synchronize()
+    ours_flat, ref_flat = [], []
+    for name, p, off, n, _w in opt._info:
+        w = opt.master[off:off + n].view(p.shape)
+        r = rel(w, same_g.master[name])
+        assert r < 1e-5, f"{name}: FlatAdamW update rel err {r:.3e} (same gradients)"
+        assert torch.equal(p.detach(), w.to(p.dtype)), f"{name}: bf16 parameter is not the rounded master"
+        ours_flat.append(w.reshape(-1).double().cpu())
+        ref_flat.append(ref_opt.master[name].reshape(-1).double())
+    whole = rel(torch.cat(ours_flat), torch.cat(ref_flat))
+    assert whole < 1e-2, f"updated parameters: rel err {whole:.3e} over the flat vector"
+    print(f"\nbf16 config-1 step: updated params rel {whole:.2e} (flat) against the fp32 oracle")
 
 
 def test_gpt_fused_vs_torch_paths(dev):
