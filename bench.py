@@ -555,7 +555,7 @@ def micro_results(micro, iters, only=None):
     return out
 
 
-def kernel_rooflines(iters=10):
+def kernel_rooflines(iters=30):
     """Roofline entries for the non-GEMM kernels of the north star, event-timed
     in this run (1 GPU): attention forward and forward + backward at config 2
     against the bf16 tensor peak; RMSNorm forward / backward (config 3 and the
