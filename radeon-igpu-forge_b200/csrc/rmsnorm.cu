@@ -430,6 +430,23 @@ int row_blocks(int64_t rows) {
   return b < 1 ? 1 : (int)b;
 }
 
+// The warp-row backward kernels of the wider rows hold two rows of x, dy and
+// dres per warp in registers (up to ~240 per thread), so fewer blocks than
+// bwd_blocks' two per SM may be resident at once. The grid is cut to the
+// blocks that are resident together: one wave instead of two, and fewer dw
+// partials for the column reduction (the workspace is sized for the larger
+// grid, so it always suffices).
+template <typename K> int resident_grid(K k, size_t smem, int blocks) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kWarps * 32, smem) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();  // leave no sticky error behind; keep the grid as it is
+    return blocks;
+  }
+  const int cap = fxb::num_sms() * per_sm;
+  return blocks < cap ? blocks : cap;
+}
+
 int bwd_blocks(int64_t rows) {
   // two blocks per SM, each warp two rows per pass with all their loads in
   // flight: enough bytes outstanding for HBM, and few dw partials to reduce
@@ -446,7 +463,7 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
   constexpr int E = Vec<T>::N;
   const int vpl = (D / E + 31) / 32;
   const bool long_rows = D > kWarpRowMaxD<T>;
-  const int blocks = long_rows ? row_blocks(rows) : bwd_blocks(rows);
+  int blocks = long_rows ? row_blocks(rows) : bwd_blocks(rows);
   const size_t smem = (size_t)kWarps * D * sizeof(float);
   auto X = static_cast<const T*>(x);
   auto W = static_cast<const T*>(w);
@@ -457,6 +474,7 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
     auto k = rmsnorm_bwd_kernel<T, V>;                                                   \
     if (smem > 48 * 1024)                                                                \
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
+    blocks = resident_grid(k, smem, blocks);                                             \
     fxb::pdl_launch(k, blocks, kWarps * 32, smem, st, X, W, rstd, G, static_cast<const T*>(dres), DX, ws, rows, D); \
     break;                                                                               \
   }
