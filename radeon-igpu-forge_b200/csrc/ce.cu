@@ -159,11 +159,15 @@ ce_cached_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __rest
 }
 
 // Rows of up to kSmemRowMax bytes (V = 32768 in 16-bit is 64 KB): the row is
-// brought into shared memory by one bulk asynchronous copy, both passes run
-// out of shared memory (online max / sum-of-exp, then the gradient written
-// back in place), and one bulk copy stores the gradient row. Three blocks per
-// SM keep loads, arithmetic and stores of different rows overlapped; the
-// logits are read from HBM once and the gradient written once.
+// brought into shared memory by one bulk asynchronous copy, three passes run
+// out of shared memory (the row maximum; exp(x - max) once per element, summed
+// and, with a gradient, kept in place; the gradient scaled in place), and one
+// bulk copy stores the gradient row. One exponential per element keeps the
+// special-function pipe at half the load of an online max / sum followed by
+// a second exponential pass. (With a gradient the kept exp(x - max) is
+// rounded to the row type before it is scaled.) Three blocks per SM keep
+// loads, arithmetic and stores of different rows overlapped; the logits are
+// read from HBM once and the gradient written once.
 constexpr int kSmemRowMax = 72 * 1024;
 constexpr int kSmemThreads = 256;
 
@@ -201,57 +205,58 @@ ce_smem_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restri
     ok = mbar_wait(bar, phase, err, FXB_DERR_CE_WAIT);
     phase ^= 1;
     if (!ok) break;  // uniform: every thread saw the same barrier
-    // pass 1: online max and sum of exp2 over this thread's vectors
-    float m = -INFINITY, s = 0.f;
+    const int64_t t = target[r];
+    const bool valid = (t != ignore_index) && (t >= 0) && (t < (int64_t)V);
+    // the target logit, read before pass 2 overwrites the row
+    if (tid == 0) s_xt = valid ? to_f<T>(reinterpret_cast<const T*>(srow_raw)[t]) : 0.f;
+    // pass 1: row maximum (no exponentials)
+    float m = -INFINITY;
     for (int v = tid; v < nvec; v += kSmemThreads) {
       float f[E];
       unpack_row<T>(srow_raw, v, f);
-      float vm = f[0];
 #pragma unroll
-      for (int j = 1; j < E; ++j) vm = fmaxf(vm, f[j]);
-      const float mn = fmaxf(m, vm);
-      if (mn == -INFINITY) continue;  // nothing but -inf so far: m, s unchanged
-      const float mnl = mn * kLog2e;
-      float add = 0.f;
-#pragma unroll
-      for (int j = 0; j < E; ++j) add += exp2f(fmaf(f[j], kLog2e, -mnl));
-      s = s * exp2f((m - mn) * kLog2e) + add;  // m = -inf: s = 0 * 0 + add
-      m = mn;
+      for (int j = 0; j < E; ++j) m = fmaxf(m, f[j]);
     }
-    // block combine of (m, s)
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      const float mn = fmaxf(m, m2);
-      s = (mn == -INFINITY) ? 0.f : s * exp2f((m - mn) * kLog2e) + s2 * exp2f((m2 - mn) * kLog2e);
-      m = mn;
-    }
-    const int64_t t = target[r];
-    const bool valid = (t != ignore_index) && (t >= 0) && (t < (int64_t)V);
-    if (lane == 0) { red_m[wid] = m; red_s[wid] = s; }
-    if (tid == 0) s_xt = valid ? to_f<T>(reinterpret_cast<const T*>(srow_raw)[t]) : 0.f;
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red_m[wid] = m;
     __syncthreads();
-    float M = red_m[0], S = red_s[0];
+    float M = red_m[0];
 #pragma unroll
-    for (int w = 1; w < NW; ++w) {
-      const float m2 = red_m[w], s2 = red_s[w];
-      const float mn = fmaxf(M, m2);
-      S = (mn == -INFINITY) ? 0.f : S * exp2f((M - mn) * kLog2e) + s2 * exp2f((m2 - mn) * kLog2e);
-      M = mn;
+    for (int w = 1; w < NW; ++w) M = fmaxf(M, red_m[w]);
+    // pass 2: one exp2 per element; its sum, and (with a gradient) the value
+    // exp(x - M) kept in place for pass 3
+    const float Ml = (M == -INFINITY) ? 0.f : M * kLog2e;  // all -inf: every term is 0
+    float s = 0.f;
+    for (int v = tid; v < nvec; v += kSmemThreads) {
+      float f[E];
+      unpack_row<T>(srow_raw, v, f);
+      float e4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        f[j] = exp2f(fmaf(f[j], kLog2e, -Ml));
+        e4[j & 3] += f[j];
+      }
+      s += (e4[0] + e4[1]) + (e4[2] + e4[3]);
+      if (grad) pack_row<T>(srow_raw, v, f);
     }
+    s = warp_sum(s);
+    if (lane == 0) red_s[wid] = s;
+    __syncthreads();
+    float S = red_s[0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) S += red_s[w];
     const float xt = s_xt;
     if (tid == 0) row_loss[r] = valid ? M + log2f(S) * kLn2 - xt : 0.f;
     if (grad) {
-      // pass 2: gradient in place in shared memory, then one bulk store
+      // pass 3: gradient in place in shared memory, then one bulk store
       const float scale = valid ? gm / S : 0.f;
-      const float Ml = M * kLog2e;
       for (int v = tid; v < nvec; v += kSmemThreads) {
         float f[E];
         unpack_row<T>(srow_raw, v, f);
 #pragma unroll
         for (int j = 0; j < E; ++j) {
-          f[j] = exp2f(fmaf(f[j], kLog2e, -Ml)) * scale;
+          f[j] *= scale;
           if ((int64_t)(v * E + j) == t && valid) f[j] -= gm;
         }
         pack_row<T>(srow_raw, v, f);
