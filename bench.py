@@ -145,15 +145,55 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU baseline
+def _reference_fxlm():
+    """The reference's own ml/fxlm package when its source tree is given
+    (FXB_REFERENCE_ROOT, or baseline/_ref holding ml/fxlm), loaded under a
+    private name with its HIP loader stubbed, so that its PyTorch paths run
+    on the CPU; None when no tree is given."""
+    import importlib.util
+    import types
+    for root in (os.environ.get("FXB_REFERENCE_ROOT"), os.path.join(ROOT, "baseline", "_ref")):
+        pkg = os.path.join(root, "ml", "fxlm") if root else None
+        if not pkg or not os.path.isfile(os.path.join(pkg, "model.py")):
+            continue
+        if "fxgpu.hip_kernel" not in sys.modules:
+            def _no_hip(*_a, **_k):
+                raise RuntimeError("HIP kernels are not available on this host")
+            parent = types.ModuleType("fxgpu")
+            parent.__path__ = []
+            stub = types.ModuleType("fxgpu.hip_kernel")
+            stub.compile_kernel = stub.compile_module = stub.launch = _no_hip
+            sys.modules.setdefault("fxgpu", parent)
+            sys.modules["fxgpu.hip_kernel"] = stub
+        spec = importlib.util.spec_from_file_location("ref_fxlm", os.path.join(pkg, "__init__.py"),
+                                                      submodule_search_locations=[pkg])
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules["ref_fxlm"] = mod
+        spec.loader.exec_module(mod)
+        import importlib
+        return importlib.import_module("ref_fxlm.model")
+    return None
+
+
 def cpu_baseline(steps=3, warmup=1):
-    """The reference's PyTorch path (oracle/gpt.py) in fp32 on the host cores:
-    one 1024-token sequence per step, forward + backward + FlatAdamW step."""
+    """The reference's PyTorch path in fp32 on the host cores: one 1024-token
+    sequence per step, forward + backward + FlatAdamW step. The model is the
+    reference's own ml/fxlm/model.py (torch attention, norm and CE paths) when
+    its source tree is given (see _reference_fxlm), else its restatement in
+    oracle/gpt.py. The optimizer step is oracle/gpt.py's FlatAdamW restatement
+    in both cases: the reference's FlatAdamW runs HIP kernels only."""
     import torch
     from oracle import gpt as og
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     torch.manual_seed(3)
-    m = og.RefGPT(**CFG4)
+    ref = _reference_fxlm()
+    if ref is not None:
+        m = ref.GPT(ref.GPTConfig(**CFG4, attn_impl="sdpa", norm_impl="torch", ce_impl="torch"))
+        kind, what = "reference", "the reference's ml/fxlm/model.py (torch paths)"
+    else:
+        m = og.RefGPT(**CFG4)
+        kind, what = "port", "oracle/gpt.py restating ml/fxlm/model.py torch path"
     opt = og.OracleFlatAdamW(list(m.named_parameters()), lr=6e-4, weight_decay=0.1,
                              max_grad_norm=1.0, init_scale=1.0)
     x, y = og.zipf_tokens(CFG4["vocab_size"], 1, SEQ, seed=3)
@@ -170,9 +210,9 @@ def cpu_baseline(steps=3, warmup=1):
         if i >= warmup:
             times.append(time.perf_counter() - t0)
     tps = SEQ / statistics.mean(times)
-    return {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+    return {"value": tps, "unit": "tokens/s", "cores": threads, "kind": kind,
             "sample": f"1 x {SEQ} tokens per step, {steps} timed steps after {warmup} warm-up "
-                      f"(fp32, oracle/gpt.py restating ml/fxlm/model.py torch path + FlatAdamW)"}
+                      f"(fp32, {what} + FlatAdamW)"}
 
 
 def run_reference(args, rank, world):
