@@ -41,7 +41,10 @@ template <typename T> FXB_DEV void store_vec(T* p, const float* f) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-// VPL = 16-byte vectors per lane (row length D <= VPL * 32 * Vec<T>::N)
+// VPL = 16-byte vectors per lane (row length D <= VPL * 32 * Vec<T>::N).
+// Each warp takes two rows per pass (rows r and r + the grid's warp count)
+// and issues all of their loads before using any, so that enough bytes are
+// in flight per SM at the step's small row counts.
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
@@ -59,31 +62,49 @@ rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restri
   }
   const int64_t warp0 = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * kWarps;
-  for (int64_t r = warp0; r < rows; r += nwarps) {
-    const T* xr = x + r * D;
-    float xv[VPL][E];
-    float ss = 0.f;
+  for (int64_t r0 = warp0; r0 < rows; r0 += 2 * nwarps) {
+    const int64_t r1 = r0 + nwarps;
+    const bool two = r1 < rows;  // warp-uniform
+    float xv[2][VPL][E];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      int v = i * 32 + lane;
-      if (v < nvec) {
-        load_vec<T>(xr + (int64_t)v * E, xv[i]);
+    for (int k = 0; k < 2; ++k) {
+      const T* xr = x + (k ? r1 : r0) * D;
 #pragma unroll
-        for (int j = 0; j < E; ++j) ss += xv[i][j] * xv[i][j];
+      for (int i = 0; i < VPL; ++i) {
+        int v = i * 32 + lane;
+        if (v < nvec && (k == 0 || two)) {
+          load_vec<T>(xr + (int64_t)v * E, xv[k][i]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < E; ++j) xv[k][i][j] = 0.f;
+        }
       }
     }
-    ss = warp_sum(ss);
-    const float rs = rsqrtf(ss / (float)D + eps);
-    if (lane == 0) rstd[r] = rs;
-    T* yr = y + r * D;
+    float ss[2] = {0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      int v = i * 32 + lane;
-      if (v < nvec) {
-        float o[E];
+    for (int k = 0; k < 2; ++k)
 #pragma unroll
-        for (int j = 0; j < E; ++j) o[j] = xv[i][j] * rs * wv[i][j];
-        store_vec<T>(yr + (int64_t)v * E, o);
+      for (int i = 0; i < VPL; ++i)
+#pragma unroll
+        for (int j = 0; j < E; ++j) ss[k] += xv[k][i][j] * xv[k][i][j];
+    ss[0] = warp_sum(ss[0]);
+    ss[1] = warp_sum(ss[1]);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (k == 1 && !two) break;
+      const int64_t r = k ? r1 : r0;
+      const float rs = rsqrtf(ss[k] / (float)D + eps);
+      if (lane == 0) rstd[r] = rs;
+      T* yr = y + r * D;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        int v = i * 32 + lane;
+        if (v < nvec) {
+          float o[E];
+#pragma unroll
+          for (int j = 0; j < E; ++j) o[j] = xv[k][i][j] * rs * wv[i][j];
+          store_vec<T>(yr + (int64_t)v * E, o);
+        }
       }
     }
   }
@@ -384,7 +405,7 @@ int launch_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows,
                cudaStream_t st) {
   constexpr int E = Vec<T>::N;
   const int vpl = (D / E + 31) / 32;
-  int64_t blocks64 = (rows + kWarps - 1) / kWarps;
+  int64_t blocks64 = (rows + 2 * kWarps - 1) / (2 * kWarps);  // two rows per warp
   int cap = fxb::num_sms() * 16;
   int blocks = (int)(blocks64 < cap ? blocks64 : cap);
   if (blocks < 1) blocks = 1;

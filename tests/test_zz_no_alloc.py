@@ -1,9 +1,11 @@
 """fxb_rmsnorm_bwd_static (no allocation, file-scope device scratch) against
-fxb_rmsnorm_bwd (caller workspace), through the C ABI.
+fxb_rmsnorm_bwd (caller workspace), through the C ABI, and on its own against
+fp32 PyTorch autograd.
 
 Two calls of the static entry in a row on different shapes and inputs (the
 second one reuses the scratch the first one left behind), each compared with
-the workspace entry on the same inputs; then the size limit.
+the workspace entry on the same inputs and with F.rms_norm's fp32 gradients;
+then the size limit.
 """
 import pytest
 import torch
@@ -62,7 +64,32 @@ def test_static_scratch_matches_workspace_entry_twice(dev):
         # 1e-6 relative (they are expected to agree exactly)
         torch.testing.assert_close(dx_new.float(), dx_ref.float(), rtol=1e-6, atol=1e-6)
         torch.testing.assert_close(dw_new, dw_ref, rtol=1e-6, atol=1e-6)
+        # and on its own against fp32 autograd through F.rms_norm on the same
+        # rounded inputs, with the reference's tolerance rule (2 x the error
+        # of torch's own low-precision backward, + 1e-3)
+        gx32, gw32 = _torch_grads(x, w, dy, torch.float32)
+        gx16, gw16 = _torch_grads(x, w, dy, dtype)
+        if with_res:
+            gx32 = gx32 + dres.float()
+            gx16 = (gx16.float() + dres.float()).to(dtype)
+        if acc:
+            gw32 = gw32 + dw0
+            gw16 = gw16.float() + dw0
+        for ours, r32, lp, nm in ((dx_new, gx32, gx16, "dx"), (dw_new, gw32, gw16, "dw")):
+            e_our = (ours.float() - r32).abs().max().item()
+            e_lp = (lp.float() - r32).abs().max().item()
+            assert e_our <= 2 * e_lp + 1e-3, f"{nm} ({rows}x{D}): err {e_our:.3e} vs torch-lowp {e_lp:.3e}"
     assert _lib.device_error(clear=True) == 0
+
+
+def _torch_grads(x, w, dy, dtype):
+    """d(rms_norm(x, w)) / dx and / dw contracted with dy, by PyTorch autograd
+    in `dtype` (eps 1e-6, as the rstd the test passes)."""
+    import torch.nn.functional as F
+    xr = x.detach().to(dtype).requires_grad_()
+    wr = w.detach().to(dtype).requires_grad_()
+    F.rms_norm(xr, (x.shape[1],), wr, 1e-6).backward(dy.to(dtype))
+    return xr.grad, wr.grad.float()
 
 
 def test_static_scratch_rejects_oversize(dev):
