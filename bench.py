@@ -276,8 +276,34 @@ def attn_tflops(dev, iters=10):
     e2.record()
     torch.cuda.synchronize()
     tf, tb = e0.elapsed_time(e1) / iters, e1.elapsed_time(e2) / iters
-    return {"fwd_tflops": fwd_flops / tf / 1e9, "fwd_bwd_tflops": 3 * fwd_flops / (tf + tb) / 1e9,
-            "fwd_ms": tf, "bwd_ms": tb, "shape": "B16 H12 S1024 D64 causal bf16"}
+    out = {"fwd_tflops": fwd_flops / tf / 1e9, "fwd_bwd_tflops": 3 * fwd_flops / (tf + tb) / 1e9,
+           "fwd_ms": tf, "bwd_ms": tb, "shape": "B16 H12 S1024 D64 causal bf16"}
+    out["library"] = _sdpa_library_tflops(q, k, v, do, fwd_flops, iters)
+    return out
+
+
+def _sdpa_library_tflops(q, k, v, do, fwd_flops, iters):
+    """The same attention through torch's scaled_dot_product_attention, one
+    backend at a time (cuDNN, flash), on (B, H, S, D) views of the same
+    tensors: library kernels beside this build's, for context. A backend that
+    does not run on this GPU reports its error instead."""
+    import torch
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    F = torch.nn.functional
+    res = {}
+    qt, kt, vt, dot = (t.transpose(1, 2) for t in (q, k, v, do))
+    for name, be in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION)):
+        try:
+            with sdpa_kernel([be]):
+                qg, kg, vg = (t.detach().requires_grad_(True) for t in (qt, kt, vt))
+                tf = _time_ms(lambda: F.scaled_dot_product_attention(qt, kt, vt, is_causal=True), iters)
+                o = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True)
+                tfb = _time_ms(lambda: torch.autograd.grad(o, (qg, kg, vg), dot, retain_graph=True), iters)
+            res[name] = {"fwd_tflops": fwd_flops / tf / 1e9, "fwd_ms": tf, "bwd_ms": tfb,
+                         "fwd_bwd_tflops": 3 * fwd_flops / (tf + tfb) / 1e9}
+        except Exception as e:  # backend unavailable for this GPU / dtype / layout
+            res[name] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"}
+    return res
 
 
 # ---------------------------------------------------------------- per-kernel microbenchmarks
