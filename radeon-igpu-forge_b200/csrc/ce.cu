@@ -158,126 +158,212 @@ ce_cached_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __rest
   }
 }
 
-// Rows of up to kSmemRowMax bytes (V = 32768 in 16-bit is 64 KB): the row is
-// brought into shared memory by one bulk asynchronous copy, three passes run
-// out of shared memory (the row maximum; exp(x - max) once per element, summed
-// and, with a gradient, kept in place; the gradient scaled in place), and one
-// bulk copy stores the gradient row. One exponential per element keeps the
-// special-function pipe at half the load of an online max / sum followed by
-// a second exponential pass. (With a gradient the kept exp(x - max) is
-// rounded to the row type before it is scaled.) Three blocks per SM keep
-// loads, arithmetic and stores of different rows overlapped; the logits are
-// read from HBM once and the gradient written once.
+// Rows of up to kSmemRowMax bytes (V = 32768 in 16-bit is 64 KB) go through
+// a ring of three row buffers in shared memory, one persistent block per SM
+// (rows blockIdx.x, blockIdx.x + gridDim.x, ...). A producer warp keeps the
+// ring moving with bulk asynchronous copies: it stores each finished gradient
+// row and, once that store has read its buffer, loads the row three places
+// further into it. So while the 16 compute warps work on row k, the gradient
+// of row k-1 drains and rows k+1 and k+2 are loaded or loading: HBM sees a
+// steady stream of reads and writes instead of each row's load, arithmetic
+// and store in turn. Per row, each compute thread works on its own 16-byte
+// vectors:
+//  - pass A: its maximum m_t (16-bit rows: paired max on the packed halves,
+//    exact), then exp(x - m_t) once per element, summed, and with a gradient
+//    kept in place (rounded to the row type);
+//  - one barrier of the compute warps combines the (m_t, sum) pairs into the
+//    row's maximum M and S = sum exp(x - M) (each warp combines the per-warp
+//    pairs itself, in the same order, so every thread holds the same M, S);
+//  - pass B (with a gradient): grad = kept * (mul / S) * exp(m_t - M), and
+//    minus mul at the target.
+// The logits are read from HBM once and the gradient written once (in place
+// allowed). Exponentials: ex2.approx for 16-bit rows (rounded to 8 or 11
+// bits afterwards), exp2f for fp32 rows.
 constexpr int kSmemRowMax = 72 * 1024;
-constexpr int kSmemThreads = 256;
+constexpr int kRingCompute = 512;  // compute threads (warps 0-15)
+constexpr int kRingWarps = kRingCompute / 32;
+constexpr int kRingThreads = kRingCompute + 32;  // + the producer warp
+constexpr int kRingBufs = 3;
+
+// running maximum over the 16-byte vectors of a thread (16-bit rows: paired
+// max on the packed halves)
+template <typename T> struct RowMax {
+  uint32_t p = std::is_same<T, __half>::value ? 0xfc00fc00u : 0xff80ff80u;  // a pair of -inf
+  float f = -INFINITY;
+  FXB_DEV void max2(uint32_t w) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) asm("max.bf16x2 %0, %0, %1;" : "+r"(p) : "r"(w));
+    else asm("max.f16x2 %0, %0, %1;" : "+r"(p) : "r"(w));
+  }
+  FXB_DEV void add(const uint4& u) {
+    if constexpr (sizeof(T) == 2) {
+      max2(u.x); max2(u.y); max2(u.z); max2(u.w);
+    } else {
+      f = fmaxf(fmaxf(f, __uint_as_float(u.x)),
+                fmaxf(__uint_as_float(u.y), fmaxf(__uint_as_float(u.z), __uint_as_float(u.w))));
+    }
+  }
+  FXB_DEV float get() const {
+    if constexpr (sizeof(T) == 2) {
+      const float2 v = unpack2<T>(p);
+      return fmaxf(v.x, v.y);
+    } else {
+      return f;
+    }
+  }
+};
+
+template <typename T> FXB_DEV float ce_exp2(float x) {
+  if constexpr (sizeof(T) == 2) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+  } else {
+    return exp2f(x);
+  }
+}
+
+// barrier of the compute warps (named barrier 1) that also ANDs a predicate
+FXB_DEV bool compute_bar_and(bool v) {
+  int r;
+  asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.and.pred q, 1, %2, p;\n\t"
+               "selp.s32 %0, 1, 0, q;\n\t}"
+               : "=r"(r) : "r"((int)v), "n"(kRingCompute) : "memory");
+  return r != 0;
+}
 
 template <typename T>
-__global__ void __launch_bounds__(kSmemThreads)
-ce_smem_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
+__global__ void __launch_bounds__(kRingThreads, 1)
+ce_ring_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ target,
                T* grad, float* __restrict__ row_loss, const float* __restrict__ mul,
-               int64_t rows, int V, int64_t ignore_index, int* err) {
+               int64_t rows, int V, int64_t ignore_index, uint32_t buf_bytes, int* err) {
   constexpr int E = CEVec<T>::N;
-  constexpr int NW = kSmemThreads / 32;
-  extern __shared__ __align__(128) uint8_t srow_raw[];
-  __shared__ __align__(8) uint64_t full_bar;
-  __shared__ float red_m[NW], red_s[NW];
+  extern __shared__ __align__(128) uint8_t ring_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kRingBufs], done_bar[kRingBufs];
+  __shared__ float red_m[kRingWarps], red_s[kRingWarps];
   __shared__ float s_xt;
-  const uint32_t srow = smem_u32(srow_raw);
-  const uint32_t bar = smem_u32(&full_bar);
+  const uint32_t ring = smem_u32(ring_raw);
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int nvec = V / E;
   const uint32_t row_bytes = (uint32_t)V * sizeof(T);
+  const int64_t r0 = blockIdx.x, G = gridDim.x;
+  const int64_t nk = (rows - r0 + G - 1) / G;  // rows of this block (>= 1)
   if (tid == 0) {
-    mbar_init(bar, 1);
+    for (int i = 0; i < kRingBufs; ++i) {
+      mbar_init(smem_u32(&full_bar[i]), 1);  // the row's bulk load landed
+      mbar_init(smem_u32(&done_bar[i]), 1);  // the compute warps are done with the row
+    }
     fence_mbar_init();
   }
   __syncthreads();
   pdl_trigger();
   pdl_wait();  // inputs come from the previous kernel on the stream
-  const float gm = grad ? *mul : 0.f;
-  uint32_t phase = 0;
-  bool ok = true;
-  if (tid == 0 && (int64_t)blockIdx.x < rows) {
-    mbar_expect_tx(bar, row_bytes);
-    bulk_load_g2s(srow, logits + (int64_t)blockIdx.x * ld, row_bytes, bar);
-  }
-  for (int64_t r = blockIdx.x; r < rows && ok; r += gridDim.x) {
-    ok = mbar_wait(bar, phase, err, FXB_DERR_CE_WAIT);
-    phase ^= 1;
-    if (!ok) break;  // uniform: every thread saw the same barrier
-    const int64_t t = target[r];
-    const bool valid = (t != ignore_index) && (t >= 0) && (t < (int64_t)V);
-    // the target logit, read before pass 2 overwrites the row
-    if (tid == 0) s_xt = valid ? to_f<T>(reinterpret_cast<const T*>(srow_raw)[t]) : 0.f;
-    // pass 1: row maximum (no exponentials)
-    float m = -INFINITY;
-    for (int v = tid; v < nvec; v += kSmemThreads) {
-      float f[E];
-      unpack_row<T>(srow_raw, v, f);
-#pragma unroll
-      for (int j = 0; j < E; ++j) m = fmaxf(m, f[j]);
+
+  if (wid == kRingWarps) {
+    // ------------------------------------------------ producer (lane 0)
+    if (lane == 0) {
+      auto load = [&](int64_t u) {
+        const uint32_t bar = smem_u32(&full_bar[u % kRingBufs]);
+        mbar_expect_tx(bar, row_bytes);
+        bulk_load_g2s(ring + (uint32_t)(u % kRingBufs) * buf_bytes, logits + (r0 + u * G) * ld, row_bytes, bar);
+      };
+      int64_t loaded = 0;
+      for (; loaded < kRingBufs && loaded < nk; ++loaded) load(loaded);
+      for (int64_t u = 0; u < nk; ++u) {
+        const int b = (int)(u % kRingBufs);
+        if (!mbar_wait(smem_u32(&done_bar[b]), (uint32_t)((u / kRingBufs) & 1), err, FXB_DERR_CE_WAIT)) break;
+        if (grad) {
+          bulk_store_s2g(grad + (r0 + u * G) * ld, ring + (uint32_t)b * buf_bytes, row_bytes);
+          bulk_commit();
+        }
+        if (loaded < nk) {
+          if (grad) bulk_wait_read0();  // the store has read the buffer that the next load fills
+          load(loaded++);
+        }
+      }
+      // every load issued has landed (after an expired wait too) and every
+      // store has completed before shared memory goes away
+      for (int64_t u = loaded > kRingBufs ? loaded - kRingBufs : 0; u < loaded; ++u)
+        mbar_wait(smem_u32(&full_bar[u % kRingBufs]), (uint32_t)((u / kRingBufs) & 1), err, FXB_DERR_CE_WAIT);
+      bulk_wait_all0();
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red_m[wid] = m;
-    __syncthreads();
-    float M = red_m[0];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) M = fmaxf(M, red_m[w]);
-    // pass 2: one exp2 per element; its sum, and (with a gradient) the value
-    // exp(x - M) kept in place for pass 3
-    const float Ml = (M == -INFINITY) ? 0.f : M * kLog2e;  // all -inf: every term is 0
-    float s = 0.f;
-    for (int v = tid; v < nvec; v += kSmemThreads) {
+    __syncwarp();
+    return;
+  }
+
+  // ------------------------------------------------ compute warps 0-15
+  const float gm = grad ? *mul : 0.f;
+  int64_t t_next = target[r0];
+  for (int64_t k = 0; k < nk; ++k) {
+    const int64_t r = r0 + k * G;
+    const int b = (int)(k % kRingBufs);
+    uint8_t* srow = ring_raw + b * buf_bytes;
+    const int64_t t = t_next;
+    if (k + 1 < nk) t_next = target[r + G];  // one row ahead
+    const bool got = mbar_wait(smem_u32(&full_bar[b]), (uint32_t)((k / kRingBufs) & 1), err, FXB_DERR_CE_WAIT);
+    if (!compute_bar_and(got)) break;
+    const bool valid = (t != ignore_index) && (t >= 0) && (t < (int64_t)V);
+    const int tv = valid ? (int)(t / E) : -1;  // the vector holding the target
+    const int tj = valid ? (int)(t - (int64_t)tv * E) : 0;
+    // pass A
+    RowMax<T> rm;
+    for (int v = tid; v < nvec; v += kRingCompute) rm.add(reinterpret_cast<const uint4*>(srow)[v]);
+    const float m_t = rm.get();
+    const float ml = (m_t == -INFINITY) ? 0.f : m_t * kLog2e;  // all -inf: every term is 0
+    float s_t = 0.f;
+    for (int v = tid; v < nvec; v += kRingCompute) {
       float f[E];
-      unpack_row<T>(srow_raw, v, f);
+      unpack_row<T>(srow, v, f);
+      if (v == tv) {
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+          if (j == tj) s_xt = f[j];  // the target logit, before it is overwritten
+      }
       float e4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < E; ++j) {
-        f[j] = exp2f(fmaf(f[j], kLog2e, -Ml));
+        f[j] = ce_exp2<T>(fmaf(f[j], kLog2e, -ml));
         e4[j & 3] += f[j];
       }
-      s += (e4[0] + e4[1]) + (e4[2] + e4[3]);
-      if (grad) pack_row<T>(srow_raw, v, f);
+      s_t += (e4[0] + e4[1]) + (e4[2] + e4[3]);
+      if (grad) pack_row<T>(srow, v, f);
     }
-    s = warp_sum(s);
-    if (lane == 0) red_s[wid] = s;
-    __syncthreads();
-    float S = red_s[0];
+    // (m_t, s_t) -> per-warp pairs -> the row's M and S
+    float mw = m_t;
 #pragma unroll
-    for (int w = 1; w < NW; ++w) S += red_s[w];
-    const float xt = s_xt;
-    if (tid == 0) row_loss[r] = valid ? M + log2f(S) * kLn2 - xt : 0.f;
+    for (int o = 16; o; o >>= 1) mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, o));
+    const float rel = (m_t == -INFINITY) ? 0.f : exp2f((m_t - mw) * kLog2e);
+    const float sw = warp_sum(s_t * rel);
+    if (lane == 0) {
+      red_m[wid] = mw;
+      red_s[wid] = sw;
+    }
+    named_bar_sync(1, kRingCompute);
+    const float pm = lane < kRingWarps ? red_m[lane] : -INFINITY;
+    const float M = warp_max(pm);
+    const float S = warp_sum(pm == -INFINITY ? 0.f : red_s[lane & (kRingWarps - 1)] * exp2f((pm - M) * kLog2e));
+    if (tid == 0) row_loss[r] = valid ? M + log2f(S) * kLn2 - s_xt : 0.f;
     if (grad) {
-      // pass 3: gradient in place in shared memory, then one bulk store
-      const float scale = valid ? gm / S : 0.f;
-      for (int v = tid; v < nvec; v += kSmemThreads) {
+      // pass B: the gradient in place, stored by the producer
+      const float sc = (valid && m_t != -INFINITY) ? gm / S * exp2f((m_t - M) * kLog2e) : 0.f;
+      for (int v = tid; v < nvec; v += kRingCompute) {
         float f[E];
-        unpack_row<T>(srow_raw, v, f);
+        unpack_row<T>(srow, v, f);
 #pragma unroll
-        for (int j = 0; j < E; ++j) {
-          f[j] *= scale;
-          if ((int64_t)(v * E + j) == t && valid) f[j] -= gm;
+        for (int j = 0; j < E; ++j) f[j] *= sc;
+        if (v == tv) {
+#pragma unroll
+          for (int j = 0; j < E; ++j)
+            if (j == tj) f[j] -= gm;
         }
-        pack_row<T>(srow_raw, v, f);
-      }
-      fence_proxy_async_smem();
-    }
-    __syncthreads();  // row consumed (and the gradient staged)
-    if (tid == 0) {
-      if (grad) {
-        bulk_store_s2g(grad + r * ld, srow, row_bytes);
-        bulk_commit();
-        bulk_wait_read0();  // the buffer is free once the store has read it
-      }
-      const int64_t rn = r + gridDim.x;
-      if (rn < rows) {
-        mbar_expect_tx(bar, row_bytes);
-        bulk_load_g2s(srow, logits + rn * ld, row_bytes, bar);
+        pack_row<T>(srow, v, f);
       }
     }
+    // this thread's shared-memory accesses of the row come before the
+    // producer's bulk copies out of / into the buffer
+    fence_proxy_async_smem();
+    named_bar_sync(1, kRingCompute);  // row consumed, gradient staged, s_xt / red_* free for the next row
+    if (tid == 0) mbar_arrive(smem_u32(&done_bar[b]));
   }
-  if (tid == 0) bulk_wait_all0();
 }
 
 // Generic path (any V, any alignment): block per row, three streaming passes.
@@ -340,18 +426,20 @@ int launch_ce(const void* lg, int64_t ld, const int64_t* tg, void* gr, float* lo
   if (vec_ok && row_bytes > 32 * 1024 && row_bytes <= (size_t)kSmemRowMax && (ld * sizeof(T)) % 16 == 0) {
     int* err = fxb::dev_error_ptr();
     if (!err) return FXB_ECUDA;
-    auto k = ce_smem_kernel<T>;
+    auto k = ce_ring_kernel<T>;
+    const uint32_t buf_bytes = (uint32_t)((row_bytes + 127) / 128 * 128);
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
       int r = fxb::check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   kSmemRowMax), "ce smem attribute");
+                                                   kRingBufs * kSmemRowMax), "ce ring attribute");
       if (r) return r;
       attr_set[dev] = true;
     }
-    int blocks = (int)(rows < (int64_t)sms * 3 ? rows : (int64_t)sms * 3);
-    fxb::pdl_launch(k, blocks, kSmemThreads, row_bytes, st, L, ld, tg, G, loss, mul, rows, V, ign, err);
+    int blocks = (int)(rows < (int64_t)sms ? rows : (int64_t)sms);
+    fxb::pdl_launch(k, blocks, kRingThreads, (size_t)kRingBufs * buf_bytes, st, L, ld, tg, G, loss, mul, rows,
+                    V, ign, buf_bytes, err);
     return fxb::check_launch("ce_fwd_grad(smem)");
   }
   if (vec_ok && nvec <= 512 * 16) {
