@@ -902,6 +902,19 @@ __global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, T16* __re
 }
 
 
+// Persistent: one CTA per SM walks work items (key tile, batch*head) in rounds
+// of gridDim.x items (CTA order in even rounds, reverse order in odd ones);
+// items are numbered key tile major, so with a causal mask (key tile kt meets
+// nqt - kt query tiles) they come heaviest first and the CTAs' totals even
+// out. Per item the CTA walks the query tiles that see its key tile. Tensor
+// memory stays allocated across items and every ring and barrier runs on
+// across them (phases from the running tile count u and item count k), so
+// one item's last tiles, its dK / dV epilogue and the next item's K / V load
+// overlap instead of each CTA filling and draining the pipeline alone:
+//  - the next item's K / V are prefetched into L2 when an item starts and
+//    loaded once every MMA of the item has completed (kv_empty);
+//  - the next item's first dV / dK MMAs wait until the softmax warps have
+//    read the finished dK / dV out of tensor memory (acc_empty).
 template <int FMT>
 __global__ void __launch_bounds__(768, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -934,20 +947,31 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t dq_full = s_full + 24u;
   const uint32_t dq_empty = s_full + 32u;
   const uint32_t acc_full = s_full + 40u;
-  const uint32_t pt_free = s_full + 48u;  // dV of the tile has read P^T from tensor memory
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (pt_free + 8u - base));
+  const uint32_t pt_free = s_full + 48u;   // dV of the tile has read P^T from tensor memory
+  const uint32_t kv_empty = s_full + 56u;  // every MMA of the item has completed: K / V free
+  const uint32_t acc_empty = s_full + 64u; // the softmax warps have read the item's dK / dV
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (acc_empty + 8u - base));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // one CTA per (key tile, batch*head), numbered key tile major: with a causal
-  // mask key tile kt meets nqt - kt query tiles, so the CTAs are launched
-  // heaviest first and the last ones to start are the shortest
   const int BH = p.B * p.H;
-  const int kt = (int)(blockIdx.x / BH);
-  const int bh = (int)(blockIdx.x - kt * BH);
-  const int b = bh / p.H, h = bh - b * p.H;
-  const int kv0 = kt * TILE;
-  const int i0 = p.causal ? kt : 0;
-  const int n_it = p.nqt - i0;
+  const int n_items = p.nkt * BH;
+  auto item_of = [&](int k) {
+    const int r = k * (int)gridDim.x;
+    return (k & 1) ? r + (int)gridDim.x - 1 - (int)blockIdx.x : r + (int)blockIdx.x;
+  };
+  // item w -> key tile, batch*head and its query tiles [i0, nqt)
+  struct Item { int kv0, bh, b, h, i0, n_it; };
+  auto item = [&](int w) {
+    Item t;
+    const int kt = w / BH;
+    t.bh = w - kt * BH;
+    t.b = t.bh / p.H;
+    t.h = t.bh - t.b * p.H;
+    t.kv0 = kt * TILE;
+    t.i0 = p.causal ? kt : 0;
+    t.n_it = p.nqt - t.i0;
+    return t;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -962,6 +986,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     mbar_init(dq_empty, 128);  // every dQ flush thread
     mbar_init(acc_full, 1);
     mbar_init(pt_free, 1);
+    mbar_init(kv_empty, 1);
+    mbar_init(acc_empty, 512);  // every softmax thread
     fence_mbar_init();
   }
   if (warp == kBwd64WarpMma) {
@@ -979,54 +1005,80 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   if (warp == kBwd64WarpTma) {
     // ------------------------------------------------ producer: TMA (lane 0)
-    // plus the query tile's LSE (log2 units) and delta, four queries per lane,
-    // into the same double buffer as Q / dO
+    // plus each query tile's LSE (log2 units) and delta, four queries per
+    // lane, into the same ring stage as its Q / dO
     if (lane == 0) {
       tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV); tma_prefetch_desc(&tmDO);
-      mbar_expect_tx(kv_full, 2 * QB);
-      tma_load_4d(sK, &tmK, kv_full, 0, kv0, h, b);
-      tma_load_4d(sV, &tmV, kv_full, 0, kv0, h, b);
     }
     __syncwarp();
-    int armed = 0;
+    bool ok = true;
+    int u = 0;        // query tiles issued (all items)
+    int kv_loads = 0; // K / V loads issued
     // LSE / delta of a query tile are read from global memory one tile ahead
     // into registers, so that their latency passes while the producer waits
     // for the stage to be freed instead of after it
     float nl[4], nd[4];
-    auto prefetch = [&](int it) {
-      const int qq0 = (i0 + it) * TILE;
+    auto prefetch = [&](int bh, int qt) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int q = qq0 + lane * 4 + i;
+        const int q = qt * TILE + lane * 4 + i;
         const bool v = q < p.T;
         nl[i] = v ? p.lse[(int64_t)bh * p.T + q] * kLog2e : INFINITY;
         nd[i] = v ? p.delta[(int64_t)bh * p.T + q] : 0.f;
       }
     };
-    if (n_it > 0) prefetch(0);
-    for (int it = 0; it < n_it; ++it) {
-      const int st = it % QS;
-      const int qq0 = (i0 + it) * TILE;
-      if (!mbar_wait_warp(qdo_empty(st), ((it / QS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
+    if (item_of(0) < n_items) {
+      const Item t0 = item(item_of(0));
+      prefetch(t0.bh, t0.i0);
+    }
+    for (int k = 0, w = item_of(0); w < n_items && ok; w = item_of(++k)) {
+      const Item t = item(w);
+      const int wn = item_of(k + 1);
       if (lane == 0) {
-        mbar_expect_tx(qdo_full(st), 2 * QB);
-        tma_load_4d(sQ + st * QB, &tmQ, qdo_full(st), 0, qq0, h, b);
-        tma_load_4d(sDO + st * QB, &tmDO, qdo_full(st), 0, qq0, h, b);
+        // K / V of this item, once every MMA of the previous item has completed
+        if (!mbar_wait(kv_empty, (k & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) ok = false;
+        if (ok) {
+          mbar_expect_tx(kv_full, 2 * QB);
+          tma_load_4d(sK, &tmK, kv_full, 0, t.kv0, t.h, t.b);
+          tma_load_4d(sV, &tmV, kv_full, 0, t.kv0, t.h, t.b);
+          ++kv_loads;
+          if (wn < n_items) {  // the next item's K / V into L2
+            const Item tn = item(wn);
+            tma_prefetch_l2_4d(&tmK, 0, tn.kv0, tn.h, tn.b);
+            tma_prefetch_l2_4d(&tmV, 0, tn.kv0, tn.h, tn.b);
+          }
+        }
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      for (int it = 0; it < t.n_it && ok; ++it, ++u) {
+        const int st = u % QS;
+        const int qq0 = (t.i0 + it) * TILE;
+        if (!mbar_wait_warp(qdo_empty(st), ((u / QS) & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_expect_tx(qdo_full(st), 2 * QB);
+          tma_load_4d(sQ + st * QB, &tmQ, qdo_full(st), 0, qq0, t.h, t.b);
+          tma_load_4d(sDO + st * QB, &tmDO, qdo_full(st), 0, qq0, t.h, t.b);
+        }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        lse_s[st * 128 + lane * 4 + i] = nl[i];
-        del_s[st * 128 + lane * 4 + i] = nd[i];
+        for (int i = 0; i < 4; ++i) {
+          lse_s[st * 128 + lane * 4 + i] = nl[i];
+          del_s[st * 128 + lane * 4 + i] = nd[i];
+        }
+        mbar_arrive(qdo_full(st));
+        if (it + 1 < t.n_it) {
+          prefetch(t.bh, t.i0 + it + 1);
+        } else if (wn < n_items) {
+          const Item tn = item(wn);
+          prefetch(tn.bh, tn.i0);
+        }
       }
-      mbar_arrive(qdo_full(st));
-      armed = it + 1;
-      if (it + 1 < n_it) prefetch(it + 1);
     }
     if (lane == 0) {
-      mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
-      for (int it = (armed > QS ? armed - QS : 0); it < armed; ++it)
-        mbar_wait(qdo_full(it % QS), (it / QS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      // every copy issued has landed before shared memory goes away
+      if (kv_loads > 0) mbar_wait(kv_full, (kv_loads - 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
+      for (int v = (u > QS ? u - QS : 0); v < u; ++v)
+        mbar_wait(qdo_full(v % QS), (v / QS) & 1, p.err, FXB_DERR_ATTN_WAIT);
     }
     __syncwarp();
   } else if (warp == kBwd64WarpMma) {
@@ -1035,14 +1087,16 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       constexpr uint32_t I_SS = umma_idesc_f16(FMT, 0, 0, TILE, TILE);  // S^T, dP^T
       constexpr uint32_t I_KV = umma_idesc_f16(FMT, 0, 1, TILE, DH);    // dV, dK
       constexpr uint32_t I_Q = umma_idesc_f16(FMT, 1, 1, TILE, DH);     // dQ
-      bool ok = mbar_wait(kv_full, 0, p.err, FXB_DERR_ATTN_WAIT);
-      // S^T and dP^T of query tile `it` (once its Q / dO have landed and the
-      // previous S^T / dP^T have been read out of tensor memory)
-      auto issue_s = [&](int it) -> bool {
-        const int st = it % QS;
+      bool ok = true;
+      int u = 0;  // query tiles of all items so far
+      int k = 0;
+      // S^T and dP^T of the running tile v (once its Q / dO have landed and
+      // the previous S^T / dP^T have been read out of tensor memory)
+      auto issue_s = [&](int v) -> bool {
+        const int st = v % QS;
         const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
-        if (!mbar_wait(qdo_full(st), (it / QS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
-        if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(qdo_full(st), (v / QS) & 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
+        if (!mbar_wait(s_empty, (v & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) return false;
         tc_fence_after();
         const uint64_t kd = kmajor_desc0(sK), qd = kmajor_desc0(q_s);
         const uint64_t vd = kmajor_desc0(sV), dod = kmajor_desc0(do_s);
@@ -1055,41 +1109,51 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         umma_commit(s_full);
         return true;
       };
-      if (ok && n_it > 0) ok = issue_s(0);
-      for (int it = 0; it < n_it && ok; ++it) {
-        // the next tile's scores run on the tensor core while the softmax
-        // warps turn this tile's scores into P^T and dS^T
-        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
-        const int st = it % QS;
-        const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
-        if (!mbar_wait(ds_full, it & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t ds_s = sDS + (uint32_t)(it & 1) * 32768u;
-        const uint64_t dsd = kmajor_desc0(ds_s);
-        const uint64_t dom = mnmajor_desc0(do_s), qm = mnmajor_desc0(q_s);
+      for (int w = item_of(0); w < n_items && ok; w = item_of(++k)) {
+        const Item t = item(w);
+        if (!mbar_wait(kv_full, k & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+        const int u0 = u;
+        if (t.n_it > 0 && !issue_s(u0)) { ok = false; break; }
+        for (int it = 0; it < t.n_it && ok; ++it, ++u) {
+          // the next tile's scores run on the tensor core while the softmax
+          // warps turn this tile's scores into P^T and dS^T
+          if (it + 1 < t.n_it && !issue_s(u + 1)) { ok = false; break; }
+          const int st = u % QS;
+          const uint32_t q_s = sQ + st * QB, do_s = sDO + st * QB;
+          if (!mbar_wait(ds_full, u & 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          // the previous item's dK / dV have left tensor memory
+          if (it == 0 && !mbar_wait(acc_empty, (k & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ds_s = sDS + (uint32_t)(u & 1) * 32768u;
+          const uint64_t dsd = kmajor_desc0(ds_s);
+          const uint64_t dom = mnmajor_desc0(do_s), qm = mnmajor_desc0(q_s);
 #pragma unroll
-        for (int kk = 0; kk < TILE / 16; ++kk)  // A = P^T from tensor memory, 16 queries = 8 columns
-          umma_f16_ta(tDV, tPT + kk * 8, desc_add(dom, mnmajor_off(kk)), I_KV, (it > 0 || kk > 0));
-        // completes when dV has read P^T and every earlier MMA (the previous
-        // tile's dQ, the last reader of the other dS^T buffer) is done
-        umma_commit(pt_free);
+          for (int kk = 0; kk < TILE / 16; ++kk)  // A = P^T from tensor memory, 16 queries = 8 columns
+            umma_f16_ta(tDV, tPT + kk * 8, desc_add(dom, mnmajor_off(kk)), I_KV, (it > 0 || kk > 0));
+          // completes when dV has read P^T and every earlier MMA (the previous
+          // tile's dQ, the last reader of the other dS^T buffer) is done
+          umma_commit(pt_free);
 #pragma unroll
-        for (int kk = 0; kk < TILE / 16; ++kk)
-          umma_f16(tDK, desc_add(dsd, kmajor_off(kk)), desc_add(qm, mnmajor_off(kk)), I_KV,
-                   (it > 0 || kk > 0));
-        // Q / dO of this tile have no readers after dK (dQ reads dS and K): the
-        // producer may load tile it + QS into the stage now
-        umma_commit(qdo_empty(st));
-        if (!mbar_wait(dq_empty, (it & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
-        tc_fence_after();
-        const uint64_t dsm = mnmajor_desc0(ds_s), km = mnmajor_desc0(sK);
+          for (int kk = 0; kk < TILE / 16; ++kk)
+            umma_f16(tDK, desc_add(dsd, kmajor_off(kk)), desc_add(qm, mnmajor_off(kk)), I_KV,
+                     (it > 0 || kk > 0));
+          // Q / dO of this tile have no readers after dK (dQ reads dS and K): the
+          // producer may load tile u + QS into the stage now
+          umma_commit(qdo_empty(st));
+          if (!mbar_wait(dq_empty, (u & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t dsm = mnmajor_desc0(ds_s), km = mnmajor_desc0(sK);
 #pragma unroll
-        for (int kk = 0; kk < TILE / 16; ++kk)
-          umma_f16(tDQ, desc_add(dsm, mnmajor_off(kk)), desc_add(km, mnmajor_off(kk)), I_Q, kk > 0);
-        umma_commit(dq_full);
+          for (int kk = 0; kk < TILE / 16; ++kk)
+            umma_f16(tDQ, desc_add(dsm, mnmajor_off(kk)), desc_add(km, mnmajor_off(kk)), I_Q, kk > 0);
+          umma_commit(dq_full);
+        }
+        if (!ok) break;
+        umma_commit(acc_full);  // dK / dV of the item are final
+        umma_commit(kv_empty);  // and K / V have no readers left
       }
-      umma_commit(acc_full);
-      mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT);
+      // every MMA issued has completed before tensor memory is freed
+      if (k > 0) mbar_wait(acc_full, (k - 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
     }
     __syncwarp();
   } else if (warp >= kBwd64WarpFlush) {
@@ -1105,38 +1169,43 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t stg = sDQ + (uint32_t)quarter * 4096u;
     const int sw = (lane >> 1) & 3;
-    for (int it = 0; it < n_it; ++it) {
-      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) break;
-      tc_fence_after();
+    bool ok = true;
+    int u = 0;
+    for (int k = 0, w = item_of(0); w < n_items && ok; w = item_of(++k)) {
+      const Item t = item(w);
+      for (int it = 0; it < t.n_it; ++it, ++u) {
+        if (!__all_sync(0xffffffffu, mbar_wait(dq_full, u & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
-      for (int rd = 0; rd < 2; ++rd) {
-        uint32_t rr[32];
-        tmem_ld16(tDQ + lane_off + rd * 32, rr);
-        tmem_ld16(tDQ + lane_off + rd * 32 + 16, rr + 16);
-        tmem_wait_ld();
-        if (rd == 1) {
-          tc_fence_before();
-          mbar_arrive(dq_empty);  // the dQ partial has left tensor memory
-        }
-        if (lane == 0) bulk_wait_read0();  // the previous round's reductions have read the staging
-        __syncwarp();
+        for (int rd = 0; rd < 2; ++rd) {
+          uint32_t rr[32];
+          tmem_ld16(tDQ + lane_off + rd * 32, rr);
+          tmem_ld16(tDQ + lane_off + rd * 32 + 16, rr + 16);
+          tmem_wait_ld();
+          if (rd == 1) {
+            tc_fence_before();
+            mbar_arrive(dq_empty);  // the dQ partial has left tensor memory
+          }
+          if (lane == 0) bulk_wait_read0();  // the previous round's reductions have read the staging
+          __syncwarp();
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t row = stg + (uint32_t)c * 2048u + (uint32_t)lane * 64u;
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t row = stg + (uint32_t)c * 2048u + (uint32_t)lane * 64u;
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            st_shared_v4(row + (uint32_t)((j ^ sw) << 4),
-                         make_uint4(rr[16 * c + 4 * j], rr[16 * c + 4 * j + 1], rr[16 * c + 4 * j + 2],
-                                    rr[16 * c + 4 * j + 3]));
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
+            for (int j = 0; j < 4; ++j)
+              st_shared_v4(row + (uint32_t)((j ^ sw) << 4),
+                           make_uint4(rr[16 * c + 4 * j], rr[16 * c + 4 * j + 1], rr[16 * c + 4 * j + 2],
+                                      rr[16 * c + 4 * j + 3]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-            tma_reduce_add_3d(&tmDQ, stg + (uint32_t)c * 2048u, rd * 32 + c * 16,
-                              (i0 + it) * TILE + quarter * 32, bh);
-          bulk_commit();
+            for (int c = 0; c < 2; ++c)
+              tma_reduce_add_3d(&tmDQ, stg + (uint32_t)c * 2048u, rd * 32 + c * 16,
+                                (t.i0 + it) * TILE + quarter * 32, t.bh);
+            bulk_commit();
+          }
         }
       }
     }
@@ -1150,114 +1219,119 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     // through the tensor-memory and barrier latencies of the chain
     const int quarter = warp & 3, part = warp >> 2;
     const int r = quarter * 32 + lane;
-    const int kv = kv0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int qc0 = part * 32;
     bool ok = true;
-    // P^T / dS^T of tile it are computed while the dV / dK / dQ MMAs of tile
-    // it-1 run, 16 queries at a time, each half stored as soon as it is done
-    // (P^T to tensor memory, dS^T to shared buffer it & 1) once the previous
-    // tile's dV has read P^T (pt_free, which also covers the dQ of tile it-2,
+    int u = 0;
+    // P^T / dS^T of tile u are computed while the dV / dK / dQ MMAs of tile
+    // u-1 run, 16 queries at a time, each half stored as soon as it is done
+    // (P^T to tensor memory, dS^T to shared buffer u & 1) once the previous
+    // tile's dV has read P^T (pt_free, which also covers the dQ of tile u-2,
     // the last reader of this dS^T buffer).
     // The query tile's LSE / delta were written to the ring stage by the
     // producer warp before it arrived on qdo_full; waiting on that barrier here
     // makes them visible.
-    for (int it = 0; it < n_it; ++it) {
-      const int q0 = (i0 + it) * TILE;
-      const int sb = it % QS;
-      if (!ok) continue;
-      // waits are made warp-uniform: the tensor-memory loads that follow are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(qdo_full(sb), (it / QS) & 1, p.err, FXB_DERR_ATTN_WAIT)) ||
-          !__all_sync(0xffffffffu, mbar_wait(s_full, it & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; continue; }
-      tc_fence_after();
-      const bool diag = p.causal && (q0 < kv0 + TILE);
-      // tile-uniform: every (key, query) pair of the tile is kept (queries past
-      // T carry LSE = +inf, so their P and dS are zero without a mask)
-      const bool full = !diag && kv0 + TILE <= p.T;
-      uint8_t* ds = gbase + (sDS - base) + (it & 1) * 32768;
+    for (int k = 0, w = item_of(0); w < n_items && ok; w = item_of(++k)) {
+      const Item t = item(w);
+      const int kv = t.kv0 + r;
+      for (int it = 0; it < t.n_it; ++it, ++u) {
+        const int q0 = (t.i0 + it) * TILE;
+        const int sb = u % QS;
+        // waits are made warp-uniform: the tensor-memory loads that follow are warp-collective
+        if (!__all_sync(0xffffffffu, mbar_wait(qdo_full(sb), (u / QS) & 1, p.err, FXB_DERR_ATTN_WAIT)) ||
+            !__all_sync(0xffffffffu, mbar_wait(s_full, u & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; break; }
+        tc_fence_after();
+        const bool diag = p.causal && (q0 < t.kv0 + TILE);
+        // tile-uniform: every (key, query) pair of the tile is kept (queries past
+        // T carry LSE = +inf, so their P and dS are zero without a mask)
+        const bool full = !diag && t.kv0 + TILE <= p.T;
+        uint8_t* ds = gbase + (sDS - base) + (u & 1) * 32768;
 #pragma unroll
-      for (int hq = 0; hq < 2; ++hq) {
-        uint32_t sr[16], dr[16];
-        tmem_ld16(tST + lane_off + qc0 + hq * 16, sr);
-        tmem_ld16(tDPT + lane_off + qc0 + hq * 16, dr);
-        tmem_wait_ld();
-        if (hq == 1) {
-          tc_fence_before();
-          mbar_arrive(s_empty);  // S^T / dP^T are in registers: the next tile's may overwrite them
-        }
-        // the 16 queries' LSE (log2 units) and delta: 16-byte shared loads
-        float ls[16], dl[16];
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const float4 a = *reinterpret_cast<const float4*>(lse_s + sb * 128 + qc0 + hq * 16 + 4 * v4);
-          const float4 c = *reinterpret_cast<const float4*>(del_s + sb * 128 + qc0 + hq * 16 + 4 * v4);
-          ls[4 * v4] = a.x; ls[4 * v4 + 1] = a.y; ls[4 * v4 + 2] = a.z; ls[4 * v4 + 3] = a.w;
-          dl[4 * v4] = c.x; dl[4 * v4 + 1] = c.y; dl[4 * v4 + 2] = c.z; dl[4 * v4 + 3] = c.w;
-        }
-        uint32_t pw[8], dw[8];  // P^T and dS^T of 16 queries, 16-bit pairs
-        if (full) {
-          // no causal or key-row mask in this tile: exp2, subtract, multiply, pack
-#pragma unroll
-          for (int qc = 0; qc < 16; qc += 2) {
-            const float e0 = ex2_ftz(fmaf(__uint_as_float(sr[qc]), p.scale_log2, -ls[qc]));
-            const float e1 = ex2_ftz(fmaf(__uint_as_float(sr[qc + 1]), p.scale_log2, -ls[qc + 1]));
-            pw[qc >> 1] = pack2<T16>(e0, e1);
-            dw[qc >> 1] = pack2<T16>(e0 * (__uint_as_float(dr[qc]) - dl[qc]),
-                                     e1 * (__uint_as_float(dr[qc + 1]) - dl[qc + 1]));
+        for (int hq = 0; hq < 2; ++hq) {
+          uint32_t sr[16], dr[16];
+          tmem_ld16(tST + lane_off + qc0 + hq * 16, sr);
+          tmem_ld16(tDPT + lane_off + qc0 + hq * 16, dr);
+          tmem_wait_ld();
+          if (hq == 1) {
+            tc_fence_before();
+            mbar_arrive(s_empty);  // S^T / dP^T are in registers: the next tile's may overwrite them
           }
-        } else {
+          // the 16 queries' LSE (log2 units) and delta: 16-byte shared loads
+          float ls[16], dl[16];
 #pragma unroll
-          for (int qc = 0; qc < 16; qc += 2) {
-            float pp[2], dd[2];
+          for (int v4 = 0; v4 < 4; ++v4) {
+            const float4 a = *reinterpret_cast<const float4*>(lse_s + sb * 128 + qc0 + hq * 16 + 4 * v4);
+            const float4 c = *reinterpret_cast<const float4*>(del_s + sb * 128 + qc0 + hq * 16 + 4 * v4);
+            ls[4 * v4] = a.x; ls[4 * v4 + 1] = a.y; ls[4 * v4 + 2] = a.z; ls[4 * v4 + 3] = a.w;
+            dl[4 * v4] = c.x; dl[4 * v4 + 1] = c.y; dl[4 * v4 + 2] = c.z; dl[4 * v4 + 3] = c.w;
+          }
+          uint32_t pw[8], dw[8];  // P^T and dS^T of 16 queries, 16-bit pairs
+          if (full) {
+            // no causal or key-row mask in this tile: exp2, subtract, multiply, pack
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              float e = ex2_ftz(fmaf(__uint_as_float(sr[qc + i]), p.scale_log2, -ls[qc + i]));
-              if (kv >= p.T || (diag && q0 + qc0 + hq * 16 + qc + i < kv)) e = 0.f;
-              pp[i] = e;
-              dd[i] = e * (__uint_as_float(dr[qc + i]) - dl[qc + i]);
+            for (int qc = 0; qc < 16; qc += 2) {
+              const float e0 = ex2_ftz(fmaf(__uint_as_float(sr[qc]), p.scale_log2, -ls[qc]));
+              const float e1 = ex2_ftz(fmaf(__uint_as_float(sr[qc + 1]), p.scale_log2, -ls[qc + 1]));
+              pw[qc >> 1] = pack2<T16>(e0, e1);
+              dw[qc >> 1] = pack2<T16>(e0 * (__uint_as_float(dr[qc]) - dl[qc]),
+                                       e1 * (__uint_as_float(dr[qc + 1]) - dl[qc + 1]));
             }
-            pw[qc >> 1] = pack2<T16>(pp[0], pp[1]);
-            dw[qc >> 1] = pack2<T16>(dd[0], dd[1]);
-          }
-        }
-        if (hq == 0 && it > 0 &&
-            !__all_sync(0xffffffffu, mbar_wait(pt_free, (it - 1) & 1, p.err, FXB_DERR_ATTN_WAIT))) {
-          ok = false;
-          break;
-        }
-        if (hq == 0) tc_fence_after();
-        tmem_st8(tPT + lane_off + part * 16 + hq * 8, pw);
+          } else {
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
-          *reinterpret_cast<uint4*>(ds + sw128_offset(r, part * 4 + hq * 2 + u)) =
-              make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+            for (int qc = 0; qc < 16; qc += 2) {
+              float pp[2], dd[2];
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                float e = ex2_ftz(fmaf(__uint_as_float(sr[qc + i]), p.scale_log2, -ls[qc + i]));
+                if (kv >= p.T || (diag && q0 + qc0 + hq * 16 + qc + i < kv)) e = 0.f;
+                pp[i] = e;
+                dd[i] = e * (__uint_as_float(dr[qc + i]) - dl[qc + i]);
+              }
+              pw[qc >> 1] = pack2<T16>(pp[0], pp[1]);
+              dw[qc >> 1] = pack2<T16>(dd[0], dd[1]);
+            }
+          }
+          if (hq == 0 && u > 0 &&
+              !__all_sync(0xffffffffu, mbar_wait(pt_free, (u - 1) & 1, p.err, FXB_DERR_ATTN_WAIT))) {
+            ok = false;
+            break;
+          }
+          if (hq == 0) tc_fence_after();
+          tmem_st8(tPT + lane_off + part * 16 + hq * 8, pw);
+#pragma unroll
+          for (int v2 = 0; v2 < 2; ++v2)
+            *reinterpret_cast<uint4*>(ds + sw128_offset(r, part * 4 + hq * 2 + v2)) =
+                make_uint4(dw[4 * v2], dw[4 * v2 + 1], dw[4 * v2 + 2], dw[4 * v2 + 3]);
+        }
+        if (!ok) break;
+        tmem_wait_st();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(ds_full);
       }
-      if (!ok) continue;
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(ds_full);
-    }
-    // final dK (scaled) and dV for key row kv, head dims part*16..+16
-    if (__all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0, p.err, FXB_DERR_ATTN_WAIT))) {
+      if (!ok) break;
+      // the item's final dK (scaled) and dV for key row kv, head dims part*16..+16
+      if (!__all_sync(0xffffffffu, mbar_wait(acc_full, k & 1, p.err, FXB_DERR_ATTN_WAIT))) { ok = false; break; }
       tc_fence_after();
       uint32_t rk[16], rv[16];
       tmem_ld16(tDK + lane_off + part * 16, rk);
       tmem_ld16(tDV + lane_off + part * 16, rv);
       tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(acc_empty);  // the next item's first dV / dK MMAs may overwrite them
       if (kv < p.T) {
-        T16* krow = static_cast<T16*>(p.dk) + b * p.dk_sb + (int64_t)kv * p.dk_st + h * p.dk_sh + part * 16;
-        T16* vrow = static_cast<T16*>(p.dv) + b * p.dv_sb + (int64_t)kv * p.dv_st + h * p.dv_sh + part * 16;
+        T16* krow = static_cast<T16*>(p.dk) + t.b * p.dk_sb + (int64_t)kv * p.dk_st + t.h * p.dk_sh + part * 16;
+        T16* vrow = static_cast<T16*>(p.dv) + t.b * p.dv_sb + (int64_t)kv * p.dv_st + t.h * p.dv_sh + part * 16;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int v2 = 0; v2 < 2; ++v2) {
           float fk[8], fv[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            fk[i] = __uint_as_float(rk[8 * u + i]) * p.scale;
-            fv[i] = __uint_as_float(rv[8 * u + i]);
+            fk[i] = __uint_as_float(rk[8 * v2 + i]) * p.scale;
+            fv[i] = __uint_as_float(rv[8 * v2 + i]);
           }
-          *reinterpret_cast<uint4*>(krow + 8 * u) = pack8<T16>(fk);
-          *reinterpret_cast<uint4*>(vrow + 8 * u) = pack8<T16>(fv);
+          *reinterpret_cast<uint4*>(krow + 8 * v2) = pack8<T16>(fk);
+          *reinterpret_cast<uint4*>(vrow + 8 * v2) = pack8<T16>(fv);
         }
       }
     }
@@ -1853,7 +1927,8 @@ int launch_bwd(const fxb_attn_args* a, cudaStream_t st) {
     if ((r = set_smem(k, bwd_smem()))) return r;
     once[dev & 63] = true;
   }
-  dim3 grid((unsigned)(p.nkt * a->B * a->H));
+  const int items = p.nkt * a->B * a->H;
+  dim3 grid((unsigned)(items < fxb::num_sms() ? items : fxb::num_sms()));  // persistent
   fxb::pdl_launch(k, grid, kBwd64Threads, bwd_smem(), st, mq, mk, mv, mdo, mdq, p);
   if ((r = fxb::check_launch("attn_bwd"))) return r;
   const int64_t n = rows * (DH / 8);

@@ -267,6 +267,13 @@ FXB_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+// hint: bring a tile of a 4-D tensor map into L2 (no shared memory, no barrier)
+FXB_DEV void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
 // shared -> global tile store and fp32 add-reduction (bulk-group completion);
 // the coordinates are never negative here
 FXB_DEV void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
