@@ -34,10 +34,11 @@ constexpr int kFwdThreads = 576;  // forward: warps 0-15 softmax, 16 MMA, 17 TMA
 constexpr int kBwdThreads = 576;  // backward: warps 0-15 softmax / dS, 16 MMA, 17 TMA
 constexpr int kBwdWarpMma = 16, kBwdWarpTma = 17;
 // head-dim-64 backward: warps 0-15 softmax / dS (four per TMEM lane quarter),
-// 16-19 dQ flush (one per quarter), 20 MMA, 21 TMA; the register cap comes
-// from 768 threads (6 warps x 80 registers per sub-partition)
-constexpr int kBwd64Threads = 704;
-constexpr int kBwd64WarpFlush = 16, kBwd64WarpMma = 20, kBwd64WarpTma = 21;
+// 16-19 dQ flush (one per quarter), 20 MMA, 21 TMA for Q / dO, 22 TMA for
+// K / V; the register cap comes from 768 threads (6 warps x 80 registers per
+// sub-partition)
+constexpr int kBwd64Threads = 736;
+constexpr int kBwd64WarpFlush = 16, kBwd64WarpMma = 20, kBwd64WarpTma = 21, kBwd64WarpKV = 22;
 constexpr int kBwdQS = 3;  // head-dim-64 backward: Q / dO ring stages
 constexpr int kFwdWarpMma = 16, kFwdWarpTma = 17;
 // Forward pipeline depths: K/V ring stages and Q buffers (shared memory:
@@ -1013,8 +1014,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     __syncwarp();
     bool ok = true;
-    int u = 0;        // query tiles issued (all items)
-    int kv_loads = 0; // K / V loads issued
+    int u = 0;  // query tiles issued (all items)
     // LSE / delta of a query tile are read from global memory one tile ahead
     // into registers, so that their latency passes while the producer waits
     // for the stage to be freed instead of after it
@@ -1035,22 +1035,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     for (int k = 0, w = item_of(0); w < n_items && ok; w = item_of(++k)) {
       const Item t = item(w);
       const int wn = item_of(k + 1);
-      if (lane == 0) {
-        // K / V of this item, once every MMA of the previous item has completed
-        if (!mbar_wait(kv_empty, (k & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) ok = false;
-        if (ok) {
-          mbar_expect_tx(kv_full, 2 * QB);
-          tma_load_4d(sK, &tmK, kv_full, 0, t.kv0, t.h, t.b);
-          tma_load_4d(sV, &tmV, kv_full, 0, t.kv0, t.h, t.b);
-          ++kv_loads;
-          if (wn < n_items) {  // the next item's K / V into L2
-            const Item tn = item(wn);
-            tma_prefetch_l2_4d(&tmK, 0, tn.kv0, tn.h, tn.b);
-            tma_prefetch_l2_4d(&tmV, 0, tn.kv0, tn.h, tn.b);
-          }
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
       for (int it = 0; it < t.n_it && ok; ++it, ++u) {
         const int st = u % QS;
         const int qq0 = (t.i0 + it) * TILE;
@@ -1076,9 +1060,37 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     if (lane == 0) {
       // every copy issued has landed before shared memory goes away
-      if (kv_loads > 0) mbar_wait(kv_full, (kv_loads - 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
       for (int v = (u > QS ? u - QS : 0); v < u; ++v)
         mbar_wait(qdo_full(v % QS), (v / QS) & 1, p.err, FXB_DERR_ATTN_WAIT);
+    }
+    __syncwarp();
+  } else if (warp == kBwd64WarpKV) {
+    // ------------------------------------------------ K / V loads (lane 0)
+    // each item's K / V, once every MMA of the previous item has completed;
+    // a warp of its own, so that neither the Q / dO ring nor the LSE / delta
+    // reads delay it. The next item's K / V and first query tiles are
+    // prefetched into L2 meanwhile.
+    if (lane == 0) {
+      int k = 0;
+      for (int w = item_of(0); w < n_items; w = item_of(++k)) {
+        const Item t = item(w);
+        if (!mbar_wait(kv_empty, (k & 1) ^ 1, p.err, FXB_DERR_ATTN_WAIT)) break;
+        mbar_expect_tx(kv_full, 2 * QB);
+        tma_load_4d(sK, &tmK, kv_full, 0, t.kv0, t.h, t.b);
+        tma_load_4d(sV, &tmV, kv_full, 0, t.kv0, t.h, t.b);
+        const int wn = item_of(k + 1);
+        if (wn < n_items) {
+          const Item tn = item(wn);
+          tma_prefetch_l2_4d(&tmK, 0, tn.kv0, tn.h, tn.b);
+          tma_prefetch_l2_4d(&tmV, 0, tn.kv0, tn.h, tn.b);
+          for (int j = 0; j < QS - 1 && j < tn.n_it; ++j) {
+            tma_prefetch_l2_4d(&tmQ, 0, (tn.i0 + j) * TILE, tn.h, tn.b);
+            tma_prefetch_l2_4d(&tmDO, 0, (tn.i0 + j) * TILE, tn.h, tn.b);
+          }
+        }
+      }
+      // the last load issued has landed before shared memory goes away
+      if (k > 0) mbar_wait(kv_full, (k - 1) & 1, p.err, FXB_DERR_ATTN_WAIT);
     }
     __syncwarp();
   } else if (warp == kBwd64WarpMma) {
