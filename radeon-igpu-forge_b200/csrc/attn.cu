@@ -11,15 +11,17 @@
 // views, no copies, no multicast) feeds shared memory; one thread issues
 // tcgen05.mma into tensor memory; softmax warps read scores with tcgen05.ld,
 // several warps per TMEM lane quarter, each owning a slice of a tile's columns
-// (forward: 16 warps, row maxima exchanged through shared memory once per
-// tile, row sums combined at the end; persistent CTAs, P written to and O
-// accumulated in TMEM, lazily rescaled: details at the kernel). Backward
-// works per key tile: S^T and dP^T land in TMEM, dV and dK accumulate in TMEM
+// (forward at head dim 128: 16 warps, row maxima exchanged through shared
+// memory once per tile; at head dim 64: two query tiles per CTA and one
+// softmax thread per query row; both persistent, P written to and O
+// accumulated in TMEM, lazily rescaled: details at the kernels). Backward
+// works per key tile (at head dim 64 in persistent CTAs that walk (key tile,
+// batch*head) items): S^T and dP^T land in TMEM, dV and dK accumulate in TMEM
 // across query tiles, and each dQ partial is staged in shared memory and
 // added into an fp32 workspace with asynchronous TMA reductions. Every wait
 // is bounded (FXB_DERR_ATTN_WAIT); after an expired wait a thread keeps
-// stepping through its loop without work so that named barriers are always
-// met by every participant.
+// stepping through its loop without work, or leaves it, so that named
+// barriers are always met by every participant.
 #include <cstdlib>
 
 #include "common.cuh"

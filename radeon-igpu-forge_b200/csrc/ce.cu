@@ -5,9 +5,11 @@
 // atomically adds it into one scalar, ce.hip:89-92; here each row's loss is
 // stored and the caller sums them in a fixed order, so the result does not
 // depend on scheduling), grad = (softmax - onehot) * (*mul), zero for rows
-// whose target is ignore_index or out of [0, V) (ce.hip:43,97-115). The B200 layout keeps
-// the whole row in registers (16-byte vectors), so logits are read from HBM
-// once and the gradient written once; the gradient may overwrite the logits.
+// whose target is ignore_index or out of [0, V) (ce.hip:43,97-115). The B200
+// layout keeps a row in registers (16-byte vectors) up to 8K-16K columns, or in
+// a ring of shared-memory row buffers (32-72 KB rows, V = 32768 in 16-bit), so
+// logits are read from HBM once and the gradient written once; the gradient
+// may overwrite the logits.
 #include "common.cuh"
 #include "internal.h"
 
